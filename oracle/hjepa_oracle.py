@@ -1,0 +1,565 @@
+"""ORACLE ONLY -- test infrastructure, never the product path.
+
+A numpy restatement of the reference's H-JEPA gradient planner (src/hjepa-plan.cpp). Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline leg may import it, and only as the checker.
+
+Parity pin: the restatement is checked against the reference's own planner source compiled
+unmodified against a ggml shim (oracle/Makefile -> oracle/_ref/libhjepa_ref.so) and against the golden
+vectors that library produced (tests/golden/, written by tests/golden/make_golden.py).
+
+Arithmetic follows the reference: float32 values, LayerNorm statistics and the cost reduction in
+float64, the same expression order in the element-wise ops. The matrix products are numpy/BLAS
+float32 and therefore differ from the reference's row-by-row axpy in the last bits only.
+Weights are dequantised with the `gguf` package (gguf-py 0.19.0, an implementation independent of
+both this project and the reference) from the file's own bytes.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+
+f32 = np.float32
+
+
+# ---------------------------------------------------------------------------------------------
+# weights (src/hjepa-plan.cpp:48-206)
+# ---------------------------------------------------------------------------------------------
+def load_tensors(path: str) -> tuple[dict, dict]:
+    """name -> float32 array in PyTorch row-major shape, plus the metadata fields as python values."""
+    import gguf
+    r = gguf.GGUFReader(path)
+    out = {}
+    for t in r.tensors:
+        shape = tuple(int(x) for x in reversed([int(v) for v in t.shape]))
+        data = gguf.quants.dequantize(t.data, t.tensor_type)
+        out[t.name] = np.ascontiguousarray(np.asarray(data, dtype=np.float32).reshape(shape))
+    meta = {}
+    for k, fld in r.fields.items():
+        try:
+            meta[k] = fld.contents()
+        except Exception:
+            pass
+    return out, meta
+
+
+@dataclass
+class Lin:
+    w: np.ndarray            # [out, in]
+    b: Optional[np.ndarray]  # [out] or None
+
+    def __call__(self, x):
+        y = x @ self.w.T
+        if self.b is not None:
+            y = y + self.b
+        return y.astype(f32)
+
+    def back(self, gy):
+        return (gy @ self.w).astype(f32)
+
+
+@dataclass
+class LevelW:
+    hp: dict
+    pos0: np.ndarray
+    act0: Optional[Lin] = None
+    act2: Optional[Lin] = None
+    pact0: Optional[Lin] = None
+    pact2: Optional[Lin] = None
+    in_proj: Optional[Lin] = None
+    cond_proj: Optional[Lin] = None
+    out_proj: Optional[Lin] = None
+    proj0: Optional[Lin] = None
+    proj2: Optional[Lin] = None
+    norm_w: Optional[np.ndarray] = None
+    norm_b: Optional[np.ndarray] = None
+    blocks: list = field(default_factory=list)
+    enc_in_w: Optional[np.ndarray] = None
+    enc_in_b: Optional[np.ndarray] = None
+    enc_out_w: Optional[np.ndarray] = None
+    enc_out_b: Optional[np.ndarray] = None
+    enc_fc1: Optional[Lin] = None
+    enc_fc2: Optional[Lin] = None
+    ae_fc1: Optional[Lin] = None
+    ae_fc2: Optional[Lin] = None
+    ae_out_w: Optional[np.ndarray] = None
+    ae_out_b: Optional[np.ndarray] = None
+    queue: Optional[np.ndarray] = None
+
+
+class Model:
+    """The planner's f32 view of an H-JEPA file (build_plan_model, src/hjepa-plan.cpp:143-206)."""
+
+    def __init__(self, path: str):
+        T, meta = load_tensors(path)
+        self.T = T
+        g = lambda k, d=None: meta.get("jepa.hjepa." + k, d)
+        self.ln_eps = float(g("ln_eps", 1e-5))
+        self.adaln_eps = float(g("adaln_eps", 1e-6))
+        n = int(g("n_levels"))
+        keys = ["embed_dim", "stride", "action_dim", "act_embed_dim", "pred_dim", "pred_n_layer", "pred_n_head",
+                "pred_head_dim", "pred_ffn_dim", "pred_n_frames"]
+        self.levels = []
+        for li in range(n):
+            hp = {k: int(g(k)[li]) for k in keys}
+            for k in ("enc_kind", "act_enc_kind", "pred_kind"):
+                hp[k] = str(g(k)[li])
+            p = f"lvl.{li + 1}."
+            inner = hp["pred_n_head"] * hp["pred_head_dim"]
+            L = LevelW(hp=hp, pos0=T[p + "pred.pos_embed"][0].copy())
+            L.act0, L.act2 = self.lin(p + "act_embed.0"), self.lin(p + "act_embed.2")
+            L.pact0, L.pact2 = self.lin(p + "pred.act_embed.0"), self.lin(p + "pred.act_embed.2")
+            L.in_proj, L.cond_proj = self.lin(p + "pred.in_proj"), self.lin(p + "pred.cond_proj")
+            L.out_proj = self.lin(p + "pred.out_proj")
+            L.proj0, L.proj2 = self.lin(p + "pred.proj.0"), self.lin(p + "pred.proj.2")
+            L.norm_w, L.norm_b = T.get(p + "pred.norm.weight"), T.get(p + "pred.norm.bias")
+            for i in range(hp["pred_n_layer"]):
+                q = p + f"pred.blk.{i}."
+                L.blocks.append(dict(
+                    adaln=self.lin(q + "adaln"),
+                    v=self.lin(q + "attn_qkv", 2 * inner, inner),      # the value third (hjepa-plan.cpp:170-171)
+                    out=self.lin(q + "attn_out"), up=self.lin(q + "ffn_up"), down=self.lin(q + "ffn_down"),
+                    ln1_w=T.get(q + "ln1.weight"), ln1_b=T.get(q + "ln1.bias"),
+                    ln2_w=T.get(q + "ln2.weight"), ln2_b=T.get(q + "ln2.bias")))
+            L.enc_in_w, L.enc_in_b = T.get(p + "enc.in_norm.weight"), T.get(p + "enc.in_norm.bias")
+            L.enc_out_w, L.enc_out_b = T.get(p + "enc.out_norm.weight"), T.get(p + "enc.out_norm.bias")
+            L.enc_fc1, L.enc_fc2 = self.lin(p + "enc.fc1"), self.lin(p + "enc.fc2")
+            L.ae_fc1, L.ae_fc2 = self.lin(p + "act_enc.fc1"), self.lin(p + "act_enc.fc2")
+            L.ae_out_w, L.ae_out_b = T.get(p + "act_enc.out_norm.weight"), T.get(p + "act_enc.out_norm.bias")
+            L.queue = T.get(p + "act_queue")
+            self.levels.append(L)
+
+    def lin(self, name, row0=0, rows=None) -> Optional[Lin]:
+        w = self.T.get(name + ".weight")
+        if w is None:
+            return None
+        b = self.T.get(name + ".bias")
+        rows = w.shape[0] - row0 if rows is None else rows
+        return Lin(np.ascontiguousarray(w[row0:row0 + rows]), None if b is None else b[row0:row0 + rows].copy())
+
+
+# ---------------------------------------------------------------------------------------------
+# element-wise ops with their gradients (src/hjepa-plan.cpp:290-475)
+# ---------------------------------------------------------------------------------------------
+def ln_fwd(x, w, b, eps):
+    """Two-pass mean / variance in float64, inverse std rounded to float32 (hjepa-plan.cpp:299-315)."""
+    xd = x.astype(np.float64)
+    mean = xd.mean(axis=1, keepdims=True)
+    var = ((xd - mean) ** 2).mean(axis=1, keepdims=True)
+    inv = (1.0 / np.sqrt(var + float(f32(eps)))).astype(f32)
+    xhat = (xd - mean).astype(f32) * inv
+    y = xhat
+    if w is not None:
+        y = xhat * w
+    if b is not None:
+        y = y + b
+    return y.astype(f32), (xhat, inv)
+
+
+def ln_bwd(gy, cache, w):
+    xhat, inv = cache
+    gh = gy * w if w is not None else gy
+    gh = gh.astype(f32)
+    m1 = gh.astype(np.float64).mean(axis=1, keepdims=True)
+    m2 = (gh.astype(np.float64) * xhat.astype(np.float64)).mean(axis=1, keepdims=True)
+    return ((gh.astype(np.float64) - m1 - xhat.astype(np.float64) * m2) * inv.astype(np.float64)).astype(f32)
+
+
+def _erf(x):
+    return np.vectorize(math.erf, otypes=[np.float64])(x)
+
+
+def act_fwd(x, kind):
+    if kind == "silu":
+        return (x / (f32(1) + np.exp(-x))).astype(f32)
+    if kind == "relu":
+        return np.where(x > 0, x, f32(0)).astype(f32)
+    return (f32(0.5) * x * (f32(1) + _erf(x * f32(0.70710678118654752)).astype(f32))).astype(f32)
+
+
+def act_bwd(gy, x, kind):
+    if kind == "silu":
+        s = (f32(1) / (f32(1) + np.exp(-x))).astype(f32)
+        dv = s * (f32(1) + x * (f32(1) - s))
+    elif kind == "relu":
+        dv = (x > 0).astype(f32)
+    else:
+        dv = f32(0.5) * (f32(1) + _erf(x * f32(0.70710678118654752)).astype(f32)) + \
+            x * f32(0.39894228040143268) * np.exp(f32(-0.5) * x * x)
+    return (gy * dv.astype(f32)).astype(f32)
+
+
+# ---------------------------------------------------------------------------------------------
+# one predictor step with a context of one state (build_step, hjepa-plan.cpp:630-651)
+# ---------------------------------------------------------------------------------------------
+class StepTape:
+    """Forward values kept for the backward pass of one step."""
+
+
+def step_fwd(m: Model, L: LevelW, s, e):
+    t = StepTape()
+    c = e
+    if L.pact0 is not None:
+        t.pact_u = L.pact0(c)
+        c = L.pact2(act_fwd(t.pact_u, "silu"))
+    x = (s + L.pos0).astype(f32)
+    if L.in_proj is not None:
+        x = L.in_proj(x)
+    if L.cond_proj is not None:
+        c = L.cond_proj(c)
+    t.c = c
+    cs = act_fwd(c, "silu")
+    D = x.shape[1]
+    t.blocks = []
+    for B in L.blocks:
+        bt = {}
+        mod = B["adaln"](cs)
+        bt["mod"] = mod
+        bt["x0"] = x
+        z, bt["ln0a"] = ln_fwd(x, None, None, m.adaln_eps)
+        h = (z * (f32(1) + mod[:, D:2 * D]) + mod[:, 0:D]).astype(f32)
+        bt["za"] = z
+        if B["ln1_w"] is not None:
+            bt["fa"] = h
+            h, bt["ln1"] = ln_fwd(h, B["ln1_w"], B["ln1_b"], m.ln_eps)
+        o = B["out"](B["v"](h))
+        bt["o"] = o
+        x = (x + o * mod[:, 2 * D:3 * D]).astype(f32)
+        bt["x1"] = x
+        z, bt["ln0m"] = ln_fwd(x, None, None, m.adaln_eps)
+        bt["zm"] = z
+        h = (z * (f32(1) + mod[:, 4 * D:5 * D]) + mod[:, 3 * D:4 * D]).astype(f32)
+        if B["ln2_w"] is not None:
+            h, bt["ln2"] = ln_fwd(h, B["ln2_w"], B["ln2_b"], m.ln_eps)
+        u = B["up"](h)
+        bt["u"] = u
+        dn = B["down"](act_fwd(u, "gelu"))
+        bt["dn"] = dn
+        x = (x + dn * mod[:, 5 * D:6 * D]).astype(f32)
+        t.blocks.append(bt)
+    x, t.norm = ln_fwd(x, L.norm_w, L.norm_b, m.ln_eps)
+    if L.out_proj is not None:
+        x = L.out_proj(x)
+    if L.proj0 is not None:
+        t.proj_u = L.proj0(x)
+        x = L.proj2(act_fwd(t.proj_u, "gelu"))
+    return x, t
+
+
+def step_bwd(m: Model, L: LevelW, t: StepTape, gx):
+    """Gradient of one step: d next -> (d s, d e)."""
+    if L.proj0 is not None:
+        gx = L.proj0.back(act_bwd(L.proj2.back(gx), t.proj_u, "gelu"))
+    if L.out_proj is not None:
+        gx = L.out_proj.back(gx)
+    gx = ln_bwd(gx, t.norm, L.norm_w)
+    D = gx.shape[1]
+    gcs = None
+    for B, bt in reversed(list(zip(L.blocks, t.blocks))):
+        mod = bt["mod"]
+        gm = np.zeros_like(mod)
+        # x2 = x1 + dn * gate_m
+        gm[:, 5 * D:6 * D] = gx * bt["dn"]
+        gdn = (gx * mod[:, 5 * D:6 * D]).astype(f32)
+        gh = B["up"].back(act_bwd(B["down"].back(gdn), bt["u"], "gelu"))
+        if B["ln2_w"] is not None:
+            gh = ln_bwd(gh, bt["ln2"], B["ln2_w"])
+        gm[:, 4 * D:5 * D] = gh * bt["zm"]
+        gm[:, 3 * D:4 * D] = gh
+        gz = (gh * (f32(1) + mod[:, 4 * D:5 * D])).astype(f32)
+        gx = (gx + ln_bwd(gz, bt["ln0m"], None)).astype(f32)
+        # x1 = x0 + o * gate_a
+        gm[:, 2 * D:3 * D] = gx * bt["o"]
+        go = (gx * mod[:, 2 * D:3 * D]).astype(f32)
+        gh = B["v"].back(B["out"].back(go))
+        if B["ln1_w"] is not None:
+            gh = ln_bwd(gh, bt["ln1"], B["ln1_w"])
+        gm[:, D:2 * D] = gh * bt["za"]
+        gm[:, 0:D] = gh
+        gz = (gh * (f32(1) + mod[:, D:2 * D])).astype(f32)
+        gx = (gx + ln_bwd(gz, bt["ln0a"], None)).astype(f32)
+        g = B["adaln"].back(gm.astype(f32))
+        gcs = g if gcs is None else (gcs + g).astype(f32)
+    gc = act_bwd(gcs, t.c, "silu")
+    if L.cond_proj is not None:
+        gc = L.cond_proj.back(gc)
+    if L.in_proj is not None:
+        gx = L.in_proj.back(gx)
+    ge = gc
+    if L.pact0 is not None:
+        ge = L.pact0.back(act_bwd(L.pact2.back(gc), t.pact_u, "silu"))
+    return gx, ge
+
+
+def act_embed_fwd(L: LevelW, a):
+    if L.act0 is None:
+        return a, None
+    u = L.act0(a)
+    return L.act2(act_fwd(u, "silu")), u
+
+
+def act_embed_bwd(L: LevelW, u, ge):
+    if L.act0 is None:
+        return ge
+    return L.act0.back(act_bwd(L.act2.back(ge), u, "silu"))
+
+
+def encode_up_fwd(m: Model, up: LevelW, s):
+    """build_encode_up (hjepa-plan.cpp:654-660)."""
+    if up.hp["enc_kind"] == "identity":
+        return s, None
+    x, c1 = ln_fwd(s, up.enc_in_w, up.enc_in_b, m.ln_eps)
+    u = up.enc_fc1(x)
+    x = up.enc_fc2(act_fwd(u, "gelu"))
+    c2 = None
+    if up.enc_out_w is not None:
+        x, c2 = ln_fwd(x, up.enc_out_w, up.enc_out_b, m.ln_eps)
+    return x, (c1, u, c2)
+
+
+def encode_up_bwd(up: LevelW, cache, gx):
+    if cache is None:
+        return gx
+    c1, u, c2 = cache
+    if c2 is not None:
+        gx = ln_bwd(gx, c2, up.enc_out_w)
+    gx = up.enc_fc1.back(act_bwd(up.enc_fc2.back(gx), u, "gelu"))
+    return ln_bwd(gx, c1, up.enc_in_w)
+
+
+# ---------------------------------------------------------------------------------------------
+# cost of candidates (chunk_cost, hjepa-plan.cpp:689-810)
+# ---------------------------------------------------------------------------------------------
+@dataclass
+class CostSpec:
+    level: int = 1
+    horizon: int = 1
+    s0: np.ndarray = None
+    goal: np.ndarray = None          # [n_goal, D_goal]
+    n_goal: int = 1
+    goal_level: int = 1
+    dense: bool = False
+    goal_action: Optional[np.ndarray] = None
+    cost_last_n: int = 1
+    intermediate_cost_weight: float = 1.0
+    action_cost_weight: float = 0.0
+
+
+def scored_states(m: Model, cs: CostSpec) -> int:
+    n = cs.horizon + 1
+    for lv in range(cs.level + 1, cs.goal_level + 1):
+        stride = 1 if cs.dense else m.levels[lv - 1].hp["stride"]
+        n = (n - 1) // stride + 1
+    return n - 1
+
+
+def batch_cost(m: Model, cs: CostSpec, actions, want_grad=True, want_states=False):
+    """costs [n], grad [n, T, A] (or None), states [n, T+1, D] (or None) of candidates `actions`."""
+    L = m.levels[cs.level - 1]
+    n, T, A = actions.shape
+    D = L.hp["embed_dim"]
+    s = np.broadcast_to(cs.s0.astype(f32), (n, D)).copy()
+    preds = [s]
+    tapes, emb_u = [], []
+    for step in range(T):
+        e, u = act_embed_fwd(L, np.ascontiguousarray(actions[:, step, :]).astype(f32))
+        emb_u.append(u)
+        s, tp = step_fwd(m, L, s, e)
+        tapes.append(tp)
+        preds.append(s)
+    # encode the predicted stream up to the goal's level
+    idx = list(range(T + 1))
+    vals = list(preds)
+    enc_caches = []           # per level above: (kept indices into the previous list, caches)
+    for lv in range(cs.level + 1, cs.goal_level + 1):
+        up = m.levels[lv - 1]
+        stride = 1 if cs.dense else up.hp["stride"]
+        keep = list(range(0, len(vals), stride))
+        new_vals, caches = [], []
+        for k in keep:
+            v, c = encode_up_fwd(m, up, vals[k])
+            new_vals.append(v)
+            caches.append(c)
+        enc_caches.append((up, keep, caches))
+        vals = new_vals
+    scored = vals[1:]
+    W = min(max(1, cs.cost_last_n), len(scored))
+    costs = np.zeros(n, np.float32)
+    gscored = [None] * len(scored)
+    for j in range(W):
+        k = len(scored) - W + j
+        g = cs.goal[0 if cs.n_goal == 1 else j].astype(f32)
+        w = f32(cs.intermediate_cost_weight) if (cs.intermediate_cost_weight != 1.0 and W > 1 and j < W - 1) else f32(1)
+        diff = (scored[k] - g).astype(f32)
+        acc = (diff.astype(np.float64) ** 2).sum(axis=1)
+        costs = (costs + w * acc.astype(f32)).astype(f32)
+        if want_grad:
+            gscored[k] = (f32(2) * w * diff).astype(f32)
+    if cs.action_cost_weight != 0.0 and cs.goal_action is not None and cs.goal_level == cs.level + 1 and not cs.dense:
+        raise NotImplementedError("oracle: the action cost is not restated")
+    grad = None
+    if want_grad:
+        # back through the encoders, top level first
+        gvals = [None] + gscored
+        for up, keep, caches in reversed(enc_caches):
+            prev = [None] * (max(keep) + 1 if keep else 0)
+            for k, c, gv in zip(keep, caches, gvals):
+                if gv is not None:
+                    prev[k] = encode_up_bwd(up, c, gv)
+            gvals = prev
+        gpred = [None] * (T + 1)
+        for k, gv in enumerate(gvals):
+            if k <= T:
+                gpred[k] = gv
+        grad = np.zeros_like(actions, dtype=f32)
+        gs = gpred[T] if gpred[T] is not None else np.zeros((n, D), f32)
+        for step in reversed(range(T)):
+            gs_prev, ge = step_bwd(m, L, tapes[step], gs)
+            grad[:, step, :] = act_embed_bwd(L, emb_u[step], ge)
+            gs = gs_prev
+            if gpred[step] is not None:
+                gs = (gs + gpred[step]).astype(f32)
+    states = np.stack(preds, axis=1) if want_states else None
+    return costs, grad, states
+
+
+# ---------------------------------------------------------------------------------------------
+# one level's solve (solve_level, hjepa-plan.cpp:904-959)
+# ---------------------------------------------------------------------------------------------
+def prior_of(L: LevelW, clip_sigma: float):
+    A = L.hp["action_dim"]
+    q = L.queue
+    mean = np.zeros(A, f32)
+    std = np.ones(A, f32)
+    lo = hi = None
+    if q is not None and q.size:
+        qd = q.astype(np.float64)
+        mu = qd.mean(axis=0)
+        var = ((qd - mu) ** 2).sum(axis=0) / qd.shape[0]
+        mean = mu.astype(f32)
+        std = np.maximum(np.sqrt(var).astype(f32), f32(1e-4))
+    if clip_sigma > 0:
+        lo = (mean - f32(clip_sigma) * std).astype(f32)
+        hi = (mean + f32(clip_sigma) * std).astype(f32)
+    elif q is not None and q.size:
+        n = q.shape[0]
+        lo, hi = np.zeros(A, f32), np.zeros(A, f32)
+        for a in range(A):
+            col = np.sort(q[:, a].astype(f32))
+
+            def quant(p):
+                pos = p * (n - 1)
+                i0 = int(math.floor(pos))
+                i1 = min(i0 + 1, n - 1)
+                fr = pos - i0
+                return f32(float(col[i0]) + (float(col[i1]) - float(col[i0])) * fr)
+            lo[a], hi[a] = quant(0.02), quant(0.98)
+    return mean, std, lo, hi
+
+
+def solve_level(m: Model, cs: CostSpec, lp: dict, noise):
+    """`noise(n)` returns n standard-normal draws (the jepa_randn_fn). Returns actions, states, cost, iters."""
+    L = m.levels[cs.level - 1]
+    A, T, S = L.hp["action_dim"], cs.horizon, max(1, lp["n_samples"])
+    mean, std, lo, hi = prior_of(L, lp["action_clip_sigma"])
+    x = np.broadcast_to(mean, (S, T, A)).astype(f32).copy()
+    if S > 1:
+        z = noise((S - 1) * T * A).reshape(S - 1, T, A).astype(f32)
+        x[1:] = (x[1:] + z * std * f32(lp["var_scale"])).astype(f32)
+    b1, b2, eps = f32(0.9), f32(0.999), f32(1e-8)
+    mm = np.zeros_like(x)
+    vv = np.zeros_like(x)
+    best, stalled, iters = math.inf, 0, 0
+    lr, wd = f32(lp["lr"]), f32(lp["weight_decay"])
+    for step in range(lp["n_steps"]):
+        costs, g, _ = batch_cost(m, cs, x, want_grad=True)
+        c1 = f32(1) - np.power(b1, f32(step + 1), dtype=f32)
+        c2 = f32(1) - np.power(b2, f32(step + 1), dtype=f32)
+        step_size = f32(lr / c1)
+        c2s = np.sqrt(c2, dtype=f32)
+        x = (x * (f32(1) - lr * wd)).astype(f32)
+        mm = (b1 * mm + (f32(1) - b1) * g).astype(f32)
+        vv = (b2 * vv + (f32(1) - b2) * g * g).astype(f32)
+        x = (x - step_size * mm / (np.sqrt(vv) / c2s + eps)).astype(f32)
+        if lp["action_noise"] > 0:
+            z = noise(S * T * A).reshape(S, T, A).astype(f32)
+            x = (x + z * f32(lp["action_noise"])).astype(f32)
+        if lo is not None:
+            x = np.minimum(np.maximum(x, lo), hi).astype(f32)
+        iters = step + 1
+        if lp["early_stop_patience"] > 0:
+            score = float(costs.min())
+            improved = (not math.isfinite(best)) or (best - score > lp["early_stop_rel_delta"] * max(abs(best), 1e-12))
+            if improved:
+                best, stalled = score, 0
+            else:
+                stalled += 1
+                if stalled >= lp["early_stop_patience"] and step + 1 >= lp["min_its"]:
+                    break
+    costs, _, states = batch_cost(m, cs, x, want_grad=False, want_states=True)
+    top = int(np.argmin(costs))
+    return x[top].copy(), states[top].copy(), float(costs[top]), iters
+
+
+def plan(m: Model, states, goals, levels: list, noise_for_level):
+    """jepa_hjepa_plan (hjepa-plan.cpp:1165-1256): the levels top-down. `noise_for_level(lv)` gives
+    that level's jepa_randn_fn. Returns (level-1 actions, info dict)."""
+    n_levels = len(m.levels)
+    info = {"planned": [0] * n_levels, "cost": [0.0] * n_levels, "iters": [0] * n_levels, "goal_level": [0] * n_levels}
+    upper = None
+    skipped_goal_level = 0
+    upper_anchored = True
+    for lv in range(n_levels, 0, -1):
+        lp = levels[lv - 1]
+        if lv > 1 and lp["horizon"] == 1:
+            skipped_goal_level = (skipped_goal_level or lv) if lp["horizon_one_goal_upper"] else 0
+            upper = None
+            continue
+        cs = CostSpec(level=lv, horizon=lp["horizon"], s0=states[lv - 1], cost_last_n=lp["cost_last_n"],
+                      intermediate_cost_weight=lp["intermediate_cost_weight"],
+                      action_cost_weight=lp["action_cost_weight"])
+        if upper is None:
+            cs.goal_level = skipped_goal_level or lv
+            cs.goal = np.asarray(goals[cs.goal_level - 1], f32).reshape(1, -1)
+            cs.n_goal = 1
+            cs.dense = cs.goal_level > lv
+            anchored = True
+        else:
+            up = m.levels[lv]
+            u_act, u_states = upper
+            n_up = u_states.shape[0]
+            n_sub = min(levels[lv]["num_subgoals"], n_up - 1)
+            gb = u_states[1:1 + n_sub].copy()
+            anchored = False
+            if 1 + levels[lv]["num_subgoals"] >= n_up and upper_anchored:
+                gb[n_sub - 1] = goals[lv]
+                anchored = True
+            cs.goal_level, cs.goal, cs.n_goal = lv + 1, gb, n_sub
+            cs.goal_action = u_act[:n_sub].copy()
+            if n_sub > 1:
+                expected = (lp["horizon"] + up.hp["stride"]) // up.hp["stride"] - 1
+                if n_sub != expected:
+                    raise ValueError("subgoal count does not match the horizon")
+        a, st, c, it = solve_level(m, cs, lp, noise_for_level(lv))
+        upper = (a, st)
+        info["planned"][lv - 1], info["cost"][lv - 1], info["iters"][lv - 1] = 1, c, it
+        info["goal_level"][lv - 1] = cs.goal_level
+        upper_anchored = anchored
+        skipped_goal_level = 0
+    return upper[0], info
+
+
+def replay(draws):
+    """A noise source over recorded draws (the jepa_randn_fn of the reference's tests)."""
+    buf = np.asarray(draws, f32).ravel()
+    pos = [0]
+
+    def fn(n):
+        out = np.zeros(n, f32)
+        k = min(n, buf.size - pos[0])
+        out[:k] = buf[pos[0]:pos[0] + k]
+        pos[0] += k
+        return out
+    return fn
