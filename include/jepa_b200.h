@@ -1,0 +1,52 @@
+// jepa-b200 extensions: entry points this engine adds next to the jepa.cpp API (include/jepa.h).
+//
+// None of these replaces a reference function; they expose the engine's own pieces so that its kernels
+// can be checked and timed through the same C ABI (plain pointers and sizes, host memory, int 0 / -1
+// returns with the reason in jepa_error_text()), and so that a multi-GPU host can shard a planner.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#include "jepa.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)   // every declaration below is exported
+#endif
+
+// Version string of this engine ("jepa-b200 <version>").
+const char * jepa_b200_version(void);
+
+// C[M,N] = A[M,K] * B[N,K]^T on the current CUDA device through the tcgen05 3xTF32 GEMM of the planner
+// (host buffers, row-major). A kernel check: the planner's linears all run through this kernel.
+int jepa_b200_gemm(const float * A, const float * B, int M, int N, int K, float * C);
+
+// Same product timed on the device: `reps` launches on device-resident operands, returns the mean
+// milliseconds per launch in *ms (CUDA events around the launches).
+int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms);
+
+// Dequantise `rows` GGUF rows of `ne0` values of ggml type `ggml_type` (0 f32, 1 f16, 2 q4_0, 8 q8_0,
+// 30 bf16) from the host bytes `src` into host float32 `dst` by the device kernel the weight loader uses.
+int jepa_b200_dequant(uint32_t ggml_type, const void * src, int64_t rows, int64_t ne0, float * dst);
+
+// Candidate sharding of the planners over `world` GPUs, one process (and one context) per GPU.
+// Rank r plans candidates [r*S/world, (r+1)*S/world) of every level; the ranks exchange only each
+// level's (min cost, index) and the winning plan, through NCCL over NVLink. `nccl_id` is the
+// 128-byte ncclUniqueId from jepa_b200_nccl_unique_id() on rank 0, broadcast by the host.
+// world == 1 turns sharding off. Must be called before the first planner call on `ctx`.
+int jepa_b200_nccl_unique_id(void * out128);
+int jepa_b200_context_set_shard(jepa_context * ctx, int rank, int world, const void * nccl_id);
+
+// Device milliseconds of the last planner call on this context (CUDA events on its stream), and the
+// number of kernels it launched.
+double jepa_b200_last_plan_ms(const jepa_context * ctx);
+long long jepa_b200_last_plan_launches(const jepa_context * ctx);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,355 @@
+// tcgen05 / TMEM / TMA GEMM for sm_100a: C[M,N] = A[M,K] * B[N,K]^T in 3xTF32, fused epilogues.
+//
+// Every dense contraction of the planner (the predictor's V / out / up / down linears, their
+// transposed backward products, the time-batched adaLN modulation and its backward) runs here.
+//
+// Kernel shape (one 128 x BN output tile per CTA, 6 warps):
+//   warp 0      TMA producer: per K-step of 32 it loads A_hi, A_lo (128 x 32 f32 each) and B_hi, B_lo
+//               (BN x 32) into one pipeline stage, 128-byte swizzled, completion on the stage's mbarrier
+//   warp 1      TMEM allocator and MMA issuer: one elected thread issues, per stage, 4 K-slices x 3
+//               tcgen05.mma.kind::tf32 (hi*hi, hi*lo, lo*hi) into a 128 x BN float32 accumulator in
+//               TMEM, then tcgen05.commit releases the stage to the producer
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (each warp owns the TMEM lane quadrant
+//               warp % 4), bias / GELU / gated residual / split, stores to global memory
+// Operand split (hi = x with the low 13 mantissa bits cleared, lo = x - hi) is done by whoever
+// produces the operand, so the mainloop is pure TMA -> tensor core.
+// Every mbarrier wait is bounded (about two seconds of clock64): on a timeout the kernel raises an
+// error flag the host reads, drains what it issued, frees its TMEM and returns.
+#include "kernels.h"
+#include "common.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace jb {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;                  // 32 f32 = one 128-byte swizzle row
+constexpr long long WAIT_LIMIT = 4000000000LL;   // clock64 cycles (~2 s at 1.9 GHz)
+
+__device__ int g_gemm_error = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void * p) {
+    return (uint32_t) __cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// bounded wait; false = gave up (the error flag is raised)
+__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > WAIT_LIMIT) {
+            atomicExch(&g_gemm_error, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * map, int x, int y, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(smem_u32(dst)), "l"((uint64_t) map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 B, 8-row atoms 1024 B apart (SBO), LBO unused (1),
+// descriptor version 1 (sm_100), layout type 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t) ((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t) 1 << 16;
+    d |= (uint64_t) (1024 >> 4) << 32;
+    d |= (uint64_t) 1 << 46;
+    d |= (uint64_t) 2 << 61;
+    return d;
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t * bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float split_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
+
+__device__ __forceinline__ float gelu_f(float x) {
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+__device__ __forceinline__ float gelu_grad(float v) {
+    return 0.5f * (1.0f + erff(v * 0.70710678118654752f)) + v * 0.39894228040143268f * expf(-0.5f * v * v);
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
+              const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
+              int M, int N, int K, GemmEpi ep) {
+    constexpr uint32_t A_BYTES = BM * BK * 4;
+    constexpr uint32_t B_BYTES = BN * BK * 4;
+    constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    // two accumulators: hi*hi in columns [0, BN), the small cross terms hi*lo + lo*hi in [BN, 2 BN).
+    // The tensor core's float32 accumulation rounds toward zero per instruction; keeping the small terms
+    // apart cuts the number of truncations the large partial sum sees by three.
+    constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    // instruction descriptor: D f32 (bit 4), A/B tf32 (2 << 7, 2 << 10), K-major both, N >> 3, M >> 4
+    constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    __shared__ __align__(8) uint64_t full_bar[STAGES];
+    __shared__ __align__(8) uint64_t empty_bar[STAGES];
+    __shared__ __align__(8) uint64_t acc_bar;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int num_k = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        mbar_init(&acc_bar, 1);
+        abort_sh = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(&tmem_base_sh)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_sh;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kt = 0; kt < num_k; kt++) {
+                const int s = kt % STAGES;
+                const uint32_t ph = (uint32_t) (kt / STAGES) & 1u;
+                if (kt >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1)) { abort_sh = 1; break; }
+                if (*(volatile int *) &abort_sh) break;
+                uint8_t * st = smem + (size_t) s * STAGE_BYTES;
+                mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+                tma_load_2d(st, &tA_hi, kt * BK, m0, &full_bar[s]);
+                tma_load_2d(st + A_BYTES, &tA_lo, kt * BK, m0, &full_bar[s]);
+                tma_load_2d(st + 2 * A_BYTES, &tB_hi, kt * BK, n0, &full_bar[s]);
+                tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, kt * BK, n0, &full_bar[s]);
+                issued = kt + 1;
+            }
+            if (*(volatile int *) &abort_sh) {
+                // drain: the copies of the last stages it armed must land before the CTA exits
+                for (int kt = issued - STAGES < 0 ? 0 : issued - STAGES; kt < issued; kt++) {
+                    mbar_wait(&full_bar[kt % STAGES], (uint32_t) (kt / STAGES) & 1u, 5);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int kt = 0; kt < num_k && ok; kt++) {
+                const int s = kt % STAGES;
+                const uint32_t ph = (uint32_t) (kt / STAGES) & 1u;
+                if (!mbar_wait(&full_bar[s], ph, 2)) { abort_sh = 1; ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a_hi = smem_u32(smem + (size_t) s * STAGE_BYTES);
+                const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; kk++) {
+                    const uint32_t off = (uint32_t) kk * 32;   // 8 tf32 = 32 bytes along K
+                    const uint64_t dah = sw128_desc(a_hi + off), dal = sw128_desc(a_lo + off);
+                    const uint64_t dbh = sw128_desc(b_hi + off), dbl = sw128_desc(b_lo + off);
+                    mma_tf32(tmem + BN, dal, dbh, IDESC, (kt | kk) != 0);
+                    mma_tf32(tmem + BN, dah, dbl, IDESC, 1);
+                    mma_tf32(tmem, dah, dbh, IDESC, (kt | kk) != 0);
+                }
+                mma_commit(&empty_bar[s]);
+            }
+            mma_commit(&acc_bar);   // also on abort: completes once the issued MMAs are done
+        }
+    } else {
+        // epilogue warps 2..5: TMEM lane quadrant = warp % 4
+        const int q = warp & 3;
+        const bool ok = mbar_wait(&acc_bar, 0, 3);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (ok && !*(volatile int *) &abort_sh) {
+            const int row = m0 + q * 32 + lane;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t r[32], r2[32];
+                tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) c0, r);
+                tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) (BN + c0), r2);
+                if (row >= M || n0 + c0 >= N) continue;
+                const int nc = min(32, N - (n0 + c0));
+                const int col0 = n0 + c0;
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    if (j >= nc) break;
+                    const int col = col0 + j;
+                    float v = __uint_as_float(r[j]) + __uint_as_float(r2[j]);
+                    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) v = v + ep.bias[col];
+                    switch (ep.mode) {
+                        case EPI_F32:
+                            ep.out0[(size_t) row * ep.ld0 + col] = v;
+                            break;
+                        case EPI_SPLIT: {
+                            const float h = split_hi(v);
+                            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+                            ep.out_lo[(size_t) row * ep.ld_split + col] = v - h;
+                        } break;
+                        case EPI_F32_SPLIT: {
+                            ep.out0[(size_t) row * ep.ld0 + col] = v;
+                            const float h = split_hi(v);
+                            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+                            ep.out_lo[(size_t) row * ep.ld_split + col] = v - h;
+                        } break;
+                        case EPI_GELU_SPLIT: {
+                            ep.out0[(size_t) row * ep.ld0 + col] = v;
+                            const float gv = gelu_f(v);
+                            const float h = split_hi(gv);
+                            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+                            ep.out_lo[(size_t) row * ep.ld_split + col] = gv - h;
+                        } break;
+                        case EPI_GATED: {
+                            ep.out0[(size_t) row * ep.ld0 + col] = v;
+                            const float g = ep.gate[(size_t) row * ep.ld_gate + col];
+                            ep.out1[(size_t) row * ep.ld1 + col] = ep.aux[(size_t) row * ep.ld_aux + col] + v * g;
+                        } break;
+                        case EPI_DGELU_SPLIT: {
+                            const float d = v * gelu_grad(ep.aux[(size_t) row * ep.ld_aux + col]);
+                            const float h = split_hi(d);
+                            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+                            ep.out_lo[(size_t) row * ep.ld_split + col] = d - h;
+                        } break;
+                        default: break;
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side: tensor maps and launch
+// ---------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool load_encode() {
+    std::call_once(g_encode_once, []() {
+        void * fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            g_encode = (PFN_cuTensorMapEncodeTiled_v12000) fn;
+        }
+    });
+    return g_encode != nullptr;
+}
+
+bool make_map(CUtensorMap * map, const float * base, int rows, int cols, int ld, int box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t) cols, (cuuint64_t) rows};
+    const cuuint64_t strides[1] = {(cuuint64_t) ld * 4};
+    const cuuint32_t box[2] = {(cuuint32_t) BK, (cuuint32_t) box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *) base, dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES>
+int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
+    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+    if (!make_map(&ta_hi, A.hi, M, K, A.ld, BM) || !make_map(&ta_lo, A.lo, M, K, A.ld, BM) ||
+        !make_map(&tb_hi, B.hi, N, K, B.ld, BN) || !make_map(&tb_lo, B.lo, N, K, B.ld, BN)) {
+        log("jepa: gemm: cuTensorMapEncodeTiled refused an operand (M %d N %d K %d, ld %d / %d)\n", M, N, K, A.ld, B.ld);
+        return -1;
+    }
+    constexpr size_t smem = (size_t) STAGES * (2 * BM * BK * 4 + 2 * BN * BK * 4) + 1024;
+    static bool attr_set = false;
+    if (!attr_set) {
+        JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem));
+        attr_set = true;
+    }
+    const dim3 grid((unsigned) ((M + BM - 1) / BM), (unsigned) ((N + BN - 1) / BN));
+    k_gemm_tf32x3<BN, STAGES><<<grid, 192, smem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep);
+    JB_CUDA(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace
+
+int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    if (!load_encode()) {
+        log("jepa: gemm: the CUDA driver does not provide cuTensorMapEncodeTiled\n");
+        return -1;
+    }
+    if ((A.ld & 3) || (B.ld & 3) || ((uintptr_t) A.hi & 15) || ((uintptr_t) A.lo & 15) || ((uintptr_t) B.hi & 15) ||
+        ((uintptr_t) B.lo & 15)) {
+        log("jepa: gemm: operands need 16-byte aligned rows (ld %d / %d)\n", A.ld, B.ld);
+        return -1;
+    }
+    const long tiles128 = (long) ((M + BM - 1) / BM) * ((N + 127) / 128);
+    if (tiles128 >= 148) return launch<128, 3>(A, B, M, N, K, ep, st);
+    return launch<64, 4>(A, B, M, N, K, ep, st);
+}
+
+int gemm_error_flag(cudaStream_t st) {
+    int v = 0;
+    cudaMemcpyFromSymbolAsync(&v, g_gemm_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+    cudaStreamSynchronize(st);
+    return v;
+}
+
+}  // namespace jb

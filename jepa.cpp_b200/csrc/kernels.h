@@ -1,0 +1,145 @@
+// Launchers of the sm_100a kernels (implemented in gemm_tc.cu, rowwise.cu, dequant.cu).
+//
+// Data layout everywhere: row-major [rows][cols] float32, one row per candidate (or per candidate and
+// time step), leading dimension = row stride in elements. "Split" operands are the two float32 planes
+// (hi, lo) of the 3xTF32 scheme: hi = x with the low 13 mantissa bits cleared (exact in TF32),
+// lo = x - hi (exact in float32); a product is accumulated as hi*hi + hi*lo + lo*hi, which keeps
+// about 21 bits of each operand instead of TF32's 11.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace jb {
+
+// ------------------------------------------------------------------------------------------
+// tcgen05 GEMM: C[M,N] = A[M,K] * B[N,K]^T (both operands K-contiguous), split operands, fused epilogue
+// ------------------------------------------------------------------------------------------
+enum EpiMode : int {
+    EPI_F32 = 0,         // out0 = acc + bias
+    EPI_SPLIT = 1,       // (out_hi, out_lo) = split(acc + bias)
+    EPI_GELU_SPLIT = 2,  // out0 = u = acc + bias ; (out_hi, out_lo) = split(gelu(u))
+    EPI_GATED = 3,       // out0 = o = acc + bias ; out1 = aux + o * gate
+    EPI_DGELU_SPLIT = 4, // (out_hi, out_lo) = split(acc * gelu'(aux))
+    EPI_F32_SPLIT = 5,   // out0 = acc + bias and (out_hi, out_lo) = split(acc + bias)
+};
+
+struct GemmEpi {
+    int mode = EPI_F32;
+    const float * bias = nullptr;   // [N] or null
+    float * out0 = nullptr; int ld0 = 0;
+    float * out_hi = nullptr; float * out_lo = nullptr; int ld_split = 0;
+    const float * aux = nullptr; int ld_aux = 0;
+    const float * gate = nullptr; int ld_gate = 0;
+    float * out1 = nullptr; int ld1 = 0;
+};
+
+struct SplitMat {                    // a split operand: two float32 planes with one leading dimension
+    const float * hi = nullptr;
+    const float * lo = nullptr;
+    int ld = 0;
+};
+
+// Returns 0, or -1 after logging (unsupported shape / a CUDA error).
+int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st);
+
+// Error flag the tensor-core kernels raise when a bounded wait gives up (0 = fine). Host reads it.
+int gemm_error_flag(cudaStream_t st);
+
+// ------------------------------------------------------------------------------------------
+// SIMT linear for shapes the tensor-core path does not take (tiny K or N):
+//   y[r][o] = sum_i x[r][i] * w[o][i] + b[o]          (w row-major [N][K])
+// ------------------------------------------------------------------------------------------
+void linear_simt(const float * x, int ldx, const float * w, const float * b, float * y, int ldy,
+                 int M, int N, int K, cudaStream_t st);
+
+// ------------------------------------------------------------------------------------------
+// row-wise kernels (one warp per row)
+// ------------------------------------------------------------------------------------------
+struct LnStats { double mean; float inv; float pad; };
+
+// adaLN block prologue: h = ln?( LN0(x) * (1 + mod[sc]) + mod[sh] ), split out; stats saved
+void block_pre(const float * x, int ldx, const float * mod, int ld_mod, int sh_off, int sc_off,
+               const float * ln_w, const float * ln_b, float eps0, float eps1,
+               float * h_hi, float * h_lo, int ldh, LnStats * st0, LnStats * st1, int M, int D, cudaStream_t st);
+
+// LayerNorm with optional affine: y = LN(x) * w + b. Writes f32 y (if y) and/or split (if hi/lo).
+void layer_norm(const float * x, int ldx, const float * w, const float * b, float eps,
+                float * y, int ldy, float * hi, float * lo, LnStats * stats, int M, int D, cudaStream_t st);
+
+// LayerNorm backward: gx = LN_bwd(gy) (+ residual add of `gres` when given), then optionally the
+// gated-residual head of the block below it:
+//   dmod[gate_col] = gx * dn ; (d_hi, d_lo) = split(gx * gate)
+void layer_norm_bwd(const float * gy, int ldgy, const float * x, int ldx, const LnStats * stats, const float * w,
+                    const float * gres, int ldres, float * gx, int ldgx,
+                    const float * dn, int lddn, const float * gate, int ld_gate,
+                    float * dmod_hi, float * dmod_lo, int ld_dmod, float * d_hi, float * d_lo, int ldd,
+                    int M, int D, cudaStream_t st);
+
+// adaLN block backward of one half (the MLP half or the attention half), fused:
+//   gz  = ln?_bwd(gh)                              (ln weight optional)
+//   dmod[sc] = gz * LN0(x) ; dmod[sh] = gz
+//   gx  = gres + LN0_bwd(gz * (1 + mod[sc]))
+//   then the gated-residual head of the next half down (optional):
+//   dmod[gate2] = gx * a2 ; (d_hi, d_lo) = split(gx * mod2[gate2])
+struct BlockBwdArgs {
+    const float * gh; int ldgh;
+    const float * gres; int ldres;
+    const float * x; int ldx;                 // the half's input (recomputes LN0)
+    const LnStats * st0; const LnStats * st1; // LN0 and the inner ln statistics
+    const float * ln_w; const float * ln_b;   // inner ln (null = none)
+    const float * mod; int ld_mod; int sh_off; int sc_off;
+    float * dmod_hi; float * dmod_lo; int ld_dmod;
+    float * gx; int ldgx;
+    // head of the next half down (null a2 = none)
+    const float * a2; int lda2; const float * mod2; int ld_mod2; int gate2_off;
+    float * dmod2_hi; float * dmod2_lo; int ld_dmod2;
+    float * d_hi; float * d_lo; int ldd;
+    int M, D;
+    float eps0, eps1;
+};
+void block_bwd(const BlockBwdArgs & a, cudaStream_t st);
+
+// ------------------------------------------------------------------------------------------
+// element-wise kernels
+// ------------------------------------------------------------------------------------------
+void split_f32(const float * x, int ldx, float * hi, float * lo, int ldo, int M, int N, cudaStream_t st);
+void add_row_vec(const float * x, int ldx, const float * row, float * y, int ldy, int M, int N, cudaStream_t st);
+// act: 0 gelu_erf, 2 silu, 3 relu (the reference's jepa_act_id values)
+void act_fwd(const float * x, int ldx, float * y, int ldy, int M, int N, int act, cudaStream_t st);
+void act_bwd(const float * gy, int ldgy, const float * x, int ldx, float * gx, int ldgx, int M, int N, int act,
+             bool accumulate, cudaStream_t st);
+void add_inplace(float * y, int ldy, const float * x, int ldx, int M, int N, cudaStream_t st);
+void copy_rows(const float * x, int ldx, float * y, int ldy, int M, int N, cudaStream_t st);
+void fill_f32(float * y, float v, size_t n, cudaStream_t st);
+
+// actions x [S][T][A] -> a_all [(t*S + r)][A]
+void gather_actions(const float * x, float * a_all, int S, int T, int A, cudaStream_t st);
+// d a_all [(t*S + r)][A] -> grad [S][T][A]
+void scatter_actions(const float * da, float * grad, int S, int T, int A, cudaStream_t st);
+
+// squared-L2 cost of `W` scored state sets against their goals (double accumulation per row):
+//   cost[r] += w_j * sum_i (p_j[r][i] - g_j[i])^2 ; gp_j[r][i] += 2 * w_j * diff (if want_grad)
+void cost_l2(const float * const * preds, const float * goals, const float * weights, float * const * gpreds,
+             int W, int M, int D, int ldp, float * cost, bool want_grad, cudaStream_t st);
+
+// AdamW + optional noise + clamp, then the t-major copy of the updated actions:
+//   x *= 1 - lr*wd ; m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g g ; x -= step_size m / (sqrt(v)/c2s + eps)
+//   x += z * noise_std ; x = min(max(x, lo[a]), hi[a])
+// sched[2*k], sched[2*k+1] hold step_size and c2s of iteration k; *step_ctr is the iteration index and
+// is incremented by the kernel, so one captured graph replays every iteration.
+void adam_step(float * x, float * m, float * v, const float * grad_tmajor, float * a_all,
+               const float * sched, int * step_ctr, float lr_wd, const float * z, float noise_std,
+               const float * lo, const float * hi, int S, int T, int A, cudaStream_t st);
+
+// index of the first minimum of cost[0..n) (std::min_element semantics) and its value
+void argmin_first(const float * cost, int n, int * idx, float * val, cudaStream_t st);
+
+// ------------------------------------------------------------------------------------------
+// dequantisation: GGUF row bytes -> float32, bit-exact with the block formats
+// ------------------------------------------------------------------------------------------
+int dequant_rows(uint32_t ggml_type, const void * src, float * dst, int64_t rows, int64_t ne0, cudaStream_t st);
+// dst[c][r] = src[r][c]  (rows x cols -> cols x rows)
+void transpose_f32(const float * src, float * dst, int rows, int cols, cudaStream_t st);
+
+}  // namespace jb

@@ -1,0 +1,117 @@
+// Kernel-level entry points of include/jepa_b200.h: the planner's GEMM and dequantisation kernels
+// reached through the C ABI with host buffers, for parity tests and isolated timing.
+#include "kernels.h"
+#include "common.h"
+#include "../../include/jepa_b200.h"
+
+#include <vector>
+
+namespace {
+
+struct DevBuf {
+    void * p = nullptr;
+    ~DevBuf() { if (p) cudaFree(p); }
+    bool alloc(size_t bytes) { return cudaMalloc(&p, bytes) == cudaSuccess; }
+    float * f() const { return (float *) p; }
+};
+
+// split planes of a host matrix, uploaded
+bool upload_split(const float * h, size_t n, DevBuf & raw, DevBuf & hi, DevBuf & lo, int rows, int cols, cudaStream_t st) {
+    if (!raw.alloc(n * 4) || !hi.alloc(n * 4) || !lo.alloc(n * 4)) return false;
+    if (cudaMemcpyAsync(raw.p, h, n * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) return false;
+    jb::split_f32(raw.f(), cols, hi.f(), lo.f(), cols, rows, cols, st);
+    return true;
+}
+
+}  // namespace
+
+extern "C" const char * jepa_b200_version(void) { return "jepa-b200 0.1.0"; }
+
+extern "C" int jepa_b200_gemm(const float * A, const float * B, int M, int N, int K, float * C) {
+    if (!A || !B || !C || M < 1 || N < 1 || K < 1 || (K & 3)) {
+        jb::log("jepa: jepa_b200_gemm: need host buffers and M, N, K >= 1 with K a multiple of 4\n");
+        return -1;
+    }
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    DevBuf ar, ah, al, br, bh, bl, c;
+    int rc = -1;
+    if (upload_split(A, (size_t) M * K, ar, ah, al, M, K, st) && upload_split(B, (size_t) N * K, br, bh, bl, N, K, st) &&
+        c.alloc((size_t) M * N * 4)) {
+        jb::GemmEpi ep;
+        ep.mode = jb::EPI_F32;
+        ep.out0 = c.f();
+        ep.ld0 = N;
+        rc = jb::gemm_tc({ah.f(), al.f(), K}, {bh.f(), bl.f(), K}, M, N, K, ep, st);
+        if (rc == 0 && !jb::cuda_ok(cudaMemcpyAsync(C, c.p, (size_t) M * N * 4, cudaMemcpyDeviceToHost, st), "copy C")) rc = -1;
+        if (rc == 0 && !jb::cuda_ok(cudaStreamSynchronize(st), "gemm")) rc = -1;
+        if (rc == 0 && jb::gemm_error_flag(st) != 0) {
+            jb::log("jepa: jepa_b200_gemm: the tensor-core kernel timed out waiting on its pipeline\n");
+            rc = -1;
+        }
+    } else {
+        jb::log("jepa: jepa_b200_gemm: device allocation or upload failed\n");
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+extern "C" int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms) {
+    if (M < 1 || N < 1 || K < 1 || (K & 3) || reps < 1 || !ms) return -1;
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    DevBuf ah, al, bh, bl, c;
+    int rc = -1;
+    if (ah.alloc((size_t) M * K * 4) && al.alloc((size_t) M * K * 4) && bh.alloc((size_t) N * K * 4) &&
+        bl.alloc((size_t) N * K * 4) && c.alloc((size_t) M * N * 4)) {
+        cudaMemsetAsync(ah.p, 0, (size_t) M * K * 4, st);
+        cudaMemsetAsync(al.p, 0, (size_t) M * K * 4, st);
+        cudaMemsetAsync(bh.p, 0, (size_t) N * K * 4, st);
+        cudaMemsetAsync(bl.p, 0, (size_t) N * K * 4, st);
+        jb::GemmEpi ep;
+        ep.out0 = c.f();
+        ep.ld0 = N;
+        rc = jb::gemm_tc({ah.f(), al.f(), K}, {bh.f(), bl.f(), K}, M, N, K, ep, st);   // warm-up
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaEventRecord(e0, st);
+        for (int i = 0; i < reps && rc == 0; i++) rc = jb::gemm_tc({ah.f(), al.f(), K}, {bh.f(), bl.f(), K}, M, N, K, ep, st);
+        cudaEventRecord(e1, st);
+        if (rc == 0 && jb::cuda_ok(cudaEventSynchronize(e1), "gemm bench")) {
+            float t = 0;
+            cudaEventElapsedTime(&t, e0, e1);
+            *ms = t / reps;
+        } else {
+            rc = -1;
+        }
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+extern "C" int jepa_b200_dequant(uint32_t type, const void * src, int64_t rows, int64_t ne0, float * dst) {
+    if (!src || !dst || rows < 1 || ne0 < 1) return -1;
+    size_t row_bytes = 0;
+    switch (type) {
+        case 0: row_bytes = (size_t) ne0 * 4; break;
+        case 1: case 30: row_bytes = (size_t) ne0 * 2; break;
+        case 8: row_bytes = (size_t) (ne0 / 32) * 34; break;
+        case 2: row_bytes = (size_t) (ne0 / 32) * 18; break;
+        default: jb::log("jepa: jepa_b200_dequant: unsupported ggml type %u\n", type); return -1;
+    }
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    DevBuf s, d;
+    int rc = -1;
+    if (s.alloc(row_bytes * (size_t) rows) && d.alloc((size_t) rows * ne0 * 4) &&
+        cudaMemcpyAsync(s.p, src, row_bytes * (size_t) rows, cudaMemcpyHostToDevice, st) == cudaSuccess) {
+        rc = jb::dequant_rows(type, s.p, d.f(), rows, ne0, st);
+        if (rc == 0 && !jb::cuda_ok(cudaMemcpyAsync(dst, d.p, (size_t) rows * ne0 * 4, cudaMemcpyDeviceToHost, st), "copy")) rc = -1;
+        if (rc == 0 && !jb::cuda_ok(cudaStreamSynchronize(st), "dequant")) rc = -1;
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}

@@ -64,22 +64,24 @@ def fptr(a) -> "C._Pointer":
 
 
 def declare_planner(lib: C.CDLL) -> C.CDLL:
-    """Argument and return types of the H-JEPA planner entry points (include/jepa.h:313-373)."""
+    """Argument and return types of the H-JEPA planner entry points (include/jepa.h:313-373) that `lib` exports."""
     vp = C.c_void_p
-    lib.jepa_hjepa_level_plan_default.restype = LevelPlan
-    lib.jepa_hjepa_level_plan_default.argtypes = []
-    lib.jepa_hjepa_plan_cost.restype = C.c_int
-    lib.jepa_hjepa_plan_cost.argtypes = [vp, C.c_int, FP, C.POINTER(Goal), C.POINTER(LevelPlan), FP, C.c_int,
-                                         C.c_int, FP, FP]
-    lib.jepa_hjepa_solve.restype = C.c_int
-    lib.jepa_hjepa_solve.argtypes = [vp, C.c_int, FP, C.POINTER(Goal), C.POINTER(LevelPlan), RANDN_FN, vp,
-                                     FP, FP, FP, C.POINTER(C.c_int)]
-    lib.jepa_hjepa_horizons.restype = C.c_int
-    lib.jepa_hjepa_horizons.argtypes = [vp, C.POINTER(LevelPlan), C.c_int, C.c_int, C.c_int, C.c_int,
-                                        C.POINTER(C.c_int)]
-    lib.jepa_hjepa_plan.restype = C.c_int
-    lib.jepa_hjepa_plan.argtypes = [vp, C.POINTER(FP), C.POINTER(FP), C.POINTER(LevelPlan), C.c_int, RANDN_FN,
-                                    vp, FP, C.POINTER(PlanInfo)]
+    sigs = {
+        "jepa_hjepa_level_plan_default": (LevelPlan, []),
+        "jepa_hjepa_plan_cost": (C.c_int, [vp, C.c_int, FP, C.POINTER(Goal), C.POINTER(LevelPlan), FP, C.c_int,
+                                           C.c_int, FP, FP]),
+        "jepa_hjepa_solve": (C.c_int, [vp, C.c_int, FP, C.POINTER(Goal), C.POINTER(LevelPlan), RANDN_FN, vp,
+                                       FP, FP, FP, C.POINTER(C.c_int)]),
+        "jepa_hjepa_horizons": (C.c_int, [vp, C.POINTER(LevelPlan), C.c_int, C.c_int, C.c_int, C.c_int,
+                                          C.POINTER(C.c_int)]),
+        "jepa_hjepa_plan": (C.c_int, [vp, C.POINTER(FP), C.POINTER(FP), C.POINTER(LevelPlan), C.c_int, RANDN_FN,
+                                      vp, FP, C.POINTER(PlanInfo)]),
+    }
+    for name, (res, args) in sigs.items():
+        if hasattr(lib, name):
+            f = getattr(lib, name)
+            f.restype = res
+            f.argtypes = args
     return lib
 
 
