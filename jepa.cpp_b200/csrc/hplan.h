@@ -1,0 +1,146 @@
+// H-JEPA gradient planner on the GPU: device weights, per-solve workspaces and the forward / backward
+// sweep of the candidate rollout (the reference's host tape, src/hjepa-plan.cpp:208-810, re-planned as
+// whole-batch kernels).
+#pragma once
+
+#include "kernels.h"
+#include "model.h"
+
+#include <map>
+#include <memory>
+#include <vector>
+
+namespace jb {
+
+// One linear layer on the device. w / wt are float32 [out][in] / [in][out]; the split planes are the
+// tensor-core operands of the forward (y = x W^T, K = in) and backward (dx = dy W, K = out) products.
+struct DLin {
+    int in = 0, out = 0;
+    float * w = nullptr, * wt = nullptr;
+    float * w_hi = nullptr, * w_lo = nullptr, * wt_hi = nullptr, * wt_lo = nullptr;
+    float * b = nullptr;
+    explicit operator bool() const { return in > 0; }
+    bool tc_fwd() const { return in >= 16 && (in % 4) == 0 && out >= 16; }
+    bool tc_bwd() const { return out >= 16 && (out % 4) == 0 && in >= 16; }
+};
+
+struct DBlock {
+    DLin v, out, up, down;
+    float * ln1_w = nullptr, * ln1_b = nullptr, * ln2_w = nullptr, * ln2_b = nullptr;
+};
+
+struct DLevel {
+    HLevel hp;
+    int D = 0, P = 0, F = 0, I = 0, L = 0, A = 0, E = 0, C = 0;   // state, predictor, ffn, inner, layers, action, act-embed, cond widths
+    float * pos0 = nullptr;
+    DLin act0, act2, pact0, pact2, in_proj, cond_proj, out_proj, proj0, proj2;
+    float * norm_w = nullptr, * norm_b = nullptr;
+    std::vector<DBlock> blocks;
+    DLin adaln;                       // every block's adaLN linear stacked: [6 P L][P]
+    // this level's state encoder (applied to states of the level below)
+    float * enc_in_w = nullptr, * enc_in_b = nullptr, * enc_out_w = nullptr, * enc_out_b = nullptr;
+    DLin enc_fc1, enc_fc2;
+    std::vector<float> queue;         // host: recorded latent actions [n][A]
+};
+
+// Device buffers of one encoder application in the goal-projection chain.
+struct EncStage {
+    int lv = 0;                       // level whose encoder runs
+    std::vector<int> src_pos;         // positions (in the previous list) it reads
+    int n = 0;                        // states encoded (excluding the context state)
+    float * in = nullptr;             // gathered inputs [n S][Din]
+    LnStats * st1 = nullptr, * st2 = nullptr;
+    float * h_hi = nullptr, * h_lo = nullptr;   // in_norm output, split
+    float * u = nullptr;              // fc1 pre-activation [n S][H]
+    float * g_hi = nullptr, * g_lo = nullptr;   // gelu(u), split
+    float * y = nullptr;              // fc2 output [n S][Dout]
+    float * out = nullptr;            // after out_norm [n S][Dout] (= y when there is none)
+    float * gout = nullptr, * gy = nullptr, * gin = nullptr;   // gradients
+    float * d_hi = nullptr, * d_lo = nullptr;
+};
+
+struct Workspace {
+    int level = 0, S = 0, T = 0;
+    Arena arena;
+    // actions / optimiser
+    float * x = nullptr, * m = nullptr, * v = nullptr, * grad = nullptr, * a_all = nullptr, * da_all = nullptr;
+    float * sched = nullptr, * z = nullptr, * lo = nullptr, * hi = nullptr;
+    int * step_ctr = nullptr;
+    // conditioning path over R = T S rows
+    float * ae_u = nullptr, * ae_s = nullptr, * e = nullptr, * pa_u = nullptr, * pa_s = nullptr, * c0 = nullptr;
+    float * cpre = nullptr, * cs_hi = nullptr, * cs_lo = nullptr, * mod = nullptr, * dmod_hi = nullptr, * dmod_lo = nullptr;
+    float * dcs = nullptr, * dc = nullptr, * tmpR = nullptr, * tmpR2 = nullptr;
+    // rollout
+    float * states = nullptr;         // [(T+1) S][D]
+    float * gstate = nullptr;         // [(T+1) S][D] cost gradients wrt the states
+    float * xs = nullptr;             // [T][L+1][S][P]
+    float * xmid = nullptr, * o = nullptr, * dn = nullptr;   // [T][L][S][P]
+    float * u = nullptr;              // [T][L][S][F]
+    LnStats * sta0 = nullptr, * sta1 = nullptr, * stm0 = nullptr, * stm1 = nullptr;   // [T][L][S]
+    LnStats * stn = nullptr;          // [T][S]
+    float * yn = nullptr;             // final-norm output when a projection follows [T][S][P]
+    float * yo = nullptr, * pu = nullptr;   // out_proj output / proj0 pre-activation [T][S][*]
+    // scratch
+    float * h_hi = nullptr, * h_lo = nullptr, * v_hi = nullptr, * v_lo = nullptr, * g_hi = nullptr, * g_lo = nullptr;
+    float * gx = nullptr, * gmid = nullptr, * gh = nullptr, * d_hi = nullptr, * d_lo = nullptr, * du_hi = nullptr, * du_lo = nullptr;
+    float * dv_hi = nullptr, * dv_lo = nullptr, * gtmp = nullptr, * gtmp2 = nullptr, * sp_hi = nullptr, * sp_lo = nullptr;
+    // cost
+    float * cost = nullptr, * goals = nullptr, * weights = nullptr;
+    const float ** pred_ptrs = nullptr;
+    float ** gpred_ptrs = nullptr;
+    int * best_idx = nullptr;
+    float * best_val = nullptr;
+    std::vector<EncStage> enc;
+    // captured graphs
+    cudaGraphExec_t g_iter = nullptr, g_fwd = nullptr;
+    std::string graph_key, iter_key;
+    long long iter_nodes = 0, fwd_nodes = 0;
+    ~Workspace();
+};
+
+// What one batch_cost evaluates (reference: cost_spec, src/hjepa-plan.cpp:689-701)
+struct CostSpec {
+    int level = 1, horizon = 1;
+    const float * s0 = nullptr;
+    const float * goal = nullptr;
+    int n_goal = 1, goal_level = 1;
+    bool dense = false;
+    const float * goal_action = nullptr;
+    int cost_last_n = 1;
+    float intermediate_cost_weight = 1.0f, action_cost_weight = 0.0f;
+};
+
+struct SolveOut {
+    std::vector<float> actions, states;
+    float cost = 0.0f;
+    int iters = 0;
+};
+
+struct NoiseSource;
+
+struct HPlanner {
+    jepa_context * ctx = nullptr;
+    float ln_eps = 1e-5f, adaln_eps = 1e-6f;
+    std::vector<DLevel> levels;
+    std::vector<void *> allocations;
+    std::map<int, std::unique_ptr<Workspace>> ws;   // one workspace per level
+    long long launches = 0;
+
+    ~HPlanner();
+    bool build(const jepa_model & m);
+    Workspace * workspace(int level, int S, int T, const CostSpec & cs);
+    // costs [S] and (optionally) grad [S][T][A] of host actions; all host buffers
+    int plan_cost(const CostSpec & cs, const float * actions, int S, float * costs, float * grad);
+    int solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, NoiseSource & noise, SolveOut & out);
+
+    // pieces
+    int forward(Workspace & w, const CostSpec & cs, bool want_grad);
+    int backward(Workspace & w, const CostSpec & cs);
+    bool cost_tables(Workspace & w, const CostSpec & cs);
+    int lin_fwd(const DLin & L, const float * x, int ldx, const float * x_hi, const float * x_lo, int M, float * y, int ldy,
+                float * y_hi, float * y_lo, Workspace & w);
+    int lin_bwd(const DLin & L, const float * dy, int lddy, const float * dy_hi, const float * dy_lo, int M, float * dx, int lddx,
+                Workspace & w);
+};
+
+}  // namespace jb

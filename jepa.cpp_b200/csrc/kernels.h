@@ -127,9 +127,10 @@ void cost_l2(const float * const * preds, const float * goals, const float * wei
 //   x *= 1 - lr*wd ; m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g g ; x -= step_size m / (sqrt(v)/c2s + eps)
 //   x += z * noise_std ; x = min(max(x, lo[a]), hi[a])
 // sched[2*k], sched[2*k+1] hold step_size and c2s of iteration k; *step_ctr is the iteration index and
-// is incremented by the kernel, so one captured graph replays every iteration.
+// is incremented by the kernel, so one captured graph replays every iteration. The noise of iteration k
+// is z + k * z_stride (z_stride 0: one slot refilled by the host every iteration).
 void adam_step(float * x, float * m, float * v, const float * grad_tmajor, float * a_all,
-               const float * sched, int * step_ctr, float lr_wd, const float * z, float noise_std,
+               const float * sched, int * step_ctr, float lr_wd, const float * z, float noise_std, size_t z_stride,
                const float * lo, const float * hi, int S, int T, int A, cudaStream_t st);
 
 // index of the first minimum of cost[0..n) (std::min_element semantics) and its value

@@ -331,8 +331,8 @@ __global__ void k_cost_l2(CostArgs c) {
 
 __global__ void k_adam(float * __restrict__ x, float * __restrict__ m, float * __restrict__ v, const float * __restrict__ g_t,
                        float * __restrict__ a_all, const float * __restrict__ sched, int * step_ctr, float lr_wd,
-                       const float * __restrict__ z, float noise_std, const float * __restrict__ lo, const float * __restrict__ hi,
-                       int S, int T, int A) {
+                       const float * __restrict__ z, float noise_std, size_t z_stride, const float * __restrict__ lo,
+                       const float * __restrict__ hi, int S, int T, int A) {
     const size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x;   // over [S][T][A]
     const size_t N = (size_t) S * T * A;
     const int k = *(volatile int *) step_ctr;
@@ -348,7 +348,7 @@ __global__ void k_adam(float * __restrict__ x, float * __restrict__ m, float * _
         const float mv = b1 * m[idx] + (1.0f - b1) * g;
         const float vv = b2 * v[idx] + (1.0f - b2) * g * g;
         xv = xv - step_size * mv / (sqrtf(vv) / c2s + eps);
-        if (z) xv = xv + z[idx] * noise_std;
+        if (z) xv = xv + z[(size_t) k * z_stride + idx] * noise_std;
         if (lo) xv = fminf(fmaxf(xv, lo[a]), hi[a]);
         x[idx] = xv;
         m[idx] = mv;
@@ -487,10 +487,10 @@ void cost_l2(const float * const * preds, const float * goals, const float * wei
 }
 
 void adam_step(float * x, float * m, float * v, const float * grad_tmajor, float * a_all, const float * sched,
-               int * step_ctr, float lr_wd, const float * z, float noise_std, const float * lo, const float * hi, int S,
-               int T, int A, cudaStream_t st) {
+               int * step_ctr, float lr_wd, const float * z, float noise_std, size_t z_stride, const float * lo,
+               const float * hi, int S, int T, int A, cudaStream_t st) {
     const size_t n = (size_t) S * T * A;
-    k_adam<<<blocks_for(n), 256, 0, st>>>(x, m, v, grad_tmajor, a_all, sched, step_ctr, lr_wd, z, noise_std, lo, hi, S, T, A);
+    k_adam<<<blocks_for(n), 256, 0, st>>>(x, m, v, grad_tmajor, a_all, sched, step_ctr, lr_wd, z, noise_std, z_stride, lo, hi, S, T, A);
 }
 
 void argmin_first(const float * cost, int n, int * idx, float * val, cudaStream_t st) {

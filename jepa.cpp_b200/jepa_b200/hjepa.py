@@ -1,0 +1,128 @@
+"""Python view of the engine's H-JEPA planner through its C ABI (libjepa.so), mirroring the planner
+calls of the reference's binding (python/src/jepa_cpp/model.py:994-1127): one model + context, costs
+and gradients of candidates, one level's solve, the top-down hierarchy. Host numpy arrays in and out.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import capi
+from . import lib as jlib
+
+
+class Planner:
+    def __init__(self, path: str, device: int = -1, verbose: bool = False):
+        self.lib = L = jlib.load()
+        L.jepa_model_load.restype = C.c_void_p
+        L.jepa_model_load.argtypes = [C.c_char_p, C.c_bool]
+        L.jepa_context_new.restype = C.c_void_p
+        L.jepa_context_new.argtypes = [C.c_void_p, _CtxParams]
+        L.jepa_context_default_params.restype = _CtxParams
+        L.jepa_hjepa_embed_dim.argtypes = [C.c_void_p, C.c_int]
+        L.jepa_hjepa_action_dim.argtypes = [C.c_void_p, C.c_int]
+        L.jepa_hjepa_n_levels.argtypes = [C.c_void_p]
+        L.jepa_error_reset()
+        if device >= 0:
+            L.jepa_model_load_ex.restype = C.c_void_p
+            L.jepa_model_load_ex.argtypes = [C.c_char_p, C.POINTER(_ModelParams)]
+            mp = _ModelParams(verbose, device)
+            self.model = L.jepa_model_load_ex(path.encode(), C.byref(mp))
+        else:
+            self.model = L.jepa_model_load(path.encode(), verbose)
+        if not self.model:
+            raise RuntimeError(f"jepa_model_load({path}) failed: {jlib.error_text()}")
+        self.ctx = L.jepa_context_new(self.model, L.jepa_context_default_params())
+        if not self.ctx:
+            raise RuntimeError(f"jepa_context_new failed: {jlib.error_text()}")
+        self.n_levels = L.jepa_hjepa_n_levels(self.model)
+
+    def close(self) -> None:
+        if getattr(self, "ctx", None):
+            self.lib.jepa_context_free(C.c_void_p(self.ctx))
+            self.lib.jepa_model_free(C.c_void_p(self.model))
+            self.ctx = self.model = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def embed_dim(self, level: int) -> int:
+        return self.lib.jepa_hjepa_embed_dim(self.model, level)
+
+    def action_dim(self, level: int) -> int:
+        return self.lib.jepa_hjepa_action_dim(self.model, level)
+
+    def set_shard(self, rank: int, world: int, nccl_id: Optional[bytes]) -> None:
+        buf = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
+        if self.lib.jepa_b200_context_set_shard(self.ctx, rank, world, buf) != 0:
+            raise RuntimeError(f"jepa_b200_context_set_shard failed: {jlib.error_text()}")
+
+    def last_ms(self) -> float:
+        return self.lib.jepa_b200_last_plan_ms(self.ctx)
+
+    def last_launches(self) -> int:
+        return self.lib.jepa_b200_last_plan_launches(self.ctx)
+
+    def plan_cost(self, level, state, goal, actions, goal_level=0, dense=0, plan: Optional[dict] = None,
+                  want_grad=True, goal_actions=None):
+        actions = np.ascontiguousarray(actions, np.float32)
+        S, T, _ = actions.shape
+        state = np.ascontiguousarray(state, np.float32)
+        goal = np.ascontiguousarray(np.atleast_2d(goal), np.float32)
+        ga = None if goal_actions is None else np.ascontiguousarray(goal_actions, np.float32)
+        g = capi.Goal(capi.fptr(goal), goal.shape[0], goal_level, dense, capi.fptr(ga))
+        lp = capi.LevelPlan.of(**plan) if plan is not None else None
+        costs = np.zeros(S, np.float32)
+        grad = np.zeros_like(actions) if want_grad else None
+        rc = self.lib.jepa_hjepa_plan_cost(self.ctx, level, capi.fptr(state), C.byref(g),
+                                           C.byref(lp) if lp is not None else None, capi.fptr(actions), S, T,
+                                           capi.fptr(costs), capi.fptr(grad))
+        if rc != 0:
+            raise RuntimeError(f"jepa_hjepa_plan_cost failed: {jlib.error_text()}")
+        return costs, grad
+
+    def solve(self, level, state, goal, plan: dict, noise=None, goal_level=0, n_goal=None):
+        goal = np.ascontiguousarray(np.atleast_2d(goal), np.float32)
+        state = np.ascontiguousarray(state, np.float32)
+        g = capi.Goal(capi.fptr(goal), n_goal or goal.shape[0], goal_level, 0, capi.fptr(None))
+        lp = capi.LevelPlan.of(**plan)
+        T, A, D = plan["horizon"], self.action_dim(level), self.embed_dim(level)
+        act = np.zeros((T, A), np.float32)
+        st = np.zeros((T + 1, D), np.float32)
+        cost, it = C.c_float(), C.c_int()
+        rp = capi.Replay(noise) if noise is not None else None
+        fn = rp.fn if rp is not None else capi.RANDN_FN()
+        rc = self.lib.jepa_hjepa_solve(self.ctx, level, capi.fptr(state), C.byref(g), C.byref(lp), fn, None,
+                                       capi.fptr(act), capi.fptr(st), C.byref(cost), C.byref(it))
+        if rc != 0:
+            raise RuntimeError(f"jepa_hjepa_solve failed: {jlib.error_text()}")
+        return act, st, cost.value, it.value, (rp.pos if rp is not None else None)
+
+    def plan(self, states: Sequence[np.ndarray], goals: Sequence[np.ndarray], plans: Sequence[dict], noise=None):
+        n = len(plans)
+        sts = [np.ascontiguousarray(s, np.float32) for s in states]
+        gls = [np.ascontiguousarray(g, np.float32) for g in goals]
+        SP = (capi.FP * n)(*[capi.fptr(s) for s in sts])
+        GP = (capi.FP * n)(*[capi.fptr(g) for g in gls])
+        lps = (capi.LevelPlan * n)(*[capi.LevelPlan.of(**p) for p in plans])
+        out = np.zeros((plans[0]["horizon"], self.action_dim(1)), np.float32)
+        info = capi.PlanInfo()
+        rp = capi.Replay(noise) if noise is not None else None
+        fn = rp.fn if rp is not None else capi.RANDN_FN()
+        rc = self.lib.jepa_hjepa_plan(self.ctx, SP, GP, lps, n, fn, None, capi.fptr(out), C.byref(info))
+        if rc != 0:
+            raise RuntimeError(f"jepa_hjepa_plan failed: {jlib.error_text()}")
+        return out, info, (rp.pos if rp is not None else None)
+
+
+class _CtxParams(C.Structure):
+    _fields_ = [("n_threads", C.c_int), ("use_flash_attn", C.c_bool), ("verbose", C.c_bool), ("flash_kv", C.c_int)]
+
+
+class _ModelParams(C.Structure):
+    _fields_ = [("verbose", C.c_bool), ("device", C.c_int)]
