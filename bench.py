@@ -1,0 +1,337 @@
+"""Benchmark of the H-JEPA gradient planner on B200, and the reference arm.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2]
+
+Workload (N = 1): BASELINE configs[1] -- a 2-level H-JEPA hierarchy, q8_0 GGUF, seeded random init
+(weights N(0, 0.02), biases 0, LayerNorm gamma 1), each level's predictor 6 layers x 384 wide, 6 heads,
+MLP 1536; level 2 plans 4 steps over 384-d subgoal latents, level 1 plans 16 steps of 2-d actions
+scored against level 2's subgoals; 256 candidates, 50 Adam steps per level (early stopping off,
+weight decay 0). Start and goal latents N(0, 1); candidates initialised U[-1, 1] through the
+jepa_randn_fn hook (prior mean 0, std 1, candidate 0 at the mean), as the measurement rule maps it.
+
+A step is one jepa_hjepa_plan call (both levels: 100 grad-steps). The metric is grad-steps/s, where a
+grad-step is one Adam iteration of one level over the config's 256 candidates. With N GPUs the plan
+holds 256 N candidates sharded 256 per GPU (candidate sharding, one NCCL exchange per level): weak
+scaling, value = N * 100 * K / (max over ranks of the device time).
+
+`value` is device time (CUDA events on the planner's stream around each call, weights resident);
+`e2e` is host wall-clock around the same C-ABI calls with host buffers in and out. The reference arm
+runs the reference's own planner source (src/hjepa-plan.cpp, compiled against the ggml shim, oracle/)
+on the host cores, one level-1 and one level-2 gradient evaluation per step.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "jepa.cpp_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+from jepa_b200 import capi, synth  # noqa: E402
+
+METRIC = "H-JEPA plan grad-steps/s & V-JEPA2-AC CEM candidates/s at 1/2/4/8 B200"
+UNIT = "grad-steps/s"
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+
+
+def row_step_flops(lv: synth.Level) -> float:
+    """Forward GEMM FLOPs of one predictor row-step (adaLN 12P^2, V and out 2PI each, up and down 2PF each
+    per layer, plus the action Linear), the measurement rule's per-unit figure."""
+    P, I, F = lv.P(), lv.n_head * lv.hd(), lv.ffn_dim
+    return lv.n_layer * (12 * P * P + 4 * P * I + 4 * P * F) + 2 * lv.E() * P
+
+
+def plan_flops(spec: synth.HJepaSpec, plans: list, S: int) -> float:
+    """Algorithmic FLOPs of one jepa_hjepa_plan: per level n_steps x (forward + backward-to-inputs) of
+    S x T row-steps plus the final forward, plus the goal-projection encoders of the level below."""
+    total = 0.0
+    for k, (lv, p) in enumerate(zip(spec.levels, plans)):
+        rows = S * p["horizon"]
+        f = row_step_flops(lv)
+        enc = 0.0
+        if k + 1 < len(spec.levels):   # this level's predictions are encoded by the level above's encoder
+            up = spec.levels[k + 1]
+            n_enc = p["horizon"] // up.stride
+            h = up.enc_hidden or up.embed_dim
+            enc = S * n_enc * (2 * lv.embed_dim * h + 2 * h * up.embed_dim)
+        total += p["n_steps"] * (2 * rows * f + 2 * enc) + rows * f + enc
+    return total
+
+
+def peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, gpu: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={gpu}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def setup_model(cfg: int, workdir: str) -> tuple[str, synth.HJepaSpec, list]:
+    spec, plans = synth.hjepa_config(cfg)
+    path = os.path.join(workdir, f"bench-cfg{cfg}.gguf")
+    if not os.path.exists(path):
+        synth.write_hjepa(path, spec, seed=cfg)
+    return path, spec, plans
+
+
+def inputs(spec: synth.HJepaSpec, seed: int = 1):
+    rng = np.random.default_rng(seed)
+    states = [rng.normal(size=l.embed_dim).astype(np.float32) for l in spec.levels]
+    goals = [rng.normal(size=l.embed_dim).astype(np.float32) for l in spec.levels]
+    return states, goals
+
+
+def uniform_draws(spec, plans, S):
+    """U[-1, 1] values standing in for the candidates' initial perturbation (prior mean 0, std 1)."""
+    n = sum((S - 1) * p["horizon"] * l.action_dim for l, p in zip(spec.levels, plans))
+    return np.random.default_rng(7).uniform(-1.0, 1.0, n).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------------------------
+def cpu_reference(path, spec, plans, S, steps, warmup, threads):
+    """The reference planner (oracle/_ref) on the host: one gradient evaluation of every level per step."""
+    import ref
+    if not ref.available():
+        return None
+    P = ref.RefPlanner(path, n_threads=threads)
+    states, goals = inputs(spec)
+    rng = np.random.default_rng(3)
+    levels = []
+    for k, (lv, p) in enumerate(zip(spec.levels, plans)):
+        level = k + 1
+        T, A = p["horizon"], lv.action_dim
+        acts = rng.uniform(-1, 1, (S, T, A)).astype(np.float32)
+        if level < len(spec.levels):
+            up = spec.levels[level]
+            n_goal = p["cost_last_n"]
+            goal = rng.normal(size=(n_goal, up.embed_dim)).astype(np.float32)
+            g = capi.Goal(capi.fptr(goal), n_goal, level + 1, 0, capi.fptr(None))
+        else:
+            goal = goals[k].reshape(1, -1)
+            g = capi.Goal(capi.fptr(goal), 1, 0, 0, capi.fptr(None))
+        lp = capi.LevelPlan.of(**p)
+        levels.append((level, acts, goal, g, lp, np.zeros(S, np.float32), np.zeros_like(acts)))
+
+    def one():
+        for level, acts, goal, g, lp, costs, grad in levels:
+            s0 = states[level - 1]
+            rc = P.lib.jepa_hjepa_plan_cost(P.ctx, level, capi.fptr(s0), C.byref(g), C.byref(lp), capi.fptr(acts),
+                                            S, acts.shape[1], capi.fptr(costs), capi.fptr(grad))
+            assert rc == 0
+    for _ in range(warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = time.perf_counter() - t0
+    P.close()
+    return dt / steps   # seconds per (one grad-step of every level)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    with tempfile.TemporaryDirectory() as tmp:
+        path, spec, plans = setup_model(args.config, os.environ.get("JEPA_BENCH_DIR", tmp))
+        S = plans[0]["n_samples"]
+        per = cpu_reference(path, spec, plans, S, args.steps, args.warmup, threads)
+    base = {"metric": METRIC, "unit": UNIT, "impl": "reference", "higher_is_better": True, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "dtype": "f32", "data": "synthetic", "scaling": "weak",
+            "config": {"workload": f"hjepa-config{args.config}", "levels": len(spec.levels), "candidates": S}}
+    if per is None:
+        base["unavailable"] = "oracle/_ref/libhjepa_ref.so is not built (needs the reference tree at build time)"
+        print(json.dumps(base))
+        return
+    n_levels = len(plans)
+    value = n_levels / per          # grad-steps of the config's candidates per second
+    sample = (f"{args.steps} step(s) x one gradient evaluation of each of the {n_levels} levels at S={S} "
+              f"(one Adam iteration per level), reference src/hjepa-plan.cpp via oracle/_ref, {threads} threads")
+    base.update({"value": value, "ms_per_step": per * 1e3,
+                 "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+                 "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                 "vs_baseline": None})
+    print(json.dumps(base))
+
+
+# ---------------------------------------------------------------------------------------------
+def run_ours(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    from jepa_b200.hjepa import Planner
+    from jepa_b200 import lib as jlib
+
+    workdir = os.environ.get("JEPA_BENCH_DIR", tempfile.gettempdir())
+    path = os.path.join(workdir, f"bench-cfg{args.config}.gguf")
+    spec, plans = synth.hjepa_config(args.config)
+    if rank == 0 and not os.path.exists(path):
+        synth.write_hjepa(path + ".tmp", spec, seed=args.config)
+        os.replace(path + ".tmp", path)
+    if dist:
+        dist.barrier()
+    S1 = plans[0]["n_samples"]
+    S = S1 * world
+    plans = [dict(p, n_samples=S) for p in plans]
+    P = Planner(path, device=local)
+    if world > 1:
+        uid = C.create_string_buffer(128)
+        if rank == 0:
+            assert jlib.load().jepa_b200_nccl_unique_id(uid) == 0
+        obj = [bytes(uid.raw)] if rank == 0 else [None]
+        dist.broadcast_object_list(obj, src=0)
+        P.set_shard(rank, world, obj[0])
+    states, goals = inputs(spec)
+    draws = uniform_draws(spec, plans, S)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")   # 256 MiB > L2
+
+    def step():
+        out, info, used = P.plan(states, goals, plans, noise=draws)
+        return P.last_ms(), P.last_launches(), out, info
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = Clocks(local)
+    dev_ms, launches, wall = 0.0, 0, 0.0
+    for _ in range(args.steps):
+        flush.fill_(1.0)                       # L2 flushed between timed iterations
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ms, nl, out, info = step()
+        wall += time.perf_counter() - t0
+        dev_ms += ms
+        launches += nl
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = clk.stop()
+    t = torch.tensor([dev_ms, wall], dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms, wall = float(t[0]), float(t[1])
+    grad_steps = sum(p["n_steps"] for p in plans) * args.steps * world   # in units of the config's 256 candidates
+    value = grad_steps / (dev_ms / 1e3)
+    e2e = grad_steps / wall
+    peak_tf, peak_hbm, peak_kind = peaks()
+    flops = plan_flops(spec, plans, S) * args.steps
+    achieved_tf = flops / (dev_ms / 1e3) / 1e12
+    A = spec.levels[0].action_dim
+    h2d = sum(l.embed_dim * 4 * 2 for l in spec.levels) + draws.nbytes + \
+        sum(S1 * p["horizon"] * l.action_dim * 4 for l, p in zip(spec.levels, plans))
+    d2h = plans[0]["horizon"] * A * 4 + sum((p["horizon"] + 1) * l.embed_dim * 4 + p["horizon"] * l.action_dim * 4 + 8
+                                            for l, p in zip(spec.levels, plans))
+    if rank == 0:
+        res = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded random-init q8_0 GGUF, N(0,1) latents, U[-1,1] candidates)",
+            "config": {"workload": f"hjepa-config{args.config}: 2-level q8_0, D384 L6 F1536, horizons 16/4, "
+                                   f"{S1} candidates per GPU, 50 Adam steps per level",
+                       "candidates_total": S, "parallelism": f"candidates sharded over {world} GPU(s)",
+                       "l2": "flushed (256 MiB write) before every timed step; working set > L2",
+                       "arith": "3xTF32 tensor-core GEMMs (tcgen05), f32 element-wise"},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved_tf / peak_tf, "traffic": None,
+                         "scope": "whole plan: algorithmic GEMM FLOPs / device time of the jepa_hjepa_plan call",
+                         "peak_kind": f"bf16 dense, {peak_kind}"},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                per = cpu_reference(path, spec, [dict(p, n_samples=S1) for p in plans], S1, 1, 0, os.cpu_count() or 1)
+            except Exception as e:   # the baseline is reported, never required
+                per = None
+                res["cpu_baseline_error"] = str(e)
+            if per is not None:
+                res["cpu_baseline"] = {"value": len(plans) / per, "unit": UNIT, "cores": os.cpu_count() or 1,
+                                       "kind": "reference",
+                                       "sample": "one gradient evaluation of each level at S=256 (one Adam iteration per "
+                                                 "level) with the reference's src/hjepa-plan.cpp via oracle/_ref"}
+        print(json.dumps(res))
+    del flush
+    P.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
