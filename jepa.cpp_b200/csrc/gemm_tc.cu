@@ -17,6 +17,7 @@
 // error flag the host reads, drains what it issued, frees its TMEM and returns.
 #include "kernels.h"
 #include "common.h"
+#include "launch.h"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -121,23 +122,149 @@ __device__ __forceinline__ float gelu_grad(float v) {
     return 0.5f * (1.0f + erff(v * 0.70710678118654752f)) + v * 0.39894228040143268f * expf(-0.5f * v * v);
 }
 
+// the fused epilogue of one output element (v = the accumulated product, before the bias)
+__device__ __forceinline__ void apply_epi(const GemmEpi & ep, int row, int col, float v) {
+    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) v = v + ep.bias[col];
+    switch (ep.mode) {
+        case EPI_F32:
+            ep.out0[(size_t) row * ep.ld0 + col] = v;
+            break;
+        case EPI_SPLIT: {
+            const float h = split_hi(v);
+            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+            ep.out_lo[(size_t) row * ep.ld_split + col] = v - h;
+        } break;
+        case EPI_F32_SPLIT: {
+            ep.out0[(size_t) row * ep.ld0 + col] = v;
+            const float h = split_hi(v);
+            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+            ep.out_lo[(size_t) row * ep.ld_split + col] = v - h;
+        } break;
+        case EPI_GELU_SPLIT: {
+            ep.out0[(size_t) row * ep.ld0 + col] = v;
+            const float gv = gelu_f(v);
+            const float h = split_hi(gv);
+            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+            ep.out_lo[(size_t) row * ep.ld_split + col] = gv - h;
+        } break;
+        case EPI_GATED: {
+            ep.out0[(size_t) row * ep.ld0 + col] = v;
+            const float g = ep.gate[(size_t) row * ep.ld_gate + col];
+            ep.out1[(size_t) row * ep.ld1 + col] = ep.aux[(size_t) row * ep.ld_aux + col] + v * g;
+        } break;
+        case EPI_DGELU_SPLIT: {
+            const float d = v * gelu_grad(ep.aux[(size_t) row * ep.ld_aux + col]);
+            const float h = split_hi(d);
+            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+            ep.out_lo[(size_t) row * ep.ld_split + col] = d - h;
+        } break;
+        default: break;
+    }
+}
+
+__device__ __forceinline__ float4 f4_add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+__device__ __forceinline__ float4 f4_mul(float4 a, float4 b) { return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w); }
+__device__ __forceinline__ float4 f4_hi(float4 a) { return make_float4(split_hi(a.x), split_hi(a.y), split_hi(a.z), split_hi(a.w)); }
+__device__ __forceinline__ float4 f4_sub(float4 a, float4 b) { return make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w); }
+__device__ __forceinline__ float4 ld4(const float * p) { return *(const float4 *) p; }
+__device__ __forceinline__ void st4(float * p, float4 v) { *(float4 *) p = v; }
+
+// four consecutive columns of the fused epilogue: vector loads / stores when the operands allow it
+// (ep.vec: every pointer 16-byte aligned, every leading dimension a multiple of 4), else element-wise
+__device__ __forceinline__ void apply_epi4(const GemmEpi & ep, int row, int col, int N, float4 v) {
+    if (!ep.vec || col + 3 >= N) {
+        const float e[4] = {v.x, v.y, v.z, v.w};
+        for (int j = 0; j < 4; j++) if (col + j < N) apply_epi(ep, row, col + j, e[j]);
+        return;
+    }
+    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) v = f4_add(v, ld4(ep.bias + col));
+    switch (ep.mode) {
+        case EPI_F32: st4(ep.out0 + (size_t) row * ep.ld0 + col, v); break;
+        case EPI_SPLIT: {
+            const float4 h = f4_hi(v);
+            st4(ep.out_hi + (size_t) row * ep.ld_split + col, h);
+            st4(ep.out_lo + (size_t) row * ep.ld_split + col, f4_sub(v, h));
+        } break;
+        case EPI_F32_SPLIT: {
+            st4(ep.out0 + (size_t) row * ep.ld0 + col, v);
+            const float4 h = f4_hi(v);
+            st4(ep.out_hi + (size_t) row * ep.ld_split + col, h);
+            st4(ep.out_lo + (size_t) row * ep.ld_split + col, f4_sub(v, h));
+        } break;
+        case EPI_GELU_SPLIT: {
+            st4(ep.out0 + (size_t) row * ep.ld0 + col, v);
+            const float4 g = make_float4(gelu_f(v.x), gelu_f(v.y), gelu_f(v.z), gelu_f(v.w));
+            const float4 h = f4_hi(g);
+            st4(ep.out_hi + (size_t) row * ep.ld_split + col, h);
+            st4(ep.out_lo + (size_t) row * ep.ld_split + col, f4_sub(g, h));
+        } break;
+        case EPI_GATED: {
+            st4(ep.out0 + (size_t) row * ep.ld0 + col, v);
+            const float4 g = ld4(ep.gate + (size_t) row * ep.ld_gate + col);
+            st4(ep.out1 + (size_t) row * ep.ld1 + col, f4_add(ld4(ep.aux + (size_t) row * ep.ld_aux + col), f4_mul(v, g)));
+        } break;
+        case EPI_DGELU_SPLIT: {
+            const float4 u = ld4(ep.aux + (size_t) row * ep.ld_aux + col);
+            const float4 d = f4_mul(v, make_float4(gelu_grad(u.x), gelu_grad(u.y), gelu_grad(u.z), gelu_grad(u.w)));
+            const float4 h = f4_hi(d);
+            st4(ep.out_hi + (size_t) row * ep.ld_split + col, h);
+            st4(ep.out_lo + (size_t) row * ep.ld_split + col, f4_sub(d, h));
+        } break;
+        default: break;
+    }
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ float ld_peer(uint32_t local_saddr, uint32_t rank) {
+    uint32_t remote;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_saddr), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float4 ld_peer4(uint32_t local_saddr, uint32_t rank) {
+    uint32_t remote;
+    float4 v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_saddr), "r"(rank));
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(remote) : "memory");
+    return v;
+}
+
+// One 128 x BN tile of C per CTA, or -- split-K -- one K-slice of it per CTA of a (1, 1, splits) cluster.
+// Epilogue (both cases): the tile's partial sum goes TMEM -> registers -> a padded shared-memory tile; with
+// splits > 1 a cluster barrier follows and each CTA reduces its 128 / splits rows over every peer's tile
+// through distributed shared memory, in rank order (a fixed order: the result does not depend on timing),
+// then applies the fused epilogue with row-contiguous (coalesced) stores.
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
               const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
-              int M, int N, int K, GemmEpi ep) {
+              int M, int N, int K, int splits, GemmEpi ep) {
     constexpr uint32_t A_BYTES = BM * BK * 4;
     constexpr uint32_t B_BYTES = BN * BK * 4;
     constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    constexpr int PLD = BN + 4;            // padded row of the staged partial tile (conflict-free float4 row writes)
     // two accumulators: hi*hi in columns [0, BN), the small cross terms hi*lo + lo*hi in [BN, 2 BN).
     // The tensor core's float32 accumulation rounds toward zero per instruction; keeping the small terms
     // apart cuts the number of truncations the large partial sum sees by three.
     constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
     // instruction descriptor: D f32 (bit 4), A/B tf32 (2 << 7, 2 << 10), K-major both, N >> 3, M >> 4
     constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
+    static_assert((size_t) BM * PLD * 4 <= (size_t) STAGES * STAGE_BYTES, "staged tile must fit in the pipeline buffers");
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    float * tile = (float *) smem;          // reused after the mainloop: [BM][PLD] partial sums
     __shared__ __align__(8) uint64_t full_bar[STAGES];
     __shared__ __align__(8) uint64_t empty_bar[STAGES];
     __shared__ __align__(8) uint64_t acc_bar;
@@ -147,6 +274,10 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
     const int num_k = (K + BK - 1) / BK;
+    const int split = splits > 1 ? (int) cluster_rank() : 0;
+    const int kt_per = (num_k + splits - 1) / splits;
+    const int kt0 = split * kt_per, kt1 = min(num_k, kt0 + kt_per);
+    const int nkt = kt1 > kt0 ? kt1 - kt0 : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
@@ -160,18 +291,29 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                      :: "r"(smem_u32(&tmem_base_sh)), "r"(TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    if (threadIdx.x == 32) {
+        asm volatile("prefetch.tensormap [%0];" :: "l"((uint64_t) &tA_hi) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"((uint64_t) &tA_lo) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"((uint64_t) &tB_hi) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"((uint64_t) &tB_lo) : "memory");
+    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_sh;
+    // the setup above overlapped the previous kernel (programmatic dependent launch); its outputs are
+    // read from here on
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 0) {
         if (lane == 0) {
             int issued = 0;
-            for (int kt = 0; kt < num_k; kt++) {
-                const int s = kt % STAGES;
-                const uint32_t ph = (uint32_t) (kt / STAGES) & 1u;
-                if (kt >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1)) { abort_sh = 1; break; }
+            for (int i = 0; i < nkt; i++) {
+                const int kt = kt0 + i;
+                const int s = i % STAGES;
+                const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
+                if (i >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1)) { abort_sh = 1; break; }
                 if (*(volatile int *) &abort_sh) break;
                 uint8_t * st = smem + (size_t) s * STAGE_BYTES;
                 mbar_expect_tx(&full_bar[s], STAGE_BYTES);
@@ -179,22 +321,21 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 tma_load_2d(st + A_BYTES, &tA_lo, kt * BK, m0, &full_bar[s]);
                 tma_load_2d(st + 2 * A_BYTES, &tB_hi, kt * BK, n0, &full_bar[s]);
                 tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, kt * BK, n0, &full_bar[s]);
-                issued = kt + 1;
+                issued = i + 1;
             }
             if (*(volatile int *) &abort_sh) {
-                // drain: the copies of the last stages it armed must land before the CTA exits
-                for (int kt = issued - STAGES < 0 ? 0 : issued - STAGES; kt < issued; kt++) {
-                    mbar_wait(&full_bar[kt % STAGES], (uint32_t) (kt / STAGES) & 1u, 5);
+                // drain: the copies of the last stages it armed must land before the buffers are reused
+                for (int i = issued - STAGES < 0 ? 0 : issued - STAGES; i < issued; i++) {
+                    mbar_wait(&full_bar[i % STAGES], (uint32_t) (i / STAGES) & 1u, 5);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            bool ok = true;
-            for (int kt = 0; kt < num_k && ok; kt++) {
-                const int s = kt % STAGES;
-                const uint32_t ph = (uint32_t) (kt / STAGES) & 1u;
-                if (!mbar_wait(&full_bar[s], ph, 2)) { abort_sh = 1; ok = false; break; }
+            for (int i = 0; i < nkt; i++) {
+                const int s = i % STAGES;
+                const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
+                if (!mbar_wait(&full_bar[s], ph, 2)) { abort_sh = 1; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t a_hi = smem_u32(smem + (size_t) s * STAGE_BYTES);
                 const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
@@ -203,80 +344,87 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                     const uint32_t off = (uint32_t) kk * 32;   // 8 tf32 = 32 bytes along K
                     const uint64_t dah = sw128_desc(a_hi + off), dal = sw128_desc(a_lo + off);
                     const uint64_t dbh = sw128_desc(b_hi + off), dbl = sw128_desc(b_lo + off);
-                    mma_tf32(tmem + BN, dal, dbh, IDESC, (kt | kk) != 0);
+                    mma_tf32(tmem + BN, dal, dbh, IDESC, (i | kk) != 0);
                     mma_tf32(tmem + BN, dah, dbl, IDESC, 1);
-                    mma_tf32(tmem, dah, dbh, IDESC, (kt | kk) != 0);
+                    mma_tf32(tmem, dah, dbh, IDESC, (i | kk) != 0);
                 }
                 mma_commit(&empty_bar[s]);
             }
-            mma_commit(&acc_bar);   // also on abort: completes once the issued MMAs are done
+            mma_commit(&acc_bar);   // also on abort / with no K-slice: completes once the issued MMAs are done
         }
     } else {
-        // epilogue warps 2..5: TMEM lane quadrant = warp % 4
+        // epilogue warps 2..5 (TMEM lane quadrant = warp % 4)
         const int q = warp & 3;
         const bool ok = mbar_wait(&acc_bar, 0, 3);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (ok && !*(volatile int *) &abort_sh) {
-            const int row = m0 + q * 32 + lane;
+        const int r = q * 32 + lane;
+        const bool have = ok && nkt > 0 && !*(volatile int *) &abort_sh;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                uint32_t r[32], r2[32];
-                tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) c0, r);
-                tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) (BN + c0), r2);
-                if (row >= M || n0 + c0 >= N) continue;
-                const int nc = min(32, N - (n0 + c0));
-                const int col0 = n0 + c0;
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t a[32], b[32];
+            tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) c0, a);
+            tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) (BN + c0), b);
+            if (splits == 1) {
+                // one CTA per tile: straight from the accumulator to the fused epilogue, a row per thread
+                const int row = m0 + r;
+                if (have && row < M) {
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    if (j >= nc) break;
-                    const int col = col0 + j;
-                    float v = __uint_as_float(r[j]) + __uint_as_float(r2[j]);
-                    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) v = v + ep.bias[col];
-                    switch (ep.mode) {
-                        case EPI_F32:
-                            ep.out0[(size_t) row * ep.ld0 + col] = v;
-                            break;
-                        case EPI_SPLIT: {
-                            const float h = split_hi(v);
-                            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
-                            ep.out_lo[(size_t) row * ep.ld_split + col] = v - h;
-                        } break;
-                        case EPI_F32_SPLIT: {
-                            ep.out0[(size_t) row * ep.ld0 + col] = v;
-                            const float h = split_hi(v);
-                            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
-                            ep.out_lo[(size_t) row * ep.ld_split + col] = v - h;
-                        } break;
-                        case EPI_GELU_SPLIT: {
-                            ep.out0[(size_t) row * ep.ld0 + col] = v;
-                            const float gv = gelu_f(v);
-                            const float h = split_hi(gv);
-                            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
-                            ep.out_lo[(size_t) row * ep.ld_split + col] = gv - h;
-                        } break;
-                        case EPI_GATED: {
-                            ep.out0[(size_t) row * ep.ld0 + col] = v;
-                            const float g = ep.gate[(size_t) row * ep.ld_gate + col];
-                            ep.out1[(size_t) row * ep.ld1 + col] = ep.aux[(size_t) row * ep.ld_aux + col] + v * g;
-                        } break;
-                        case EPI_DGELU_SPLIT: {
-                            const float d = v * gelu_grad(ep.aux[(size_t) row * ep.ld_aux + col]);
-                            const float h = split_hi(d);
-                            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
-                            ep.out_lo[(size_t) row * ep.ld_split + col] = d - h;
-                        } break;
-                        default: break;
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 v = make_float4(__uint_as_float(a[j]) + __uint_as_float(b[j]),
+                                                     __uint_as_float(a[j + 1]) + __uint_as_float(b[j + 1]),
+                                                     __uint_as_float(a[j + 2]) + __uint_as_float(b[j + 2]),
+                                                     __uint_as_float(a[j + 3]) + __uint_as_float(b[j + 3]));
+                        apply_epi4(ep, row, n0 + c0 + j, N, v);
                     }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 v = have ? make_float4(__uint_as_float(a[j]) + __uint_as_float(b[j]),
+                                                        __uint_as_float(a[j + 1]) + __uint_as_float(b[j + 1]),
+                                                        __uint_as_float(a[j + 2]) + __uint_as_float(b[j + 2]),
+                                                        __uint_as_float(a[j + 3]) + __uint_as_float(b[j + 3]))
+                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    *(float4 *) &tile[r * PLD + c0 + j] = v;
                 }
             }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
+    if (splits > 1) {
+        cluster_sync_all();
+        // each CTA reduces its rows over every K-slice of the cluster: all peer loads first, then the
+        // sum in rank order (a fixed order), then the fused epilogue, four columns per thread
+        if (warp >= 2 && !*(volatile int *) &abort_sh) {
+            const int rows_per = (BM + splits - 1) / splits;
+            const int rs = split * rows_per, re = min(BM, rs + rows_per);
+            const int t = threadIdx.x - 64;
+            const uint32_t tile_s = smem_u32(tile);
+            constexpr int C4 = BN / 4;
+            for (int idx = t; idx < (re - rs) * C4; idx += 128) {
+                const int rr = rs + idx / C4, cc = (idx % C4) * 4;
+                const uint32_t off = tile_s + (uint32_t) (rr * PLD + cc) * 4;
+                float4 part[8];
+#pragma unroll
+                for (int p = 0; p < 8; p++) if (p < splits) part[p] = ld_peer4(off, (uint32_t) p);
+                float4 v = part[0];
+#pragma unroll
+                for (int p = 1; p < 8; p++) {
+                    if (p < splits) { v.x = v.x + part[p].x; v.y = v.y + part[p].y; v.z = v.z + part[p].z; v.w = v.w + part[p].w; }
+                }
+                const int row = m0 + rr;
+                if (row < M) apply_epi4(ep, row, n0 + cc, N, v);
+            }
+        }
+        cluster_sync_all();   // peers read this CTA's tile until here
+    } else {
+        __syncthreads();
+    }
     if (warp == 1) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
     }
 }
+
 
 // ---------------------------------------------------------------------------------------------
 // host side: tensor maps and launch
@@ -308,7 +456,7 @@ bool make_map(CUtensorMap * map, const float * base, int rows, int cols, int ld,
 }
 
 template <int BN, int STAGES>
-int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
+int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
     if (!make_map(&ta_hi, A.hi, M, K, A.ld, BM) || !make_map(&ta_lo, A.lo, M, K, A.ld, BM) ||
         !make_map(&tb_hi, B.hi, N, K, B.ld, BN) || !make_map(&tb_lo, B.lo, N, K, B.ld, BN)) {
@@ -319,16 +467,44 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, const Ge
     static bool attr_set = false;
     if (!attr_set) {
         JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem));
+        JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         attr_set = true;
     }
-    const dim3 grid((unsigned) ((M + BM - 1) / BM), (unsigned) ((N + BN - 1) / BN));
-    k_gemm_tf32x3<BN, STAGES><<<grid, 192, smem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep);
-    JB_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) ((M + BM - 1) / BM), (unsigned) ((N + BN - 1) / BN), (unsigned) splits);
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = (unsigned) splits;
+    cfg.attrs = attr;
+    cfg.numAttrs = splits > 1 ? 2 : 1;
+    JB_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tf32x3<BN, STAGES>, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, splits, ep));
     return 0;
+}
+
+bool aligned16(const void * p) { return ((uintptr_t) p & 15) == 0; }
+
+bool vec_ok(const GemmEpi & ep, int N) {
+    if (N % 4) return false;
+    const void * ptrs[] = {ep.bias, ep.out0, ep.out_hi, ep.out_lo, ep.aux, ep.gate, ep.out1};
+    for (const void * p : ptrs) if (p && !aligned16(p)) return false;
+    const int lds[] = {ep.out0 ? ep.ld0 : 0, ep.out_hi ? ep.ld_split : 0, ep.aux ? ep.ld_aux : 0, ep.gate ? ep.ld_gate : 0,
+                       ep.out1 ? ep.ld1 : 0};
+    for (int l : lds) if (l % 4) return false;
+    return true;
 }
 
 }  // namespace
 
+// Tile / split choice: wide outputs (the time-batched adaLN modulation) take 128-wide tiles, one CTA
+// per tile; the per-step products take 64-wide tiles and split K over a cluster of up to 8 CTAs, so
+// that about one CTA per SM streams a K-slice instead of a dozen CTAs streaming everything.
 int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     if (!load_encode()) {
@@ -340,9 +516,20 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
         log("jepa: gemm: operands need 16-byte aligned rows (ld %d / %d)\n", A.ld, B.ld);
         return -1;
     }
-    const long tiles128 = (long) ((M + BM - 1) / BM) * ((N + 127) / 128);
-    if (tiles128 >= 148) return launch<128, 3>(A, B, M, N, K, ep, st);
-    return launch<64, 4>(A, B, M, N, K, ep, st);
+    GemmEpi e = ep;
+    e.vec = vec_ok(ep, N) ? 1 : 0;
+    // The tile shape and the K split depend on (N, K) only, never on M: a row's arithmetic (and so its
+    // bits) is then the same whatever batch of rows it is computed in.
+    if (N >= 4096) return launch<128, 3>(A, B, M, N, K, 1, e, st);
+    const int num_k = (K + BK - 1) / BK;
+    long s = (148 + 2L * ((N + 63) / 64) - 1) / (2L * ((N + 63) / 64));   // about one CTA per SM at 256 rows
+    if (s > 8) s = 8;
+    if (s > num_k) s = num_k;
+    if (s < 1) s = 1;
+    int splits = (int) s;
+    const int kt_per = (num_k + splits - 1) / splits;
+    splits = (num_k + kt_per - 1) / kt_per;   // no empty K-slices
+    return launch<64, 4>(A, B, M, N, K, splits, e, st);
 }
 
 int gemm_error_flag(cudaStream_t st) {

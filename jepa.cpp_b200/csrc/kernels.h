@@ -32,6 +32,7 @@ struct GemmEpi {
     const float * aux = nullptr; int ld_aux = 0;
     const float * gate = nullptr; int ld_gate = 0;
     float * out1 = nullptr; int ld1 = 0;
+    int vec = 0;                    // set by gemm_tc: float4 epilogue allowed
 };
 
 struct SplitMat {                    // a split operand: two float32 planes with one leading dimension

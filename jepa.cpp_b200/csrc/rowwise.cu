@@ -13,6 +13,7 @@
 // row re-read from L1 for each pass instead of being held in registers.
 #include "kernels.h"
 #include "common.h"
+#include "launch.h"
 
 namespace jb {
 
@@ -201,6 +202,245 @@ __global__ void k_block_bwd(BlockBwdArgs a) {
         }
     }
 }
+
+// ---------------------------------------------------------------------------------------------
+// Register-resident variants for rows of up to 32 V floats: every pass over the row issues all of its
+// loads at once (element i = lane + 32 k, coalesced per warp instruction) and keeps the values in
+// registers, so a pass costs one memory latency instead of one per element. Same arithmetic, same
+// expression order as the loop kernels above (bit-identical results).
+// ---------------------------------------------------------------------------------------------
+constexpr int FAST_ROWS = 4;   // warps (= rows) per block
+
+// Programmatic dependent launch: wait for the grid this one depends on (its writes become visible),
+// then let the next grid in the stream begin launching while this one runs.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <int V>
+__device__ __forceinline__ void load_row(const float * __restrict__ p, int D, int lane, float (&v)[V]) {
+#pragma unroll
+    for (int k = 0; k < V; k++) { const int i = lane + 32 * k; v[k] = i < D ? p[i] : 0.0f; }
+}
+
+template <int V>
+__device__ __forceinline__ void stats_of(const float (&v)[V], int D, int lane, float eps, double & mean, float & inv) {
+    double s = 0;
+#pragma unroll
+    for (int k = 0; k < V; k++) if (lane + 32 * k < D) s += (double) v[k];
+    mean = warp_sum(s) / D;
+    double q = 0;
+#pragma unroll
+    for (int k = 0; k < V; k++) if (lane + 32 * k < D) { const double c = (double) v[k] - mean; q += c * c; }
+    inv = (float) (1.0 / sqrt(warp_sum(q) / D + (double) eps));
+}
+
+template <int V>
+__global__ void __launch_bounds__(32 * FAST_ROWS)
+k_block_pre_v(const float * __restrict__ x, int ldx, const float * __restrict__ mod, int ld_mod, int sh_off, int sc_off,
+              const float * __restrict__ ln_w, const float * __restrict__ ln_b, float eps0, float eps1,
+              float * __restrict__ h_hi, float * __restrict__ h_lo, int ldh, LnStats * __restrict__ st0,
+              LnStats * __restrict__ st1, int M, int D) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
+    if (row >= M) return;
+    float xv[V], sc[V], sh[V], lw[V], lb[V];
+    load_row<V>(x + (size_t) row * ldx, D, lane, xv);
+    load_row<V>(mod + (size_t) row * ld_mod + sc_off, D, lane, sc);
+    load_row<V>(mod + (size_t) row * ld_mod + sh_off, D, lane, sh);
+    if (ln_w) load_row<V>(ln_w, D, lane, lw);
+#pragma unroll
+    for (int k = 0; k < V; k++) lb[k] = 0.0f;
+    if (ln_b) load_row<V>(ln_b, D, lane, lb);
+    double mean0; float inv0;
+    stats_of<V>(xv, D, lane, eps0, mean0, inv0);
+    if (lane == 0) st0[row] = LnStats{mean0, inv0, 0.0f};
+#pragma unroll
+    for (int k = 0; k < V; k++) xv[k] = xhat_of(xv[k], mean0, inv0) * (1.0f + sc[k]) + sh[k];   // z, the FiLM output
+    if (ln_w) {
+        double mean1; float inv1;
+        stats_of<V>(xv, D, lane, eps1, mean1, inv1);
+        if (lane == 0) st1[row] = LnStats{mean1, inv1, 0.0f};
+#pragma unroll
+        for (int k = 0; k < V; k++) xv[k] = xhat_of(xv[k], mean1, inv1) * lw[k] + lb[k];
+    }
+    float * hh = h_hi + (size_t) row * ldh;
+    float * hl = h_lo + (size_t) row * ldh;
+#pragma unroll
+    for (int k = 0; k < V; k++) {
+        const int i = lane + 32 * k;
+        if (i < D) store_split(hh, hl, i, xv[k]);
+    }
+}
+
+template <int V>
+__global__ void __launch_bounds__(32 * FAST_ROWS)
+k_layer_norm_v(const float * __restrict__ x, int ldx, const float * __restrict__ w, const float * __restrict__ b, float eps,
+               float * __restrict__ y, int ldy, float * __restrict__ hi, float * __restrict__ lo, LnStats * __restrict__ stats,
+               int M, int D) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
+    if (row >= M) return;
+    float xv[V], wv[V], bv[V];
+    load_row<V>(x + (size_t) row * ldx, D, lane, xv);
+#pragma unroll
+    for (int k = 0; k < V; k++) { wv[k] = 1.0f; bv[k] = 0.0f; }
+    if (w) load_row<V>(w, D, lane, wv);
+    if (b) load_row<V>(b, D, lane, bv);
+    double mean; float inv;
+    stats_of<V>(xv, D, lane, eps, mean, inv);
+    if (stats && lane == 0) stats[row] = LnStats{mean, inv, 0.0f};
+#pragma unroll
+    for (int k = 0; k < V; k++) {
+        const int i = lane + 32 * k;
+        if (i >= D) continue;
+        const float v = xhat_of(xv[k], mean, inv) * wv[k] + bv[k];
+        if (y) y[(size_t) row * ldy + i] = v;
+        if (hi) store_split(hi + (size_t) row * ldy, lo + (size_t) row * ldy, i, v);
+    }
+}
+
+template <int V>
+__global__ void __launch_bounds__(32 * FAST_ROWS)
+k_layer_norm_bwd_v(const float * __restrict__ gy, int ldgy, const float * __restrict__ x, int ldx,
+                   const LnStats * __restrict__ stats, const float * __restrict__ w, const float * __restrict__ gres, int ldres,
+                   float * __restrict__ gx, int ldgx, const float * __restrict__ dn, int lddn, const float * __restrict__ gate,
+                   int ld_gate, float * __restrict__ dmod_hi, float * __restrict__ dmod_lo, int ld_dmod,
+                   float * __restrict__ d_hi, float * __restrict__ d_lo, int ldd, int M, int D) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
+    if (row >= M) return;
+    const LnStats stt = stats[row];
+    float gh[V], xh[V], wv[V], gr[V], dv[V], gt[V];
+    load_row<V>(gy + (size_t) row * ldgy, D, lane, gh);
+    load_row<V>(x + (size_t) row * ldx, D, lane, xh);
+#pragma unroll
+    for (int k = 0; k < V; k++) { wv[k] = 1.0f; gr[k] = 0.0f; }
+    if (w) load_row<V>(w, D, lane, wv);
+    if (gres) load_row<V>(gres + (size_t) row * ldres, D, lane, gr);
+    if (dn) {
+        load_row<V>(dn + (size_t) row * lddn, D, lane, dv);
+        load_row<V>(gate + (size_t) row * ld_gate, D, lane, gt);
+    }
+    double m1 = 0, m2 = 0;
+#pragma unroll
+    for (int k = 0; k < V; k++) {
+        if (lane + 32 * k >= D) continue;
+        gh[k] = gh[k] * wv[k];
+        xh[k] = xhat_of(xh[k], stt.mean, stt.inv);
+        m1 += gh[k];
+        m2 += (double) gh[k] * xh[k];
+    }
+    m1 = warp_sum(m1) / D;
+    m2 = warp_sum(m2) / D;
+#pragma unroll
+    for (int k = 0; k < V; k++) {
+        const int i = lane + 32 * k;
+        if (i >= D) continue;
+        float v = (float) (((double) gh[k] - m1 - (double) xh[k] * m2) * (double) stt.inv);
+        if (gres) v = gr[k] + v;
+        gx[(size_t) row * ldgx + i] = v;
+        if (dn) {
+            store_split(dmod_hi + (size_t) row * ld_dmod, dmod_lo + (size_t) row * ld_dmod, i, v * dv[k]);
+            store_split(d_hi + (size_t) row * ldd, d_lo + (size_t) row * ldd, i, v * gt[k]);
+        }
+    }
+}
+
+template <int V>
+__global__ void __launch_bounds__(32 * FAST_ROWS) k_block_bwd_v(BlockBwdArgs a) {
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
+    if (row >= a.M) return;
+    const int D = a.D;
+    const LnStats s0 = a.st0[row];
+    // every load of the row up front (the struct's pointers may alias as far as the compiler knows)
+    float gz[V], xh[V], sc[V], z[V], lw[V], gr[V], av[V], gt[V];
+    load_row<V>(a.gh + (size_t) row * a.ldgh, D, lane, gz);
+    load_row<V>(a.x + (size_t) row * a.ldx, D, lane, xh);
+    load_row<V>(a.mod + (size_t) row * a.ld_mod + a.sc_off, D, lane, sc);
+    load_row<V>(a.gres + (size_t) row * a.ldres, D, lane, gr);
+    if (a.ln_w) {
+        load_row<V>(a.mod + (size_t) row * a.ld_mod + a.sh_off, D, lane, z);
+        load_row<V>(a.ln_w, D, lane, lw);
+    }
+    if (a.a2) {
+        load_row<V>(a.a2 + (size_t) row * a.lda2, D, lane, av);
+        load_row<V>(a.mod2 + (size_t) row * a.ld_mod2 + a.gate2_off, D, lane, gt);
+    }
+#pragma unroll
+    for (int k = 0; k < V; k++) xh[k] = xhat_of(xh[k], s0.mean, s0.inv);
+    if (a.ln_w) {
+        // inner ln backward: gz = ln_bwd(gh) over the ln's normalised input
+        const LnStats s1 = a.st1[row];
+        double n1 = 0, n2 = 0;
+#pragma unroll
+        for (int k = 0; k < V; k++) {
+            if (lane + 32 * k >= D) continue;
+            z[k] = xhat_of(xh[k] * (1.0f + sc[k]) + z[k], s1.mean, s1.inv);
+            gz[k] = gz[k] * lw[k];
+            n1 += gz[k];
+            n2 += (double) gz[k] * z[k];
+        }
+        n1 = warp_sum(n1) / D;
+        n2 = warp_sum(n2) / D;
+#pragma unroll
+        for (int k = 0; k < V; k++) gz[k] = (float) (((double) gz[k] - n1 - (double) z[k] * n2) * (double) s1.inv);
+    }
+    float * dmh = a.dmod_hi + (size_t) row * a.ld_dmod;
+    float * dml = a.dmod_lo + (size_t) row * a.ld_dmod;
+    double m1 = 0, m2 = 0;
+#pragma unroll
+    for (int k = 0; k < V; k++) {
+        const int i = lane + 32 * k;
+        if (i >= D) continue;
+        store_split(dmh, dml, a.sc_off + i, gz[k] * xh[k]);
+        store_split(dmh, dml, a.sh_off + i, gz[k]);
+        gz[k] = gz[k] * (1.0f + sc[k]);   // now the gradient into LN0's output
+        m1 += gz[k];
+        m2 += (double) gz[k] * xh[k];
+    }
+    m1 = warp_sum(m1) / D;
+    m2 = warp_sum(m2) / D;
+#pragma unroll
+    for (int k = 0; k < V; k++) {
+        const int i = lane + 32 * k;
+        if (i >= D) continue;
+        const float v = gr[k] + (float) (((double) gz[k] - m1 - (double) xh[k] * m2) * (double) s0.inv);
+        a.gx[(size_t) row * a.ldgx + i] = v;
+        if (a.a2) {
+            store_split(a.dmod2_hi + (size_t) row * a.ld_dmod2, a.dmod2_lo + (size_t) row * a.ld_dmod2, a.gate2_off + i,
+                        v * av[k]);
+            store_split(a.d_hi + (size_t) row * a.ldd, a.d_lo + (size_t) row * a.ldd, i, v * gt[k]);
+        }
+    }
+}
+
+// values per lane of the register kernels for a row of D floats (0 = use the loop kernels)
+inline int fast_v(int D) {
+    if (D % 32 != 0) return 0;
+    const int v = D / 32;
+    for (int c : {1, 2, 4, 6, 8, 12, 16, 24, 32}) if (v <= c) return c;
+    return 0;
+}
+
+#define JB_DISPATCH_V(V, ...)                                      \
+    switch (V) {                                                   \
+        case 1: { constexpr int VV = 1; __VA_ARGS__; } break;      \
+        case 2: { constexpr int VV = 2; __VA_ARGS__; } break;      \
+        case 4: { constexpr int VV = 4; __VA_ARGS__; } break;      \
+        case 6: { constexpr int VV = 6; __VA_ARGS__; } break;      \
+        case 8: { constexpr int VV = 8; __VA_ARGS__; } break;      \
+        case 12: { constexpr int VV = 12; __VA_ARGS__; } break;    \
+        case 16: { constexpr int VV = 16; __VA_ARGS__; } break;    \
+        case 24: { constexpr int VV = 24; __VA_ARGS__; } break;    \
+        default: { constexpr int VV = 32; __VA_ARGS__; } break;    \
+    }
 
 // ---------------------------------------------------------------------------------------------
 __global__ void k_linear_simt(const float * __restrict__ x, int ldx, const float * __restrict__ w, const float * __restrict__ b,
@@ -403,6 +643,12 @@ void block_pre(const float * x, int ldx, const float * mod, int ld_mod, int sh_o
                const float * ln_b, float eps0, float eps1, float * h_hi, float * h_lo, int ldh, LnStats * st0,
                LnStats * st1, int M, int D, cudaStream_t st) {
     if (M <= 0) return;
+    if (const int v = fast_v(D)) {
+        const unsigned nb = (unsigned) ((M + FAST_ROWS - 1) / FAST_ROWS);
+        JB_DISPATCH_V(v, (launch_pdl(k_block_pre_v<VV>, nb, 32 * FAST_ROWS, 0, st, x, ldx, mod, ld_mod, sh_off, sc_off, ln_w, ln_b,
+                                                                           eps0, eps1, h_hi, h_lo, ldh, st0, st1, M, D)));
+        return;
+    }
     k_block_pre<<<row_blocks(M), 32 * ROWS_PER_BLOCK, 0, st>>>(x, ldx, mod, ld_mod, sh_off, sc_off, ln_w, ln_b, eps0,
                                                               eps1, h_hi, h_lo, ldh, st0, st1, M, D);
 }
@@ -410,6 +656,11 @@ void block_pre(const float * x, int ldx, const float * mod, int ld_mod, int sh_o
 void layer_norm(const float * x, int ldx, const float * w, const float * b, float eps, float * y, int ldy, float * hi,
                 float * lo, LnStats * stats, int M, int D, cudaStream_t st) {
     if (M <= 0) return;
+    if (const int v = fast_v(D)) {
+        const unsigned nb = (unsigned) ((M + FAST_ROWS - 1) / FAST_ROWS);
+        JB_DISPATCH_V(v, (launch_pdl(k_layer_norm_v<VV>, nb, 32 * FAST_ROWS, 0, st, x, ldx, w, b, eps, y, ldy, hi, lo, stats, M, D)));
+        return;
+    }
     k_layer_norm<<<row_blocks(M), 32 * ROWS_PER_BLOCK, 0, st>>>(x, ldx, w, b, eps, y, ldy, hi, lo, stats, M, D);
 }
 
@@ -418,6 +669,13 @@ void layer_norm_bwd(const float * gy, int ldgy, const float * x, int ldx, const 
                     int ld_gate, float * dmod_hi, float * dmod_lo, int ld_dmod, float * d_hi, float * d_lo, int ldd,
                     int M, int D, cudaStream_t st) {
     if (M <= 0) return;
+    if (const int v = fast_v(D)) {
+        const unsigned nb = (unsigned) ((M + FAST_ROWS - 1) / FAST_ROWS);
+        JB_DISPATCH_V(v, (launch_pdl(k_layer_norm_bwd_v<VV>, nb, 32 * FAST_ROWS, 0, st, gy, ldgy, x, ldx, stats, w, gres, ldres, gx, ldgx,
+                                                                                dn, lddn, gate, ld_gate, dmod_hi, dmod_lo, ld_dmod,
+                                                                                d_hi, d_lo, ldd, M, D)));
+        return;
+    }
     k_layer_norm_bwd<<<row_blocks(M), 32 * ROWS_PER_BLOCK, 0, st>>>(gy, ldgy, x, ldx, stats, w, gres, ldres, gx, ldgx, dn,
                                                                    lddn, gate, ld_gate, dmod_hi, dmod_lo, ld_dmod, d_hi,
                                                                    d_lo, ldd, M, D);
@@ -425,6 +683,11 @@ void layer_norm_bwd(const float * gy, int ldgy, const float * x, int ldx, const 
 
 void block_bwd(const BlockBwdArgs & a, cudaStream_t st) {
     if (a.M <= 0) return;
+    if (const int v = fast_v(a.D)) {
+        const unsigned nb = (unsigned) ((a.M + FAST_ROWS - 1) / FAST_ROWS);
+        JB_DISPATCH_V(v, (launch_pdl(k_block_bwd_v<VV>, nb, 32 * FAST_ROWS, 0, st, a)));
+        return;
+    }
     k_block_bwd<<<row_blocks(a.M), 32 * ROWS_PER_BLOCK, 0, st>>>(a);
 }
 
