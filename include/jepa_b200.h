@@ -27,6 +27,24 @@ int jepa_b200_gemm(const float * A, const float * B, int M, int N, int K, float 
 // milliseconds per launch in *ms (CUDA events around the launches).
 int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms);
 
+// jepa_b200_gemm for callers that must not allocate device memory. No counterpart in the reference.
+// Some hosts cannot call cudaMalloc around a kernel call: a process whose device memory budget is fixed
+// at start-up, a real-time control loop where an allocation (which can synchronise the whole device)
+// would blow the cycle's deadline, or a plug-in living inside someone else's allocator. This entry point
+// computes the same product as jepa_b200_gemm from the same host buffers, but keeps the device copies of
+// A, B and C and the operand split planes in one fixed device array that the library reserves when it
+// is loaded (JEPA_B200_NOALLOC_MAX_FLOATS floats = 16 MiB, held on every GPU that loads the library
+// until the process exits), and calls no cudaMalloc / cudaFree.
+//   limit  : 3 (M K + N K) + M N floats (each part rounded up to 64), at most JEPA_B200_NOALLOC_MAX_FLOATS;
+//            larger sizes are refused with a message in jepa_error_text()
+//   set-up : the first call on a device looks up that device's copy of the array, so make that first
+//            call before any stream capture
+//   sharing: every call on a device uses the same array and leaves its contents there; calls that
+//            overlap on the GPU (from two host threads) race on it
+// Runs on the current CUDA device and its legacy default stream; returns 0 or -1.
+#define JEPA_B200_NOALLOC_MAX_FLOATS (4u * 1024u * 1024u)
+int jepa_b200_gemm_noalloc(const float * A, const float * B, int M, int N, int K, float * C);
+
 // Dequantise `rows` GGUF rows of `ne0` values of ggml type `ggml_type` (0 f32, 1 f16, 2 q4_0, 8 q8_0,
 // 30 bf16) from the host bytes `src` into host float32 `dst` by the device kernel the weight loader uses.
 int jepa_b200_dequant(uint32_t ggml_type, const void * src, int64_t rows, int64_t ne0, float * dst);
