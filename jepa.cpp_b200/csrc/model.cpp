@@ -275,13 +275,11 @@ jepa_model_params jepa_model_default_params(void) {
 jepa_model * jepa_model_load_ex(const char * gguf_path, const jepa_model_params * params) {
     if (!gguf_path) return nullptr;
     const jepa_model_params prm = params ? *params : jepa_model_default_params();
+    // The metadata and the host copy of the tensors load anywhere; the planners need a CUDA device, which
+    // jepa_context_new requires (a model loaded without one serves introspection and jepa_hjepa_horizons).
     int n_dev = 0;
-    if (cudaGetDeviceCount(&n_dev) != cudaSuccess || n_dev == 0) {
-        cudaGetLastError();
-        log("jepa: no CUDA device is visible; this engine runs the planners on the GPU only\n");
-        return nullptr;
-    }
-    const int dev = prm.device >= 0 ? prm.device : 0;
+    if (cudaGetDeviceCount(&n_dev) != cudaSuccess) { cudaGetLastError(); n_dev = 0; }
+    const int dev = n_dev == 0 ? -1 : (prm.device >= 0 ? prm.device : 0);
     if (dev >= n_dev) { log("jepa: device %d requested, %d CUDA device(s) present\n", dev, n_dev); return nullptr; }
     std::string err;
     auto file = jb::gguf_read(gguf_path, &err);
@@ -293,8 +291,7 @@ jepa_model * jepa_model_load_ex(const char * gguf_path, const jepa_model_params 
     if (!jb::parse(*m)) return nullptr;
     if (m->hj.present && !jb::hjepa_bind(*m)) return nullptr;
     for (const auto & t : m->file->tensors) m->n_bytes += t.nbytes;
-    cudaDeviceProp prop;
-    if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) m->device_name = "CUDA" + std::to_string(dev);
+    m->device_name = dev >= 0 ? "CUDA" + std::to_string(dev) : "none";
     if (prm.verbose) {
         log("jepa: loaded %s (%s, %s, %zu tensors, %.1f MiB) for CUDA device %d\n", m->name.c_str(), m->family.c_str(),
             jb::type_name(m->file_type == 7 ? 8 : m->file_type == 2 ? 2 : m->file_type), m->file->tensors.size(),
@@ -313,6 +310,10 @@ void jepa_model_free(jepa_model * model) { delete model; }
 
 jepa_context * jepa_context_new(jepa_model * model, jepa_context_params params) {
     if (!model) return nullptr;
+    if (model->device < 0) {
+        log("jepa: jepa_context_new: no CUDA device is visible; this engine runs the planners on the GPU only\n");
+        return nullptr;
+    }
     auto ctx = std::make_unique<jepa_context>();
     ctx->model = model;
     ctx->params = params;
@@ -437,7 +438,7 @@ void jepa_device_memory(int device, size_t * free_bytes, size_t * total_bytes) {
 
 int jepa_model_device(const jepa_model * m) { return m ? m->device : -1; }
 const char * jepa_model_device_name(const jepa_model * m) { return m ? m->device_name.c_str() : "CPU"; }
-bool jepa_model_is_gpu(const jepa_model * m) { return m != nullptr; }
+bool jepa_model_is_gpu(const jepa_model * m) { return m != nullptr && m->device >= 0; }
 void jepa_context_set_mul_mat_prec_f32(jepa_context * ctx, bool on) { if (ctx) ctx->prec_f32 = on; }
 bool jepa_context_mul_mat_prec_f32(const jepa_context * ctx) { return ctx && ctx->prec_f32; }
 void jepa_context_set_max_batch(jepa_context * ctx, int n) { if (ctx) ctx->max_batch = n > 0 ? n : 32; }
