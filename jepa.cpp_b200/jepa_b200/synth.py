@@ -255,6 +255,71 @@ def write_hjepa(path: str, spec: HJepaSpec, seed: int = 0) -> None:
 
 
 # ---------------------------------------------------------------------------------------------
+# V-JEPA 2-AC predictor (jepa.pred.kind = "ac"; reference: src/vjepa2_ac.cpp:86-156, the AC keys of
+# src/jepa-gguf.cpp:454-480)
+# ---------------------------------------------------------------------------------------------
+@dc.dataclass
+class ACSpec:
+    enc_dim: int = 1408          # width of the encoder latents the predictor reads and writes
+    pred_dim: int = 1024
+    n_layer: int = 24
+    n_head: int = 16
+    ffn_dim: int = 4096
+    grid: int = 16               # tokens per frame = grid^2
+    action_dim: int = 7
+    state_dim: int = 7
+    n_frames: int = 8            # frame slots (jepa.pred.n_frames)
+    ftype: str = "q8_0"
+    w_std: float = 0.02
+    rand_all: bool = False
+    name: str = "synthetic-vjepa2-ac"
+
+
+def write_ac(path: str, spec: ACSpec, seed: int = 0) -> None:
+    """Write a V-JEPA 2-AC predictor bundle (family vjepa2, a 1-layer encoder stub of the right width)."""
+    g = _Gen(HJepaSpec(levels=[], ftype=spec.ftype, rand_all=spec.rand_all, w_std=spec.w_std), seed)
+    w = g.w
+    D, P = spec.enc_dim, spec.pred_dim
+    w.add_kv("general.architecture", "jepa")
+    w.add_kv("general.name", spec.name)
+    w.add_kv("general.file_type", FTYPE[spec.ftype])
+    w.add_kv("jepa.schema_version", 1)
+    w.add_kv("jepa.family", "vjepa2")
+    w.add_kv("jepa.modality", "video")
+    for k, v in (("embed_dim", D), ("n_layer", 1), ("n_head", max(1, D // 64)), ("ffn_dim", 4 * D), ("patch_size", 16),
+                 ("tubelet_size", 2), ("img_size", 16 * spec.grid), ("n_frames", 64), ("in_chans", 3)):
+        w.add_kv("jepa.enc." + k, v)
+    w.add_kv("jepa.enc.ln_eps", 1e-6)
+    w.add_kv("jepa.enc.act", "gelu_erf")
+    w.add_kv("jepa.enc.pos_type", "rope3d")
+    w.add_kv("jepa.enc.rope_theta", 10000.0)
+    w.add_kv("jepa.enc.rope_freq_layout", "tiled")
+    for k, v in (("kind", "ac"), ("embed_dim", P), ("n_layer", spec.n_layer), ("n_head", spec.n_head),
+                 ("ffn_dim", spec.ffn_dim), ("out_dim", D), ("grid_size", spec.grid), ("action_dim", spec.action_dim),
+                 ("state_dim", spec.state_dim), ("n_cond_tokens", 2), ("cond_order", "action,state"),
+                 ("normalize_reps", True), ("norm_reps_eps", 1e-5), ("frame_causal", True), ("n_frames", spec.n_frames),
+                 ("ln_eps", 1e-6), ("act", "gelu_erf"), ("rope_freq_layout", "tiled")):
+        w.add_kv("jepa.pred." + k, v)
+    # encoder stub: the predictor never runs it
+    g.lin("enc.patch_embed", 3 * 2 * 16 * 16, D)
+    g.norm("enc.norm", D)
+    g.lin("pred.embed", D, P)
+    g.lin("pred.action_embed", spec.action_dim, P)
+    g.lin("pred.state_embed", spec.state_dim, P)
+    for i in range(spec.n_layer):
+        q = f"pred.blk.{i}."
+        g.norm(q + "ln1", P)
+        g.lin(q + "attn_qkv", P, 3 * P)
+        g.lin(q + "attn_out", P, P)
+        g.norm(q + "ln2", P)
+        g.lin(q + "ffn_up", P, spec.ffn_dim)
+        g.lin(q + "ffn_down", spec.ffn_dim, P)
+    g.norm("pred.norm", P)
+    g.lin("pred.proj", P, D)
+    w.write(path)
+
+
+# ---------------------------------------------------------------------------------------------
 # benchmark configurations (the BASELINE configs mapped onto the reference architecture)
 # ---------------------------------------------------------------------------------------------
 def hjepa_config(idx: int) -> tuple[HJepaSpec, list[dict]]:
