@@ -1,6 +1,6 @@
 // V-JEPA 2-AC entry points of the C API: introspection and the host utilities the reference exposes
 // (the non-affine LayerNorm, the pose update, the L1 energy, the CEM defaults), with the reference's
-// semantics (src/vjepa2_ac.cpp:161-263, :787-802). The GPU rollout and CEM live in ac.cu.
+// semantics (src/vjepa2_ac.cpp:161-263, :787-802). The GPU rollout and CEM live in ac_engine.cpp.
 #include "model.h"
 
 #include <cmath>
@@ -48,7 +48,9 @@ void jepa_ac_next_state(const jepa_model * m, const float * state, const float *
         return;
     }
     auto rot = [](const float * e, double R[3][3]) {
-        const double ca = cos(e[0]), sa = sin(e[0]), cb = cos(e[1]), sb = sin(e[1]), cc = cos(e[2]), sc = sin(e[2]);
+        // double-precision cos / sin of the float angles (the explicit casts keep the float overloads out)
+        const double a = e[0], b = e[1], c = e[2];
+        const double ca = cos(a), sa = sin(a), cb = cos(b), sb = sin(b), cc = cos(c), sc = sin(c);
         R[0][0] = cb * cc; R[0][1] = sa * sb * cc - ca * sc; R[0][2] = ca * sb * cc + sa * sc;
         R[1][0] = cb * sc; R[1][1] = sa * sb * sc + ca * cc; R[1][2] = ca * sb * sc - sa * cc;
         R[2][0] = -sb;     R[2][1] = sa * cb;                R[2][2] = ca * cb;

@@ -18,6 +18,7 @@
 #include "kernels.h"
 #include "common.h"
 #include "launch.h"
+#include "tcgen05.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -30,88 +31,11 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 32;                  // 32 f32 = one 128-byte swizzle row
-constexpr long long WAIT_LIMIT = 4000000000LL;   // clock64 cycles (~2 s at 1.9 GHz)
 
 __device__ int g_gemm_error = 0;
 
-__device__ __forceinline__ uint32_t smem_u32(const void * p) {
-    return (uint32_t) __cvta_generic_to_shared(p);
-}
+using namespace tc;
 
-__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t * bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-    return ok != 0;
-}
-
-// bounded wait; false = gave up (the error flag is raised)
-__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int code) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > WAIT_LIMIT) {
-            atomicExch(&g_gemm_error, code);
-            return false;
-        }
-    }
-    return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * map, int x, int y, uint64_t * bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        :: "r"(smem_u32(dst)), "l"((uint64_t) map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
-}
-
-// K-major operand, 128-byte swizzle: rows of 128 B, 8-row atoms 1024 B apart (SBO), LBO unused (1),
-// descriptor version 1 (sm_100), layout type 2 = SWIZZLE_128B.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t) ((saddr >> 4) & 0x3FFF);
-    d |= (uint64_t) 1 << 16;
-    d |= (uint64_t) (1024 >> 4) << 32;
-    d |= (uint64_t) 1 << 46;
-    d |= (uint64_t) 2 << 61;
-    return d;
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
-        :: "r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t * bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 :: "r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 __device__ __forceinline__ float split_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
 
@@ -313,7 +237,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 const int kt = kt0 + i;
                 const int s = i % STAGES;
                 const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
-                if (i >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1)) { abort_sh = 1; break; }
+                if (i >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1, &g_gemm_error)) { abort_sh = 1; break; }
                 if (*(volatile int *) &abort_sh) break;
                 uint8_t * st = smem + (size_t) s * STAGE_BYTES;
                 mbar_expect_tx(&full_bar[s], STAGE_BYTES);
@@ -326,7 +250,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
             if (*(volatile int *) &abort_sh) {
                 // drain: the copies of the last stages it armed must land before the buffers are reused
                 for (int i = issued - STAGES < 0 ? 0 : issued - STAGES; i < issued; i++) {
-                    mbar_wait(&full_bar[i % STAGES], (uint32_t) (i / STAGES) & 1u, 5);
+                    mbar_wait(&full_bar[i % STAGES], (uint32_t) (i / STAGES) & 1u, 5, &g_gemm_error);
                 }
             }
         }
@@ -335,7 +259,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
             for (int i = 0; i < nkt; i++) {
                 const int s = i % STAGES;
                 const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
-                if (!mbar_wait(&full_bar[s], ph, 2)) { abort_sh = 1; break; }
+                if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error)) { abort_sh = 1; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t a_hi = smem_u32(smem + (size_t) s * STAGE_BYTES);
                 const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
@@ -344,9 +268,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                     const uint32_t off = (uint32_t) kk * 32;   // 8 tf32 = 32 bytes along K
                     const uint64_t dah = sw128_desc(a_hi + off), dal = sw128_desc(a_lo + off);
                     const uint64_t dbh = sw128_desc(b_hi + off), dbl = sw128_desc(b_lo + off);
-                    mma_tf32(tmem + BN, dal, dbh, IDESC, (i | kk) != 0);
-                    mma_tf32(tmem + BN, dah, dbl, IDESC, 1);
-                    mma_tf32(tmem, dah, dbh, IDESC, (i | kk) != 0);
+                    mma_kind_tf32(tmem + BN, dal, dbh, IDESC, (i | kk) != 0);
+                    mma_kind_tf32(tmem + BN, dah, dbl, IDESC, 1);
+                    mma_kind_tf32(tmem, dah, dbh, IDESC, (i | kk) != 0);
                 }
                 mma_commit(&empty_bar[s]);
             }
@@ -355,7 +279,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     } else {
         // epilogue warps 2..5 (TMEM lane quadrant = warp % 4)
         const int q = warp & 3;
-        const bool ok = mbar_wait(&acc_bar, 0, 3);
+        const bool ok = mbar_wait(&acc_bar, 0, 3, &g_gemm_error);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int r = q * 32 + lane;
         const bool have = ok && nkt > 0 && !*(volatile int *) &abort_sh;

@@ -8,6 +8,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 #include <cstdint>
 
 namespace jb {
@@ -136,6 +137,73 @@ void adam_step(float * x, float * m, float * v, const float * grad_tmajor, float
 
 // index of the first minimum of cost[0..n) (std::min_element semantics) and its value
 void argmin_first(const float * cost, int n, int * idx, float * val, cudaStream_t st);
+
+// ------------------------------------------------------------------------------------------
+// V-JEPA 2-AC kernels (ac_kernels.cu, gemm_f16.cu, attention.cu): f16 operands, f32 accumulate
+// ------------------------------------------------------------------------------------------
+enum AcEpi : int {
+    AEPI_F32 = 0,        // out_f32[remap(row)] = acc + bias
+    AEPI_ADD_F32 = 1,    // out_f32[remap(row)] += acc + bias          (residual stream)
+    AEPI_GELU_F16 = 2,   // out_f16[row] = gelu(acc + bias)
+    AEPI_QKV = 3,        // q -> out_f16 (RoPE), k (RoPE) and v -> kv[row][0 .. 2 D)
+};
+
+struct AcGemmEpi {
+    int mode = AEPI_F32;
+    const float * bias = nullptr;
+    float * out_f32 = nullptr; int ld_f32 = 0;
+    __half * out_f16 = nullptr; int ld_f16 = 0;
+    __half * kv = nullptr; int ld_kv = 0;
+    const float * rope_cos = nullptr; const float * rope_sin = nullptr;   // [rope_rows][hd], sin sign-folded
+    int rope_rows = 1, D = 0, hd = 64;
+    int remap_g = 0, remap_gout = 0, remap_off = 0;   // out row = (row / g) * gout + off + row % g (g = 0: row)
+};
+
+// C[M,N] = A[M,K] * B[N,K]^T, A and B f16 row-major (K contiguous), tcgen05 kind::f16, f32 accumulate
+int gemm_f16(const __half * A, int lda, const __half * B, int ldb, int M, int N, int K, const AcGemmEpi & ep, cudaStream_t st);
+int gemm_f16_error_flag(cudaStream_t st);
+
+// Attention of the rows of `n_qframes` consecutive frames over their key frames. Frames are whole blocks
+// (block-causal across frames: a frame sees every row of the frames up to its own), so no mask is needed
+// inside a frame: query frame k of the call sees key frames 0 .. key_frames0 + k * key_step - 1.
+constexpr int AC_MAX_FRAMES = 32;
+struct AttnArgs {
+    const __half * q = nullptr; int ldq = 0;      // row r of query frame k of candidate c: q + c*q_cand + (k*q_frame + r)*ldq
+    long long q_cand = 0;
+    int nq = 0;                                   // query rows per frame
+    int n_qframes = 1, q_frame = 0;               // query frames in this call, rows between them
+    __half * out = nullptr; int ldo = 0;          // same row indexing as q
+    long long o_cand = 0;
+    int key_frames0 = 1, key_step = 1;            // key frames of query frame 0; growth per query frame (1 causal, 0 full)
+    const __half * kv[AC_MAX_FRAMES] = {};        // per key frame: [cand][kv_rows][ld_kv], k at col 0, v at col D
+    long long kv_cand_stride[AC_MAX_FRAMES] = {}; // elements between candidates (0: shared by all)
+    int kv_rows = 0, ld_kv = 0, D = 0, n_head = 0, hd = 64;
+    int n_cand = 0;
+    float scale = 0.125f;
+};
+int attention_f16(const AttnArgs & a, cudaStream_t st);
+
+// Two-level row gather: in = (r / (g1 g2)) * s2 + ((r / g1) % g2) * s1 + off + r % g1  (g1 = 0: in = r)
+struct RowMap {
+    int g1 = 0, g2 = 1, s1 = 0, s2 = 0, off = 0;
+};
+// LayerNorm of f32 rows (optional affine) to f16 rows; input rows gathered through `map`
+void ln_to_f16(const float * x, int ldx, const float * w, const float * b, float eps, __half * y, int ldy, int M, int D,
+               RowMap map, cudaStream_t st);
+// the reference's non-affine normalisation between rollout steps (jepa_ac_normalize) in place, plus an f16 copy
+void ac_normalize_rows(float * x, int ld, __half * y16, int ldy, int M, int D, float eps, cudaStream_t st);
+// f32 -> f16 rows, input rows gathered through `map`
+void to_f16(const float * x, int ldx, __half * y, int ldy, int M, int N, RowMap map, cudaStream_t st);
+// conditioning rows of every (candidate, frame) block of a [n_cand][n_frames][rows_per_frame] row layout:
+// row 0 = action_embed(acts + c * act_cand + t * A), row 1 = state_embed(states + c * st_cand + t * S), f32
+void ac_cond_rows(const float * acts, long long act_cand, const float * states, long long st_cand, int A, int S,
+                  const float * wa, const float * ba, const float * ws, const float * bs, float * resid, int ld,
+                  int n_cand, int n_frames, int rows_per_frame, int D, cudaStream_t st);
+// copy rows [row0, row0 + rows) of candidate 0's block to the same rows of candidates 1 .. n_cand-1
+void ac_broadcast_rows(float * x, int ld, long long cand_rows, int row0, int rows, int n_cand, int D, cudaStream_t st);
+// energy[c] = mean |pred[c] - goal| over n values, double accumulation (jepa_ac_energy)
+void ac_energy(const float * pred, long long cand_stride, const float * goal, long long n, int n_cand, float * energy,
+               cudaStream_t st);
 
 // ------------------------------------------------------------------------------------------
 // dequantisation: GGUF row bytes -> float32, bit-exact with the block formats

@@ -77,6 +77,12 @@ bool parse(jepa_model & m) {
         a.normalize_reps = g.getb("jepa.pred.normalize_reps", false);
         a.norm_reps_eps = g.getf("jepa.pred.norm_reps_eps", 1e-5f);
         a.ln_eps = g.getf("jepa.pred.ln_eps", 1e-6f);
+        a.frame_causal = g.getb("jepa.pred.frame_causal", false);
+        a.rope_interleaved = g.gets("jepa.pred.rope_freq_layout", "") == "interleaved";
+        a.rope_theta = g.getf("jepa.enc.rope_theta", 10000.0f);
+        a.out_dim = g.geti("jepa.pred.out_dim", e.embed_dim);
+        a.act = g.gets("jepa.pred.act", "gelu_erf");
+        if (!(a.rope_theta >= 1e-6f && a.rope_theta <= 1e12f)) { log("jepa: jepa.enc.rope_theta is out of range\n"); return false; }
         if (!in_range("jepa.pred.embed_dim", a.embed_dim, 1, 65536) || !in_range("jepa.pred.n_layer", a.n_layer, 1, 1024) ||
             !in_range("jepa.pred.n_head", a.n_head, 1, 1024) || !in_range("jepa.pred.ffn_dim", a.ffn_dim, 1, 1048576) ||
             !in_range("jepa.pred.action_dim", a.action_dim, 1, 65536) || !in_range("jepa.pred.state_dim", a.state_dim, 1, 65536) ||

@@ -36,6 +36,11 @@ struct ACParams {
     int action_dim = 0, state_dim = 0, n_cond_tokens = 0, grid_size = 0, n_frames = 0;
     bool normalize_reps = false;
     float norm_reps_eps = 1e-5f, ln_eps = 1e-6f;
+    bool frame_causal = false;          // block-causal mask over frames (jepa.pred.frame_causal)
+    bool rope_interleaved = false;      // jepa.pred.rope_freq_layout == "interleaved" (else tiled)
+    float rope_theta = 10000.0f;        // jepa.enc.rope_theta
+    int out_dim = 0;                    // jepa.pred.out_dim (defaults to the encoder width)
+    std::string act = "gelu_erf";       // jepa.pred.act
 };
 
 struct EncParams {

@@ -69,6 +69,10 @@ bool Shard::bcast_host(float * host, size_t n, int root, cudaStream_t st) {
     return ok;
 }
 
+bool Shard::allgather_f32(const float * send, float * recv, size_t n, cudaStream_t st) {
+    return nccl_ok(ncclAllGather(send, recv, n, ncclFloat, comm, st), "ncclAllGather(energy)");
+}
+
 }  // namespace jb
 
 extern "C" int jepa_b200_nccl_unique_id(void * out128) {
@@ -84,6 +88,7 @@ extern "C" int jepa_b200_context_set_shard(jepa_context * ctx, int rank, int wor
     if (!ctx || world < 1 || rank < 0 || rank >= world) return -1;
     ctx->shard.reset();
     ctx->hplan.reset();   // workspaces are sized for the rank's slice
+    ctx->ac.reset();
     if (world == 1) return 0;
     if (!nccl_id) return -1;
     cudaSetDevice(ctx->device);

@@ -24,6 +24,8 @@ struct Shard {
     float min_f32(float v, cudaStream_t st);
     void argmin_global(float cost, int gidx, float * cost_out, int * gidx_out, int * owner, cudaStream_t st);
     bool bcast_host(float * host, size_t n, int root, cudaStream_t st);
+    // every rank's n device floats, in rank order, into recv [world * n] on every rank (CEM energies)
+    bool allgather_f32(const float * send, float * recv, size_t n, cudaStream_t st);
 };
 
 }  // namespace jb

@@ -178,7 +178,9 @@ def next_state(state, action):
         return np.array([[cb * cc, sa * sb * cc - ca * sc, ca * sb * cc + sa * sc],
                          [cb * sc, sa * sb * sc + ca * cc, ca * sb * sc - sa * cc],
                          [-sb, sa * cb, ca * cb]])
-    R = rot(action[3:6]) @ rot(state[3:6])
+    Dm, P = rot(action[3:6]), rot(state[3:6])
+    # R = Dm P, each entry summed left to right in double (no fused multiply-add)
+    R = np.array([[Dm[i, 0] * P[0, j] + Dm[i, 1] * P[1, j] + Dm[i, 2] * P[2, j] for j in range(3)] for i in range(3)])
     s = max(-1.0, min(1.0, -R[2, 0]))
     beta = math.asin(s)
     if abs(s) < 1.0 - 1e-9:
@@ -229,39 +231,60 @@ def energy(pred, goal):
     return (d.sum(1) / d.shape[1]).astype(f32)
 
 
-def cem(m: ACModel, latents, n_seed, seed_actions, seed_states, goal, p: dict, noise):
-    """jepa_ac_plan with explicit noise [cem_steps, H, K, 4]. Returns (actions [H, A], best energy per it)."""
-    K, H, A = p["samples"], p["horizon"], m.A
+def cem(m: ACModel, latents, n_seed, seed_actions, seed_states, goal, p: dict, noise, rollout_fn=None, A=None):
+    """jepa_ac_plan with explicit noise [cem_steps, H, K, 4] (src/vjepa2_ac.cpp:829-946). Returns
+    (actions [H, A], best energy per iteration, elite index sets per iteration).
+
+    rollout_fn(acts [K, H, A]) -> [K, H, HW, E] replaces the numpy rollout (a test drives the refit with the
+    GPU's predictions to check the CEM arithmetic on its own). The refit follows the reference's float /
+    double mix exactly: elite sums and squared deviations accumulate in double in elite order, the
+    momentum terms multiply two floats in float (mn * momentum) before the double sum."""
+    K, H = p["samples"], p["horizon"]
+    A = A if A is not None else m.A
+    mm, ms = f32(p["momentum_mean"]), f32(p["momentum_std"])
+    mmg, msg = f32(p["momentum_mean_gripper"]), f32(p["momentum_std_gripper"])
+    maxnorm, gclamp = f32(p["maxnorm"]), f32(p["gripper_clamp"])
     mean = np.zeros((H, 4), f32)
     sd = np.zeros((H, 4), f32)
-    sd[:, :3] = p["maxnorm"]
-    sd[:, 3] = 1.0
-    best = []
+    sd[:, :3] = maxnorm
+    sd[:, 3] = f32(1.0)
+    best, elites = [], []
+    topk = p["topk"]
     for it in range(p["cem_steps"]):
         acts = np.zeros((K, H, A), f32)
         for h in range(H):
             z = noise[it, h].astype(f32)                     # [K, 4]
             v = (z * sd[h] + mean[h]).astype(f32)
-            v[:, :3] = np.clip(v[:, :3], -p["maxnorm"], p["maxnorm"])
-            v[:, 3] = np.clip(v[:, 3], -p["gripper_clamp"], p["gripper_clamp"])
+            v[:, :3] = np.minimum(np.maximum(v[:, :3], -maxnorm), maxnorm)
+            v[:, 3] = np.minimum(np.maximum(v[:, 3], -gclamp), gclamp)
             acts[:, h, 0:3] = v[:, :3]
             acts[:, h, 6] = v[:, 3]
-        roll = rollout(m, latents, n_seed, seed_actions, seed_states, acts)
+        roll = rollout_fn(acts) if rollout_fn is not None else rollout(m, latents, n_seed, seed_actions, seed_states, acts)
         e = energy(roll[:, H - 1], goal)
         order = np.argsort(e, kind="stable")
         best.append(float(e[order[0]]))
+        elites.append(order[:topk].copy())
         for h in range(H):
-            el = acts[order[:p["topk"]], h][:, [0, 1, 2, 6]].astype(np.float64)
-            mu = el.mean(0)
-            denom = p["topk"] - 1 if p["topk"] > 1 else 1
-            var = np.sqrt(((el - mu) ** 2).sum(0) / denom)
+            el = [[float(acts[c, h, 0]), float(acts[c, h, 1]), float(acts[c, h, 2]), float(acts[c, h, 6])] for c in order[:topk]]
+            mu = [0.0] * 4
+            for row in el:
+                for j in range(4):
+                    mu[j] += row[j]
+            mu = [x / float(topk) for x in mu]
+            var = [0.0] * 4
+            for row in el:
+                for j in range(4):
+                    d = row[j] - mu[j]
+                    var[j] += d * d
+            denom = float(topk - 1) if topk > 1 else 1.0
+            var = [math.sqrt(x / denom) for x in var]
             for j in range(3):
-                mean[h, j] = f32(mu[j] * (1.0 - p["momentum_mean"]) + float(mean[h, j]) * p["momentum_mean"])
-                sd[h, j] = f32(var[j] * (1.0 - p["momentum_std"]) + float(sd[h, j]) * p["momentum_std"])
-            mean[h, 3] = f32(mu[3] * (1.0 - p["momentum_mean_gripper"]) + float(mean[h, 3]) * p["momentum_mean_gripper"])
-            sd[h, 3] = f32(var[3] * (1.0 - p["momentum_std_gripper"]) + float(sd[h, 3]) * p["momentum_std_gripper"])
+                mean[h, j] = f32(mu[j] * (1.0 - float(mm)) + float(f32(mean[h, j] * mm)))
+                sd[h, j] = f32(var[j] * (1.0 - float(ms)) + float(f32(sd[h, j] * ms)))
+            mean[h, 3] = f32(mu[3] * (1.0 - float(mmg)) + float(f32(mean[h, 3] * mmg)))
+            sd[h, 3] = f32(var[3] * (1.0 - float(msg)) + float(f32(sd[h, 3] * msg)))
     out = np.zeros((H, A), f32)
     out[:, 0:3] = mean[:, 0:3]
     g = mean[:, 3]
-    out[:, 6] = np.where(np.abs(g) < p["round_gripper"], 0.0, g)
-    return out, np.array(best, f32)
+    out[:, 6] = np.where(np.abs(g) < f32(p["round_gripper"]), f32(0.0), g)
+    return out, np.array(best, f32), elites
