@@ -68,13 +68,14 @@ def plan_flops(spec: synth.HJepaSpec, plans: list, S: int) -> float:
     return total
 
 
-def peaks():
+def peaks(sustained: bool = False):
     try:
         with open(PEAKS_PATH) as f:
             d = json.load(f)
-        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+        tf = float(d["bf16_tflops_sustained"] if sustained else d["bf16_tflops"])
+        return tf, float(d["hbm_gbs"]), "measured"
     except Exception:
-        return 1590.0, 6650.0, "fallback"
+        return (1400.0 if sustained else 1590.0), 6650.0, "fallback"
 
 
 class Clocks:
@@ -183,6 +184,28 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
+    if args.config == 4:
+        # the reference's AC path is ggml CPU code that cannot be built here; its numpy restatement stands in
+        spec = ac_spec()
+        with tempfile.TemporaryDirectory() as tmp:
+            path = os.path.join(os.environ.get("JEPA_BENCH_DIR", tmp), "bench-cfg4.gguf")
+            if not os.path.exists(path):
+                synth.write_ac(path, spec, seed=4)
+            for _ in range(args.warmup):
+                ac_cpu_port(path, spec)
+            sec = sum(ac_cpu_port(path, spec) for _ in range(args.steps)) / max(args.steps, 1)
+        value = 1.0 / sec
+        sample = ("one candidate-iteration per step (one candidate through both horizon steps, each re-evaluating the "
+                  "whole context, plus its energy), numpy restatement oracle/ac_oracle.py, f32, BLAS threads")
+        print(json.dumps({"metric": METRIC, "unit": AC_UNIT, "impl": "reference", "higher_is_better": True,
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "dtype": "f32",
+                          "data": "synthetic", "scaling": "weak", "value": value, "ms_per_step": sec * 1e3,
+                          "config": {"workload": "vjepa2-ac-config4", "candidates": 1},
+                          "cpu_baseline": {"value": value, "unit": AC_UNIT, "cores": threads, "kind": "port",
+                                           "sample": sample},
+                          "e2e": {"value": value, "unit": AC_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                          "vs_baseline": None}))
+        return
     with tempfile.TemporaryDirectory() as tmp:
         path, spec, plans = setup_model(args.config, os.environ.get("JEPA_BENCH_DIR", tmp))
         S = plans[0]["n_samples"]
@@ -206,6 +229,178 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------------------------------------
+# V-JEPA 2-AC CEM
+# ---------------------------------------------------------------------------------------------
+AC_UNIT = "CEM candidates/s"
+AC_K, AC_H, AC_ITERS, AC_TOPK, AC_SEED_FRAMES = 800, 2, 10, 10, 2
+
+
+def ac_spec() -> synth.ACSpec:
+    """24 layers x 1024, 16 heads, MLP 4096, 16 x 16 patches of 1408-d ViT-g latents, 7-d actions / poses,
+    q8_0, weights N(0, 0.02), biases 0, LayerNorm gamma 1."""
+    return synth.ACSpec(enc_dim=1408, pred_dim=1024, n_layer=24, n_head=16, ffn_dim=4096, grid=16, n_frames=4,
+                        ftype="q8_0", name="bench-vjepa2-ac")
+
+
+def ac_inputs(spec: synth.ACSpec, K: int):
+    rng = np.random.default_rng(4)
+    HW = spec.grid * spec.grid
+    latents = rng.normal(size=(AC_SEED_FRAMES * HW, spec.enc_dim)).astype(np.float32)
+    seed_action = rng.normal(0, 0.05, size=(AC_SEED_FRAMES - 1, spec.action_dim)).astype(np.float32)
+    states = rng.normal(0, 0.3, size=(AC_SEED_FRAMES, spec.state_dim)).astype(np.float32)
+    goal = rng.normal(size=(HW, spec.enc_dim)).astype(np.float32)
+    noise = np.random.default_rng(4).standard_normal((AC_ITERS, AC_H, K, 4)).astype(np.float32)
+    return latents, seed_action, states, goal, noise
+
+
+def ac_flops(spec: synth.ACSpec):
+    """Per candidate-iteration: (algorithmic GFLOP as the reference evaluates it -- every step re-runs the
+    whole context, block-causal attention, shared frames embedded once -- , GFLOP this engine executes --
+    only each step's new frame, keys / values of earlier frames cached, the shared frame once per plan)."""
+    D, F, L, HW, E = spec.pred_dim, spec.ffn_dim, spec.n_layer, spec.grid ** 2, spec.enc_dim
+    R = HW + 2
+    per_row = 2 * (4 * D * D + 2 * F * D) * L
+    alg = ex = 0.0
+    for s in range(AC_H):
+        T = AC_SEED_FRAMES + s
+        alg += T * R * per_row + 4 * D * R * R * T * (T + 1) / 2 * L + 2 * HW * E * D * s + 2 * HW * D * E
+        ex += R * per_row + 4 * D * R * (T * R) * L + (2 * HW * E * D if s > 0 else 0) + 2 * HW * D * E
+    return alg / 1e9, ex / 1e9
+
+
+def ac_cpu_port(path, spec, seconds_cap=60.0):
+    """The numpy restatement (oracle/ac_oracle.py) of the reference's rollout, the way the reference runs
+    it: one candidate carried through both horizon steps, each step re-evaluating the whole context
+    (predict_all over T = 2 then 3 frames), then its L1 energy. Returns seconds per candidate-iteration."""
+    import ac_oracle
+    m = ac_oracle.ACModel(path)
+    latents, seed_action, states, goal, _ = ac_inputs(spec, 1)
+    acts = np.random.default_rng(5).normal(0, 0.02, size=(1, AC_H, spec.action_dim)).astype(np.float32)
+    t0 = time.perf_counter()
+    roll = ac_oracle.rollout(m, latents, AC_SEED_FRAMES, seed_action, states, acts)
+    ac_oracle.energy(roll[:, -1], goal)
+    return time.perf_counter() - t0
+
+
+def kernel_profile(L, call, last_ms):
+    """Run `call` once with the library's per-kernel event timing on; returns ({kind: {n, ms, flops, bytes}},
+    the call's device ms)."""
+    L.jepa_b200_kprof_begin.restype = None
+    L.jepa_b200_kprof_end.argtypes = [C.c_char_p, C.c_size_t]
+    L.jepa_b200_kprof_end.restype = C.c_int
+    L.jepa_b200_kprof_begin()
+    call()
+    total = last_ms()
+    buf = C.create_string_buffer(1 << 16)
+    L.jepa_b200_kprof_end(buf, len(buf))
+    kinds = {}
+    for line in buf.value.decode().splitlines():
+        k, n, ms, fl, by = line.split()
+        kinds[k] = {"n": int(n), "ms": float(ms), "flops": float(fl), "bytes": float(by)}
+    return kinds, total
+
+
+def run_ac(args, rank, world, local, dist, primary: bool):
+    from jepa_b200.ac import ACWorldModel
+    from jepa_b200 import lib as jlib
+    import torch
+    spec = ac_spec()
+    workdir = os.environ.get("JEPA_BENCH_DIR", tempfile.gettempdir())
+    path = os.path.join(workdir, "bench-cfg4.gguf")
+    if rank == 0 and not os.path.exists(path):
+        synth.write_ac(path + ".tmp", spec, seed=4)
+        os.replace(path + ".tmp", path)
+    if dist:
+        dist.barrier()
+    K = AC_K * world
+    latents, seed_action, states, goal, noise = ac_inputs(spec, K)
+    wm = ACWorldModel(path, device=local)
+    if world > 1:
+        uid = C.create_string_buffer(128)
+        if rank == 0:
+            assert jlib.load().jepa_b200_nccl_unique_id(uid) == 0
+        obj = [bytes(uid.raw)] if rank == 0 else [None]
+        dist.broadcast_object_list(obj, src=0)
+        wm.set_shard(rank, world, obj[0])
+    h = wm.context_new(latents, AC_SEED_FRAMES, seed_action, states)
+    params = wm.cem_params(samples=K, topk=AC_TOPK, cem_steps=AC_ITERS, horizon=AC_H)
+    L = jlib.load()
+    for _ in range(max(3, args.warmup)):
+        wm.plan(h, goal, params, noise=noise)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = Clocks(local)
+    dev_ms, wall, launches = 0.0, 0.0, 0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        out, energy = wm.plan(h, goal, params, noise=noise)
+        wall += time.perf_counter() - t0
+        dev_ms += wm.last_ms()
+        launches += L.jepa_b200_last_plan_launches(C.c_void_p(wm.ctx))
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = clk.stop()
+    # per-kernel device times: one more plan with every instrumented launch bracketed by CUDA events
+    kinds, plan_ms_prof = kernel_profile(L, lambda: wm.plan(h, goal, params, noise=noise), wm.last_ms)
+    t = torch.tensor([dev_ms, wall], dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms, wall = float(t[0]), float(t[1])
+    cands = K * AC_ITERS * args.steps
+    value, e2e = cands / (dev_ms / 1e3), cands / wall
+    alg, ex = ac_flops(spec)
+    peak_tf, _, peak_kind = peaks(sustained=True)
+    g = kinds.get("gemm_f16", {"n": 0, "ms": 0.0, "flops": 0.0})
+    gemm_tf = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else None
+    per_gpu_k = AC_K
+    n_seq = AC_SEED_FRAMES + AC_H - 1
+    h2d = goal.nbytes + noise.nbytes + AC_ITERS * per_gpu_k * n_seq * (spec.action_dim + spec.state_dim) * 4
+    d2h = AC_ITERS * K * 4 + AC_H * spec.action_dim * 4 + AC_ITERS * 4
+    res = {
+        "metric": METRIC, "value": value, "unit": AC_UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic (seeded random-init q8_0 GGUF, N(0,1) context / goal latents, N(0,1) CEM noise)",
+        "config": {"workload": f"vjepa2-ac-config4: CEM {AC_K} samples per GPU x {AC_ITERS} iterations, horizon {AC_H}, "
+                               f"top-{AC_TOPK}, {AC_SEED_FRAMES} observed frames x 256 x 1408, predictor 24 x 1024 "
+                               f"(16 heads, MLP 4096), q8_0 weights held as f16",
+                   "candidates_total": K, "parallelism": f"candidates sharded over {world} GPU(s), one NCCL all-gather "
+                                                         f"of energies per CEM iteration",
+                   "l2": "working set (keys / values 40 GB, activations 4 GB per GPU) far above L2",
+                   "arith": "f16 operands, f32 accumulate (tcgen05 kind::f16), f32 residual stream",
+                   "gflop_per_candidate_iteration": {"algorithmic": round(alg, 1), "executed": round(ex, 1)}},
+        "e2e": {"value": e2e, "unit": AC_UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": (gemm_tf / peak_tf) if gemm_tf else None, "traffic": None,
+                     "kernel": "k_gemm_f16 (tcgen05 kind::f16)",
+                     "scope": f"2 M N K per launch / CUDA-event duration per launch, summed over the {g['n']} GEMM "
+                              f"launches of one plan ({g['ms']:.1f} of {plan_ms_prof:.1f} ms)",
+                     "peak_kind": f"bf16/f16 dense sustained, {peak_kind}",
+                     "whole_plan_executed_tflops": ex * 1e9 * K / world * AC_ITERS / (plan_ms_prof / 1e3) / 1e12},
+        "clocks": clocks,
+        "kernels": {k: {"launches": v["n"], "ms": round(v["ms"], 3), "share": round(v["ms"] / plan_ms_prof, 4),
+                        **({"tflops": round(v["flops"] / v["ms"] / 1e9, 1)} if v["flops"] else {}),
+                        **({"gbs": round(v["bytes"] / v["ms"] / 1e6, 1)} if v["bytes"] else {})}
+                    for k, v in sorted(kinds.items(), key=lambda kv: -kv[1]["ms"])},
+    }
+    if world == 1 and not args.no_cpu_baseline and rank == 0:
+        try:
+            sec = ac_cpu_port(path, spec)
+            res["cpu_baseline"] = {"value": 1.0 / sec, "unit": AC_UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+                                   "sample": "one candidate-iteration (one candidate through both horizon steps, each "
+                                             "re-evaluating the whole context as the reference does, plus its energy) "
+                                             "with the numpy restatement oracle/ac_oracle.py (f32, BLAS threads)"}
+        except Exception as e:
+            res["cpu_baseline_error"] = str(e)
+    wm.close()
+    if rank == 0 and primary:
+        print(json.dumps(res))
+    return res
+
+
+# ---------------------------------------------------------------------------------------------
 def run_ours(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -219,6 +414,12 @@ def run_ours(args):
     torch.cuda.set_device(local)
     from jepa_b200.hjepa import Planner
     from jepa_b200 import lib as jlib
+    if args.config == 4:
+        run_ac(args, rank, world, local, dist, primary=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     workdir = os.environ.get("JEPA_BENCH_DIR", tempfile.gettempdir())
     path = os.path.join(workdir, f"bench-cfg{args.config}.gguf")
@@ -310,9 +511,16 @@ def run_ours(args):
                                        "kind": "reference",
                                        "sample": "one gradient evaluation of each level at S=256 (one Adam iteration per "
                                                  "level) with the reference's src/hjepa-plan.cpp via oracle/_ref"}
-        print(json.dumps(res))
     del flush
     P.close()
+    if not args.no_ac:
+        # the metric's second half: V-JEPA 2-AC CEM candidates/s on the same GPUs
+        ac = run_ac(args, rank, world, local, dist, primary=False)
+        if rank == 0:
+            res["ac_cem"] = {k: ac[k] for k in ("value", "unit", "ms_per_step", "dtype", "config", "e2e", "gpu_launches",
+                                                 "roofline", "clocks", "cpu_baseline", "cpu_baseline_error") if k in ac}
+    if rank == 0:
+        print(json.dumps(res))
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -326,6 +534,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ac", action="store_true", help="skip the V-JEPA 2-AC CEM leg of the default (config 2) run")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

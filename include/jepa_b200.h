@@ -62,6 +62,22 @@ int jepa_b200_context_set_shard(jepa_context * ctx, int rank, int world, const v
 double jepa_b200_last_plan_ms(const jepa_context * ctx);
 long long jepa_b200_last_plan_launches(const jepa_context * ctx);
 
+// C[M,N] = f16(A)[M,K] * f16(B)[N,K]^T with f32 accumulation through the V-JEPA 2-AC predictor's
+// tcgen05 kind::f16 GEMM (host f32 buffers, rounded to f16 on the device; K a multiple of 8). A kernel
+// check: every linear of the AC predictor runs through this kernel.
+int jepa_b200_gemm_f16(const float * A, const float * B, int M, int N, int K, float * C);
+// Same product timed on device-resident operands: mean milliseconds per launch over `reps` launches.
+int jepa_b200_gemm_f16_bench(int M, int N, int K, int reps, double * ms);
+
+// Per-kernel device timing for measurement runs. Between begin and end, every launch of the engine's
+// instrumented kernels (the AC predictor's GEMM, attention and row kernels) in this process is bracketed
+// by CUDA events on its stream. end() synchronises and writes one line per kernel kind into `out`
+// ("<kind> <launches> <total ms> <algorithmic FLOPs> <algorithmic bytes>\n", at most cap bytes with the
+// terminating 0) and returns the number of kinds (-1 if an event failed). The events cost a little
+// overlap between neighbouring kernels, so time the headline numbers without it.
+void jepa_b200_kprof_begin(void);
+int jepa_b200_kprof_end(char * out, size_t cap);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

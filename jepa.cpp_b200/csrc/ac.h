@@ -75,6 +75,7 @@ struct ACEngine {
     const void * shared_owner = nullptr;
     uint64_t shared_gen = 0;
     int shared_frames = 0;
+    long long launches = 0;                      // kernels launched (running count; callers take differences)
 
     ~ACEngine();
     bool init(const jepa_model & m, cudaStream_t st);

@@ -11,6 +11,7 @@
 #include "ac.h"
 #include "model.h"
 #include "shard.h"
+#include "kprof.h"
 
 #include "../../include/jepa.h"
 
@@ -278,6 +279,7 @@ int ACEngine::pass(const PassSpec & p, cudaStream_t st) {
         if (p.lat_cand[k] == 0) {
             ep.remap_gout = R;
             if (gemm_f16(p.lat[k], E, wembed, E, HW, D, E, ep, st) != 0) return -1;
+            KTimer kt("ac_broadcast", st, 0, 8.0 * HW * D * (p.n_cand - 1));
             ac_broadcast_rows(X, D, (long long) p.nf * R, k * R + 2, HW, p.n_cand, D, st);
         } else {
             if (p.lat_cand[k] != (long long) HW * E) { log("jepa: ac predictor: latent rows of a frame must be contiguous\n"); return -1; }
@@ -286,7 +288,10 @@ int ACEngine::pass(const PassSpec & p, cudaStream_t st) {
         }
     }
     // 2. action / state rows
-    ac_cond_rows(p.acts, p.act_cand, p.sts, p.st_cand, A, S, wact, bact, wst, bst, X, D, p.n_cand, p.nf, R, D, st);
+    {
+        KTimer kt("ac_cond_rows", st, 4.0 * p.n_cand * p.nf * D * (A + S), 8.0 * p.n_cand * p.nf * D);
+        ac_cond_rows(p.acts, p.act_cand, p.sts, p.st_cand, A, S, wact, bact, wst, bst, X, D, p.n_cand, p.nf, R, D, st);
+    }
 
     // 3. blocks
     AttnArgs at;
@@ -301,7 +306,10 @@ int ACEngine::pass(const PassSpec & p, cudaStream_t st) {
     for (int l = 0; l < L; l++) {
         const ACLayer & ly = layers[(size_t) l];
         __half * kv = p.kv_out + (size_t) l * p.kv_layer;
-        ln_to_f16(X, D, ly.ln1_w, ly.ln1_b, ln_eps, Hn, D, M, D, RowMap{}, st);
+        {
+            KTimer kt("layer_norm_f16", st, 0, 6.0 * M * D);
+            ln_to_f16(X, D, ly.ln1_w, ly.ln1_b, ln_eps, Hn, D, M, D, RowMap{}, st);
+        }
         AcGemmEpi eq;
         eq.mode = AEPI_QKV; eq.bias = ly.bqkv; eq.out_f16 = Q; eq.ld_f16 = D; eq.kv = kv; eq.ld_kv = 2 * D;
         eq.rope_cos = cos0; eq.rope_sin = sin0; eq.rope_rows = p.nf * R; eq.D = D; eq.hd = HD;
@@ -318,7 +326,10 @@ int ACEngine::pass(const PassSpec & p, cudaStream_t st) {
         AcGemmEpi eo;
         eo.mode = AEPI_ADD_F32; eo.bias = ly.bout; eo.out_f32 = X; eo.ld_f32 = D;
         if (gemm_f16(O, D, ly.wout, D, M, D, D, eo, st) != 0) return -1;
-        ln_to_f16(X, D, ly.ln2_w, ly.ln2_b, ln_eps, Hn, D, M, D, RowMap{}, st);
+        {
+            KTimer kt("layer_norm_f16", st, 0, 6.0 * M * D);
+            ln_to_f16(X, D, ly.ln2_w, ly.ln2_b, ln_eps, Hn, D, M, D, RowMap{}, st);
+        }
         AcGemmEpi eu;
         eu.mode = AEPI_GELU_F16; eu.bias = ly.bup; eu.out_f16 = U; eu.ld_f16 = F;
         if (gemm_f16(Hn, D, ly.wup, D, M, F, D, eu, st) != 0) return -1;
@@ -332,16 +343,24 @@ int ACEngine::pass(const PassSpec & p, cudaStream_t st) {
         const int mo = p.n_cand * p.n_out * HW;
         RowMap g;
         g.g1 = HW; g.g2 = p.n_out; g.s1 = R; g.s2 = p.nf * R; g.off = (p.nf - p.n_out) * R + 2;
-        ln_to_f16(X, D, norm_w, norm_b, ln_eps, Hn, D, mo, D, g, st);
+        {
+            KTimer kt("layer_norm_f16", st, 0, 6.0 * mo * D);
+            ln_to_f16(X, D, norm_w, norm_b, ln_eps, Hn, D, mo, D, g, st);
+        }
         AcGemmEpi ep;
         ep.mode = AEPI_F32; ep.bias = bproj; ep.out_f32 = p.out; ep.ld_f32 = OUT;
         if (gemm_f16(Hn, D, wproj, D, mo, OUT, D, ep, st) != 0) return -1;
+        KTimer kt("ac_normalize", st, 0, (double) mo * OUT * (8.0 + (p.out16 ? 2.0 : 0.0)));
         if (p.normalize) {
             ac_normalize_rows(p.out, OUT, p.out16, OUT, mo, OUT, norm_eps, st);
         } else if (p.out16) {
             to_f16(p.out, OUT, p.out16, OUT, mo, OUT, RowMap{}, st);
         }
     }
+    long long n = 1 + 7LL * L;                                        // conditioning rows, 7 per layer
+    for (int k = 0; k < p.nf; k++) n += (p.lat_cand[k] == 0 && p.n_cand > 1) ? 2 : 1;
+    if (p.n_out > 0) n += 2 + ((p.normalize || p.out16) ? 1 : 0);
+    launches += n;
     return cuda_ok(cudaGetLastError(), "ac predictor launch") ? 0 : -1;
 }
 
@@ -545,7 +564,11 @@ int rollout(ACEngine & e, jepa_context * ctx, const RolloutReq & q, const char *
                 JB_CUDA(cudaMemcpy2DAsync(q.out + ((size_t) c0 * q.H + s) * HW * OUT, (size_t) q.H * HW * OUT * 4, P,
                                           (size_t) HW * OUT * 4, (size_t) HW * OUT * 4, (size_t) kc, cudaMemcpyDeviceToHost, st));
             }
-            if (s + 1 == q.H && q.energy) ac_energy(P, (long long) HW * OUT, q.goal, (long long) HW * OUT, kc, q.energy + c0, st);
+            if (s + 1 == q.H && q.energy) {
+                KTimer kt("ac_energy", st, 3.0 * kc * HW * OUT, 4.0 * ((double) kc + 1) * HW * OUT);
+                ac_energy(P, (long long) HW * OUT, q.goal, (long long) HW * OUT, kc, q.energy + c0, st);
+                e.launches++;
+            }
         }
     }
     JB_CUDA(cudaStreamSynchronize(st));
@@ -564,6 +587,7 @@ const __half * upload_seed16(ACEngine & e, jepa_context * ctx, const float * hos
     __half * h = (__half *) ((char *) buf.p + round256(n * 4));
     if (!cuda_ok(cudaMemcpyAsync(f, host, n * 4, cudaMemcpyHostToDevice, ctx->stream), "context upload")) return nullptr;
     to_f16(f, e.E, h, e.E, n_frames * e.HW, e.E, RowMap{}, ctx->stream);
+    e.launches++;
     return h;
 }
 
@@ -630,6 +654,7 @@ int predict(jepa_context * ctx, const float * context, int T, int B, const float
     const int Kc = (int) std::min<long long>(std::min<long long>(B, kc_max), 65535);
 
     Events ev;
+    const long long l0 = e->launches;
     cudaEventRecord(ev.a, st);
     out->n_tokens = (int64_t) n_out * HW * B;
     out->dim = OUT;
@@ -665,6 +690,7 @@ int predict(jepa_context * ctx, const float * context, int T, int B, const float
             RowMap m;
             m.g1 = HW; m.g2 = 1; m.s2 = T * HW; m.off = k * HW;
             to_f16(cf, E, ch + (size_t) k * kc * HW * E, E, kc * HW, E, m, st);
+            e->launches++;
         }
         PassSpec p;
         p.n_cand = kc; p.f0 = 0; p.nf = T; p.full = !e->causal;
@@ -684,6 +710,7 @@ int predict(jepa_context * ctx, const float * context, int T, int B, const float
     float ms = 0;
     cudaEventElapsedTime(&ms, ev.a, ev.b);
     ctx->last_ms = ms;
+    ctx->last_launches = e->launches - l0;
     return 0;
 }
 
@@ -699,6 +726,7 @@ int rollout_host(jepa_context * ctx, const float * context, int n_seed, const fl
     }
     ScratchBuf seed;
     Events ev;
+    const long long l0 = e->launches;
     cudaEventRecord(ev.a, ctx->stream);
     const __half * s16 = upload_seed16(*e, ctx, context, n_seed, seed.b);
     if (!s16) return -1;
@@ -711,6 +739,7 @@ int rollout_host(jepa_context * ctx, const float * context, int n_seed, const fl
     float ms = 0;
     cudaEventElapsedTime(&ms, ev.a, ev.b);
     ctx->last_ms = ms;
+    ctx->last_launches = e->launches - l0;
     return rc;
 }
 
@@ -846,10 +875,12 @@ int jepa_ac_rollout_cached(jepa_context * ctx, jepa_ac_context * h, const float 
     if (!e) return -1;
     ScratchBuf seed;
     Events ev;
+    const long long l0 = e->launches;
     cudaEventRecord(ev.a, ctx->stream);
     const size_t n = (size_t) h->n_frames * e->HW * e->E;
     if (!e->grow(seed.b, n * 2, "the context latents")) return -1;
     to_f16(h->slab, e->E, (__half *) seed.b.p, e->E, h->n_frames * e->HW, e->E, RowMap{}, ctx->stream);
+    e->launches++;
     RolloutReq q;
     q.seed16 = (const __half *) seed.b.p; q.n_seed = h->n_frames;
     q.seed_actions = h->n_frames > 1 ? h->actions.data() : nullptr; q.seed_states = h->states.data();
@@ -861,6 +892,7 @@ int jepa_ac_rollout_cached(jepa_context * ctx, jepa_ac_context * h, const float 
     float ms = 0;
     cudaEventElapsedTime(&ms, ev.a, ev.b);
     ctx->last_ms = ms;
+    ctx->last_launches = e->launches - l0;
     return rc;
 }
 
@@ -914,12 +946,14 @@ int jepa_ac_plan(jepa_context * ctx, jepa_ac_context * handle, const float * goa
     float * en_d = (float *) ((char *) dev.b.p + round256(goal_n * 4));
     float * all_d = (float *) ((char *) en_d + round256((size_t) Kr * 4));
     Events ev;
+    const long long l0 = e->launches;
     cudaEventRecord(ev.a, st);
     JB_CUDA(cudaMemcpyAsync(goal_d, goal, goal_n * 4, cudaMemcpyHostToDevice, st));
     JB_CUDA(cudaMemsetAsync(en_d, 0, (size_t) Kr * 4, st));
     const size_t n_seed_el = (size_t) handle->n_frames * e->HW * e->E;
     if (!e->grow(seed.b, n_seed_el * 2, "the context latents")) return -1;
     to_f16(handle->slab, e->E, (__half *) seed.b.p, e->E, handle->n_frames * e->HW, e->E, RowMap{}, st);
+    e->launches++;
 
     for (int it = 0; it < q.cem_steps; it++) {
         for (int h = 0; h < H; h++) {
@@ -1000,6 +1034,7 @@ int jepa_ac_plan(jepa_context * ctx, jepa_ac_context * handle, const float * goa
     float ms = 0;
     cudaEventElapsedTime(&ms, ev.a, ev.b);
     ctx->last_ms = ms;
+    ctx->last_launches = e->launches - l0;
     return 0;
 }
 

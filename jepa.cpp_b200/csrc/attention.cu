@@ -12,6 +12,7 @@
 #include "kernels.h"
 #include "common.h"
 #include "launch.h"
+#include "kprof.h"
 
 namespace jb {
 
@@ -225,6 +226,10 @@ int attention_f16(const AttnArgs & a, cudaStream_t st) {
     }
     const int qtiles = (a.nq + QROWS - 1) / QROWS;
     const dim3 grid((unsigned) (qtiles * a.n_qframes), (unsigned) a.n_head, (unsigned) a.n_cand);
+    double keys = 0;
+    for (int k = 0; k < a.n_qframes; k++) keys += (double) (a.key_frames0 + k * a.key_step) * a.kv_rows;
+    KTimer kt("attention", st, 4.0 * a.n_head * a.hd * a.nq * keys * a.n_cand,
+              2.0 * a.n_cand * (2.0 * a.n_qframes * a.nq * a.n_head * a.hd + 2.0 * keys * a.n_head * a.hd));
     switch (a.hd) {
         case 16: JB_CUDA(launch_pdl(k_attention<16>, grid, dim3(128), 0, st, a)); break;
         case 32: JB_CUDA(launch_pdl(k_attention<32>, grid, dim3(128), 0, st, a)); break;

@@ -2,10 +2,11 @@
 // V-JEPA 2-AC predictor -- the context embedding, the fused q/k/v projection, the attention output, the
 // MLP up / down projections and the output projection, over all candidates' rows at once.
 //
-// One 128 x 256 tile per CTA, 6 warps: warp 0 issues TMA loads of 128 x 64 A and 256 x 64 B f16 tiles
+// Persistent, one CTA per SM, 10 warps: warp 0 issues TMA loads of 128 x 64 A and 256 x 64 B f16 tiles
 // (128-byte swizzle) into a 4-stage mbarrier pipeline; one thread of warp 1 issues 4 x
-// tcgen05.mma.kind::f16 (K = 16) per stage into a 128 x 256 f32 accumulator in TMEM; warps 2..5 read it
-// with tcgen05.ld and apply the fused epilogue:
+// tcgen05.mma.kind::f16 (K = 16) per stage into one of two 128 x 256 f32 accumulators in TMEM; warps
+// 2..9 read the other accumulator with tcgen05.ld (two warps per lane quadrant) and apply the fused
+// epilogue while the next tile's products run:
 //   AEPI_QKV      bias, 3-D RoPE on q and k from per-row cos / sin tables, q to its buffer, k and v into
 //                 the frame's key / value cache slot (f16)
 //   AEPI_ADD_F32  bias and the residual add into the f32 stream, with a row remap (the patch rows of a
@@ -18,6 +19,7 @@
 #include "common.h"
 #include "launch.h"
 #include "tcgen05.cuh"
+#include "kprof.h"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -114,12 +116,18 @@ __device__ __forceinline__ void epilogue32(const AcGemmEpi & ep, int row, int co
     }
 }
 
-__global__ void __launch_bounds__(192, 1)
+constexpr int EPI_WARPS = 8;                       // two per TMEM lane quadrant, 128 columns each
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+
+// Persistent: one CTA per SM walks the tiles (n fastest, so neighbouring CTAs share the A rows). Two
+// TMEM accumulators of 256 columns: the epilogue of tile i reads one while the MMA warp fills the other
+// with tile i+1.
+__global__ void __launch_bounds__(THREADS, 1)
 k_gemm_f16(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB, int M, int N, int K, AcGemmEpi ep) {
     constexpr uint32_t A_BYTES = BM * BK * 2;
     constexpr uint32_t B_BYTES = BN * BK * 2;
     constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-    constexpr uint32_t TMEM_COLS = BN;
+    constexpr uint32_t TMEM_COLS = 2 * BN;
     // instruction descriptor: D f32 (bit 4), A / B f16 (format 0), K-major both, N >> 3, M >> 4
     constexpr uint32_t IDESC = (1u << 4) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
 
@@ -127,17 +135,19 @@ k_gemm_f16(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUten
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     __shared__ __align__(8) uint64_t full_bar[STAGES];
     __shared__ __align__(8) uint64_t empty_bar[STAGES];
-    __shared__ __align__(8) uint64_t acc_bar;
+    __shared__ __align__(8) uint64_t accf_bar[2];      // MMA -> epilogue: accumulator b holds a finished tile
+    __shared__ __align__(8) uint64_t acce_bar[2];      // epilogue -> MMA: accumulator b has been read
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
     const int num_k = (K + BK - 1) / BK;
+    const int tiles_n = (N + BN - 1) / BN;
+    const int total = ((M + BM - 1) / BM) * tiles_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-        mbar_init(&acc_bar, 1);
+        for (int b = 0; b < 2; b++) { mbar_init(&accf_bar[b], 1); mbar_init(&acce_bar[b], EPI_WARPS); }
         abort_sh = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -160,56 +170,77 @@ k_gemm_f16(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUten
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued = 0;
-            for (int kt = 0; kt < num_k; kt++) {
-                const int s = kt % STAGES;
-                const uint32_t ph = (uint32_t) (kt / STAGES) & 1u;
-                if (kt >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1, &g_f16_error)) { abort_sh = 1; break; }
-                if (*(volatile int *) &abort_sh) break;
-                uint8_t * st = smem + (size_t) s * STAGE_BYTES;
-                mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-                tma_load_2d(st, &tA, kt * BK, m0, &full_bar[s]);
-                tma_load_2d(st + A_BYTES, &tB, kt * BK, n0, &full_bar[s]);
-                issued = kt + 1;
+            int kt = 0;
+            for (int t = blockIdx.x; t < total && !*(volatile int *) &abort_sh; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+                for (int k = 0; k < num_k; k++, kt++) {
+                    const int s = kt % STAGES;
+                    const uint32_t ph = (uint32_t) (kt / STAGES) & 1u;
+                    if (kt >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1, &g_f16_error)) { abort_sh = 1; break; }
+                    if (*(volatile int *) &abort_sh) break;
+                    uint8_t * st = smem + (size_t) s * STAGE_BYTES;
+                    mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+                    tma_load_2d(st, &tA, k * BK, m0, &full_bar[s]);
+                    tma_load_2d(st + A_BYTES, &tB, k * BK, n0, &full_bar[s]);
+                }
             }
             if (*(volatile int *) &abort_sh) {
-                for (int kt = issued - STAGES < 0 ? 0 : issued - STAGES; kt < issued; kt++) {
-                    mbar_wait(&full_bar[kt % STAGES], (uint32_t) (kt / STAGES) & 1u, 5, &g_f16_error);
+                // let the copies already issued land before the CTA exits
+                for (int j = kt - STAGES < 0 ? 0 : kt - STAGES; j < kt; j++) {
+                    mbar_wait(&full_bar[j % STAGES], (uint32_t) (j / STAGES) & 1u, 5, &g_f16_error);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            for (int kt = 0; kt < num_k; kt++) {
-                const int s = kt % STAGES;
-                const uint32_t ph = (uint32_t) (kt / STAGES) & 1u;
-                if (!mbar_wait(&full_bar[s], ph, 2, &g_f16_error)) { abort_sh = 1; break; }
+            int kt = 0, i = 0;
+            for (int t = blockIdx.x; t < total && !*(volatile int *) &abort_sh; t += gridDim.x, i++) {
+                const int b = i & 1;
+                if (i >= 2 && !mbar_wait(&acce_bar[b], (uint32_t) ((i >> 1) - 1) & 1u, 4, &g_f16_error)) { abort_sh = 1; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t a = smem_u32(smem + (size_t) s * STAGE_BYTES), b = a + A_BYTES;
+                const uint32_t d = tmem + (uint32_t) (b * BN);
+                for (int k = 0; k < num_k; k++, kt++) {
+                    const int s = kt % STAGES;
+                    const uint32_t ph = (uint32_t) (kt / STAGES) & 1u;
+                    if (!mbar_wait(&full_bar[s], ph, 2, &g_f16_error)) { abort_sh = 1; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t a = smem_u32(smem + (size_t) s * STAGE_BYTES), bb = a + A_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; kk++) {
-                    const uint32_t off = (uint32_t) kk * 32;   // 16 f16 = 32 bytes along K
-                    mma_kind_f16(tmem, sw128_desc(a + off), sw128_desc(b + off), IDESC, (kt | kk) != 0);
+                    for (int kk = 0; kk < BK / 16; kk++) {
+                        const uint32_t off = (uint32_t) kk * 32;   // 16 f16 = 32 bytes along K
+                        mma_kind_f16(d, sw128_desc(a + off), sw128_desc(bb + off), IDESC, (k | kk) != 0);
+                    }
+                    mma_commit(&empty_bar[s]);
                 }
-                mma_commit(&empty_bar[s]);
+                if (*(volatile int *) &abort_sh) break;
+                mma_commit(&accf_bar[b]);
             }
-            mma_commit(&acc_bar);
         }
     } else {
-        const int q = warp & 3;
-        const bool ok = mbar_wait(&acc_bar, 0, 3, &g_f16_error);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int row = m0 + q * 32 + lane;
-        const bool live = ok && num_k > 0 && !*(volatile int *) &abort_sh;
+        const int q = warp & 3;                 // TMEM lane quadrant this warp may read
+        const int half = (warp - 2) >> 2;       // which 128 of the 256 columns
+        int i = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, i++) {
+            const int b = i & 1;
+            const bool ok = mbar_wait(&accf_bar[b], (uint32_t) (i >> 1) & 1u, 3, &g_f16_error);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (!ok || *(volatile int *) &abort_sh) { abort_sh = 1; break; }
+            const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+            const int row = m0 + q * 32 + lane;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) c0, r);
-            if (!live || row >= M || n0 + c0 >= N) continue;
-            float v[32];
+            for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) (b * BN + c0), r);
+                if (row < M && n0 + c0 < N) {
+                    float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
-            epilogue32(ep, row, n0 + c0, N, v);
+                    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                    epilogue32(ep, row, n0 + c0, N, v);
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce_bar[b]);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -218,6 +249,8 @@ k_gemm_f16(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUten
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
     }
 }
+
+int g_num_sms = 0;
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode16 = nullptr;
 std::once_flag g_encode16_once;
@@ -265,8 +298,16 @@ int gemm_f16(const __half * A, int lda, const __half * B, int ldb, int M, int N,
         JB_CUDA(cudaFuncSetAttribute(k_gemm_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem));
         attr_set = true;
     }
-    const dim3 grid((unsigned) ((M + BM - 1) / BM), (unsigned) ((N + BN - 1) / BN));
-    JB_CUDA(launch_pdl(k_gemm_f16, grid, dim3(192), smem, st, ta, tb, M, N, K, ep));
+    if (g_num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const long long tiles = (long long) ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const dim3 grid((unsigned) (tiles < g_num_sms ? tiles : g_num_sms));
+    KTimer kt("gemm_f16", st, 2.0 * M * N * K);
+    JB_CUDA(launch_pdl(k_gemm_f16, grid, dim3(THREADS), smem, st, ta, tb, M, N, K, ep));
     return 0;
 }
 

@@ -92,6 +92,69 @@ extern "C" int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms) 
     return rc;
 }
 
+// C = f16(A) f16(B)^T through the V-JEPA 2-AC tensor-core GEMM (f32 accumulate, plain f32 epilogue)
+extern "C" int jepa_b200_gemm_f16(const float * A, const float * B, int M, int N, int K, float * C) {
+    if (!A || !B || !C || M < 1 || N < 1 || K < 1 || (K & 7)) return -1;
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    DevBuf a32, b32, a16, b16, c;
+    int rc = -1;
+    if (a32.alloc((size_t) M * K * 4) && b32.alloc((size_t) N * K * 4) && a16.alloc((size_t) M * K * 2) &&
+        b16.alloc((size_t) N * K * 2) && c.alloc((size_t) M * N * 4)) {
+        cudaMemcpyAsync(a32.p, A, (size_t) M * K * 4, cudaMemcpyHostToDevice, st);
+        cudaMemcpyAsync(b32.p, B, (size_t) N * K * 4, cudaMemcpyHostToDevice, st);
+        jb::to_f16(a32.f(), K, (__half *) a16.p, K, M, K, jb::RowMap{}, st);
+        jb::to_f16(b32.f(), K, (__half *) b16.p, K, N, K, jb::RowMap{}, st);
+        jb::AcGemmEpi ep;
+        ep.mode = jb::AEPI_F32;
+        ep.out_f32 = c.f();
+        ep.ld_f32 = N;
+        rc = jb::gemm_f16((const __half *) a16.p, K, (const __half *) b16.p, K, M, N, K, ep, st);
+        if (rc == 0) {
+            rc = jb::cuda_ok(cudaMemcpyAsync(C, c.p, (size_t) M * N * 4, cudaMemcpyDeviceToHost, st), "gemm_f16") &&
+                 jb::cuda_ok(cudaStreamSynchronize(st), "gemm_f16") ? 0 : -1;
+        }
+        if (rc == 0 && jb::gemm_f16_error_flag(st) != 0) { jb::log("jepa: gemm_f16: pipeline wait timed out\n"); rc = -1; }
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+// the same product timed on device-resident operands (zeros): mean ms per launch over `reps` launches
+extern "C" int jepa_b200_gemm_f16_bench(int M, int N, int K, int reps, double * ms) {
+    if (M < 1 || N < 1 || K < 1 || (K & 7) || reps < 1 || !ms) return -1;
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    DevBuf a16, b16, c;
+    int rc = -1;
+    if (a16.alloc((size_t) M * K * 2) && b16.alloc((size_t) N * K * 2) && c.alloc((size_t) M * N * 4)) {
+        cudaMemsetAsync(a16.p, 0, (size_t) M * K * 2, st);
+        cudaMemsetAsync(b16.p, 0, (size_t) N * K * 2, st);
+        jb::AcGemmEpi ep;
+        ep.mode = jb::AEPI_F32;
+        ep.out_f32 = c.f();
+        ep.ld_f32 = N;
+        rc = jb::gemm_f16((const __half *) a16.p, K, (const __half *) b16.p, K, M, N, K, ep, st);
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaEventRecord(e0, st);
+        for (int i = 0; i < reps && rc == 0; i++) rc = jb::gemm_f16((const __half *) a16.p, K, (const __half *) b16.p, K, M, N, K, ep, st);
+        cudaEventRecord(e1, st);
+        if (rc == 0 && jb::cuda_ok(cudaEventSynchronize(e1), "gemm_f16 bench")) {
+            float t = 0;
+            cudaEventElapsedTime(&t, e0, e1);
+            *ms = t / reps;
+        } else {
+            rc = -1;
+        }
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
 extern "C" int jepa_b200_dequant(uint32_t type, const void * src, int64_t rows, int64_t ne0, float * dst) {
     if (!src || !dst || rows < 1 || ne0 < 1) return -1;
     size_t row_bytes = 0;

@@ -1,8 +1,9 @@
-"""Kernel microbenchmark: the planner's tcgen05 GEMM at given shapes, through the C ABI.
+"""Kernel microbenchmark: the planners' tcgen05 GEMMs at given shapes, through the C ABI.
 
-    python -m jepa_b200.kbench M N K [reps]
+    python -m jepa_b200.kbench M N K [reps] [--f16]
 
 Prints the mean device time per launch (CUDA events) and the algorithmic TFLOP/s (2 M N K per launch).
+Without --f16 it times the H-JEPA planner's 3xTF32 GEMM, with --f16 the V-JEPA 2-AC predictor's f16 GEMM.
 Used for isolated kernel timing and as a small, self-contained target for ncu captures.
 """
 from __future__ import annotations
@@ -13,15 +14,21 @@ import sys
 from . import lib as jlib
 
 
-def gemm(M: int, N: int, K: int, reps: int = 20) -> float:
+def gemm(M: int, N: int, K: int, reps: int = 20, f16: bool = False) -> float:
     ms = C.c_double()
-    if jlib.load().jepa_b200_gemm_bench(M, N, K, reps, C.byref(ms)) != 0:
+    L = jlib.load()
+    fn = L.jepa_b200_gemm_f16_bench if f16 else L.jepa_b200_gemm_bench
+    fn.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
+    if fn(M, N, K, reps, C.byref(ms)) != 0:
         raise RuntimeError(jlib.error_text())
     return ms.value
 
 
 if __name__ == "__main__":
-    M, N, K = (int(x) for x in sys.argv[1:4])
-    reps = int(sys.argv[4]) if len(sys.argv) > 4 else 20
-    t = gemm(M, N, K, reps)
-    print(f"gemm M={M} N={N} K={K}: {t * 1e3:.2f} us/launch, {2.0 * M * N * K / (t * 1e-3) / 1e12:.2f} TFLOP/s")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    f16 = "--f16" in sys.argv
+    M, N, K = (int(x) for x in args[:3])
+    reps = int(args[3]) if len(args) > 3 else 20
+    t = gemm(M, N, K, reps, f16)
+    kind = "f16" if f16 else "3xtf32"
+    print(f"gemm[{kind}] M={M} N={N} K={K}: {t * 1e3:.2f} us/launch, {2.0 * M * N * K / (t * 1e-3) / 1e12:.2f} TFLOP/s")

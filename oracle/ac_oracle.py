@@ -70,8 +70,14 @@ def layer_norm(x, w, b, eps):
 
 
 def gelu(x):
-    from math import erf
-    e = np.vectorize(erf, otypes=[np.float64])(x.astype(np.float64) / math.sqrt(2.0))
+    """GELU with the exact erf, evaluated in double (scipy's vectorised erf when present, else math.erf)."""
+    z = x.astype(np.float64) / math.sqrt(2.0)
+    try:
+        from scipy.special import erf as verf
+        e = verf(z)
+    except ImportError:
+        from math import erf
+        e = np.vectorize(erf, otypes=[np.float64])(z)
     return (0.5 * x * (1.0 + e)).astype(f32)
 
 

@@ -27,6 +27,23 @@ def test_gemm_3xtf32_matches_f64(M, N, K):
     assert err < 1e-5 * max(1.0, K / 1536), err
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (16, 1024, 1408), (300, 192, 96), (1, 8, 8), (1000, 3072, 1024),
+                                   (517, 1024, 4096), (2064, 1408, 1024), (40000, 512, 256)])
+def test_gemm_f16_matches_f64_of_f16_operands(M, N, K):
+    """The AC predictor's tcgen05 kind::f16 GEMM (persistent, two TMEM accumulators) against a float64
+    product of the same f16-rounded operands: only the f32 accumulation differs."""
+    L = jlib.load()
+    L.jepa_b200_gemm_f16.argtypes = [capi.FP, capi.FP, C.c_int, C.c_int, C.c_int, capi.FP]
+    rng = np.random.default_rng(M * 3 + N + K)
+    A = rng.normal(size=(M, K)).astype(np.float32)
+    B = rng.normal(size=(N, K)).astype(np.float32)
+    Cm = np.zeros((M, N), np.float32)
+    assert L.jepa_b200_gemm_f16(capi.fptr(A), capi.fptr(B), M, N, K, capi.fptr(Cm)) == 0, jlib.error_text()
+    ref = A.astype(np.float16).astype(np.float64) @ B.astype(np.float16).astype(np.float64).T
+    err = np.abs(Cm - ref).max() / np.abs(ref).max()
+    assert err < 2e-5 * max(1.0, K / 1024), err
+
+
 def _host_dequant(t, raw, rows, ne0):
     import gguf
     qt = {0: gguf.GGMLQuantizationType.F32, 1: gguf.GGMLQuantizationType.F16,
