@@ -352,7 +352,10 @@ def run_ac(args, rank, world, local, dist, primary: bool):
     value, e2e = cands / (dev_ms / 1e3), cands / wall
     alg, ex = ac_flops(spec)
     peak_tf, _, peak_kind = peaks(sustained=True)
-    g = kinds.get("gemm_f16", {"n": 0, "ms": 0.0, "flops": 0.0})
+    g = {"n": 0, "ms": 0.0, "flops": 0.0}
+    for k, v in kinds.items():
+        if k.startswith("gemm_f16"):
+            g = {"n": g["n"] + v["n"], "ms": g["ms"] + v["ms"], "flops": g["flops"] + v["flops"]}
     gemm_tf = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else None
     per_gpu_k = AC_K
     n_seq = AC_SEED_FRAMES + AC_H - 1

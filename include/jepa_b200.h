@@ -69,6 +69,11 @@ int jepa_b200_gemm_f16(const float * A, const float * B, int M, int N, int K, fl
 // Same product timed on device-resident operands: mean milliseconds per launch over `reps` launches.
 int jepa_b200_gemm_f16_bench(int M, int N, int K, int reps, double * ms);
 
+// The AC predictor's attention timed alone: the last of `n_frames` frames of `rows` rows attends to every
+// row of all of them, for `n_cand` candidates and `heads` heads of width `hd` (16, 32 or 64), on
+// pseudo-random device-resident f16 operands. Mean milliseconds per launch over `reps` launches.
+int jepa_b200_attention_bench(int n_cand, int n_frames, int rows, int heads, int hd, int reps, double * ms);
+
 // Per-kernel device timing for measurement runs. Between begin and end, every launch of the engine's
 // instrumented kernels (the AC predictor's GEMM, attention and row kernels) in this process is bracketed
 // by CUDA events on its stream. end() synchronises and writes one line per kernel kind into `out`

@@ -63,7 +63,8 @@ struct ACEngine {
     const __half * wembed = nullptr, * wproj = nullptr;
     const float * bembed = nullptr, * bproj = nullptr, * wact = nullptr, * bact = nullptr, * wst = nullptr, * bst = nullptr;
     const float * norm_w = nullptr, * norm_b = nullptr;
-    float * rope_cos = nullptr, * rope_sin = nullptr;   // [slots][R][HD], sin sign-folded
+    float * rope_cos = nullptr, * rope_sin = nullptr;   // [slots + 2 grid][rope_d] per-axis tables, sin sign-folded
+    int rope_d = 0, grid = 1;
 
     // grow-only device buffers
     struct Buf {

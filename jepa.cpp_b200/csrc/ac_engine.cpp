@@ -132,35 +132,28 @@ struct ACUpload {
     }
 };
 
-// 3-D RoPE tables of every frame slot (src/rope3d.cpp:9-134 semantics): per-axis width d = 2((hd/3)/2),
+// 3-D RoPE tables (src/rope3d.cpp:9-134 semantics), factorised per axis: per-axis width d = 2((hd/3)/2),
 // omega_k = 1 / theta^(k / (d/2)) in float, angle = position * omega (float), tiled layout uses
-// omega[j mod d/2] and the interleaved one omega[j / 2]; lanes past 3d keep the identity; the rotation's
-// sign is folded into the even lanes of sin. Conditioning rows of frame t sit at (t, 0, 0).
+// omega[j mod d/2] and the interleaved one omega[j / 2]; rows [0, slots) hold the frame axis at t = row,
+// rows [slots, slots + grid) the grid-row axis, rows [slots + grid, slots + 2 grid) the grid-column axis.
+// The rotation's sign is folded into the even lanes of sin (axis offsets are multiples of d, so a lane's
+// parity inside its axis is its parity inside the head). Lanes past 3d keep the identity.
 void rope_tables(const ACEngine & e, const ACParams & p, std::vector<float> & cosv, std::vector<float> & sinv) {
-    const int hd = e.HD, d = 2 * ((hd / 3) / 2), half = d / 2, grid = p.grid_size;
-    cosv.assign((size_t) e.slots * e.R * hd, 1.0f);
-    sinv.assign((size_t) e.slots * e.R * hd, 0.0f);
-    std::vector<float> omega((size_t) std::max(half, 1));
+    const int d = e.rope_d, half = d / 2, grid = p.grid_size;
+    const int n = e.slots + 2 * grid;
+    cosv.assign((size_t) std::max(n * d, 1), 1.0f);
+    sinv.assign((size_t) std::max(n * d, 1), 0.0f);
+    if (d == 0) return;
+    std::vector<float> omega((size_t) half);
     for (int k = 0; k < half; k++) omega[(size_t) k] = 1.0f / powf(p.rope_theta, (float) k / (float) half);
-    auto axis = [&](float pos, float * c, float * s) {
+    for (int r = 0; r < n; r++) {
+        const float pos = (float) (r < e.slots ? r : r < e.slots + grid ? r - e.slots : r - e.slots - grid);
         for (int j = 0; j < d; j++) {
             const int k = p.rope_interleaved ? j / 2 : j % half;
             const float ang = pos * omega[(size_t) k];
-            c[j] = cosf(ang);
-            s[j] = sinf(ang);
-        }
-    };
-    for (int t = 0; t < e.slots; t++) {
-        for (int r = 0; r < e.R; r++) {
-            const int i = r < 2 ? 0 : r - 2;
-            float * c = &cosv[((size_t) t * e.R + r) * hd];
-            float * s = &sinv[((size_t) t * e.R + r) * hd];
-            if (d > 0) {
-                axis((float) t, c, s);
-                axis((float) (i / grid), c + d, s + d);
-                axis((float) (i % grid), c + 2 * d, s + 2 * d);
-            }
-            for (int j = 0; j < hd; j += 2) s[j] = -s[j];
+            cosv[(size_t) r * d + j] = cosf(ang);
+            const float sv = sinf(ang);
+            sinv[(size_t) r * d + j] = (j % 2 == 0) ? -sv : sv;
         }
     }
 }
@@ -243,6 +236,8 @@ bool ACEngine::init(const jepa_model & m, cudaStream_t st) {
     bproj = up.vec("pred.proj.bias", OUT, false);
     if (!up.ok) return false;
 
+    rope_d = 2 * ((HD / 3) / 2);
+    grid = p.grid_size;
     std::vector<float> cosv, sinv;
     rope_tables(*this, p, cosv, sinv);
     rope_cos = up.alloc<float>(cosv.size());
@@ -301,8 +296,6 @@ int ACEngine::pass(const PassSpec & p, cudaStream_t st) {
     at.key_step = p.full ? 0 : 1;
     at.kv_rows = R; at.ld_kv = 2 * D; at.D = D; at.n_head = NH; at.hd = HD; at.n_cand = p.n_cand;
     at.scale = 1.0f / sqrtf((float) HD);
-    const float * cos0 = rope_cos + (size_t) p.f0 * R * HD;
-    const float * sin0 = rope_sin + (size_t) p.f0 * R * HD;
     for (int l = 0; l < L; l++) {
         const ACLayer & ly = layers[(size_t) l];
         __half * kv = p.kv_out + (size_t) l * p.kv_layer;
@@ -312,7 +305,8 @@ int ACEngine::pass(const PassSpec & p, cudaStream_t st) {
         }
         AcGemmEpi eq;
         eq.mode = AEPI_QKV; eq.bias = ly.bqkv; eq.out_f16 = Q; eq.ld_f16 = D; eq.kv = kv; eq.ld_kv = 2 * D;
-        eq.rope_cos = cos0; eq.rope_sin = sin0; eq.rope_rows = p.nf * R; eq.D = D; eq.hd = HD;
+        eq.rope_cos = rope_cos; eq.rope_sin = rope_sin; eq.rope_d = rope_d; eq.rope_slots = slots; eq.rope_grid = grid;
+        eq.rope_slot0 = p.f0; eq.rope_nf = p.nf; eq.rope_frame_rows = R; eq.rope_cond = 2; eq.D = D; eq.hd = HD;
         if (gemm_f16(Hn, D, ly.wqkv, D, M, 3 * D, D, eq, st) != 0) return -1;
         for (int f = 0; f < p.f0; f++) {
             at.kv[f] = p.keys[f].base + (size_t) l * p.keys[f].layer_stride;

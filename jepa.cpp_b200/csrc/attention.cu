@@ -49,13 +49,25 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *(uint32_t *) &h;
 }
 
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // HD: head width (16, 32 or 64). Query fragments: HD/16 k-chunks; output: HD/8 n-tiles of 8 columns.
+// Issue-bound on the legacy tensor path, so the non-MMA work is trimmed: key rows are located per block
+// with one division per block (a 64-key block spans at most two frames of kv_rows >= 64 rows; shorter
+// frames take the per-row division), only the last block
+// is masked, warps whose 16 rows all lie past the frame skip the products, and the softmax uses one fused
+// multiply-add and ex2 per score.
 template <int HD>
 __global__ void __launch_bounds__(128) k_attention(AttnArgs a) {
     constexpr int PAD = HD + 8;     // padded smem row: conflict-free ldmatrix
     constexpr int KC = HD / 16;     // k-chunks of Q K^T
     constexpr int NT = HD / 8;      // n-tiles of the output
     constexpr int CH = HD / 8;      // 16-byte chunks per row
+    constexpr int PER = KB * CH / 128;   // chunks of K (and of V) each thread copies per block
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ __align__(16) __half sq[QROWS][PAD];
@@ -68,6 +80,7 @@ __global__ void __launch_bounds__(128) k_attention(AttnArgs a) {
     const int nkf = a.key_frames0 + qf * a.key_step;
     const int nkeys = nkf * a.kv_rows;
     const int nblk = (nkeys + KB - 1) / KB;
+    const bool active = q0 + warp * 16 < a.nq;     // this warp has at least one query row
     const __half * qbase = a.q + (size_t) cand * a.q_cand + (size_t) qf * a.q_frame * a.ldq + head * HD;
 
     for (int c = tid; c < QROWS * CH; c += 128) {
@@ -75,15 +88,24 @@ __global__ void __launch_bounds__(128) k_attention(AttnArgs a) {
         const int qr = q0 + r;
         cp_async16(&sq[r][ch * 8], qbase + (size_t) (qr < a.nq ? qr : 0) * a.ldq + ch * 8, qr < a.nq);
     }
+    // this thread copies rows r0 + j * (128 / CH) of every block, chunk ch
+    const int ch = tid % CH, r0 = tid / CH;
     auto load_kv = [&](int blk, int buf) {
-        for (int c = tid; c < KB * CH; c += 128) {
-            const int r = c / CH, ch = c % CH;
-            const int key = blk * KB + r;
+        const int key0 = blk * KB;
+        const int f0 = key0 / a.kv_rows;                 // one division per block
+        const int edge = (f0 + 1) * a.kv_rows;          // first key of the next frame
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int r = r0 + j * (128 / CH);
+            const int key = key0 + r;
             const bool valid = key < nkeys;
-            const int f = valid ? key / a.kv_rows : 0, kr = valid ? key % a.kv_rows : 0;
-            const __half * base = a.kv[f] + (size_t) cand * a.kv_cand_stride[f] + (size_t) kr * a.ld_kv + head * HD + ch * 8;
+            int f = key < edge ? f0 : f0 + 1;
+            if (a.kv_rows < KB) f = key / a.kv_rows;      // frames shorter than a block (small models)
+            const int kr = key - f * a.kv_rows;
+            const __half * base = valid ? a.kv[f] + (size_t) cand * a.kv_cand_stride[f] + (size_t) kr * a.ld_kv + head * HD + ch * 8
+                                        : a.kv[0];
             cp_async16(&sk[buf][r][ch * 8], base, valid);
-            cp_async16(&sv[buf][r][ch * 8], base + a.D, valid);
+            cp_async16(&sv[buf][r][ch * 8], base + (valid ? a.D : 0), valid);
         }
     };
     load_kv(0, 0);
@@ -107,92 +129,101 @@ __global__ void __launch_bounds__(128) k_attention(AttnArgs a) {
             cp_async_wait<0>();
         }
         __syncthreads();
-        if (blk == 0) {
+        if (active) {
+            if (blk == 0) {
+#pragma unroll
+                for (int kc = 0; kc < KC; kc++) {
+                    const int r = warp * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+                    const int c = kc * 16 + (lane / 16) * 8;
+                    ldsm_x4(qa[kc], &sq[r][c]);
+                }
+            }
+            // S = Q K^T: 16 rows x 64 keys per warp, 8 n-tiles of 8 keys
+            float s[8][4];
+#pragma unroll
+            for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
 #pragma unroll
             for (int kc = 0; kc < KC; kc++) {
-                const int r = warp * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
-                const int c = kc * 16 + (lane / 16) * 8;
-                ldsm_x4(qa[kc], &sq[r][c]);
+#pragma unroll
+                for (int jn = 0; jn < 8; jn += 2) {
+                    uint32_t kb[4];
+                    const int kr = jn * 8 + (lane % 8) + (lane / 16) * 8;
+                    const int kcol = kc * 16 + ((lane / 8) % 2) * 8;
+                    ldsm_x4(kb, &sk[buf][kr][kcol]);
+                    mma16816(s[jn], qa[kc], kb[0], kb[1]);
+                    mma16816(s[jn + 1], qa[kc], kb[2], kb[3]);
+                }
             }
-        }
-        // S = Q K^T: 16 rows x 64 keys per warp, 8 n-tiles of 8 keys
-        float s[8][4];
+            if (blk + 1 == nblk && nkeys % KB) {         // only the last block can run past the keys
 #pragma unroll
-        for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+                for (int j = 0; j < 8; j++) {
 #pragma unroll
-        for (int kc = 0; kc < KC; kc++) {
-#pragma unroll
-            for (int jn = 0; jn < 8; jn += 2) {
-                uint32_t kb[4];
-                const int kr = jn * 8 + (lane % 8) + (lane / 16) * 8;
-                const int kcol = kc * 16 + ((lane / 8) % 2) * 8;
-                ldsm_x4(kb, &sk[buf][kr][kcol]);
-                mma16816(s[jn], qa[kc], kb[0], kb[1]);
-                mma16816(s[jn + 1], qa[kc], kb[2], kb[3]);
+                    for (int e = 0; e < 4; e++) {
+                        if (blk * KB + j * 8 + 2 * t + (e & 1) >= nkeys) s[j][e] = -INFINITY;
+                    }
+                }
             }
-        }
-        // keys past the end are -inf; online softmax over rows g and g + 8 of the warp's 16
-        float mx[2] = {-INFINITY, -INFINITY};
+            // online softmax over rows g and g + 8 of the warp's 16
+            float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int key = blk * KB + j * 8 + 2 * t + (e & 1);
-                if (key >= nkeys) s[j][e] = -INFINITY;
-                mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
+            for (int j = 0; j < 8; j++) {
+                mx[0] = fmaxf(mx[0], fmaxf(s[j][0], s[j][1]));
+                mx[1] = fmaxf(mx[1], fmaxf(s[j][2], s[j][3]));
             }
-        }
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-        }
-        float mnew[2], corr[2], sum[2] = {0.0f, 0.0f};
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            mnew[h] = fmaxf(mrow[h], mx[h]);
-            corr[h] = mrow[h] == -INFINITY ? 0.0f : exp2f((mrow[h] - mnew[h]) * sl2);
-            mrow[h] = mnew[h];
-        }
-        uint32_t pa[4][4];              // P as A fragments: 4 k-chunks of 16 keys
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            float p[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                p[e] = s[j][e] == -INFINITY ? 0.0f : exp2f((s[j][e] - mnew[e >> 1]) * sl2);
-                sum[e >> 1] += p[e];
+            for (int h = 0; h < 2; h++) {
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
             }
-            const int kc = j >> 1;
-            if ((j & 1) == 0) { pa[kc][0] = pack_h2(p[0], p[1]); pa[kc][1] = pack_h2(p[2], p[3]); }
-            else              { pa[kc][2] = pack_h2(p[0], p[1]); pa[kc][3] = pack_h2(p[2], p[3]); }
-        }
+            float nm[2], corr[2], sum[2] = {0.0f, 0.0f};
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
-            sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
-            lrow[h] = lrow[h] * corr[h] + sum[h];
-        }
+            for (int h = 0; h < 2; h++) {
+                const float mnew = fmaxf(mrow[h], mx[h]);    // finite: every block has a valid key
+                corr[h] = ex2((mrow[h] - mnew) * sl2);        // ex2(-inf) = 0 on the first block
+                mrow[h] = mnew;
+                nm[h] = -mnew * sl2;
+            }
+            uint32_t pa[4][4];              // P as A fragments: 4 k-chunks of 16 keys
 #pragma unroll
-        for (int j = 0; j < NT; j++) {
-            o[j][0] *= corr[0]; o[j][1] *= corr[0];
-            o[j][2] *= corr[1]; o[j][3] *= corr[1];
-        }
-        // O += P V, V [key][dim] read transposed
+            for (int j = 0; j < 8; j++) {
+                float p[4];
 #pragma unroll
-        for (int kc = 0; kc < 4; kc++) {
+                for (int e = 0; e < 4; e++) {
+                    p[e] = ex2(__fmaf_rn(s[j][e], sl2, nm[e >> 1]));   // -inf -> 0
+                    sum[e >> 1] += p[e];
+                }
+                const int kc = j >> 1;
+                if ((j & 1) == 0) { pa[kc][0] = pack_h2(p[0], p[1]); pa[kc][1] = pack_h2(p[2], p[3]); }
+                else              { pa[kc][2] = pack_h2(p[0], p[1]); pa[kc][3] = pack_h2(p[2], p[3]); }
+            }
 #pragma unroll
-            for (int jn = 0; jn < NT; jn += 2) {
-                uint32_t vb[4];
-                const int vr = kc * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
-                const int vc = jn * 8 + (lane / 16) * 8;
-                ldsm_x4_t(vb, &sv[buf][vr][vc]);
-                mma16816(o[jn], pa[kc], vb[0], vb[1]);
-                mma16816(o[jn + 1], pa[kc], vb[2], vb[3]);
+            for (int h = 0; h < 2; h++) {
+                sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
+                sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
+                lrow[h] = __fmaf_rn(lrow[h], corr[h], sum[h]);
+            }
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                o[j][0] *= corr[0]; o[j][1] *= corr[0];
+                o[j][2] *= corr[1]; o[j][3] *= corr[1];
+            }
+            // O += P V, V [key][dim] read transposed
+#pragma unroll
+            for (int kc = 0; kc < 4; kc++) {
+#pragma unroll
+                for (int jn = 0; jn < NT; jn += 2) {
+                    uint32_t vb[4];
+                    const int vr = kc * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+                    const int vc = jn * 8 + (lane / 16) * 8;
+                    ldsm_x4_t(vb, &sv[buf][vr][vc]);
+                    mma16816(o[jn], pa[kc], vb[0], vb[1]);
+                    mma16816(o[jn + 1], pa[kc], vb[2], vb[3]);
+                }
             }
         }
         __syncthreads();   // this buffer is refilled by the next iteration's prefetch
     }
+    if (!active) return;
     __half * obase = a.out + (size_t) cand * a.o_cand + (size_t) qf * a.q_frame * a.ldo + head * HD;
 #pragma unroll
     for (int h = 0; h < 2; h++) {

@@ -154,8 +154,13 @@ struct AcGemmEpi {
     float * out_f32 = nullptr; int ld_f32 = 0;
     __half * out_f16 = nullptr; int ld_f16 = 0;
     __half * kv = nullptr; int ld_kv = 0;
-    const float * rope_cos = nullptr; const float * rope_sin = nullptr;   // [rope_rows][hd], sin sign-folded
-    int rope_rows = 1, D = 0, hd = 64;
+    // 3-D RoPE, factorised per axis: cos / sin tables [slots + 2 grid][d] (frame rows, then grid rows, then grid
+    // columns; d = 2 ((hd / 3) / 2) lanes per axis, the rotation's sign folded into the even lanes of sin). Row r
+    // of the GEMM is row (r mod frame_rows) of frame slot rope_slot0 + (r / frame_rows) mod rope_nf; its first
+    // rope_cond rows sit at grid position (0, 0), patch p at (p / grid, p mod grid).
+    const float * rope_cos = nullptr; const float * rope_sin = nullptr;
+    int rope_d = 0, rope_slots = 0, rope_grid = 1, rope_slot0 = 0, rope_nf = 1, rope_frame_rows = 1, rope_cond = 2;
+    int D = 0, hd = 64;
     int remap_g = 0, remap_gout = 0, remap_off = 0;   // out row = (row / g) * gout + off + row % g (g = 0: row)
 };
 

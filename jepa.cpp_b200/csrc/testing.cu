@@ -15,6 +15,14 @@ struct DevBuf {
     float * f() const { return (float *) p; }
 };
 
+__global__ void k_fill_h(__half * p, size_t n, uint32_t seed, float scale) {
+    for (size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        uint32_t h = (uint32_t) i * 2654435761u ^ seed;
+        h ^= h >> 15; h *= 2246822519u; h ^= h >> 13;
+        p[i] = __float2half_rn(((float) (h & 0xffff) / 65535.0f - 0.5f) * scale);
+    }
+}
+
 // split planes of a host matrix, uploaded
 bool upload_split(const float * h, size_t n, DevBuf & raw, DevBuf & hi, DevBuf & lo, int rows, int cols, cudaStream_t st) {
     if (!raw.alloc(n * 4) || !hi.alloc(n * 4) || !lo.alloc(n * 4)) return false;
@@ -128,8 +136,8 @@ extern "C" int jepa_b200_gemm_f16_bench(int M, int N, int K, int reps, double * 
     DevBuf a16, b16, c;
     int rc = -1;
     if (a16.alloc((size_t) M * K * 2) && b16.alloc((size_t) N * K * 2) && c.alloc((size_t) M * N * 4)) {
-        cudaMemsetAsync(a16.p, 0, (size_t) M * K * 2, st);
-        cudaMemsetAsync(b16.p, 0, (size_t) N * K * 2, st);
+        k_fill_h<<<1184, 256, 0, st>>>((__half *) a16.p, (size_t) M * K, 3u, 2.0f);
+        k_fill_h<<<1184, 256, 0, st>>>((__half *) b16.p, (size_t) N * K, 4u, 0.1f);
         jb::AcGemmEpi ep;
         ep.mode = jb::AEPI_F32;
         ep.out_f32 = c.f();
@@ -142,6 +150,52 @@ extern "C" int jepa_b200_gemm_f16_bench(int M, int N, int K, int reps, double * 
         for (int i = 0; i < reps && rc == 0; i++) rc = jb::gemm_f16((const __half *) a16.p, K, (const __half *) b16.p, K, M, N, K, ep, st);
         cudaEventRecord(e1, st);
         if (rc == 0 && jb::cuda_ok(cudaEventSynchronize(e1), "gemm_f16 bench")) {
+            float t = 0;
+            cudaEventElapsedTime(&t, e0, e1);
+            *ms = t / reps;
+        } else {
+            rc = -1;
+        }
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+
+// The AC predictor's attention timed alone: the last of `n_frames` frames of `rows` rows attends to all
+// of them, for `n_cand` candidates and `heads` heads of width `hd` (keys / values contiguous per
+// candidate, pseudo-random f16 values). Mean milliseconds per launch over `reps` launches.
+extern "C" int jepa_b200_attention_bench(int n_cand, int n_frames, int rows, int heads, int hd, int reps, double * ms) {
+    if (n_cand < 1 || n_frames < 1 || n_frames > jb::AC_MAX_FRAMES || rows < 1 || heads < 1 || reps < 1 || !ms) return -1;
+    const int D = heads * hd;
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    DevBuf q, kv, o;
+    int rc = -1;
+    const size_t nq = (size_t) n_cand * rows * D, nkv = (size_t) n_cand * n_frames * rows * 2 * D;
+    if (q.alloc(nq * 2) && kv.alloc(nkv * 2) && o.alloc(nq * 2)) {
+        k_fill_h<<<1184, 256, 0, st>>>((__half *) q.p, nq, 1u, 2.0f);
+        k_fill_h<<<1184, 256, 0, st>>>((__half *) kv.p, nkv, 2u, 2.0f);
+        jb::AttnArgs a;
+        a.q = (const __half *) q.p; a.ldq = D; a.q_cand = (long long) rows * D; a.nq = rows; a.n_qframes = 1; a.q_frame = rows;
+        a.out = (__half *) o.p; a.ldo = D; a.o_cand = a.q_cand;
+        a.key_frames0 = n_frames; a.key_step = 0;
+        for (int f = 0; f < n_frames; f++) {
+            a.kv[f] = (const __half *) kv.p + (size_t) f * rows * 2 * D;
+            a.kv_cand_stride[f] = (long long) n_frames * rows * 2 * D;
+        }
+        a.kv_rows = rows; a.ld_kv = 2 * D; a.D = D; a.n_head = heads; a.hd = hd; a.n_cand = n_cand;
+        a.scale = 1.0f / sqrtf((float) hd);
+        rc = jb::attention_f16(a, st);
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaEventRecord(e0, st);
+        for (int i = 0; i < reps && rc == 0; i++) rc = jb::attention_f16(a, st);
+        cudaEventRecord(e1, st);
+        if (rc == 0 && jb::cuda_ok(cudaEventSynchronize(e1), "attention bench")) {
             float t = 0;
             cudaEventElapsedTime(&t, e0, e1);
             *ms = t / reps;
