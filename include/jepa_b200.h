@@ -69,10 +69,14 @@ int jepa_b200_gemm_f16(const float * A, const float * B, int M, int N, int K, fl
 // Same product timed on device-resident operands: mean milliseconds per launch over `reps` launches.
 int jepa_b200_gemm_f16_bench(int M, int N, int K, int reps, double * ms);
 
-// The AC predictor's attention timed alone: the last of `n_frames` frames of `rows` rows attends to every
-// row of all of them, for `n_cand` candidates and `heads` heads of width `hd` (16, 32 or 64), on
-// pseudo-random device-resident f16 operands. Mean milliseconds per launch over `reps` launches.
-int jepa_b200_attention_bench(int n_cand, int n_frames, int rows, int heads, int hd, int reps, double * ms);
+// The AC predictor's attention: the last of `n_frames` frames of `rows` rows attends to every row of all of
+// them, for `n_cand` candidates and `heads` heads of width `hd` (16, 32 or 64). q [n_cand][rows][heads hd],
+// kv [n_cand][n_frames rows][2 heads hd] (keys, then values), out like q: host f32, f16 on the device.
+// impl: 0 the kernel the predictor would pick, 1 the mma.sync kernel, 2 the tcgen05 kernel (hd 64, rows <= 384).
+int jepa_b200_attention(const float * q, const float * kv, int n_cand, int n_frames, int rows, int heads, int hd,
+                        int impl, float * out);
+// The same attention timed alone on pseudo-random device-resident f16 operands: mean milliseconds per launch.
+int jepa_b200_attention_bench(int n_cand, int n_frames, int rows, int heads, int hd, int impl, int reps, double * ms);
 
 // Per-kernel device timing for measurement runs. Between begin and end, every launch of the engine's
 // instrumented kernels (the AC predictor's GEMM, attention and row kernels) in this process is bracketed

@@ -261,6 +261,8 @@ int attention_f16(const AttnArgs & a, cudaStream_t st) {
     for (int k = 0; k < a.n_qframes; k++) keys += (double) (a.key_frames0 + k * a.key_step) * a.kv_rows;
     KTimer kt("attention", st, 4.0 * a.n_head * a.hd * a.nq * keys * a.n_cand,
               2.0 * a.n_cand * (2.0 * a.n_qframes * a.nq * a.n_head * a.hd + 2.0 * keys * a.n_head * a.hd));
+    if (a.impl != 1 && attention_tc_supported(a)) return attention_tc(a, st);
+    if (a.impl == 2) { log("jepa: attention: the tcgen05 kernel does not take this shape\n"); return -1; }
     switch (a.hd) {
         case 16: JB_CUDA(launch_pdl(k_attention<16>, grid, dim3(128), 0, st, a)); break;
         case 32: JB_CUDA(launch_pdl(k_attention<32>, grid, dim3(128), 0, st, a)); break;

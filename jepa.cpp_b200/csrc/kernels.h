@@ -185,8 +185,13 @@ struct AttnArgs {
     int kv_rows = 0, ld_kv = 0, D = 0, n_head = 0, hd = 64;
     int n_cand = 0;
     float scale = 0.125f;
+    int impl = 0;                                 // 0: the tcgen05 kernel when it takes the shape, 1: mma.sync, 2: tcgen05
 };
 int attention_f16(const AttnArgs & a, cudaStream_t st);
+// the tcgen05 attention (attention_tc.cu): head width 64, at most 288 query rows per frame
+bool attention_tc_supported(const AttnArgs & a);
+int attention_tc(const AttnArgs & a, cudaStream_t st);
+int attention_tc_error_flag(cudaStream_t st);
 
 // Two-level row gather: in = (r / (g1 g2)) * s2 + ((r / g1) % g2) * s1 + off + r % g1  (g1 = 0: in = r)
 struct RowMap {

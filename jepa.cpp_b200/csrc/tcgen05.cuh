@@ -37,17 +37,50 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
     return ok != 0;
 }
 
-// bounded wait; false = gave up (the error flag is raised)
+// bounded wait; false = gave up (the error flag is raised). try_wait suspends the thread in hardware for a
+// while before it reports "not yet", so the loop polls gently; the clock is read once per 256 polls (a
+// clock read on every poll costs issue slots that the waiting warps' neighbours need).
 __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int code, int * err) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 256; i++) {
+            if (mbar_try_wait(bar, parity)) return true;
+        }
         if (clock64() - t0 > WAIT_LIMIT) {
             atomicExch(err, code);
             return false;
         }
     }
-    return true;
+}
+
+// non-blocking probe of a phase (mbarrier.test_wait never suspends the thread)
+__device__ __forceinline__ bool mbar_test_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// bounded spin on test_wait, for short waits on the critical path where a suspended thread would resume
+// too late; the clock is read once per 256 probes
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t * bar, uint32_t parity, int code, int * err) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 256; i++) {
+            if (mbar_test_wait(bar, parity)) return true;
+        }
+        if (clock64() - t0 > WAIT_LIMIT) {
+            atomicExch(err, code);
+            return false;
+        }
+    }
 }
 
 __device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * map, int x, int y, uint64_t * bar) {

@@ -23,6 +23,10 @@ __global__ void k_fill_h(__half * p, size_t n, uint32_t seed, float scale) {
     }
 }
 
+__global__ void k_h2f(const __half * x, float * y, size_t n) {
+    for (size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) y[i] = __half2float(x[i]);
+}
+
 // split planes of a host matrix, uploaded
 bool upload_split(const float * h, size_t n, DevBuf & raw, DevBuf & hi, DevBuf & lo, int rows, int cols, cudaStream_t st) {
     if (!raw.alloc(n * 4) || !hi.alloc(n * 4) || !lo.alloc(n * 4)) return false;
@@ -167,7 +171,7 @@ extern "C" int jepa_b200_gemm_f16_bench(int M, int N, int K, int reps, double * 
 // The AC predictor's attention timed alone: the last of `n_frames` frames of `rows` rows attends to all
 // of them, for `n_cand` candidates and `heads` heads of width `hd` (keys / values contiguous per
 // candidate, pseudo-random f16 values). Mean milliseconds per launch over `reps` launches.
-extern "C" int jepa_b200_attention_bench(int n_cand, int n_frames, int rows, int heads, int hd, int reps, double * ms) {
+extern "C" int jepa_b200_attention_bench(int n_cand, int n_frames, int rows, int heads, int hd, int impl, int reps, double * ms) {
     if (n_cand < 1 || n_frames < 1 || n_frames > jb::AC_MAX_FRAMES || rows < 1 || heads < 1 || reps < 1 || !ms) return -1;
     const int D = heads * hd;
     cudaStream_t st;
@@ -188,6 +192,7 @@ extern "C" int jepa_b200_attention_bench(int n_cand, int n_frames, int rows, int
         }
         a.kv_rows = rows; a.ld_kv = 2 * D; a.D = D; a.n_head = heads; a.hd = hd; a.n_cand = n_cand;
         a.scale = 1.0f / sqrtf((float) hd);
+        a.impl = impl;
         rc = jb::attention_f16(a, st);
         cudaEvent_t e0, e1;
         cudaEventCreate(&e0);
@@ -204,6 +209,46 @@ extern "C" int jepa_b200_attention_bench(int n_cand, int n_frames, int rows, int
         }
         cudaEventDestroy(e0);
         cudaEventDestroy(e1);
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+// The AC predictor's attention on host inputs: the last of `n_frames` frames of `rows` rows attends to all
+// of them. q [n_cand][rows][heads hd], kv [n_cand][n_frames rows][2 heads hd] (k then v), out like q; all
+// f32 on the host, f16 on the device. impl: 0 auto, 1 the mma.sync kernel, 2 the tcgen05 kernel.
+extern "C" int jepa_b200_attention(const float * q, const float * kv, int n_cand, int n_frames, int rows, int heads, int hd,
+                                   int impl, float * out) {
+    if (!q || !kv || !out || n_cand < 1 || n_frames < 1 || n_frames > jb::AC_MAX_FRAMES || rows < 1 || heads < 1) return -1;
+    const int D = heads * hd;
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    const size_t nq = (size_t) n_cand * rows * D, nkv = (size_t) n_cand * n_frames * rows * 2 * D;
+    DevBuf q32, kv32, q16, kv16, o16, o32;
+    int rc = -1;
+    if (q32.alloc(nq * 4) && kv32.alloc(nkv * 4) && q16.alloc(nq * 2) && kv16.alloc(nkv * 2) && o16.alloc(nq * 2) && o32.alloc(nq * 4)) {
+        cudaMemcpyAsync(q32.p, q, nq * 4, cudaMemcpyHostToDevice, st);
+        cudaMemcpyAsync(kv32.p, kv, nkv * 4, cudaMemcpyHostToDevice, st);
+        jb::to_f16(q32.f(), D, (__half *) q16.p, D, n_cand * rows, D, jb::RowMap{}, st);
+        jb::to_f16(kv32.f(), 2 * D, (__half *) kv16.p, 2 * D, n_cand * n_frames * rows, 2 * D, jb::RowMap{}, st);
+        jb::AttnArgs a;
+        a.q = (const __half *) q16.p; a.ldq = D; a.q_cand = (long long) rows * D; a.nq = rows; a.n_qframes = 1; a.q_frame = rows;
+        a.out = (__half *) o16.p; a.ldo = D; a.o_cand = a.q_cand;
+        a.key_frames0 = n_frames; a.key_step = 0;
+        for (int f = 0; f < n_frames; f++) {
+            a.kv[f] = (const __half *) kv16.p + (size_t) f * rows * 2 * D;
+            a.kv_cand_stride[f] = (long long) n_frames * rows * 2 * D;
+        }
+        a.kv_rows = rows; a.ld_kv = 2 * D; a.D = D; a.n_head = heads; a.hd = hd; a.n_cand = n_cand;
+        a.scale = 1.0f / sqrtf((float) hd);
+        a.impl = impl;
+        rc = jb::attention_f16(a, st);
+        if (rc == 0) {
+            k_h2f<<<1184, 256, 0, st>>>((const __half *) o16.p, o32.f(), nq);
+            rc = jb::cuda_ok(cudaMemcpyAsync(out, o32.p, nq * 4, cudaMemcpyDeviceToHost, st), "attention") &&
+                 jb::cuda_ok(cudaStreamSynchronize(st), "attention") ? 0 : -1;
+        }
+        if (rc == 0 && jb::attention_tc_error_flag(st) != 0) { jb::log("jepa: attention: pipeline wait timed out\n"); rc = -1; }
     }
     cudaStreamDestroy(st);
     return rc;

@@ -1,7 +1,7 @@
 """Kernel microbenchmark: the planners' tcgen05 GEMMs at given shapes, through the C ABI.
 
     python -m jepa_b200.kbench M N K [reps] [--f16]
-    python -m jepa_b200.kbench --attn n_cand n_frames rows heads hd [reps]
+    python -m jepa_b200.kbench --attn n_cand n_frames rows heads hd [reps] [impl: 0 auto, 1 mma.sync, 2 tcgen05]
 
 Prints the mean device time per launch (CUDA events) and the algorithmic TFLOP/s (2 M N K per launch).
 Without --f16 it times the H-JEPA planner's 3xTF32 GEMM, with --f16 the V-JEPA 2-AC predictor's f16 GEMM.
@@ -26,11 +26,11 @@ def gemm(M: int, N: int, K: int, reps: int = 20, f16: bool = False) -> float:
     return ms.value
 
 
-def attention(n_cand: int, n_frames: int, rows: int, heads: int, hd: int, reps: int = 20) -> float:
+def attention(n_cand: int, n_frames: int, rows: int, heads: int, hd: int, reps: int = 20, impl: int = 0) -> float:
     ms = C.c_double()
     L = jlib.load()
-    L.jepa_b200_attention_bench.argtypes = [C.c_int] * 6 + [C.POINTER(C.c_double)]
-    if L.jepa_b200_attention_bench(n_cand, n_frames, rows, heads, hd, reps, C.byref(ms)) != 0:
+    L.jepa_b200_attention_bench.argtypes = [C.c_int] * 7 + [C.POINTER(C.c_double)]
+    if L.jepa_b200_attention_bench(n_cand, n_frames, rows, heads, hd, impl, reps, C.byref(ms)) != 0:
         raise RuntimeError(jlib.error_text())
     return ms.value
 
@@ -40,9 +40,10 @@ if __name__ == "__main__":
         a = [int(x) for x in sys.argv[1:] if not x.startswith("--")]
         nc, nf, rows, heads, hd = a[:5]
         reps = a[5] if len(a) > 5 else 20
-        t = attention(nc, nf, rows, heads, hd, reps)
+        impl = a[6] if len(a) > 6 else 0
+        t = attention(nc, nf, rows, heads, hd, reps, impl)
         fl = 4.0 * nc * heads * hd * rows * (nf * rows)
-        print(f"attention cand={nc} frames={nf} rows={rows} heads={heads} hd={hd}: {t * 1e3:.2f} us/launch, "
+        print(f"attention[{impl}] cand={nc} frames={nf} rows={rows} heads={heads} hd={hd}: {t * 1e3:.2f} us/launch, "
               f"{fl / (t * 1e-3) / 1e12:.2f} TFLOP/s")
         sys.exit(0)
     args = [a for a in sys.argv[1:] if not a.startswith("--")]

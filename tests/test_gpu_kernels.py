@@ -44,6 +44,45 @@ def test_gemm_f16_matches_f64_of_f16_operands(M, N, K):
     assert err < 2e-5 * max(1.0, K / 1024), err
 
 
+def _attention_ref(q, kv, n_frames, rows, heads, hd):
+    """float64 softmax attention of the last frame's rows over every frame's keys, on f16-rounded inputs."""
+    D = heads * hd
+    q = q.astype(np.float16).astype(np.float64)
+    kv = kv.astype(np.float16).astype(np.float64)
+    out = np.zeros_like(q)
+    for c in range(q.shape[0]):
+        for h in range(heads):
+            Q = q[c, :, h * hd:(h + 1) * hd]
+            K = kv[c, :, h * hd:(h + 1) * hd]
+            V = kv[c, :, D + h * hd:D + (h + 1) * hd]
+            s = Q @ K.T / np.sqrt(hd)
+            p = np.exp(s - s.max(1, keepdims=True))
+            out[c, :, h * hd:(h + 1) * hd] = (p / p.sum(1, keepdims=True)) @ V
+    return out
+
+
+@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("n_cand,n_frames,rows,heads,hd", [(3, 3, 258, 2, 64), (2, 1, 258, 3, 64), (2, 2, 100, 2, 64),
+                                                             (1, 4, 384, 1, 64), (2, 2, 64, 2, 64), (3, 2, 18, 4, 16)])
+def test_attention_matches_f64(impl, n_cand, n_frames, rows, heads, hd):
+    """Both attention kernels (the mma.sync one and the tcgen05 one) against float64 on the same f16 inputs:
+    P is rounded to f16 before the P V product, so the bar is 3e-3 of the output scale."""
+    if impl == 2 and (hd != 64 or rows > 288):
+        pytest.skip("the tcgen05 kernel takes head width 64 and at most 288 rows")
+    L = jlib.load()
+    L.jepa_b200_attention.argtypes = [capi.FP, capi.FP] + [C.c_int] * 6 + [capi.FP]
+    rng = np.random.default_rng(n_cand * 100 + rows + heads)
+    D = heads * hd
+    q = rng.normal(size=(n_cand, rows, D)).astype(np.float32)
+    kv = rng.normal(size=(n_cand, n_frames * rows, 2 * D)).astype(np.float32)
+    out = np.zeros((n_cand, rows, D), np.float32)
+    assert L.jepa_b200_attention(capi.fptr(q), capi.fptr(kv), n_cand, n_frames, rows, heads, hd, impl, capi.fptr(out)) == 0, \
+        jlib.error_text()
+    ref = _attention_ref(q, kv, n_frames, rows, heads, hd)
+    err = np.abs(out - ref).max() / np.abs(ref).max()
+    assert err < 3e-3, err
+
+
 def _host_dequant(t, raw, rows, ne0):
     import gguf
     qt = {0: gguf.GGMLQuantizationType.F32, 1: gguf.GGMLQuantizationType.F16,
