@@ -237,12 +237,14 @@ def energy(pred, goal):
     return (d.sum(1) / d.shape[1]).astype(f32)
 
 
-def cem(m: ACModel, latents, n_seed, seed_actions, seed_states, goal, p: dict, noise, rollout_fn=None, A=None):
+def cem(m: ACModel, latents, n_seed, seed_actions, seed_states, goal, p: dict, noise, rollout_fn=None, A=None,
+        energy_fn=None):
     """jepa_ac_plan with explicit noise [cem_steps, H, K, 4] (src/vjepa2_ac.cpp:829-946). Returns
     (actions [H, A], best energy per iteration, elite index sets per iteration).
 
     rollout_fn(acts [K, H, A]) -> [K, H, HW, E] replaces the numpy rollout (a test drives the refit with the
-    GPU's predictions to check the CEM arithmetic on its own). The refit follows the reference's float /
+    GPU's predictions to check the CEM arithmetic on its own); energy_fn(acts) -> [K] replaces rollout and
+    energy together (the sharding protocol test gathers per-rank energies through it). The refit follows the reference's float /
     double mix exactly: elite sums and squared deviations accumulate in double in elite order, the
     momentum terms multiply two floats in float (mn * momentum) before the double sum."""
     K, H = p["samples"], p["horizon"]
@@ -265,8 +267,11 @@ def cem(m: ACModel, latents, n_seed, seed_actions, seed_states, goal, p: dict, n
             v[:, 3] = np.minimum(np.maximum(v[:, 3], -gclamp), gclamp)
             acts[:, h, 0:3] = v[:, :3]
             acts[:, h, 6] = v[:, 3]
-        roll = rollout_fn(acts) if rollout_fn is not None else rollout(m, latents, n_seed, seed_actions, seed_states, acts)
-        e = energy(roll[:, H - 1], goal)
+        if energy_fn is not None:
+            e = np.asarray(energy_fn(acts), np.float32)
+        else:
+            roll = rollout_fn(acts) if rollout_fn is not None else rollout(m, latents, n_seed, seed_actions, seed_states, acts)
+            e = energy(roll[:, H - 1], goal)
         order = np.argsort(e, kind="stable")
         best.append(float(e[order[0]]))
         elites.append(order[:topk].copy())
