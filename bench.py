@@ -34,6 +34,7 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+os.environ["NCCL_DEBUG"] = "WARN"     # rank 0 prints exactly one JSON line: no NCCL banner on stdout
 sys.path.insert(0, os.path.join(ROOT, "jepa.cpp_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
@@ -233,6 +234,7 @@ def run_reference(args):
 # ---------------------------------------------------------------------------------------------
 AC_UNIT = "CEM candidates/s"
 AC_K, AC_H, AC_ITERS, AC_TOPK, AC_SEED_FRAMES = 800, 2, 10, 10, 2
+AC_GEMM_TRAFFIC = 2.06e9     # DRAM bytes per k_gemm_f16 launch at the benchmark's rows (profiles/gemm_f16_ac128.md)
 
 
 def ac_spec() -> synth.ACSpec:
@@ -376,7 +378,9 @@ def run_ac(args, rank, world, local, dist, primary: bool):
         "e2e": {"value": e2e, "unit": AC_UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
-                     "frac": (gemm_tf / peak_tf) if gemm_tf else None, "traffic": None,
+                     "frac": (gemm_tf / peak_tf) if gemm_tf else None, "traffic": AC_GEMM_TRAFFIC,
+                     "traffic_note": "bytes per GEMM launch (mean of a layer's four): ncu DRAM read + write at M = 33,024 rows "
+                                     "scaled by rows to M = 206,400 (profiles/gemm_f16_ac128.md); algorithmic 2.34 GB",
                      "kernel": "k_gemm_f16 (tcgen05 kind::f16)",
                      "scope": f"2 M N K per launch / CUDA-event duration per launch, summed over the {g['n']} GEMM "
                               f"launches of one plan ({g['ms']:.1f} of {plan_ms_prof:.1f} ms)",

@@ -2,10 +2,14 @@
 
     python -m jepa_b200.kbench M N K [reps] [--f16]
     python -m jepa_b200.kbench --attn n_cand n_frames rows heads hd [reps] [impl: 0 auto, 1 mma.sync, 2 tcgen05]
+    python -m jepa_b200.kbench --ac samples cem_steps [model.gguf]
 
 Prints the mean device time per launch (CUDA events) and the algorithmic TFLOP/s (2 M N K per launch).
 Without --f16 it times the H-JEPA planner's 3xTF32 GEMM, with --f16 the V-JEPA 2-AC predictor's f16 GEMM.
 --attn times the AC predictor's attention (the last frame's rows over all frames' keys).
+--ac runs one V-JEPA 2-AC CEM plan (horizon 2, two observed frames) on a model of the benchmark's size
+(24 x 1024, 16 heads, MLP 4096, 16 x 16 patches of 1408-d latents, q8_0; written to the given path, or a
+temporary file, when absent) with `samples` candidates: a small, self-contained case of the real kernels.
 Used for isolated kernel timing and as a small, self-contained target for ncu captures.
 """
 from __future__ import annotations
@@ -35,7 +39,40 @@ def attention(n_cand: int, n_frames: int, rows: int, heads: int, hd: int, reps: 
     return ms.value
 
 
+def ac_plan(samples: int, cem_steps: int, path: str = "") -> float:
+    import os
+    import tempfile
+
+    import numpy as np
+
+    from . import synth
+    from .ac import ACWorldModel
+    if not path:
+        path = os.path.join(tempfile.gettempdir(), "kbench-ac.gguf")
+    if not os.path.exists(path):
+        synth.write_ac(path + ".tmp", synth.ACSpec(enc_dim=1408, pred_dim=1024, n_layer=24, n_head=16, ffn_dim=4096, grid=16,
+                                                   n_frames=4, ftype="q8_0", name="kbench-ac"), seed=4)
+        os.replace(path + ".tmp", path)
+    rng = np.random.default_rng(4)
+    wm = ACWorldModel(path)
+    lat = rng.normal(size=(2 * wm.HW, 1408)).astype(np.float32)
+    h = wm.context_new(lat, 2, rng.normal(0, 0.05, size=(1, 7)).astype(np.float32),
+                       rng.normal(0, 0.3, size=(2, 7)).astype(np.float32))
+    goal = rng.normal(size=(wm.HW, 1408)).astype(np.float32)
+    params = wm.cem_params(samples=samples, topk=min(10, samples), cem_steps=cem_steps, horizon=2)
+    noise = rng.standard_normal((cem_steps, 2, samples, 4)).astype(np.float32)
+    wm.plan(h, goal, params, noise=noise)
+    ms = wm.last_ms()
+    wm.close()
+    return ms
+
+
 if __name__ == "__main__":
+    if "--ac" in sys.argv:
+        a = [x for x in sys.argv[1:] if not x.startswith("--")]
+        ms = ac_plan(int(a[0]), int(a[1]), a[2] if len(a) > 2 else "")
+        print(f"ac plan samples={a[0]} cem_steps={a[1]}: {ms:.1f} ms")
+        sys.exit(0)
     if "--attn" in sys.argv:
         a = [int(x) for x in sys.argv[1:] if not x.startswith("--")]
         nc, nf, rows, heads, hd = a[:5]
