@@ -88,6 +88,28 @@ struct Uploader {
         split_f32(L.wt, L.out, L.wt_hi, L.wt_lo, L.out, L.in, L.out, st);
         ok = cuda_ok(cudaStreamSynchronize(st), "weight layout") && ok;
     }
+    // out(V(h)) as one linear: W_ov = W_out W_v (a 3xTF32 product on the device), b_ov = W_out b_v + b_out
+    DLin compose(const DLin & v, const DLin & out) {
+        DLin L;
+        if (!ok || !v || !out || out.in != v.out) return L;
+        L.in = v.in;
+        L.out = out.out;
+        L.w = alloc<float>((size_t) L.in * L.out);
+        if (!L.w) return DLin();
+        GemmEpi ep;
+        ep.out0 = L.w;
+        ep.ld0 = L.in;
+        if (gemm_tc({out.w_hi, out.w_lo, out.in}, {v.wt_hi, v.wt_lo, v.out}, out.out, v.in, v.out, ep, st)) { ok = false; return DLin(); }
+        if (v.b || out.b) {
+            L.b = alloc<float>((size_t) L.out);
+            if (!L.b) return DLin();
+            if (v.b) linear_simt(v.b, v.out, out.w, out.b, L.b, L.out, 1, out.out, out.in, st);
+            else ok = cuda_ok(cudaMemcpyAsync(L.b, out.b, (size_t) L.out * 4, cudaMemcpyDeviceToDevice, st), "compose") && ok;
+        }
+        ok = cuda_ok(cudaStreamSynchronize(st), "compose") && ok;
+        finish(L);
+        return L;
+    }
     DLin lin(const std::string & name, int64_t row0 = 0, int64_t rows = -1) {
         DLin L;
         const gguf_tensor * t = m.get(name + ".weight");
@@ -155,6 +177,7 @@ bool HPlanner::build(const jepa_model & m) {
             DBlock B;
             B.v = up.lin(q + "attn_qkv", 2 * (int64_t) L.I, L.I);   // the value third: one query over one key (hjepa-plan.cpp:170-171)
             B.out = up.lin(q + "attn_out");
+            B.ov = up.compose(B.v, B.out);
             B.up = up.lin(q + "ffn_up");
             B.down = up.lin(q + "ffn_down");
             B.ln1_w = up.vec(q + "ln1.weight"); B.ln1_b = up.vec(q + "ln1.bias");
@@ -387,13 +410,11 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
             float * xm = w.xmid + tl * S * P, * o = w.o + tl * S * P, * dn = w.dn + tl * S * P, * u = w.u + tl * S * F;
             block_pre(xin, P, mod_l, ldm, 0, P, B.ln1_w, B.ln1_b, adaln_eps, ln_eps, w.h_hi, w.h_lo, P,
                       w.sta0 + tl * S, w.sta1 + tl * S, S, P, st);
-            GemmEpi e1;
-            e1.mode = EPI_SPLIT; e1.bias = B.v.b; e1.out_hi = w.v_hi; e1.out_lo = w.v_lo; e1.ld_split = I;
-            if (gemm_tc({w.h_hi, w.h_lo, P}, {B.v.w_hi, B.v.w_lo, P}, S, I, P, e1, st)) return -1;
+            // attention half: o = out(V(h)) through the composed linear, xm = xin + gate * o
             GemmEpi e2;
-            e2.mode = EPI_GATED; e2.bias = B.out.b; e2.out0 = o; e2.ld0 = P; e2.aux = xin; e2.ld_aux = P;
+            e2.mode = EPI_GATED; e2.bias = B.ov.b; e2.out0 = o; e2.ld0 = P; e2.aux = xin; e2.ld_aux = P;
             e2.gate = mod_l + 2 * P; e2.ld_gate = ldm; e2.out1 = xm; e2.ld1 = P;
-            if (gemm_tc({w.v_hi, w.v_lo, I}, {B.out.w_hi, B.out.w_lo, I}, S, P, I, e2, st)) return -1;
+            if (gemm_tc({w.h_hi, w.h_lo, P}, {B.ov.w_hi, B.ov.w_lo, P}, S, P, P, e2, st)) return -1;
             block_pre(xm, P, mod_l, ldm, 3 * P, 4 * P, B.ln2_w, B.ln2_b, adaln_eps, ln_eps, w.h_hi, w.h_lo, P,
                       w.stm0 + tl * S, w.stm1 + tl * S, S, P, st);
             GemmEpi e3;
@@ -403,7 +424,7 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
             e4.mode = EPI_GATED; e4.bias = B.down.b; e4.out0 = dn; e4.ld0 = P; e4.aux = xm; e4.ld_aux = P;
             e4.gate = mod_l + 5 * P; e4.ld_gate = ldm; e4.out1 = xout; e4.ld1 = P;
             if (gemm_tc({w.g_hi, w.g_lo, F}, {B.down.w_hi, B.down.w_lo, F}, S, P, F, e4, st)) return -1;
-            launches += 6;
+            launches += 5;
         }
         const float * xL = x0 + (size_t) NL * S * P;
         float * s_next = w.states + (size_t) (t + 1) * S * D;
@@ -620,13 +641,10 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             a.dmod2_hi = dmh; a.dmod2_lo = dml; a.ld_dmod2 = ldm; a.d_hi = w.d_hi; a.d_lo = w.d_lo; a.ldd = P;
             a.M = S; a.D = P; a.eps0 = adaln_eps; a.eps1 = ln_eps;
             block_bwd(a, st);
-            // attention half (one query over one key: the value path)
-            GemmEpi e3;
-            e3.mode = EPI_SPLIT; e3.out_hi = w.dv_hi; e3.out_lo = w.dv_lo; e3.ld_split = I;
-            if (gemm_tc({w.d_hi, w.d_lo, P}, {B.out.wt_hi, B.out.wt_lo, P}, S, I, P, e3, st)) return -1;
+            // attention half (one query over one key: the value path, through the composed linear)
             GemmEpi e4;
             e4.out0 = w.gh; e4.ld0 = P;
-            if (gemm_tc({w.dv_hi, w.dv_lo, I}, {B.v.wt_hi, B.v.wt_lo, I}, S, P, I, e4, st)) return -1;
+            if (gemm_tc({w.d_hi, w.d_lo, P}, {B.ov.wt_hi, B.ov.wt_lo, P}, S, P, P, e4, st)) return -1;
             BlockBwdArgs b{};
             b.gh = w.gh; b.ldgh = P; b.gres = w.gmid; b.ldres = P; b.x = xin; b.ldx = P;
             b.st0 = w.sta0 + tl * S; b.st1 = w.sta1 + tl * S; b.ln_w = B.ln1_w; b.ln_b = B.ln1_b;
@@ -639,7 +657,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             }
             b.M = S; b.D = P; b.eps0 = adaln_eps; b.eps1 = ln_eps;
             block_bwd(b, st);
-            launches += 6;
+            launches += 5;
         }
         // gx = d (s_t + pos0 [-> in_proj]); pass it to the state the step read
         if (t > 0) {

@@ -26,6 +26,7 @@ struct DLin {
 
 struct DBlock {
     DLin v, out, up, down;
+    DLin ov;    // out(V(h)) composed: W_out W_v, W_out b_v + b_out (one query over one key: attention is V)
     float * ln1_w = nullptr, * ln1_b = nullptr, * ln2_w = nullptr, * ln2_b = nullptr;
 };
 
