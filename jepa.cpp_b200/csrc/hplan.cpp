@@ -195,6 +195,35 @@ bool HPlanner::build(const jepa_model & m) {
         L.enc_out_w = up.vec(p + "enc.out_norm.weight"); L.enc_out_b = up.vec(p + "enc.out_norm.bias");
         L.enc_fc1 = up.lin(p + "enc.fc1");
         L.enc_fc2 = up.lin(p + "enc.fc2");
+        // the action encoder (levels above the first; weights as the reference loads them, hjepa-plan.cpp:183-200)
+        DActEnc & ae = L.ae;
+        if (li > 0 && L.hp.act_enc_kind == "mlp") {
+            ae.kind = 1;
+            ae.fc1 = up.lin(p + "act_enc.fc1");
+            ae.fc2 = up.lin(p + "act_enc.fc2");
+        } else if (li > 0 && L.hp.act_enc_kind == "seq") {
+            ae.kind = 2;
+            ae.d = L.hp.act_enc_dim;
+            ae.n_head = L.hp.act_enc_n_head;
+            ae.step = up.lin(p + "act_enc.step");
+            ae.pos = up.vec(p + "act_enc.pos");
+            if (const gguf_tensor * t = m.get(p + "act_enc.pos")) ae.pos_n = t->nelements();
+            for (int i = 0; i < L.hp.act_enc_n_layer && up.ok; i++) {
+                const std::string q = p + "act_enc.blk." + std::to_string(i) + ".";
+                DSeqBlock B;
+                B.qkv = up.lin(q + "attn_qkv");
+                B.out = up.lin(q + "attn_out");
+                B.up = up.lin(q + "ffn_up");
+                B.down = up.lin(q + "ffn_down");
+                B.ln1_w = up.vec(q + "ln1.weight"); B.ln1_b = up.vec(q + "ln1.bias");
+                B.ln2_w = up.vec(q + "ln2.weight"); B.ln2_b = up.vec(q + "ln2.bias");
+                ae.blocks.push_back(B);
+            }
+            ae.head0 = up.lin(p + "act_enc.head.0");
+            ae.head2 = up.lin(p + "act_enc.head.2");
+            ae.headln_w = up.vec(p + "act_enc.head.ln.weight"); ae.headln_b = up.vec(p + "act_enc.head.ln.bias");
+        }
+        if (ae.kind) { ae.out_w = up.vec(p + "act_enc.out_norm.weight"); ae.out_b = up.vec(p + "act_enc.out_norm.bias"); }
         if (const gguf_tensor * q = m.get(p + "act_queue")) {
             L.queue.resize((size_t) q->nelements());
             dequant_row(q->type, q->data, L.queue.data(), q->nelements());
@@ -210,8 +239,10 @@ bool HPlanner::build(const jepa_model & m) {
 // workspace
 // ---------------------------------------------------------------------------------------------
 Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs) {
+    const int Wa = pooled_chunks(cs);
     const std::string key = std::to_string(S) + "/" + std::to_string(T) + "/" + std::to_string(cs.goal_level) + "/" +
-                            std::to_string(cs.dense) + "/" + std::to_string(cs.n_goal) + "/" + std::to_string(cs.cost_last_n);
+                            std::to_string(cs.dense) + "/" + std::to_string(cs.n_goal) + "/" + std::to_string(cs.cost_last_n) +
+                            "/" + std::to_string(Wa);
     auto it = ws.find(level);
     if (it != ws.end() && it->second->graph_key == key) return it->second.get();
     ws.erase(level);
@@ -240,6 +271,35 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs) {
         const DLevel & U = levels[(size_t) e.lv - 1];
         maxw = std::max({maxw, U.D, levels[(size_t) e.lv - 2].D, U.enc_fc1 ? U.enc_fc1.out : 0});
     }
+    // action cost: the upper level's action encoder over the last Wa whole chunks
+    PoolWs & pw = w->pool;
+    const DActEnc * ae = Wa > 0 ? &levels[(size_t) level].ae : nullptr;
+    const int Ein = L.act0 ? L.E : A, Au = Wa > 0 ? levels[(size_t) level].A : 0;
+    size_t pool_scr = 0;
+    if (ae) {
+        pw.Wa = Wa;
+        pw.stride = levels[(size_t) level].hp.stride;
+        pw.c0 = T / pw.stride - Wa;
+        pw.G = pw.stride + 1;
+        const size_t n = (size_t) Wa * S, nG = n * (size_t) pw.G;
+        const int NB = (int) ae->blocks.size();
+        pw.xs.assign((size_t) NB + 1, nullptr);
+        pw.qkv.assign((size_t) NB, nullptr); pw.probs.assign((size_t) NB, nullptr);
+        pw.xmid.assign((size_t) NB, nullptr); pw.u.assign((size_t) NB, nullptr);
+        int wide = std::max({Au, pw.stride * Ein});
+        if (ae->kind == 1) wide = std::max(wide, ae->fc1.out);
+        if (ae->kind == 2) {
+            wide = std::max({wide, ae->head0.out, pw.stride * ae->d});
+            int f = 3 * ae->d;
+            for (const DSeqBlock & B : ae->blocks) f = std::max(f, B.up.out);
+            pool_scr = nG * (size_t) f;
+            if (!group_mha_prepare(pw.G, ae->d, ae->n_head)) {
+                log("jepa: hjepa planner: a %d-token action-encoder group of width %d does not fit one CTA's shared memory\n", pw.G, ae->d);
+                return nullptr;
+            }
+        }
+        pool_scr = std::max(pool_scr, n * (size_t) wide);
+    }
     ArenaPlan ap;
     auto plan_all = [&](auto && add) {
         add((float **) &w->x, (size_t) S * T * A); add(&w->m, (size_t) S * T * A); add(&w->v, (size_t) S * T * A);
@@ -262,10 +322,36 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs) {
         add(&w->gx, sw); add(&w->gmid, sw); add(&w->gh, sw); add(&w->d_hi, sw); add(&w->d_lo, sw);
         add(&w->du_hi, sw); add(&w->du_lo, sw); add(&w->dv_hi, sw); add(&w->dv_lo, sw);
         add(&w->gtmp, sw); add(&w->gtmp2, sw);
-        add(&w->sp_hi, std::max(sw, R * maxw)); add(&w->sp_lo, std::max(sw, R * maxw));
+        add(&w->sp_hi, std::max({sw, R * maxw, pool_scr})); add(&w->sp_lo, std::max({sw, R * maxw, pool_scr}));
+        if (ae) {
+            const size_t n = (size_t) Wa * S, nG = n * (size_t) pw.G;
+            if (ae->kind == 1) {
+                add(&pw.x, n * ae->fc1.in); add(&pw.h, n * ae->fc1.out); add(&pw.r, n * ae->fc1.out);
+                if (ae->out_w) add(&pw.ypre, n * Au);
+            } else {
+                const int d = ae->d, H = ae->n_head;
+                int fmax = 1;
+                add(&pw.x, n * pw.stride * d);
+                for (size_t b = 0; b < ae->blocks.size(); b++) {
+                    const int f = ae->blocks[b].up.out;
+                    fmax = std::max(fmax, f);
+                    add(&pw.xs[b], nG * d); add(&pw.qkv[b], nG * 3 * d); add(&pw.probs[b], nG * H * pw.G);
+                    add(&pw.xmid[b], nG * d); add(&pw.u[b], nG * f);
+                }
+                add(&pw.xs.back(), nG * d);
+                add(&pw.h, nG * d); add(&pw.r, nG * fmax);
+                add(&pw.z, n * ae->head0.out); add(&pw.zg, n * ae->head0.out); add(&pw.zl, n * ae->head0.out);
+                add(&pw.ypre, n * Au);
+            }
+            add(&pw.y, n * Au); add(&pw.gy, n * Au);
+            add(&pw.ga, pool_scr); add(&pw.gb, pool_scr); add(&pw.gc, pool_scr);
+            add(&pw.ge, R * Ein);
+            add(&pw.goals, (size_t) Wa * Au); add(&pw.weights, (size_t) Wa);
+        }
         add(&w->cost, (size_t) S); add(&w->best_val, (size_t) 1);
         const int Dg = levels[(size_t) cs.goal_level - 1].D;
-        add(&w->goals, (size_t) std::max(1, cs.n_goal) * Dg); add(&w->weights, (size_t) (T + 1));
+        // one goal row per scored prediction (W <= T + 1 of them; a single goal is repeated)
+        add(&w->goals, (size_t) (T + 1) * Dg); add(&w->weights, (size_t) (T + 1));
         for (EncStage & e : w->enc) {
             const DLevel & U = levels[(size_t) e.lv - 1];
             const int Din = levels[(size_t) e.lv - 2].D, Dout = U.D;
@@ -284,6 +370,15 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs) {
     ap.add<float>((size_t) 2 * 4096);      // Adam schedule
     ap.add<int>(4);
     ap.add<void *>((size_t) 2 * (T + 1));  // cost pointer tables
+    if (ae) {   // carved in this order below
+        const size_t n = (size_t) Wa * S;
+        ap.add<LnStats>(n);
+        if (ae->kind == 2) {
+            ap.add<LnStats>(n);
+            for (size_t b = 0; b < 2 * ae->blocks.size(); b++) ap.add<LnStats>(n * (size_t) pw.G);
+        }
+        ap.add<void *>((size_t) Wa); ap.add<void *>((size_t) Wa);
+    }
     if (!w->arena.reserve(ap.bytes + 65536, ctx->device)) return nullptr;
     auto take = [&](auto ** p, size_t n) { *p = (std::remove_pointer_t<decltype(p)>) w->arena.take<float>(n); };
     plan_all(take);
@@ -301,6 +396,22 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs) {
     w->pred_ptrs = (const float **) w->arena.take<void *>((size_t) (T + 1));
     w->gpred_ptrs = (float **) w->arena.take<void *>((size_t) (T + 1));
     w->best_idx = w->arena.take<int>(1);
+    if (ae) {
+        const size_t n = (size_t) Wa * S, nG = n * (size_t) pw.G;
+        pw.sto = w->arena.take<LnStats>(n);
+        if (ae->kind == 2) {
+            pw.sth = w->arena.take<LnStats>(n);
+            pw.st1.assign(ae->blocks.size(), nullptr);
+            pw.st2.assign(ae->blocks.size(), nullptr);
+            for (size_t b = 0; b < ae->blocks.size(); b++) {
+                pw.st1[b] = w->arena.take<LnStats>(nG);
+                pw.st2[b] = w->arena.take<LnStats>(nG);
+            }
+        }
+        pw.ptrs = (const float **) w->arena.take<void *>((size_t) Wa);
+        pw.gptrs = (float **) w->arena.take<void *>((size_t) Wa);
+        if (!pw.gptrs) { log("jepa: hjepa planner: workspace carve failed\n"); return nullptr; }
+    }
     if (!w->pred_ptrs || !w->best_idx) { log("jepa: hjepa planner: workspace carve failed\n"); return nullptr; }
     Workspace * raw = w.get();
     ws[level] = std::move(w);
@@ -500,6 +611,8 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
     (void) gbase;
     cost_l2(w.pred_ptrs, w.goals, w.weights, w.gpred_ptrs, W, S, Dl, Dl, w.cost, want_grad, st);
     launches++;
+    // the action cost comes after the state cost, as the reference adds them (hjepa-plan.cpp:769-791)
+    if (w.pool.Wa > 0 && pool_forward(w, want_grad)) return -1;
     return 0;
 }
 
@@ -526,6 +639,25 @@ bool HPlanner::cost_tables(Workspace & w, const CostSpec & cs) {
     }
     std::vector<float> goals((size_t) W * Dl);
     for (int j = 0; j < W; j++) memcpy(goals.data() + (size_t) j * Dl, cs.goal + (size_t) (cs.n_goal == 1 ? 0 : j) * Dl, (size_t) Dl * 4);
+    // the action cost's tables: chunk j of the pooled rows against goal action n_goal - Wa + j, weight
+    // action_cost_weight for every chunk
+    PoolWs & pw = w.pool;
+    std::vector<const float *> pp((size_t) pw.Wa);
+    std::vector<float *> gpp((size_t) pw.Wa);
+    std::vector<float> pwt((size_t) pw.Wa, cs.action_cost_weight), pgoals;
+    if (pw.Wa > 0) {
+        const int Au = levels[(size_t) w.level].A;
+        for (int j = 0; j < pw.Wa; j++) {
+            pp[(size_t) j] = pw.y + (size_t) j * S * Au;
+            gpp[(size_t) j] = pw.gy + (size_t) j * S * Au;
+        }
+        pgoals.assign(cs.goal_action + (size_t) (cs.n_goal - pw.Wa) * Au, cs.goal_action + (size_t) cs.n_goal * Au);
+        if (!cuda_ok(cudaMemcpyAsync(pw.ptrs, pp.data(), pp.size() * sizeof(void *), cudaMemcpyHostToDevice, st), "action cost tables") ||
+            !cuda_ok(cudaMemcpyAsync(pw.gptrs, gpp.data(), gpp.size() * sizeof(void *), cudaMemcpyHostToDevice, st), "action cost tables") ||
+            !cuda_ok(cudaMemcpyAsync(pw.weights, pwt.data(), pwt.size() * 4, cudaMemcpyHostToDevice, st), "action cost weights") ||
+            !cuda_ok(cudaMemcpyAsync(pw.goals, pgoals.data(), pgoals.size() * 4, cudaMemcpyHostToDevice, st), "goal actions"))
+            return false;
+    }
     bool ok = cuda_ok(cudaMemcpyAsync(w.pred_ptrs, p.data(), (size_t) W * sizeof(void *), cudaMemcpyHostToDevice, st), "cost tables") &&
               cuda_ok(cudaMemcpyAsync(w.gpred_ptrs, gp.data(), (size_t) W * sizeof(void *), cudaMemcpyHostToDevice, st), "cost tables") &&
               cuda_ok(cudaMemcpyAsync(w.weights, wt.data(), (size_t) W * 4, cudaMemcpyHostToDevice, st), "cost weights") &&
@@ -543,6 +675,8 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
     const DLevel & L = levels[(size_t) w.level - 1];
     const int S = w.S, T = w.T, D = L.D, P = L.P, F = L.F, I = L.I, NL = L.L, A = L.A;
     const int R = S * T, ldm = 6 * P * NL;
+    // ---- the action cost's encoder, into the gradient of the pooled action embeddings
+    if (w.pool.Wa > 0 && pool_backward(w)) return -1;
     // ---- goal-projection encoders, top stage first, into the gradients of the states they read
     for (int k = (int) w.enc.size() - 1; k >= 0; k--) {
         EncStage & e = w.enc[(size_t) k];
@@ -679,7 +813,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
         if (gemm_tc({w.dmod_hi, w.dmod_lo, ldm}, {L.adaln.wt_hi, L.adaln.wt_lo, ldm}, R, P, ldm, ep, st)) return -1;
     }
     act_bwd(w.dcs, P, w.cpre, P, w.dc, P, R, P, 2, false, st); launches++;
-    const float * g = w.dc;
+    float * g = w.dc;
     int gw = P;
     if (L.cond_proj) {
         if (lin_bwd(L.cond_proj, g, gw, nullptr, nullptr, R, w.tmpR, L.C, w)) return -1;
@@ -692,13 +826,16 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
         if (lin_bwd(L.pact0, w.tmpR2, H, nullptr, nullptr, R, w.tmpR, L.E, w)) return -1;
         g = w.tmpR; gw = L.E;
     }
+    // g = d cost / d (action embeddings) through the predictor; the action cost's share joins it here
     if (L.act0) {
         const int H = L.act0.out;
+        if (w.pool.Wa > 0) { add_inplace(g, gw, w.pool.ge, L.E, R, L.E, st); launches++; }
         if (lin_bwd(L.act2, g, gw, nullptr, nullptr, R, w.tmpR2, H, w)) return -1;
         act_bwd(w.tmpR2, H, w.ae_u, H, w.tmpR2, H, R, H, 2, false, st); launches++;
         if (lin_bwd(L.act0, w.tmpR2, H, nullptr, nullptr, R, w.da_all, A, w)) return -1;
     } else {
         copy_rows(g, gw, w.da_all, A, R, A, st); launches++;
+        if (w.pool.Wa > 0) { add_inplace(w.da_all, A, w.pool.ge, A, R, A, st); launches++; }
     }
     return 0;
 }

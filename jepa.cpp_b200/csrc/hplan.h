@@ -30,8 +30,29 @@ struct DBlock {
     float * ln1_w = nullptr, * ln1_b = nullptr, * ln2_w = nullptr, * ln2_b = nullptr;
 };
 
+// One transformer block of a 'seq' action encoder (pre-norm, ReLU MLP).
+struct DSeqBlock {
+    DLin qkv, out, up, down;
+    float * ln1_w = nullptr, * ln1_b = nullptr, * ln2_w = nullptr, * ln2_b = nullptr;
+};
+
+// A level's action encoder: `stride` action embeddings of the level below -> one latent action of this
+// level (build_action_pool, src/hjepa-plan.cpp:663-684). 'mlp': concat -> fc1 -> ReLU -> fc2 (-> LN);
+// 'seq': a CLS token plus one token per step through transformer blocks, CLS -> head -> LN(1e-6).
+struct DActEnc {
+    int kind = 0;                     // 0 none, 1 mlp, 2 seq
+    DLin fc1, fc2;
+    DLin step, head0, head2;
+    std::vector<DSeqBlock> blocks;
+    float * pos = nullptr;            // [max_chunk + 1][d]
+    int64_t pos_n = 0;                // elements of pos
+    float * headln_w = nullptr, * headln_b = nullptr, * out_w = nullptr, * out_b = nullptr;
+    int d = 0, n_head = 0;
+};
+
 struct DLevel {
     HLevel hp;
+    DActEnc ae;
     int D = 0, P = 0, F = 0, I = 0, L = 0, A = 0, E = 0, C = 0;   // state, predictor, ffn, inner, layers, action, act-embed, cond widths
     float * pos0 = nullptr;
     DLin act0, act2, pact0, pact2, in_proj, cond_proj, out_proj, proj0, proj2;
@@ -60,8 +81,28 @@ struct EncStage {
     float * d_hi = nullptr, * d_lo = nullptr;
 };
 
+// Device buffers of the action cost: the last Wa whole chunks of the candidates' action embeddings pooled
+// by the upper level's action encoder, n = Wa S rows (chunk-major), G = stride + 1 tokens per row for 'seq'.
+struct PoolWs {
+    int Wa = 0, c0 = 0, stride = 0, G = 0;   // chunks scored, first chunk, steps per chunk, tokens per group
+    float * x = nullptr;              // mlp: [n][stride E] concatenated chunk; seq: step-linear outputs [Wa stride S][d]
+    std::vector<float *> xs, qkv, probs, xmid, u;   // seq: per block (xs: block inputs, one more for the output)
+    std::vector<LnStats *> st1, st2;
+    float * h = nullptr, * r = nullptr;             // mlp: fc1 pre-activation / ReLU; seq: LN / ReLU scratch
+    float * z = nullptr, * zg = nullptr, * zl = nullptr;   // seq head: head0 output, GELU, head LN
+    float * ypre = nullptr, * y = nullptr;          // before the output LN / pooled latent actions [n][Au]
+    LnStats * sth = nullptr, * sto = nullptr;
+    float * gy = nullptr;             // cost gradient wrt y
+    float * ga = nullptr, * gb = nullptr, * gc = nullptr;   // backward scratch
+    float * ge = nullptr;             // gradient wrt the embeddings, [R][E] t-major, zero outside the chunks
+    const float ** ptrs = nullptr;
+    float ** gptrs = nullptr;
+    float * goals = nullptr, * weights = nullptr;
+};
+
 struct Workspace {
     int level = 0, S = 0, T = 0;
+    PoolWs pool;
     Arena arena;
     // actions / optimiser
     float * x = nullptr, * m = nullptr, * v = nullptr, * grad = nullptr, * a_all = nullptr, * da_all = nullptr;
@@ -138,6 +179,9 @@ struct HPlanner {
     int forward(Workspace & w, const CostSpec & cs, bool want_grad);
     int backward(Workspace & w, const CostSpec & cs);
     bool cost_tables(Workspace & w, const CostSpec & cs);
+    int pooled_chunks(const CostSpec & cs) const;     // Wa: chunks the action cost compares (0 = no action cost)
+    int pool_forward(Workspace & w, bool want_grad);   // action cost, added to the costs
+    int pool_backward(Workspace & w);                  // its gradient into pool.ge
     int lin_fwd(const DLin & L, const float * x, int ldx, const float * x_hi, const float * x_lo, int M, float * y, int ldy,
                 float * y_hi, float * y_lo, Workspace & w);
     int lin_bwd(const DLin & L, const float * dy, int lddy, const float * dy_hi, const float * dy_lo, int M, float * dx, int lddx,

@@ -120,9 +120,28 @@ bool check_spec(const HPlanner & pm, const CostSpec & cs, const char * fn) {
             fn, cs.n_goal, W, cs.horizon, cs.cost_last_n);
         return false;
     }
-    if (cs.action_cost_weight != 0.0f && cs.goal_action && cs.goal_level == cs.level + 1 && !cs.dense) {
-        log("jepa: %s: the pooled-action cost (action_cost_weight != 0) is not implemented by this engine\n", fn);
-        return false;
+    if (pm.pooled_chunks(cs) > 0) {
+        const DLevel & L = pm.levels[(size_t) cs.level - 1];
+        const DLevel & U = pm.levels[(size_t) cs.level];
+        const DActEnc & ae = U.ae;
+        const int Ein = L.act0 ? L.E : L.A, stride = U.hp.stride;
+        bool complete = false;
+        if (ae.kind == 1) {
+            complete = ae.fc1 && ae.fc2 && ae.fc1.in == stride * Ein && ae.fc2.in == ae.fc1.out && ae.fc2.out == U.A;
+        } else if (ae.kind == 2) {
+            const int d = ae.d;
+            complete = d > 0 && ae.n_head > 0 && d % ae.n_head == 0 && ae.step && ae.step.in == Ein && ae.step.out == d &&
+                       ae.pos && ae.pos_n >= (int64_t) (stride + 1) * d && !ae.blocks.empty() && ae.head0 && ae.head0.in == d &&
+                       ae.head2 && ae.head2.in == ae.head0.out && ae.head2.out == U.A;
+            for (const DSeqBlock & B : ae.blocks)
+                complete = complete && B.qkv.in == d && B.qkv.out == 3 * d && B.out.in == d && B.out.out == d && B.up.in == d &&
+                           B.down.in == B.up.out && B.down.out == d && B.ln1_w && B.ln2_w;
+        }
+        if (!complete) {
+            log("jepa: %s: the action cost needs level %d's action encoder (jepa.hjepa.act_enc_kind mlp | seq with its weights)\n",
+                fn, cs.level + 1);
+            return false;
+        }
     }
     return true;
 }

@@ -125,6 +125,17 @@ void scatter_actions(const float * da, float * grad, int S, int T, int A, cudaSt
 void cost_l2(const float * const * preds, const float * goals, const float * weights, float * const * gpreds,
              int W, int M, int D, int ldp, float * cost, bool want_grad, cudaStream_t st);
 
+// action-cost pooling (pool.cu): chunk rows of the embeddings e [Wa stride S][E] <-> the concatenated
+// 'mlp' input x [Wa S][stride E]; step-linear outputs z [Wa stride S][d] <-> token groups X [Wa S][stride+1][d]
+// (back = the gradient direction: writes e / z); self-attention inside groups of G rows of qkv [rows][3 d]
+void pool_chunks(float * e, float * x, int Wa, int S, int stride, int E, bool back, cudaStream_t st);
+void pool_tokens(float * z, const float * pos, float * X, int Wa, int S, int stride, int d, bool back, cudaStream_t st);
+size_t group_mha_smem(int G, int d, int H, bool backward);
+bool group_mha_prepare(int G, int d, int H);   // false: the group does not fit one CTA's shared memory
+void group_mha_fwd(const float * qkv, float * o, float * probs, int n_groups, int G, int d, int H, cudaStream_t st);
+void group_mha_bwd(const float * go, const float * qkv, const float * probs, float * gqkv, int n_groups, int G, int d, int H,
+                   cudaStream_t st);
+
 // AdamW + optional noise + clamp, then the t-major copy of the updated actions:
 //   x *= 1 - lr*wd ; m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g g ; x -= step_size m / (sqrt(v)/c2s + eps)
 //   x += z * noise_std ; x = min(max(x, lo[a]), hi[a])

@@ -86,6 +86,13 @@ class LevelW:
     ae_fc2: Optional[Lin] = None
     ae_out_w: Optional[np.ndarray] = None
     ae_out_b: Optional[np.ndarray] = None
+    ae_step: Optional[Lin] = None             # 'seq' action encoder (hjepa-plan.cpp:183-200)
+    ae_pos: Optional[np.ndarray] = None
+    ae_blocks: list = field(default_factory=list)
+    ae_head0: Optional[Lin] = None
+    ae_head2: Optional[Lin] = None
+    ae_headln_w: Optional[np.ndarray] = None
+    ae_headln_b: Optional[np.ndarray] = None
     queue: Optional[np.ndarray] = None
 
 
@@ -128,6 +135,17 @@ class Model:
             L.enc_fc1, L.enc_fc2 = self.lin(p + "enc.fc1"), self.lin(p + "enc.fc2")
             L.ae_fc1, L.ae_fc2 = self.lin(p + "act_enc.fc1"), self.lin(p + "act_enc.fc2")
             L.ae_out_w, L.ae_out_b = T.get(p + "act_enc.out_norm.weight"), T.get(p + "act_enc.out_norm.bias")
+            L.ae_step, L.ae_pos = self.lin(p + "act_enc.step"), T.get(p + "act_enc.pos")
+            L.ae_head0, L.ae_head2 = self.lin(p + "act_enc.head.0"), self.lin(p + "act_enc.head.2")
+            L.ae_headln_w, L.ae_headln_b = T.get(p + "act_enc.head.ln.weight"), T.get(p + "act_enc.head.ln.bias")
+            i = 0
+            while T.get(p + f"act_enc.blk.{i}.attn_qkv.weight") is not None:
+                q = p + f"act_enc.blk.{i}."
+                L.ae_blocks.append(dict(qkv=self.lin(q + "attn_qkv"), out=self.lin(q + "attn_out"), up=self.lin(q + "ffn_up"),
+                                        down=self.lin(q + "ffn_down"), ln1_w=T.get(q + "ln1.weight"), ln1_b=T.get(q + "ln1.bias"),
+                                        ln2_w=T.get(q + "ln2.weight"), ln2_b=T.get(q + "ln2.bias")))
+                i += 1
+            hp["act_enc_n_head"] = int(g("act_enc_n_head", [0] * n)[li]) if g("act_enc_n_head") is not None else 0
             L.queue = T.get(p + "act_queue")
             self.levels.append(L)
 
@@ -363,9 +381,11 @@ def batch_cost(m: Model, cs: CostSpec, actions, want_grad=True, want_states=Fals
     s = np.broadcast_to(cs.s0.astype(f32), (n, D)).copy()
     preds = [s]
     tapes, emb_u = [], []
+    embs = []
     for step in range(T):
         e, u = act_embed_fwd(L, np.ascontiguousarray(actions[:, step, :]).astype(f32))
         emb_u.append(u)
+        embs.append(e)
         s, tp = step_fwd(m, L, s, e)
         tapes.append(tp)
         preds.append(s)
@@ -397,8 +417,26 @@ def batch_cost(m: Model, cs: CostSpec, actions, want_grad=True, want_states=Fals
         costs = (costs + w * acc.astype(f32)).astype(f32)
         if want_grad:
             gscored[k] = (f32(2) * w * diff).astype(f32)
+    gemb = [None] * T          # extra gradient of each step's action embedding (the action cost)
     if cs.action_cost_weight != 0.0 and cs.goal_action is not None and cs.goal_level == cs.level + 1 and not cs.dense:
-        raise NotImplementedError("oracle: the action cost is not restated")
+        # the candidates pooled into the upper level's macro-actions against the ones it chose (chunk_cost,
+        # hjepa-plan.cpp:769-791): whole chunks only, the last Wa of them
+        up = m.levels[cs.level]
+        stride = up.hp["stride"]
+        n_pooled = T // stride
+        Wa = min(max(1, cs.cost_last_n), n_pooled, cs.n_goal)
+        w = f32(cs.action_cost_weight)
+        for j in range(Wa):
+            chunk = n_pooled - Wa + j
+            steps = list(range(chunk * stride, (chunk + 1) * stride))
+            y, cache = action_pool_fwd(m, up, [embs[s] for s in steps])
+            g = cs.goal_action[cs.n_goal - Wa + j].astype(f32)
+            diff = (y - g).astype(f32)
+            acc = (diff.astype(np.float64) ** 2).sum(axis=1)
+            costs = (costs + w * acc.astype(f32)).astype(f32)
+            if want_grad:
+                for s_, ge in zip(steps, action_pool_bwd(up, cache, (f32(2) * w * diff).astype(f32))):
+                    gemb[s_] = ge if gemb[s_] is None else (gemb[s_] + ge).astype(f32)
     grad = None
     if want_grad:
         # back through the encoders, top level first
@@ -417,12 +455,116 @@ def batch_cost(m: Model, cs: CostSpec, actions, want_grad=True, want_states=Fals
         gs = gpred[T] if gpred[T] is not None else np.zeros((n, D), f32)
         for step in reversed(range(T)):
             gs_prev, ge = step_bwd(m, L, tapes[step], gs)
+            if gemb[step] is not None:
+                ge = (ge + gemb[step]).astype(f32)
             grad[:, step, :] = act_embed_bwd(L, emb_u[step], ge)
             gs = gs_prev
             if gpred[step] is not None:
                 gs = (gs + gpred[step]).astype(f32)
     states = np.stack(preds, axis=1) if want_states else None
     return costs, grad, states
+
+
+# ---------------------------------------------------------------------------------------------
+# the upper level's action encoder over one chunk of the level's action embeddings
+# (build_action_pool, hjepa-plan.cpp:663-684; op_tokens / op_mha / op_first_of_group :478-619)
+# ---------------------------------------------------------------------------------------------
+def mha_fwd(qkv, G, n_head):
+    """Self-attention inside each group of G rows; qkv [rows][3 d] = [q | k | v] (op_mha, :553-583)."""
+    rows, d3 = qkv.shape
+    d = d3 // 3
+    hd = d // n_head
+    n = rows // G
+    q = qkv[:, :d].reshape(n, G, n_head, hd).transpose(0, 2, 1, 3)
+    k = qkv[:, d:2 * d].reshape(n, G, n_head, hd).transpose(0, 2, 1, 3)
+    v = qkv[:, 2 * d:].reshape(n, G, n_head, hd).transpose(0, 2, 1, 3)
+    scale = f32(1.0) / f32(math.sqrt(hd))
+    s = (np.einsum("nhic,nhjc->nhij", q, k).astype(f32) * scale).astype(f32)
+    e = np.exp((s - s.max(-1, keepdims=True)).astype(f32)).astype(f32)
+    p = (e / e.sum(-1, keepdims=True, dtype=f32)).astype(f32)
+    o = np.einsum("nhij,nhjc->nhic", p, v).astype(f32)
+    return o.transpose(0, 2, 1, 3).reshape(rows, d).astype(f32), (q, k, v, p, scale)
+
+
+def mha_bwd(go, cache, G, n_head):
+    """op_mha's backward (:584-617): gv = p go, gs = p (go.v - sum p go.v) scale, gq = gs k, gk = gs q."""
+    q, k, v, p, scale = cache
+    n, H, _, hd = q.shape
+    gon = go.reshape(n, G, H, hd).transpose(0, 2, 1, 3)
+    gp = np.einsum("nhic,nhjc->nhij", gon, v).astype(f32)
+    gv = np.einsum("nhij,nhic->nhjc", p, gon).astype(f32)
+    dotp = (gp * p).sum(-1, keepdims=True, dtype=f32)
+    gs = (p * (gp - dotp) * scale).astype(f32)
+    gq = np.einsum("nhij,nhjc->nhic", gs, k).astype(f32)
+    gk = np.einsum("nhij,nhic->nhjc", gs, q).astype(f32)
+    back = lambda x: x.transpose(0, 2, 1, 3).reshape(n * G, H * hd)
+    return np.concatenate([back(gq), back(gk), back(gv)], axis=1).astype(f32)
+
+
+def action_pool_fwd(m: Model, up: LevelW, chunk):
+    """chunk: the level's action embeddings of `stride` consecutive steps, each [n][E] -> [n][A_up]."""
+    n = chunk[0].shape[0]
+    if up.hp["act_enc_kind"] == "mlp":
+        x = np.concatenate(chunk, axis=1).astype(f32)
+        h = up.ae_fc1(x)
+        r = act_fwd(h, "relu")
+        y = up.ae_fc2(r)
+        c_out = None
+        if up.ae_out_w is not None:
+            y, c_out = ln_fwd(y, up.ae_out_w, up.ae_out_b, m.ln_eps)
+        return y, ("mlp", h, c_out)
+    steps = [up.ae_step(e) for e in chunk]
+    L, d = len(steps), steps[0].shape[1]
+    G = L + 1
+    x = np.zeros((n, G, d), f32)
+    x[:, 0, :] = up.ae_pos[0]
+    for l in range(L):
+        x[:, l + 1, :] = (steps[l] + up.ae_pos[l + 1]).astype(f32)
+    x = x.reshape(n * G, d)
+    bc = []
+    for B in up.ae_blocks:
+        h, c1 = ln_fwd(x, B["ln1_w"], B["ln1_b"], m.ln_eps)
+        qkv = B["qkv"](h)
+        o, cm = mha_fwd(qkv, G, up.hp["act_enc_n_head"])
+        x = (x + B["out"](o)).astype(f32)
+        h2, c2 = ln_fwd(x, B["ln2_w"], B["ln2_b"], m.ln_eps)
+        u = B["up"](h2)
+        x = (x + B["down"](act_fwd(u, "relu"))).astype(f32)
+        bc.append((c1, cm, c2, u))
+    y0 = x.reshape(n, G, d)[:, 0, :].copy()
+    z = up.ae_head0(y0)
+    zg = act_fwd(z, "gelu")
+    zl, ch = ln_fwd(zg, up.ae_headln_w, up.ae_headln_b, m.ln_eps)
+    y2 = up.ae_head2(zl)
+    y, co = ln_fwd(y2, up.ae_out_w, up.ae_out_b, 1e-6)
+    return y, ("seq", G, d, bc, z, ch, co)
+
+
+def action_pool_bwd(up: LevelW, cache, gy):
+    """Gradient of the pooled action with respect to each embedding of the chunk: list of [n][E]."""
+    if cache[0] == "mlp":
+        _, h, c_out = cache
+        if c_out is not None:
+            gy = ln_bwd(gy, c_out, up.ae_out_w)
+        gx = up.ae_fc1.back(act_bwd(up.ae_fc2.back(gy), h, "relu"))
+        E = gx.shape[1] // up.hp["stride"]
+        return [np.ascontiguousarray(gx[:, i * E:(i + 1) * E]) for i in range(up.hp["stride"])]
+    _, G, d, bc, z, ch, co = cache
+    g = ln_bwd(gy, co, up.ae_out_w)
+    g = up.ae_head2.back(g)
+    g = ln_bwd(g, ch, up.ae_headln_w)
+    g = up.ae_head0.back(act_bwd(g, z, "gelu"))
+    n = g.shape[0]
+    gx = np.zeros((n, G, d), f32)
+    gx[:, 0, :] = g
+    gx = gx.reshape(n * G, d)
+    for B, (c1, cm, c2, u) in zip(reversed(up.ae_blocks), reversed(bc)):
+        gu = act_bwd(B["down"].back(gx), u, "relu")
+        gx = (gx + ln_bwd(B["up"].back(gu), c2, B["ln2_w"])).astype(f32)
+        gq = mha_bwd(B["out"].back(gx), cm, G, up.hp["act_enc_n_head"])
+        gx = (gx + ln_bwd(B["qkv"].back(gq), c1, B["ln1_w"])).astype(f32)
+    gx = gx.reshape(n, G, d)
+    return [up.ae_step.back(np.ascontiguousarray(gx[:, l + 1, :])) for l in range(G - 1)]
 
 
 # ---------------------------------------------------------------------------------------------

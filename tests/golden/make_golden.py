@@ -11,6 +11,9 @@ sha256 against the one recorded here. Cases:
   solve.*  jepa_hjepa_solve on recorded normal draws, with early stopping / action noise / clamping
   plan.*   jepa_hjepa_plan over the 2-level hierarchy
   horizons jepa_hjepa_horizons over an episode
+  acost*   jepa_hjepa_plan_cost with the action cost (the candidates' actions pooled by the upper level's
+           action encoder, 'mlp' and 'seq', against the upper level's actions; action_cost_weight != 0)
+  aplan    jepa_hjepa_plan over the hierarchy with the action cost on the lower level
 """
 from __future__ import annotations
 
@@ -41,7 +44,11 @@ def model_specs():
     P1 = synth.Level(96, 3, 3, 192, 2)
     P2 = synth.Level(96, 2, 3, 192, 6, stride=4, enc_kind="latent_mlp", enc_hidden=96, act_enc_kind="mlp")
     plain = synth.HJepaSpec(levels=[P1, P2], ftype="q8_0", rand_all=True, cond_std=0.3, w_std=0.1, name="golden-q8")
-    return {"rich": (rich, 11), "q8": (plain, 12)}
+    S1 = synth.Level(48, 2, 2, 96, 2, act_embed_hidden=16, act_embed_dim=8)
+    S2 = synth.Level(48, 2, 2, 96, 4, stride=3, enc_kind="latent_mlp", enc_hidden=32, act_enc_kind="seq", act_enc_dim=32,
+                     act_enc_n_layer=2, act_enc_n_head=2)
+    seq = synth.HJepaSpec(levels=[S1, S2], ftype="f32", rand_all=True, cond_std=0.3, w_std=0.1, name="golden-seq")
+    return {"rich": (rich, 11), "q8": (plain, 12), "seq": (seq, 13)}
 
 
 def build_model(name: str, workdir: str) -> tuple[str, str]:
@@ -153,6 +160,57 @@ def main() -> None:
             out[f"{key}.schedule"] = np.array(sched, np.int64)
             meta["cases"].append({"key": key, "kind": "horizons", "model": name, "interval": 2, "budget": 24,
                                   "horizons": [5, 3]})
+            P.close()
+        # ---- the action cost: a separate stream of draws so the cases above stay as they were
+        rng2 = np.random.default_rng(77)
+        for name in ("rich", "seq"):
+            path, digest = build_model(name, tmp)
+            meta["models"][name] = digest
+            P = ref.RefPlanner(path, n_threads=4)
+            spec, _ = model_specs()[name]
+            D = [l.embed_dim for l in spec.levels]
+            A = [l.action_dim for l in spec.levels]
+            stride = spec.levels[1].stride
+            for ci, (T, ng, ncl) in enumerate([(2 * stride, 1, 1), (3 * stride + 1, 2, 2), (2 * stride + 1, 1, 2)]):
+                key = f"{name}.acost{ci}"
+                S = 7
+                s0 = rng2.normal(size=D[0]).astype(np.float32)
+                goal = rng2.normal(size=(ng, D[1])).astype(np.float32)
+                goal_action = rng2.normal(0, 0.5, size=(ng, A[1])).astype(np.float32)
+                acts = rng2.uniform(-1.5, 1.5, (S, T, A[0])).astype(np.float32)
+                lp = plan_row(cost_last_n=ncl, action_cost_weight=0.7)
+                g = capi.Goal(capi.fptr(goal), ng, 2, 0, capi.fptr(goal_action))
+                costs = np.zeros(S, np.float32)
+                grad = np.zeros_like(acts)
+                rc = lib.jepa_hjepa_plan_cost(P.ctx, 1, capi.fptr(s0), C.byref(g), C.byref(capi.LevelPlan.of(**lp)),
+                                              capi.fptr(acts), S, T, capi.fptr(costs), capi.fptr(grad))
+                assert rc == 0, key
+                for k, v in (("s0", s0), ("goal", goal), ("goal_action", goal_action), ("actions", acts), ("costs", costs),
+                             ("grad", grad)):
+                    out[f"{key}.{k}"] = v
+                meta["cases"].append({"key": key, "kind": "cost", "model": name, "level": 1, "goal_level": 2,
+                                      "horizon": T, "dense": 0, "n_goal": ng, "plan": lp, "goal_action": True})
+            key = f"{name}.aplan"
+            T1 = 2 * stride
+            p1 = plan_row(horizon=T1, cost_last_n=2, n_steps=6, early_stop_patience=0, action_cost_weight=0.5)
+            p2 = plan_row(horizon=3, num_subgoals=2, n_steps=6, early_stop_patience=0)
+            states = [rng2.normal(size=d).astype(np.float32) for d in D]
+            goals = [rng2.normal(size=d).astype(np.float32) for d in D]
+            draws = rng2.normal(size=20000).astype(np.float32)
+            rp = capi.Replay(draws)
+            SP = (capi.FP * 2)(capi.fptr(states[0]), capi.fptr(states[1]))
+            GP = (capi.FP * 2)(capi.fptr(goals[0]), capi.fptr(goals[1]))
+            lps = (capi.LevelPlan * 2)(capi.LevelPlan.of(**p1), capi.LevelPlan.of(**p2))
+            act = np.zeros((T1, A[0]), np.float32)
+            info = capi.PlanInfo()
+            rc = lib.jepa_hjepa_plan(P.ctx, SP, GP, lps, 2, rp.fn, None, capi.fptr(act), C.byref(info))
+            assert rc == 0, key
+            for k, v in (("state1", states[0]), ("state2", states[1]), ("goal1", goals[0]), ("goal2", goals[1]),
+                         ("draws", draws[:rp.pos]), ("actions", act), ("cost", np.array(list(info.cost)[:2], np.float32)),
+                         ("iters", np.array(list(info.iters)[:2], np.int64)),
+                         ("planned", np.array(list(info.planned)[:2], np.int64))):
+                out[f"{key}.{k}"] = v
+            meta["cases"].append({"key": key, "kind": "plan", "model": name, "plans": [p1, p2]})
             P.close()
     out["meta"] = np.frombuffer(json.dumps(meta).encode(), np.uint8)
     np.savez_compressed(OUT, **out)

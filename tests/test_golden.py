@@ -1,7 +1,9 @@
 """Parity pins against the reference's own planner.
 
 tests/golden/hjepa_ref.npz holds outputs of the reference's src/hjepa-plan.cpp (built unmodified against
-the ggml shim, oracle/_ref) on seeded forged models; tests/golden/make_golden.py wrote it.
+the ggml shim, oracle/_ref) on seeded forged models; tests/golden/make_golden.py wrote it. The cases include
+the action cost (candidates pooled by the upper level's 'mlp' and 'seq' action encoders, action_cost_weight
+!= 0) on its own and inside the hierarchy.
 
 CPU (always): the oracle restatement reproduces every case; the engine's host-side horizon schedule
 (jepa_hjepa_horizons) matches exactly; the models rebuild byte for byte (sha256).
@@ -61,7 +63,9 @@ def test_oracle_cost_matches_reference(models, case):
     k = case["key"]
     cs = O.CostSpec(level=case["level"], horizon=case["horizon"], s0=g(k, "s0"), goal=g(k, "goal"), n_goal=case["n_goal"],
                     goal_level=case["goal_level"], dense=bool(case["dense"]), cost_last_n=case["plan"]["cost_last_n"],
-                    intermediate_cost_weight=case["plan"]["intermediate_cost_weight"])
+                    intermediate_cost_weight=case["plan"]["intermediate_cost_weight"],
+                    goal_action=g(k, "goal_action") if case.get("goal_action") else None,
+                    action_cost_weight=case["plan"]["action_cost_weight"])
     costs, grad, _ = O.batch_cost(m, cs, g(k, "actions"))
     assert rel(costs, g(k, "costs")) < 1e-5
     assert rel(grad, g(k, "grad")) < 1e-4
@@ -123,7 +127,8 @@ def test_gpu_cost_matches_reference(models, case):
     P = Planner(models[case["model"]])
     k = case["key"]
     costs, grad = P.plan_cost(case["level"], g(k, "s0"), g(k, "goal"), g(k, "actions"), goal_level=case["goal_level"],
-                              dense=case["dense"], plan=case["plan"])
+                              dense=case["dense"], plan=case["plan"],
+                              goal_actions=g(k, "goal_action") if case.get("goal_action") else None)
     assert rel(costs, g(k, "costs")) < 1e-3
     assert rel(grad, g(k, "grad")) < 1e-3
 
