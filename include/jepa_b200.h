@@ -62,6 +62,13 @@ int jepa_b200_context_set_shard(jepa_context * ctx, int rank, int world, const v
 double jepa_b200_last_plan_ms(const jepa_context * ctx);
 long long jepa_b200_last_plan_launches(const jepa_context * ctx);
 
+// Candidate streams of the H-JEPA solves on this context: a level's candidates (this GPU's share) run as
+// n independent chains of consecutive rows side by side on the GPU (1..8; 0 = automatic: 2 from 256
+// candidates up, else 1). Results do not depend on n (rows never interact), as the reference's results do
+// not depend on its thread count (its jepa_context_params.n_threads). Returns 0, or -1 for a non-H-JEPA
+// context or n out of range.
+int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n);
+
 // C[M,N] = f16(A)[M,K] * f16(B)[N,K]^T with f32 accumulation through the V-JEPA 2-AC predictor's
 // tcgen05 kind::f16 GEMM (host f32 buffers, rounded to f16 on the device; K a multiple of 8). A kernel
 // check: every linear of the AC predictor runs through this kernel.

@@ -93,15 +93,23 @@ __device__ __forceinline__ float4 f4_sub(float4 a, float4 b) { return make_float
 __device__ __forceinline__ float4 ld4(const float * p) { return *(const float4 *) p; }
 __device__ __forceinline__ void st4(float * p, float4 v) { *(float4 *) p = v; }
 
-// four consecutive columns of the fused epilogue: vector loads / stores when the operands allow it
-// (ep.vec: every pointer 16-byte aligned, every leading dimension a multiple of 4), else element-wise
-__device__ __forceinline__ void apply_epi4(const GemmEpi & ep, int row, int col, int N, float4 v) {
-    if (!ep.vec || col + 3 >= N) {
-        const float e[4] = {v.x, v.y, v.z, v.w};
-        for (int j = 0; j < 4; j++) if (col + j < N) apply_epi(ep, row, col + j, e[j]);
-        return;
-    }
-    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) v = f4_add(v, ld4(ep.bias + col));
+// The operands a vector epilogue reads (bias, aux, gate), loaded ahead of the values they combine with.
+struct Epi4In {
+    float4 bias, aux, gate;
+};
+
+__device__ __forceinline__ Epi4In epi_load4(const GemmEpi & ep, int row, int col) {
+    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    Epi4In in{z, z, z};
+    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) in.bias = ld4(ep.bias + col);
+    if (ep.mode == EPI_GATED || ep.mode == EPI_DGELU_SPLIT) in.aux = ld4(ep.aux + (size_t) row * ep.ld_aux + col);
+    if (ep.mode == EPI_GATED) in.gate = ld4(ep.gate + (size_t) row * ep.ld_gate + col);
+    return in;
+}
+
+// four consecutive columns of the fused epilogue, vector path (ep.vec and col + 3 < N)
+__device__ __forceinline__ void epi_store4(const GemmEpi & ep, int row, int col, float4 v, const Epi4In & in) {
+    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) v = f4_add(v, in.bias);
     switch (ep.mode) {
         case EPI_F32: st4(ep.out0 + (size_t) row * ep.ld0 + col, v); break;
         case EPI_SPLIT: {
@@ -124,11 +132,10 @@ __device__ __forceinline__ void apply_epi4(const GemmEpi & ep, int row, int col,
         } break;
         case EPI_GATED: {
             st4(ep.out0 + (size_t) row * ep.ld0 + col, v);
-            const float4 g = ld4(ep.gate + (size_t) row * ep.ld_gate + col);
-            st4(ep.out1 + (size_t) row * ep.ld1 + col, f4_add(ld4(ep.aux + (size_t) row * ep.ld_aux + col), f4_mul(v, g)));
+            st4(ep.out1 + (size_t) row * ep.ld1 + col, f4_add(in.aux, f4_mul(v, in.gate)));
         } break;
         case EPI_DGELU_SPLIT: {
-            const float4 u = ld4(ep.aux + (size_t) row * ep.ld_aux + col);
+            const float4 u = in.aux;
             const float4 d = f4_mul(v, make_float4(gelu_grad(u.x), gelu_grad(u.y), gelu_grad(u.z), gelu_grad(u.w)));
             const float4 h = f4_hi(d);
             st4(ep.out_hi + (size_t) row * ep.ld_split + col, h);
@@ -138,22 +145,25 @@ __device__ __forceinline__ void apply_epi4(const GemmEpi & ep, int row, int col,
     }
 }
 
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+// four consecutive columns of the fused epilogue: vector loads / stores when the operands allow it
+// (ep.vec: every pointer 16-byte aligned, every leading dimension a multiple of 4), else element-wise
+__device__ __forceinline__ void apply_epi4(const GemmEpi & ep, int row, int col, int N, float4 v) {
+    if (!ep.vec || col + 3 >= N) {
+        const float e[4] = {v.x, v.y, v.z, v.w};
+        for (int j = 0; j < 4; j++) if (col + j < N) apply_epi(ep, row, col + j, e[j]);
+        return;
+    }
+    epi_store4(ep, row, col, v, epi_load4(ep, row, col));
 }
+
+__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
-}
-
-__device__ __forceinline__ float ld_peer(uint32_t local_saddr, uint32_t rank) {
-    uint32_t remote;
-    float v;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_saddr), "r"(rank));
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
 }
 
 __device__ __forceinline__ float4 ld_peer4(uint32_t local_saddr, uint32_t rank) {
@@ -164,11 +174,34 @@ __device__ __forceinline__ float4 ld_peer4(uint32_t local_saddr, uint32_t rank) 
     return v;
 }
 
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local_saddr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_saddr), "r"(rank));
+    return remote;
+}
+
+// A bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory into a peer CTA's, completing on
+// the peer's mbarrier (transaction bytes). One thread issues it; the copy engine moves the data.
+__device__ __forceinline__ void bulk_to_peer(uint32_t remote_dst, uint32_t local_src, uint32_t bytes, uint32_t remote_bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(remote_dst), "r"(local_src), "r"(bytes), "r"(remote_bar) : "memory");
+}
+
+// Rows of the tile each CTA of a split-K cluster reduces and stores.
+__host__ __device__ constexpr int split_rows(int splits) { return (BM + splits - 1) / splits; }
+
 // One 128 x BN tile of C per CTA, or -- split-K -- one K-slice of it per CTA of a (1, 1, splits) cluster.
-// Epilogue (both cases): the tile's partial sum goes TMEM -> registers -> a padded shared-memory tile; with
-// splits > 1 a cluster barrier follows and each CTA reduces its 128 / splits rows over every peer's tile
-// through distributed shared memory, in rank order (a fixed order: the result does not depend on timing),
-// then applies the fused epilogue with row-contiguous (coalesced) stores.
+//
+// splits == 1: the epilogue warps go from TMEM straight to the fused epilogue, a row per thread.
+// splits > 1 (a reduce-scatter over distributed shared memory): CTA p of the cluster owns rows
+// [p R, p R + R) of the tile (R = ceil(128 / splits)). After the mainloop the epilogue warps stage the
+// partial tile in shared memory and one thread sends each peer its rows with one bulk copy into the peer's
+// receive buffer (completing on the peer's mbarrier); the owner waits for its bytes, sums the splits in rank
+// order (a fixed order: the bits do not depend on timing) from its own shared memory and applies the fused
+// epilogue with all six warps. The epilogue's operands (bias, residual, gate) are loaded right after the dependency wait, so
+// their latency hides behind the mainloop. Cluster barriers: one arrive at the start (the receive
+// barriers are initialised) waited on before the first push, one after the receive completes waited on
+// before exit (no CTA leaves while a push to or from it may be in flight).
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
@@ -177,21 +210,24 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     constexpr uint32_t A_BYTES = BM * BK * 4;
     constexpr uint32_t B_BYTES = BN * BK * 4;
     constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    constexpr int PLD = BN + 4;            // padded row of the staged partial tile (conflict-free float4 row writes)
     // two accumulators: hi*hi in columns [0, BN), the small cross terms hi*lo + lo*hi in [BN, 2 BN).
     // The tensor core's float32 accumulation rounds toward zero per instruction; keeping the small terms
     // apart cuts the number of truncations the large partial sum sees by three.
     constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
     // instruction descriptor: D f32 (bit 4), A/B tf32 (2 << 7, 2 << 10), K-major both, N >> 3, M >> 4
     constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
-    static_assert((size_t) BM * PLD * 4 <= (size_t) STAGES * STAGE_BYTES, "staged tile must fit in the pipeline buffers");
+    constexpr int C4 = BN / 4, NT = 192, PER = 2;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
-    float * tile = (float *) smem;          // reused after the mainloop: [BM][PLD] partial sums
+    constexpr int PLD = BN + 4;            // padded row of the staged partial tile (conflict-free float4 row writes)
+    float * tile = (float *) smem;         // split-K: this CTA's partial tile [BM][PLD], in the idle pipeline buffers
+    float * recv = (float *) (smem + (size_t) STAGES * STAGE_BYTES);   // split-K: the peers' partials [splits][R][PLD]
+    static_assert((size_t) BM * PLD * 4 <= (size_t) STAGES * STAGE_BYTES, "staged tile must fit in the pipeline buffers");
     __shared__ __align__(8) uint64_t full_bar[STAGES];
     __shared__ __align__(8) uint64_t empty_bar[STAGES];
     __shared__ __align__(8) uint64_t acc_bar;
+    __shared__ __align__(8) uint64_t recv_bar;
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
 
@@ -202,13 +238,18 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     const int kt_per = (num_k + splits - 1) / splits;
     const int kt0 = split * kt_per, kt1 = min(num_k, kt0 + kt_per);
     const int nkt = kt1 > kt0 ? kt1 - kt0 : 0;
+    const int R = split_rows(splits);
+    const int rs = split * R, re = min(BM, rs + R);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
         mbar_init(&acc_bar, 1);
+        mbar_init(&recv_bar, 1);
         abort_sh = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        // the partial rows the peers push here: (splits - 1) x this CTA's rows x BN floats
+        if (splits > 1) mbar_expect_tx(&recv_bar, (uint32_t) ((splits - 1) * max(0, re - rs) * PLD * 4));
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -224,11 +265,27 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (splits > 1) cluster_arrive_release();   // the receive barriers are initialised
     const uint32_t tmem = tmem_base_sh;
     // the setup above overlapped the previous kernel (programmatic dependent launch); its outputs are
     // read from here on
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    // split-K: the first round of this thread's epilogue items, and their operands, loaded now
+    const int n_items = splits > 1 && re > rs ? (re - rs) * C4 : 0;
+    const int rounds = (n_items + NT * PER - 1) / (NT * PER);
+    Epi4In in[PER];
+    auto prefetch = [&](int rd) {
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int idx = rd * NT * PER + j * NT + (int) threadIdx.x;
+            if (idx >= n_items) continue;
+            const int row = m0 + rs + idx / C4, col = n0 + (idx % C4) * 4;
+            if (row < M && ep.vec && col + 3 < N) in[j] = epi_load4(ep, row, col);
+        }
+    };
+    if (rounds > 0) prefetch(0);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -254,6 +311,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 }
             }
         }
+        __syncwarp();
+        if (splits > 1) cluster_wait();
     } else if (warp == 1) {
         if (lane == 0) {
             for (int i = 0; i < nkt; i++) {
@@ -276,6 +335,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
             }
             mma_commit(&acc_bar);   // also on abort / with no K-slice: completes once the issued MMAs are done
         }
+        __syncwarp();
+        if (splits > 1) cluster_wait();
     } else {
         // epilogue warps 2..5 (TMEM lane quadrant = warp % 4)
         const int q = warp & 3;
@@ -313,39 +374,60 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 }
             }
         }
-    }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    if (splits > 1) {
-        cluster_sync_all();
-        // each CTA reduces its rows over every K-slice of the cluster: all peer loads first, then the
-        // sum in rank order (a fixed order), then the fused epilogue, four columns per thread
-        if (warp >= 2 && !*(volatile int *) &abort_sh) {
-            const int rows_per = (BM + splits - 1) / splits;
-            const int rs = split * rows_per, re = min(BM, rs + rows_per);
-            const int t = threadIdx.x - 64;
-            const uint32_t tile_s = smem_u32(tile);
-            constexpr int C4 = BN / 4;
-            for (int idx = t; idx < (re - rs) * C4; idx += 128) {
-                const int rr = rs + idx / C4, cc = (idx % C4) * 4;
-                const uint32_t off = tile_s + (uint32_t) (rr * PLD + cc) * 4;
-                float4 part[8];
-#pragma unroll
-                for (int p = 0; p < 8; p++) if (p < splits) part[p] = ld_peer4(off, (uint32_t) p);
-                float4 v = part[0];
-#pragma unroll
-                for (int p = 1; p < 8; p++) {
-                    if (p < splits) { v.x = v.x + part[p].x; v.y = v.y + part[p].y; v.z = v.z + part[p].z; v.w = v.w + part[p].w; }
+        if (splits > 1) {
+            // the staged rows of peer p go to it in one bulk copy: [p R, p R + R) x PLD floats, contiguous
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            cluster_wait();   // every peer's receive barrier is initialised
+            if (threadIdx.x == 64) {
+                for (int p = 0; p < splits; p++) {
+                    const int prs = p * R, pre = min(BM, prs + R);
+                    if (p == split || pre <= prs) continue;
+                    const uint32_t dst = peer_addr(smem_u32(recv + (size_t) split * R * PLD), (uint32_t) p);
+                    bulk_to_peer(dst, smem_u32(tile + (size_t) prs * PLD), (uint32_t) ((pre - prs) * PLD * 4),
+                                 peer_addr(smem_u32(&recv_bar), (uint32_t) p));
                 }
-                const int row = m0 + rr;
-                if (row < M) apply_epi4(ep, row, n0 + cc, N, v);
             }
         }
-        cluster_sync_all();   // peers read this CTA's tile until here
-    } else {
-        __syncthreads();
     }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();   // the accumulator has been read (and this CTA's own partial rows are staged)
     if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+    if (splits > 1) {
+        const bool got = mbar_wait(&recv_bar, 0, 4, &g_gemm_error);   // the peers' partial rows have landed
+        cluster_arrive_relaxed();
+        if (got && !*(volatile int *) &abort_sh) {
+            for (int rd = 0; rd < rounds; rd++) {
+                if (rd > 0) prefetch(rd);
+#pragma unroll
+                for (int j = 0; j < PER; j++) {
+                    const int idx = rd * NT * PER + j * NT + (int) threadIdx.x;
+                    if (idx >= n_items) continue;
+                    const int i = idx / C4, cc = (idx % C4) * 4;
+                    const int row = m0 + rs + i, col = n0 + cc;
+                    // split p's partial: this CTA's own from the staged tile, the others from the receive buffer
+                    auto part = [&](int p) -> float4 {
+                        return p == split ? *(const float4 *) &tile[(size_t) (rs + i) * PLD + cc]
+                                          : *(const float4 *) &recv[((size_t) p * R + i) * PLD + cc];
+                    };
+                    float4 v = part(0);
+#pragma unroll
+                    for (int p = 1; p < 8; p++) {
+                        if (p < splits) {
+                            const float4 w = part(p);
+                            v.x = v.x + w.x; v.y = v.y + w.y; v.z = v.z + w.z; v.w = v.w + w.w;
+                        }
+                    }
+                    if (row >= M) continue;
+                    if (ep.vec && col + 3 < N) epi_store4(ep, row, col, v, in[j]);
+                    else apply_epi4(ep, row, col, N, v);
+                }
+            }
+        }
+        cluster_wait();   // every CTA has received everything: no push to or from this CTA is in flight
     }
 }
 
@@ -381,13 +463,15 @@ bool make_map(CUtensorMap * map, const float * base, int rows, int cols, int ld,
 
 template <int BN, int STAGES>
 int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
+    if (BN != 64 && splits > 1) { log("jepa: gemm: split-K needs the 64-wide tile\n"); return -1; }
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
     if (!make_map(&ta_hi, A.hi, M, K, A.ld, BM) || !make_map(&ta_lo, A.lo, M, K, A.ld, BM) ||
         !make_map(&tb_hi, B.hi, N, K, B.ld, BN) || !make_map(&tb_lo, B.lo, N, K, B.ld, BN)) {
         log("jepa: gemm: cuTensorMapEncodeTiled refused an operand (M %d N %d K %d, ld %d / %d)\n", M, N, K, A.ld, B.ld);
         return -1;
     }
-    constexpr size_t smem = (size_t) STAGES * (2 * BM * BK * 4 + 2 * BN * BK * 4) + 1024;
+    // pipeline stages, the split-K receive buffer (at most splits x ceil(128 / splits) <= 135 rows) and alignment
+    constexpr size_t smem = (size_t) STAGES * (2 * BM * BK * 4 + 2 * BN * BK * 4) + (BN == 64 ? (size_t) (BM + 7) * (BN + 4) * 4 : 0) + 1024;
     static bool attr_set = false;
     if (!attr_set) {
         JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem));
@@ -428,7 +512,7 @@ bool vec_ok(const GemmEpi & ep, int N) {
 
 // Tile / split choice: wide outputs (the time-batched adaLN modulation) take 128-wide tiles, one CTA
 // per tile; the per-step products take 64-wide tiles and split K over a cluster of up to 8 CTAs, so
-// that about one CTA per SM streams a K-slice instead of a dozen CTAs streaming everything.
+// that at most one CTA per SM (a single wave) streams a K-slice instead of a dozen CTAs streaming everything.
 int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     if (!load_encode()) {
@@ -446,14 +530,14 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
     // bits) is then the same whatever batch of rows it is computed in.
     if (N >= 4096) return launch<128, 3>(A, B, M, N, K, 1, e, st);
     const int num_k = (K + BK - 1) / BK;
-    long s = (148 + 2L * ((N + 63) / 64) - 1) / (2L * ((N + 63) / 64));   // about one CTA per SM at 256 rows
+    long s = 148 / (2L * ((N + 63) / 64));   // at most one CTA per SM (one wave) at 256 rows
     if (s > 8) s = 8;
     if (s > num_k) s = num_k;
     if (s < 1) s = 1;
     int splits = (int) s;
     const int kt_per = (num_k + splits - 1) / splits;
     splits = (num_k + kt_per - 1) / kt_per;   // no empty K-slices
-    return launch<64, 4>(A, B, M, N, K, splits, e, st);
+    return launch<64, 3>(A, B, M, N, K, splits, e, st);
 }
 
 int gemm_error_flag(cudaStream_t st) {

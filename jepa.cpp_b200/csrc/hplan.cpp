@@ -130,6 +130,27 @@ struct Uploader {
 HPlanner::~HPlanner() {
     ws.clear();
     for (void * p : allocations) cudaFree(p);
+    for (cudaStream_t s : side) cudaStreamDestroy(s);
+    for (cudaEvent_t e : ev) cudaEventDestroy(e);
+}
+
+int HPlanner::streams_for(int S) const {
+    const int n = n_streams > 0 ? n_streams : (S >= 256 ? 2 : 1);
+    return std::max(1, std::min({n, S, 8}));
+}
+
+bool HPlanner::ensure_streams(int n) {
+    while ((int) side.size() < n - 1) {
+        cudaStream_t s;
+        JB_CUDA_B(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        side.push_back(s);
+    }
+    while ((int) ev.size() < 2 * n) {
+        cudaEvent_t e;
+        JB_CUDA_B(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        ev.push_back(e);
+    }
+    return true;
 }
 
 Workspace::~Workspace() {
@@ -238,19 +259,23 @@ bool HPlanner::build(const jepa_model & m) {
 // ---------------------------------------------------------------------------------------------
 // workspace
 // ---------------------------------------------------------------------------------------------
-Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs) {
+Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, int chunk) {
     const int Wa = pooled_chunks(cs);
     const std::string key = std::to_string(S) + "/" + std::to_string(T) + "/" + std::to_string(cs.goal_level) + "/" +
                             std::to_string(cs.dense) + "/" + std::to_string(cs.n_goal) + "/" + std::to_string(cs.cost_last_n) +
                             "/" + std::to_string(Wa);
-    auto it = ws.find(level);
+    const int slot = level * 16 + chunk;
+    if (chunk > 0 && !ensure_streams(chunk + 1)) return nullptr;
+    auto it = ws.find(slot);
     if (it != ws.end() && it->second->graph_key == key) return it->second.get();
-    ws.erase(level);
+    ws.erase(slot);
     const DLevel & L = levels[(size_t) level - 1];
     const int D = L.D, P = L.P, F = L.F, I = L.I, NL = L.L, A = L.A;
     const size_t R = (size_t) T * S, ldm = (size_t) 6 * P * NL;
     auto w = std::make_unique<Workspace>();
     w->level = level; w->S = S; w->T = T; w->graph_key = key;
+    w->gen = ++ws_gen;
+    w->st = chunk == 0 ? ctx->stream : side[(size_t) chunk - 1];
     // encoder chain plan (goal above the planned level)
     std::vector<int> list;
     for (int t = 0; t <= T; t++) list.push_back(t);
@@ -414,7 +439,7 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs) {
     }
     if (!w->pred_ptrs || !w->best_idx) { log("jepa: hjepa planner: workspace carve failed\n"); return nullptr; }
     Workspace * raw = w.get();
-    ws[level] = std::move(w);
+    ws[slot] = std::move(w);
     return raw;
 }
 
@@ -423,7 +448,7 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs) {
 // ---------------------------------------------------------------------------------------------
 int HPlanner::lin_fwd(const DLin & L, const float * x, int ldx, const float * x_hi, const float * x_lo, int M, float * y, int ldy,
                       float * y_hi, float * y_lo, Workspace & w) {
-    cudaStream_t st = ctx->stream;
+    cudaStream_t st = w.st;
     if (L.tc_fwd()) {
         int ld = ldx;
         if (!x_hi) {
@@ -447,7 +472,7 @@ int HPlanner::lin_fwd(const DLin & L, const float * x, int ldx, const float * x_
 
 int HPlanner::lin_bwd(const DLin & L, const float * dy, int lddy, const float * dy_hi, const float * dy_lo, int M, float * dx,
                       int lddx, Workspace & w) {
-    cudaStream_t st = ctx->stream;
+    cudaStream_t st = w.st;
     if (L.tc_bwd()) {
         int ld = lddy;
         if (!dy_hi) {
@@ -469,7 +494,7 @@ int HPlanner::lin_bwd(const DLin & L, const float * dy, int lddy, const float * 
 // forward: conditioning, adaLN modulation, rollout, cost
 // ---------------------------------------------------------------------------------------------
 int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
-    cudaStream_t st = ctx->stream;
+    cudaStream_t st = w.st;
     const DLevel & L = levels[(size_t) w.level - 1];
     const int S = w.S, T = w.T, D = L.D, P = L.P, F = L.F, I = L.I, NL = L.L, A = L.A;
     const int R = S * T, ldm = 6 * P * NL;
@@ -671,7 +696,7 @@ bool HPlanner::cost_tables(Workspace & w, const CostSpec & cs) {
 // ---------------------------------------------------------------------------------------------
 int HPlanner::backward(Workspace & w, const CostSpec & cs) {
     (void) cs;
-    cudaStream_t st = ctx->stream;
+    cudaStream_t st = w.st;
     const DLevel & L = levels[(size_t) w.level - 1];
     const int S = w.S, T = w.T, D = L.D, P = L.P, F = L.F, I = L.I, NL = L.L, A = L.A;
     const int R = S * T, ldm = 6 * P * NL;

@@ -102,6 +102,8 @@ struct PoolWs {
 
 struct Workspace {
     int level = 0, S = 0, T = 0;
+    long long gen = 0;                // creation number (keys the graphs that span several workspaces)
+    cudaStream_t st = nullptr;        // the stream its kernels are launched on
     PoolWs pool;
     Arena arena;
     // actions / optimiser
@@ -135,7 +137,7 @@ struct Workspace {
     std::vector<EncStage> enc;
     // captured graphs
     cudaGraphExec_t g_iter = nullptr, g_fwd = nullptr;
-    std::string graph_key, iter_key;
+    std::string graph_key, iter_key, fwd_key;
     long long iter_nodes = 0, fwd_nodes = 0;
     ~Workspace();
 };
@@ -165,12 +167,21 @@ struct HPlanner {
     float ln_eps = 1e-5f, adaln_eps = 1e-6f;
     std::vector<DLevel> levels;
     std::vector<void *> allocations;
-    std::map<int, std::unique_ptr<Workspace>> ws;   // one workspace per level
-    long long launches = 0;
+    std::map<int, std::unique_ptr<Workspace>> ws;   // per (level, candidate stream): key level * 16 + stream
+    long long launches = 0, ws_gen = 0;
+    // A level's candidates run as `n` independent streams of consecutive rows, each with its own workspace,
+    // captured as parallel branches of one graph: every kernel is latency-bound at a few hundred rows, so
+    // two chains side by side fill the SMs one chain leaves idle. Rows never interact, so the result is
+    // the same for any stream count.
+    int n_streams = 0;                // 0 = automatic
+    std::vector<cudaStream_t> side;   // streams of the candidate streams 1..n-1
+    std::vector<cudaEvent_t> ev;      // fork / join events of the captures
 
     ~HPlanner();
     bool build(const jepa_model & m);
-    Workspace * workspace(int level, int S, int T, const CostSpec & cs);
+    Workspace * workspace(int level, int S, int T, const CostSpec & cs, int chunk = 0);
+    int streams_for(int S) const;
+    bool ensure_streams(int n);
     // costs [S] and (optionally) grad [S][T][A] of host actions; all host buffers
     int plan_cost(const CostSpec & cs, const float * actions, int S, float * costs, float * grad);
     int solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, NoiseSource & noise, SolveOut & out);

@@ -230,26 +230,39 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
     }
     out.iters = 0;
     if (Sl < 1) { log("jepa: hjepa solve: %d candidates over %d GPUs leaves rank %d without any\n", S, world, rank); return -1; }
-    Workspace * w = workspace(cs.level, Sl, T, cs);
-    if (!w) return -1;
-    if (!cost_tables(*w, cs)) return -1;
+    // the rank's candidates as nc streams of consecutive rows: stream c holds rows [cr[c], cr[c + 1])
+    const int nc = streams_for(Sl);
+    std::vector<int> cr((size_t) nc + 1);
+    for (int c = 0; c <= nc; c++) cr[(size_t) c] = (int) ((int64_t) Sl * c / nc);
+    std::vector<Workspace *> wc((size_t) nc);
+    std::string gens;
+    for (int c = 0; c < nc; c++) {
+        wc[(size_t) c] = workspace(cs.level, cr[(size_t) c + 1] - cr[(size_t) c], T, cs, c);
+        if (!wc[(size_t) c] || !cost_tables(*wc[(size_t) c], cs)) return -1;
+        gens += std::to_string(wc[(size_t) c]->gen) + ",";
+    }
+    Workspace * w0 = wc[0];
     launches = 0;
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventRecord(e0, st);
-    JB_CUDA(cudaMemcpyAsync(w->x, x.data() + (size_t) r0 * row, (size_t) Sl * row * 4, cudaMemcpyHostToDevice, st));
-    JB_CUDA(cudaMemsetAsync(w->m, 0, (size_t) Sl * row * 4, st));
-    JB_CUDA(cudaMemsetAsync(w->v, 0, (size_t) Sl * row * 4, st));
-    JB_CUDA(cudaMemsetAsync(w->step_ctr, 0, 4 * sizeof(int), st));
-    JB_CUDA(cudaMemcpyAsync(w->gtmp, cs.s0, (size_t) D * 4, cudaMemcpyHostToDevice, st));
-    copy_rows(w->gtmp, 0, w->states, D, Sl, D, st);
-    gather_actions(w->x, w->a_all, Sl, T, A, st);
-    launches += 2;
     const bool clamp = !prior.lo.empty();
-    if (clamp) {
-        JB_CUDA(cudaMemcpyAsync(w->lo, prior.lo.data(), (size_t) A * 4, cudaMemcpyHostToDevice, st));
-        JB_CUDA(cudaMemcpyAsync(w->hi, prior.hi.data(), (size_t) A * 4, cudaMemcpyHostToDevice, st));
+    for (int c = 0; c < nc; c++) {
+        Workspace * w = wc[(size_t) c];
+        const int Sc = w->S;
+        JB_CUDA(cudaMemcpyAsync(w->x, x.data() + (size_t) (r0 + cr[(size_t) c]) * row, (size_t) Sc * row * 4, cudaMemcpyHostToDevice, st));
+        JB_CUDA(cudaMemsetAsync(w->m, 0, (size_t) Sc * row * 4, st));
+        JB_CUDA(cudaMemsetAsync(w->v, 0, (size_t) Sc * row * 4, st));
+        JB_CUDA(cudaMemsetAsync(w->step_ctr, 0, 4 * sizeof(int), st));
+        JB_CUDA(cudaMemcpyAsync(w->gtmp, cs.s0, (size_t) D * 4, cudaMemcpyHostToDevice, st));
+        copy_rows(w->gtmp, 0, w->states, D, Sc, D, st);
+        gather_actions(w->x, w->a_all, Sc, T, A, st);
+        launches += 2;
+        if (clamp) {
+            JB_CUDA(cudaMemcpyAsync(w->lo, prior.lo.data(), (size_t) A * 4, cudaMemcpyHostToDevice, st));
+            JB_CUDA(cudaMemcpyAsync(w->hi, prior.hi.data(), (size_t) A * 4, cudaMemcpyHostToDevice, st));
+        }
     }
     // AdamW bias corrections, per iteration, in float on the host as the reference computes them
     const float b1 = 0.9f, b2 = 0.999f;
@@ -276,30 +289,66 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
         }
     }
     const int sched_cap = 4096;
+    // one graph over every candidate stream: stream c's kernels on its own CUDA stream, forked from and
+    // joined back into the context's stream
+    auto capture = [&](bool with_grad, cudaGraphExec_t * exec, long long * nodes, const size_t zstride) -> int {
+        cudaGraph_t g;
+        JB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        const long long l0 = launches;
+        int rc = 0;
+        if (nc > 1) rc = cuda_ok(cudaEventRecord(ev[0], st), "fork") ? 0 : -1;
+        for (int c = 1; c < nc && !rc; c++) rc = cuda_ok(cudaStreamWaitEvent(wc[(size_t) c]->st, ev[0], 0), "fork") ? 0 : -1;
+        for (int c = 0; c < nc && !rc; c++) {
+            Workspace * w = wc[(size_t) c];
+            rc = forward(*w, cs, with_grad);
+            if (!rc && with_grad) rc = backward(*w, cs);
+            if (!rc && with_grad) {
+                adam_step(w->x, w->m, w->v, w->da_all, w->a_all, w->sched, w->step_ctr, lp.lr * lp.weight_decay,
+                          zdev ? zdev + (size_t) cr[(size_t) c] * row : nullptr, lp.action_noise, zstride,
+                          clamp ? w->lo : nullptr, clamp ? w->hi : nullptr, w->S, T, A, w->st);
+                launches++;
+            }
+        }
+        for (int c = 1; c < nc && !rc; c++) {
+            rc = cuda_ok(cudaEventRecord(ev[(size_t) c], wc[(size_t) c]->st), "join") &&
+                 cuda_ok(cudaStreamWaitEvent(st, ev[(size_t) c], 0), "join") ? 0 : -1;
+        }
+        const cudaError_t ce = cudaStreamEndCapture(st, &g);
+        if (rc || ce != cudaSuccess) { cudaGetLastError(); log("jepa: hjepa solve: graph capture failed\n"); return -1; }
+        *nodes = launches - l0;
+        const cudaError_t ie = cudaGraphInstantiate(exec, g, 0);
+        cudaGraphDestroy(g);
+        return cuda_ok(ie, "cudaGraphInstantiate") ? 0 : -1;
+    };
+    // the first lowest cost over the candidate streams (stream order = row order): (value, local row)
+    auto best_of = [&](float * val, int * idx, int * which) -> int {
+        std::vector<float> v((size_t) nc);
+        std::vector<int> ix((size_t) nc);
+        for (int c = 0; c < nc; c++) {
+            Workspace * w = wc[(size_t) c];
+            argmin_first(w->cost, w->S, w->best_idx, w->best_val, st);
+            launches++;
+            JB_CUDA(cudaMemcpyAsync(&v[(size_t) c], w->best_val, 4, cudaMemcpyDeviceToHost, st));
+            JB_CUDA(cudaMemcpyAsync(&ix[(size_t) c], w->best_idx, 4, cudaMemcpyDeviceToHost, st));
+        }
+        JB_CUDA(cudaStreamSynchronize(st));
+        int b = 0;
+        for (int c = 1; c < nc; c++) if (v[(size_t) c] < v[(size_t) b]) b = c;
+        *val = v[(size_t) b];
+        *idx = cr[(size_t) b] + ix[(size_t) b];
+        if (which) *which = b;
+        return 0;
+    };
     auto run = [&]() -> int {
         const size_t zstride = (noisy && !early) ? (size_t) Sl * row : 0;
         // capture one iteration (forward, backward, AdamW) as a graph, replayed every iteration
         const std::string key = std::to_string(lp.lr * lp.weight_decay) + "/" + std::to_string(lp.action_noise) + "/" +
-                                std::to_string(clamp) + "/" + std::to_string((uintptr_t) zdev) + "/" + std::to_string(zstride);
-        if (!w->g_iter || w->iter_key != key) {
-            if (w->g_iter) { cudaGraphExecDestroy(w->g_iter); w->g_iter = nullptr; }
-            cudaGraph_t g;
-            JB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-            const long long l0 = launches;
-            int rc = forward(*w, cs, true);
-            if (!rc) rc = backward(*w, cs);
-            if (!rc) {
-                adam_step(w->x, w->m, w->v, w->da_all, w->a_all, w->sched, w->step_ctr, lp.lr * lp.weight_decay, zdev,
-                          lp.action_noise, zstride, clamp ? w->lo : nullptr, clamp ? w->hi : nullptr, Sl, T, A, st);
-                launches++;
-            }
-            const cudaError_t ce = cudaStreamEndCapture(st, &g);
-            if (rc || ce != cudaSuccess) { cudaGetLastError(); log("jepa: hjepa solve: graph capture failed\n"); return -1; }
-            w->iter_nodes = launches - l0;
-            const cudaError_t ie = cudaGraphInstantiate(&w->g_iter, g, 0);
-            cudaGraphDestroy(g);
-            if (!cuda_ok(ie, "cudaGraphInstantiate")) return -1;
-            w->iter_key = key;
+                                std::to_string(clamp) + "/" + std::to_string((uintptr_t) zdev) + "/" + std::to_string(zstride) +
+                                "/" + gens;
+        if (!w0->g_iter || w0->iter_key != key) {
+            if (w0->g_iter) { cudaGraphExecDestroy(w0->g_iter); w0->g_iter = nullptr; }
+            if (capture(true, &w0->g_iter, &w0->iter_nodes, zstride)) return -1;
+            w0->iter_key = key;
         }
         launches = 0;
         float best = INFINITY;
@@ -307,8 +356,10 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
         for (int step = 0; step < lp.n_steps; step++) {
             if (step % sched_cap == 0) {
                 const int n = std::min(sched_cap, lp.n_steps - step);
-                JB_CUDA(cudaMemcpyAsync(w->sched, sched.data() + (size_t) 2 * step, (size_t) 2 * n * 4, cudaMemcpyHostToDevice, st));
-                JB_CUDA(cudaMemsetAsync(w->step_ctr, 0, 2 * sizeof(int), st));
+                for (Workspace * w : wc) {
+                    JB_CUDA(cudaMemcpyAsync(w->sched, sched.data() + (size_t) 2 * step, (size_t) 2 * n * 4, cudaMemcpyHostToDevice, st));
+                    JB_CUDA(cudaMemsetAsync(w->step_ctr, 0, 2 * sizeof(int), st));
+                }
                 if (step > 0 && noisy && !early) {
                     log("jepa: hjepa solve: more than %d iterations with pre-drawn action noise are not supported\n", sched_cap);
                     return -1;
@@ -319,16 +370,14 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
                 noise.fill(z.data(), N);
                 JB_CUDA(cudaMemcpyAsync(zdev, z.data() + (size_t) r0 * row, (size_t) Sl * row * 4, cudaMemcpyHostToDevice, st));
             }
-            JB_CUDA(cudaGraphLaunch(w->g_iter, st));
-            launches += w->iter_nodes;
+            JB_CUDA(cudaGraphLaunch(w0->g_iter, st));
+            launches += w0->iter_nodes;
             out.iters = step + 1;
             if (early) {
                 // on the costs of the candidates BEFORE this update, as the reference does
-                argmin_first(w->cost, Sl, w->best_idx, w->best_val, st);
-                launches++;
                 float score = 0.0f;
-                JB_CUDA(cudaMemcpyAsync(&score, w->best_val, 4, cudaMemcpyDeviceToHost, st));
-                JB_CUDA(cudaStreamSynchronize(st));
+                int bi = 0;
+                if (best_of(&score, &bi, nullptr)) return -1;
                 if (sh && world > 1) score = sh->min_f32(score, st);
                 const bool improved = !std::isfinite(best) || best - score > lp.early_stop_rel_delta * std::max(std::fabs(best), 1e-12f);
                 if (improved) { best = score; stalled = 0; }
@@ -336,27 +385,16 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
             }
         }
         // final evaluation without gradient, then the first lowest-cost candidate
-        if (!w->g_fwd) {
-            cudaGraph_t g;
-            JB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-            const long long l0 = launches;
-            const int rc = forward(*w, cs, false);
-            const cudaError_t ce = cudaStreamEndCapture(st, &g);
-            if (rc || ce != cudaSuccess) { cudaGetLastError(); log("jepa: hjepa solve: graph capture failed\n"); return -1; }
-            w->fwd_nodes = launches - l0;
-            const cudaError_t ie = cudaGraphInstantiate(&w->g_fwd, g, 0);
-            cudaGraphDestroy(g);
-            if (!cuda_ok(ie, "cudaGraphInstantiate")) return -1;
+        if (!w0->g_fwd || w0->fwd_key != gens) {
+            if (w0->g_fwd) { cudaGraphExecDestroy(w0->g_fwd); w0->g_fwd = nullptr; }
+            if (capture(false, &w0->g_fwd, &w0->fwd_nodes, 0)) return -1;
+            w0->fwd_key = gens;
         }
-        JB_CUDA(cudaGraphLaunch(w->g_fwd, st));
-        launches += w->fwd_nodes;
-        argmin_first(w->cost, Sl, w->best_idx, w->best_val, st);
-        launches++;
-        int idx = 0;
+        JB_CUDA(cudaGraphLaunch(w0->g_fwd, st));
+        launches += w0->fwd_nodes;
+        int idx = 0, which = 0;
         float cost = 0.0f;
-        JB_CUDA(cudaMemcpyAsync(&idx, w->best_idx, 4, cudaMemcpyDeviceToHost, st));
-        JB_CUDA(cudaMemcpyAsync(&cost, w->best_val, 4, cudaMemcpyDeviceToHost, st));
-        JB_CUDA(cudaStreamSynchronize(st));
+        if (best_of(&cost, &idx, &which)) return -1;
         out.actions.assign(row, 0.0f);
         out.states.assign((size_t) (T + 1) * D, 0.0f);
         int owner = rank;
@@ -367,8 +405,11 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
             idx = gidx - r0;
         }
         if (owner == rank) {
-            JB_CUDA(cudaMemcpyAsync(out.actions.data(), w->x + (size_t) idx * row, row * 4, cudaMemcpyDeviceToHost, st));
-            JB_CUDA(cudaMemcpy2DAsync(out.states.data(), (size_t) D * 4, w->states + (size_t) idx * D, (size_t) Sl * D * 4,
+            for (int c = 0; c < nc; c++) if (idx >= cr[(size_t) c]) which = c;
+            const Workspace * w = wc[(size_t) which];
+            const int li = idx - cr[(size_t) which];
+            JB_CUDA(cudaMemcpyAsync(out.actions.data(), w->x + (size_t) li * row, row * 4, cudaMemcpyDeviceToHost, st));
+            JB_CUDA(cudaMemcpy2DAsync(out.states.data(), (size_t) D * 4, w->states + (size_t) li * D, (size_t) w->S * D * 4,
                                       (size_t) D * 4, (size_t) T + 1, cudaMemcpyDeviceToHost, st));
             JB_CUDA(cudaStreamSynchronize(st));
         }
@@ -400,6 +441,14 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
 using namespace jb;
 
 extern "C" {
+
+int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n) {
+    if (!ctx || n < 0 || n > 8) { log("jepa: jepa_b200_hjepa_set_streams: a context and 0..8 streams are required\n"); return -1; }
+    HPlanner * pm = planner_of(ctx, "jepa_b200_hjepa_set_streams");
+    if (!pm) return -1;
+    pm->n_streams = n;
+    return 0;
+}
 
 jepa_hjepa_level_plan jepa_hjepa_level_plan_default(void) {
     jepa_hjepa_level_plan p;

@@ -22,7 +22,7 @@ int HPlanner::pooled_chunks(const CostSpec & cs) const {
 }
 
 int HPlanner::pool_forward(Workspace & w, bool want_grad) {
-    cudaStream_t st = ctx->stream;
+    cudaStream_t st = w.st;
     PoolWs & pw = w.pool;
     const DLevel & L = levels[(size_t) w.level - 1];
     const DLevel & U = levels[(size_t) w.level];
@@ -72,7 +72,7 @@ int HPlanner::pool_forward(Workspace & w, bool want_grad) {
 }
 
 int HPlanner::pool_backward(Workspace & w) {
-    cudaStream_t st = ctx->stream;
+    cudaStream_t st = w.st;
     PoolWs & pw = w.pool;
     const DLevel & L = levels[(size_t) w.level - 1];
     const DLevel & U = levels[(size_t) w.level];

@@ -62,6 +62,11 @@ class Planner:
         if self.lib.jepa_b200_context_set_shard(self.ctx, rank, world, buf) != 0:
             raise RuntimeError(f"jepa_b200_context_set_shard failed: {jlib.error_text()}")
 
+    def set_streams(self, n: int) -> None:
+        """Candidate streams of the solves (0 = automatic); results do not depend on it."""
+        if self.lib.jepa_b200_hjepa_set_streams(self.ctx, int(n)) != 0:
+            raise RuntimeError(f"jepa_b200_hjepa_set_streams failed: {jlib.error_text()}")
+
     def last_ms(self) -> float:
         return self.lib.jepa_b200_last_plan_ms(self.ctx)
 

@@ -112,6 +112,29 @@ def test_solve_matches_oracle(tmpdir_mod, ftype, opts):
     assert abs(cost - oc) / abs(oc) < REL
 
 
+@pytest.mark.parametrize("opts", [{"early_stop_patience": 0}, {"early_stop_patience": 2, "action_noise": 0.05}])
+def test_solve_does_not_depend_on_the_stream_count(tmpdir_mod, opts):
+    # a level's candidates split into 1, 2, 3 or 5 chains side by side on the GPU: the same plan, bit for bit
+    # (the reference's counterpart: results identical for any thread count)
+    path = forged(tmpdir_mod, "f32")
+    P = Planner(path)
+    rng = np.random.default_rng(17)
+    s0 = rng.normal(size=64).astype(np.float32)
+    goal = rng.normal(size=(1, 64)).astype(np.float32)
+    draws = rng.normal(size=400000).astype(np.float32)
+    plan = solve_plan(S=301, steps=8, **opts)
+    ref = None
+    for n in (1, 2, 3, 5):
+        P.set_streams(n)
+        got = P.solve(1, s0, goal, plan, noise=draws)
+        if ref is None:
+            ref = got
+            continue
+        for a, b in zip(got[:4], ref[:4]):
+            assert np.array_equal(np.asarray(a), np.asarray(b)), n
+    P.set_streams(0)
+
+
 def test_hierarchy_matches_oracle(tmpdir_mod):
     path = forged(tmpdir_mod, "f32")
     m = O.Model(path)
