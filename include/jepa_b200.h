@@ -69,6 +69,12 @@ long long jepa_b200_last_plan_launches(const jepa_context * ctx);
 // context or n out of range.
 int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n);
 
+// Memory mode of the H-JEPA solves on this context: 0 = automatic (every step's adaLN modulation and its
+// gradient, [T S][6 P L] floats x 3, are kept when they fit the free device memory, else one step's at a time),
+// 1 = always one step at a time (the modulation recomputed in the backward: more GEMM work, far less memory).
+// Results are the same in both modes. Returns 0, or -1 for a non-H-JEPA context or a mode out of range.
+int jepa_b200_hjepa_set_step_modulation(jepa_context * ctx, int mode);
+
 // C[M,N] = f16(A)[M,K] * f16(B)[N,K]^T with f32 accumulation through the V-JEPA 2-AC predictor's
 // tcgen05 kind::f16 GEMM (host f32 buffers, rounded to f16 on the device; K a multiple of 8). A kernel
 // check: every linear of the AC predictor runs through this kernel.

@@ -267,12 +267,18 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (splits > 1) cluster_arrive_release();   // the receive barriers are initialised
     const uint32_t tmem = tmem_base_sh;
-    // the setup above overlapped the previous kernel (programmatic dependent launch); its outputs are
-    // read from here on
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-
-    // split-K: the first round of this thread's epilogue items, and their operands, loaded now
+    // B operands that do not come from the preceding kernel (weights): the first stages' B tiles are
+    // requested before the dependency wait, while that kernel still runs
+    const int pre_stages = ep.pre_b ? min(STAGES, nkt) : 0;
+    if (warp == 0 && lane == 0) {
+        for (int i = 0; i < pre_stages; i++) {
+            uint8_t * st = smem + (size_t) i * STAGE_BYTES;
+            mbar_expect_tx(&full_bar[i], STAGE_BYTES);
+            tma_load_2d(st + 2 * A_BYTES, &tB_hi, (kt0 + i) * BK, n0, &full_bar[i]);
+            tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, (kt0 + i) * BK, n0, &full_bar[i]);
+        }
+    }
+    // split-K: the first round of this thread's epilogue items, and their operands
     const int n_items = splits > 1 && re > rs ? (re - rs) * C4 : 0;
     const int rounds = (n_items + NT * PER - 1) / (NT * PER);
     Epi4In in[PER];
@@ -285,7 +291,12 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
             if (row < M && ep.vec && col + 3 < N) in[j] = epi_load4(ep, row, col);
         }
     };
-    if (rounds > 0) prefetch(0);
+    if (ep.pre_epi && rounds > 0) prefetch(0);
+    // the setup above overlapped the previous kernel (programmatic dependent launch); its outputs are
+    // read from here on
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (!ep.pre_epi && rounds > 0) prefetch(0);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -295,13 +306,16 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 const int s = i % STAGES;
                 const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
                 if (i >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1, &g_gemm_error)) { abort_sh = 1; break; }
-                if (*(volatile int *) &abort_sh) break;
+                // a stage whose B tiles are in flight always gets its A tiles (so that its barrier completes)
+                if (i >= pre_stages && *(volatile int *) &abort_sh) break;
                 uint8_t * st = smem + (size_t) s * STAGE_BYTES;
-                mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+                if (i >= pre_stages) {
+                    mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+                    tma_load_2d(st + 2 * A_BYTES, &tB_hi, kt * BK, n0, &full_bar[s]);
+                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, kt * BK, n0, &full_bar[s]);
+                }
                 tma_load_2d(st, &tA_hi, kt * BK, m0, &full_bar[s]);
                 tma_load_2d(st + A_BYTES, &tA_lo, kt * BK, m0, &full_bar[s]);
-                tma_load_2d(st + 2 * A_BYTES, &tB_hi, kt * BK, n0, &full_bar[s]);
-                tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, kt * BK, n0, &full_bar[s]);
                 issued = i + 1;
             }
             if (*(volatile int *) &abort_sh) {

@@ -127,6 +127,15 @@ struct Uploader {
 
 }  // namespace
 
+// Every product of the planner's sweep multiplies by a weight (B never comes from the kernel before), and
+// its epilogue reads only biases and operands written at least two kernels earlier (the modulation, the
+// block's input, the forward pre-activations): both are loaded before the dependency wait.
+static int wgemm(const SplitMat & A, const SplitMat & B, int M, int N, int K, GemmEpi ep, cudaStream_t st) {
+    ep.pre_b = 1;
+    ep.pre_epi = 1;
+    return gemm_tc(A, B, M, N, K, ep, st);
+}
+
 HPlanner::~HPlanner() {
     ws.clear();
     for (void * p : allocations) cudaFree(p);
@@ -326,6 +335,7 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
         pool_scr = std::max(pool_scr, n * (size_t) wide);
     }
     ArenaPlan ap;
+    size_t mod_rows = R;   // rows of mod / dmod: every step's (R), or one step's (S) in step-at-a-time mode
     auto plan_all = [&](auto && add) {
         add((float **) &w->x, (size_t) S * T * A); add(&w->m, (size_t) S * T * A); add(&w->v, (size_t) S * T * A);
         add(&w->grad, (size_t) S * T * A); add(&w->a_all, R * A); add(&w->da_all, R * A);
@@ -333,7 +343,7 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
         if (L.act0) { add(&w->ae_u, R * L.act0.out); add(&w->ae_s, R * L.act0.out); add(&w->e, R * L.E); }
         if (L.pact0) { add(&w->pa_u, R * L.pact0.out); add(&w->pa_s, R * L.pact0.out); add(&w->c0, R * L.C); }
         add(&w->cpre, R * P); add(&w->cs_hi, R * P); add(&w->cs_lo, R * P);
-        add(&w->mod, R * ldm); add(&w->dmod_hi, R * ldm); add(&w->dmod_lo, R * ldm);
+        add(&w->mod, mod_rows * ldm); add(&w->dmod_hi, mod_rows * ldm); add(&w->dmod_lo, mod_rows * ldm);
         add(&w->dcs, R * P); add(&w->dc, R * P); add(&w->tmpR, R * maxw); add(&w->tmpR2, R * maxw);
         add(&w->states, (size_t) (T + 1) * S * D); add(&w->gstate, (size_t) (T + 1) * S * D);
         add(&w->xs, (size_t) T * (NL + 1) * S * P);
@@ -390,6 +400,17 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
     };
     auto count = [&](auto ** p, size_t n) { (void) p; ap.add<float>(n); };
     plan_all(count);
+    {
+        // the modulation of every step at once (one GEMM each way) when it fits; else one step at a time
+        size_t free_b = 0, total_b = 0;
+        cudaMemGetInfo(&free_b, &total_b);
+        if ((force_step_mod || ap.bytes > free_b / 10 * 9) && T > 1) {
+            w->step_mod = true;
+            mod_rows = (size_t) S;
+            ap = ArenaPlan();
+            plan_all(count);
+        }
+    }
     ap.add<LnStats>((size_t) T * NL * S * 4 + (size_t) T * S);
     for (size_t i = 0; i < w->enc.size(); i++) ap.add<LnStats>((size_t) w->enc[i].n * S * 2);
     ap.add<float>((size_t) 2 * 4096);      // Adam schedule
@@ -462,7 +483,7 @@ int HPlanner::lin_fwd(const DLin & L, const float * x, int ldx, const float * x_
         ep.out_hi = y_hi; ep.out_lo = y_lo; ep.ld_split = ldy;
         ep.mode = y_hi ? (y ? EPI_F32_SPLIT : EPI_SPLIT) : EPI_F32;
         launches++;
-        return gemm_tc({x_hi, x_lo, ld}, {L.w_hi, L.w_lo, L.in}, M, L.out, L.in, ep, st);
+        return wgemm({x_hi, x_lo, ld}, {L.w_hi, L.w_lo, L.in}, M, L.out, L.in, ep, st);
     }
     linear_simt(x, ldx, L.w, L.b, y, ldy, M, L.out, L.in, st);
     launches++;
@@ -483,11 +504,39 @@ int HPlanner::lin_bwd(const DLin & L, const float * dy, int lddy, const float * 
         GemmEpi ep;
         ep.out0 = dx; ep.ld0 = lddx;
         launches++;
-        return gemm_tc({dy_hi, dy_lo, ld}, {L.wt_hi, L.wt_lo, L.out}, M, L.in, L.out, ep, st);
+        return wgemm({dy_hi, dy_lo, ld}, {L.wt_hi, L.wt_lo, L.out}, M, L.in, L.out, ep, st);
     }
     linear_simt(dy, lddy, L.wt, nullptr, dx, lddx, M, L.in, L.out, st);
     launches++;
     return 0;
+}
+
+// ---------------------------------------------------------------------------------------------
+// the adaLN modulation of steps [t0, t0 + nt): mod = adaln(silu(c)) for their rows, and its backward
+// dcs = dmod adaln.W for the same rows (every step at once, or one step at a time: mod / dmod then hold
+// one step's rows)
+// ---------------------------------------------------------------------------------------------
+static size_t mod_row0(const Workspace & w, int t) { return w.step_mod ? 0 : (size_t) t * w.S; }
+
+int HPlanner::step_modulation(Workspace & w, int t0, int nt) {
+    const DLevel & L = levels[(size_t) w.level - 1];
+    const int P = L.P, ldm = 6 * P * L.L;
+    GemmEpi ep;
+    ep.bias = L.adaln.b;
+    ep.out0 = w.mod + mod_row0(w, t0) * ldm; ep.ld0 = ldm;
+    launches++;
+    const size_t r0 = (size_t) t0 * w.S * P;
+    return wgemm({w.cs_hi + r0, w.cs_lo + r0, P}, {L.adaln.w_hi, L.adaln.w_lo, P}, nt * w.S, ldm, P, ep, w.st);
+}
+
+int HPlanner::step_modulation_bwd(Workspace & w, int t0, int nt) {
+    const DLevel & L = levels[(size_t) w.level - 1];
+    const int P = L.P, ldm = 6 * P * L.L;
+    GemmEpi ep;
+    ep.out0 = w.dcs + (size_t) t0 * w.S * P; ep.ld0 = P;
+    launches++;
+    const size_t m0 = mod_row0(w, t0) * ldm;
+    return wgemm({w.dmod_hi + m0, w.dmod_lo + m0, ldm}, {L.adaln.wt_hi, L.adaln.wt_lo, ldm}, nt * w.S, P, ldm, ep, w.st);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -520,17 +569,13 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
     }
     act_fwd(w.cpre, P, w.tmpR, P, R, P, 2, st); launches++;
     split_f32(w.tmpR, P, w.cs_hi, w.cs_lo, P, R, P, st); launches++;
-    {
-        GemmEpi ep;
-        ep.bias = L.adaln.b;
-        ep.out0 = w.mod; ep.ld0 = ldm;
-        launches++;
-        if (gemm_tc({w.cs_hi, w.cs_lo, P}, {L.adaln.w_hi, L.adaln.w_lo, P}, R, ldm, P, ep, st)) return -1;
-    }
+    if (!w.step_mod && step_modulation(w, 0, T)) return -1;
     // ---- rollout
     for (int t = 0; t < T; t++) {
         const float * s_t = w.states + (size_t) t * S * D;
         float * x0 = w.xs + (size_t) t * (NL + 1) * S * P;
+        // (step-at-a-time modulation: step t's, at least one kernel ahead of its first reader)
+        if (w.step_mod && step_modulation(w, t, 1)) return -1;
         if (L.in_proj) {
             add_row_vec(s_t, D, L.pos0, w.gtmp, D, S, D, st); launches++;
             if (lin_fwd(L.in_proj, w.gtmp, D, nullptr, nullptr, S, x0, P, nullptr, nullptr, w)) return -1;
@@ -539,7 +584,7 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
         }
         for (int l = 0; l < NL; l++) {
             const DBlock & B = L.blocks[(size_t) l];
-            const float * mod_l = w.mod + (size_t) t * S * ldm + (size_t) l * 6 * P;
+            const float * mod_l = w.mod + mod_row0(w, t) * ldm + (size_t) l * 6 * P;
             float * xin = x0 + (size_t) l * S * P;
             float * xout = xin + (size_t) S * P;
             const size_t tl = (size_t) t * NL + l;
@@ -550,16 +595,16 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
             GemmEpi e2;
             e2.mode = EPI_GATED; e2.bias = B.ov.b; e2.out0 = o; e2.ld0 = P; e2.aux = xin; e2.ld_aux = P;
             e2.gate = mod_l + 2 * P; e2.ld_gate = ldm; e2.out1 = xm; e2.ld1 = P;
-            if (gemm_tc({w.h_hi, w.h_lo, P}, {B.ov.w_hi, B.ov.w_lo, P}, S, P, P, e2, st)) return -1;
+            if (wgemm({w.h_hi, w.h_lo, P}, {B.ov.w_hi, B.ov.w_lo, P}, S, P, P, e2, st)) return -1;
             block_pre(xm, P, mod_l, ldm, 3 * P, 4 * P, B.ln2_w, B.ln2_b, adaln_eps, ln_eps, w.h_hi, w.h_lo, P,
                       w.stm0 + tl * S, w.stm1 + tl * S, S, P, st);
             GemmEpi e3;
             e3.mode = EPI_GELU_SPLIT; e3.bias = B.up.b; e3.out0 = u; e3.ld0 = F; e3.out_hi = w.g_hi; e3.out_lo = w.g_lo; e3.ld_split = F;
-            if (gemm_tc({w.h_hi, w.h_lo, P}, {B.up.w_hi, B.up.w_lo, P}, S, F, P, e3, st)) return -1;
+            if (wgemm({w.h_hi, w.h_lo, P}, {B.up.w_hi, B.up.w_lo, P}, S, F, P, e3, st)) return -1;
             GemmEpi e4;
             e4.mode = EPI_GATED; e4.bias = B.down.b; e4.out0 = dn; e4.ld0 = P; e4.aux = xm; e4.ld_aux = P;
             e4.gate = mod_l + 5 * P; e4.ld_gate = ldm; e4.out1 = xout; e4.ld1 = P;
-            if (gemm_tc({w.g_hi, w.g_lo, F}, {B.down.w_hi, B.down.w_lo, F}, S, P, F, e4, st)) return -1;
+            if (wgemm({w.g_hi, w.g_lo, F}, {B.down.w_hi, B.down.w_lo, F}, S, P, F, e4, st)) return -1;
             launches += 5;
         }
         const float * xL = x0 + (size_t) NL * S * P;
@@ -610,7 +655,7 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
                 GemmEpi ep;
                 ep.mode = EPI_GELU_SPLIT; ep.bias = U.enc_fc1.b; ep.out0 = e.u; ep.ld0 = H; ep.out_hi = e.g_hi; ep.out_lo = e.g_lo; ep.ld_split = H;
                 launches++;
-                if (gemm_tc({e.h_hi, e.h_lo, Din}, {U.enc_fc1.w_hi, U.enc_fc1.w_lo, Din}, n, H, Din, ep, st)) return -1;
+                if (wgemm({e.h_hi, e.h_lo, Din}, {U.enc_fc1.w_hi, U.enc_fc1.w_lo, Din}, n, H, Din, ep, st)) return -1;
             } else {
                 layer_norm(e.in, Din, U.enc_in_w, U.enc_in_b, ln_eps, w.tmpR2, Din, nullptr, nullptr, nullptr, n, Din, st);
                 linear_simt(w.tmpR2, Din, U.enc_fc1.w, U.enc_fc1.b, e.u, H, n, H, Din, st);
@@ -728,10 +773,10 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             split_f32(gy, Dout, e.d_hi, e.d_lo, Dout, n, Dout, st);
             GemmEpi ep;
             ep.mode = EPI_DGELU_SPLIT; ep.aux = e.u; ep.ld_aux = H; ep.out_hi = e.g_hi; ep.out_lo = e.g_lo; ep.ld_split = H;
-            if (gemm_tc({e.d_hi, e.d_lo, Dout}, {U.enc_fc2.wt_hi, U.enc_fc2.wt_lo, Dout}, n, H, Dout, ep, st)) return -1;
+            if (wgemm({e.d_hi, e.d_lo, Dout}, {U.enc_fc2.wt_hi, U.enc_fc2.wt_lo, Dout}, n, H, Dout, ep, st)) return -1;
             GemmEpi ep2;
             ep2.out0 = e.gin; ep2.ld0 = Din;
-            if (gemm_tc({e.g_hi, e.g_lo, H}, {U.enc_fc1.wt_hi, U.enc_fc1.wt_lo, H}, n, Din, H, ep2, st)) return -1;
+            if (wgemm({e.g_hi, e.g_lo, H}, {U.enc_fc1.wt_hi, U.enc_fc1.wt_lo, H}, n, Din, H, ep2, st)) return -1;
             launches += 3;
         } else {
             if (lin_bwd(U.enc_fc2, gy, Dout, nullptr, nullptr, n, w.tmpR2, H, w)) return -1;
@@ -749,6 +794,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
     }
     // ---- rollout, reverse
     for (int t = T - 1; t >= 0; t--) {
+        if (w.step_mod && step_modulation(w, t, 1)) return -1;   // step t's modulation, recomputed
         const float * g_next = w.gstate + (size_t) (t + 1) * S * D;
         const float * x0 = w.xs + (size_t) t * (NL + 1) * S * P;
         const float * xL = x0 + (size_t) NL * S * P;
@@ -769,28 +815,28 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
         }
         {
             const size_t tl = (size_t) t * NL + (NL - 1);
-            const float * mod_l = w.mod + (size_t) t * S * ldm + (size_t) (NL - 1) * 6 * P;
+            const float * mod_l = w.mod + mod_row0(w, t) * ldm + (size_t) (NL - 1) * 6 * P;
             layer_norm_bwd(gy, ldgy, xL, P, w.stn + (size_t) t * S, L.norm_w, nullptr, 0, w.gx, P,
                            w.dn + tl * S * P, P, mod_l + 5 * P, ldm,
-                           w.dmod_hi + (size_t) t * S * ldm + (size_t) (NL - 1) * 6 * P + 5 * P,
-                           w.dmod_lo + (size_t) t * S * ldm + (size_t) (NL - 1) * 6 * P + 5 * P, ldm,
+                           w.dmod_hi + mod_row0(w, t) * ldm + (size_t) (NL - 1) * 6 * P + 5 * P,
+                           w.dmod_lo + mod_row0(w, t) * ldm + (size_t) (NL - 1) * 6 * P + 5 * P, ldm,
                            w.d_hi, w.d_lo, P, S, P, st);
             launches++;
         }
         for (int l = NL - 1; l >= 0; l--) {
             const DBlock & B = L.blocks[(size_t) l];
             const size_t tl = (size_t) t * NL + l;
-            const float * mod_l = w.mod + (size_t) t * S * ldm + (size_t) l * 6 * P;
-            float * dmh = w.dmod_hi + (size_t) t * S * ldm + (size_t) l * 6 * P;
-            float * dml = w.dmod_lo + (size_t) t * S * ldm + (size_t) l * 6 * P;
+            const float * mod_l = w.mod + mod_row0(w, t) * ldm + (size_t) l * 6 * P;
+            float * dmh = w.dmod_hi + mod_row0(w, t) * ldm + (size_t) l * 6 * P;
+            float * dml = w.dmod_lo + mod_row0(w, t) * ldm + (size_t) l * 6 * P;
             const float * xin = x0 + (size_t) l * S * P;
             // MLP half
             GemmEpi e1;
             e1.mode = EPI_DGELU_SPLIT; e1.aux = w.u + tl * S * F; e1.ld_aux = F; e1.out_hi = w.du_hi; e1.out_lo = w.du_lo; e1.ld_split = F;
-            if (gemm_tc({w.d_hi, w.d_lo, P}, {B.down.wt_hi, B.down.wt_lo, P}, S, F, P, e1, st)) return -1;
+            if (wgemm({w.d_hi, w.d_lo, P}, {B.down.wt_hi, B.down.wt_lo, P}, S, F, P, e1, st)) return -1;
             GemmEpi e2;
             e2.out0 = w.gh; e2.ld0 = P;
-            if (gemm_tc({w.du_hi, w.du_lo, F}, {B.up.wt_hi, B.up.wt_lo, F}, S, P, F, e2, st)) return -1;
+            if (wgemm({w.du_hi, w.du_lo, F}, {B.up.wt_hi, B.up.wt_lo, F}, S, P, F, e2, st)) return -1;
             BlockBwdArgs a{};
             a.gh = w.gh; a.ldgh = P; a.gres = w.gx; a.ldres = P; a.x = w.xmid + tl * S * P; a.ldx = P;
             a.st0 = w.stm0 + tl * S; a.st1 = w.stm1 + tl * S; a.ln_w = B.ln2_w; a.ln_b = B.ln2_b;
@@ -803,7 +849,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             // attention half (one query over one key: the value path, through the composed linear)
             GemmEpi e4;
             e4.out0 = w.gh; e4.ld0 = P;
-            if (gemm_tc({w.d_hi, w.d_lo, P}, {B.ov.wt_hi, B.ov.wt_lo, P}, S, P, P, e4, st)) return -1;
+            if (wgemm({w.d_hi, w.d_lo, P}, {B.ov.wt_hi, B.ov.wt_lo, P}, S, P, P, e4, st)) return -1;
             BlockBwdArgs b{};
             b.gh = w.gh; b.ldgh = P; b.gres = w.gmid; b.ldres = P; b.x = xin; b.ldx = P;
             b.st0 = w.sta0 + tl * S; b.st1 = w.sta1 + tl * S; b.ln_w = B.ln1_w; b.ln_b = B.ln1_b;
@@ -818,6 +864,8 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             block_bwd(b, st);
             launches += 5;
         }
+        // step-at-a-time modulation: this step's dmod into its rows of dcs now, before the next step reuses dmod
+        if (w.step_mod && step_modulation_bwd(w, t, 1)) return -1;
         // gx = d (s_t + pos0 [-> in_proj]); pass it to the state the step read
         if (t > 0) {
             float * gs = w.gstate + (size_t) t * S * D;
@@ -831,12 +879,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
         }
     }
     // ---- conditioning path: every step's d(cs) through every adaLN linear in one GEMM
-    {
-        GemmEpi ep;
-        ep.out0 = w.dcs; ep.ld0 = P;
-        launches++;
-        if (gemm_tc({w.dmod_hi, w.dmod_lo, ldm}, {L.adaln.wt_hi, L.adaln.wt_lo, ldm}, R, P, ldm, ep, st)) return -1;
-    }
+    if (!w.step_mod && step_modulation_bwd(w, 0, T)) return -1;
     act_bwd(w.dcs, P, w.cpre, P, w.dc, P, R, P, 2, false, st); launches++;
     float * g = w.dc;
     int gw = P;

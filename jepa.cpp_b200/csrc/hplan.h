@@ -103,6 +103,10 @@ struct PoolWs {
 struct Workspace {
     int level = 0, S = 0, T = 0;
     long long gen = 0;                // creation number (keys the graphs that span several workspaces)
+    // step-at-a-time modulation (when every step's [T S][6PL] modulation and its gradient do not fit): the
+    // adaLN GEMM runs per step in the forward and again in the backward, dmod is folded into dcs per step.
+    // Bit-identical to the all-steps mode (a GEMM row does not depend on the batch it is in).
+    bool step_mod = false;
     cudaStream_t st = nullptr;        // the stream its kernels are launched on
     PoolWs pool;
     Arena arena;
@@ -174,6 +178,7 @@ struct HPlanner {
     // two chains side by side fill the SMs one chain leaves idle. Rows never interact, so the result is
     // the same for any stream count.
     int n_streams = 0;                // 0 = automatic
+    bool force_step_mod = false;      // step-at-a-time modulation even when every step's fits
     std::vector<cudaStream_t> side;   // streams of the candidate streams 1..n-1
     std::vector<cudaEvent_t> ev;      // fork / join events of the captures
 
@@ -190,6 +195,8 @@ struct HPlanner {
     int forward(Workspace & w, const CostSpec & cs, bool want_grad);
     int backward(Workspace & w, const CostSpec & cs);
     bool cost_tables(Workspace & w, const CostSpec & cs);
+    int step_modulation(Workspace & w, int t0, int nt);       // mod of steps [t0, t0 + nt)
+    int step_modulation_bwd(Workspace & w, int t0, int nt);   // dcs of steps [t0, t0 + nt) from dmod
     int pooled_chunks(const CostSpec & cs) const;     // Wa: chunks the action cost compares (0 = no action cost)
     int pool_forward(Workspace & w, bool want_grad);   // action cost, added to the costs
     int pool_backward(Workspace & w);                  // its gradient into pool.ge

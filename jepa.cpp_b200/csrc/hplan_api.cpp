@@ -450,6 +450,15 @@ int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n) {
     return 0;
 }
 
+int jepa_b200_hjepa_set_step_modulation(jepa_context * ctx, int mode) {
+    if (!ctx || mode < 0 || mode > 1) { log("jepa: jepa_b200_hjepa_set_step_modulation: a context and mode 0 or 1 are required\n"); return -1; }
+    HPlanner * pm = planner_of(ctx, "jepa_b200_hjepa_set_step_modulation");
+    if (!pm) return -1;
+    if (pm->force_step_mod != (mode == 1)) pm->ws.clear();   // workspaces are planned for one mode
+    pm->force_step_mod = mode == 1;
+    return 0;
+}
+
 jepa_hjepa_level_plan jepa_hjepa_level_plan_default(void) {
     jepa_hjepa_level_plan p;
     p.horizon = 1;

@@ -34,6 +34,10 @@ struct GemmEpi {
     const float * gate = nullptr; int ld_gate = 0;
     float * out1 = nullptr; int ld1 = 0;
     int vec = 0;                    // set by gemm_tc: float4 epilogue allowed
+    // Operands that do not come from the kernel right before this one in the stream (they were written at
+    // least two kernels earlier, or are weights): loaded before the dependency wait, while that kernel
+    // still runs. pre_b: the B operand (its first pipeline stages); pre_epi: bias / aux / gate.
+    int pre_b = 0, pre_epi = 0;
 };
 
 struct SplitMat {                    // a split operand: two float32 planes with one leading dimension
@@ -60,7 +64,9 @@ void linear_simt(const float * x, int ldx, const float * w, const float * b, flo
 // ------------------------------------------------------------------------------------------
 struct LnStats { double mean; float inv; float pad; };
 
-// adaLN block prologue: h = ln?( LN0(x) * (1 + mod[sc]) + mod[sh] ), split out; stats saved
+// adaLN block prologue: h = ln?( LN0(x) * (1 + mod[sc]) + mod[sh] ), split out; stats saved.
+// mod and the ln weights are read before the dependency wait: they must have been written at least two
+// kernels earlier in the stream (x may come from the kernel right before).
 void block_pre(const float * x, int ldx, const float * mod, int ld_mod, int sh_off, int sc_off,
                const float * ln_w, const float * ln_b, float eps0, float eps1,
                float * h_hi, float * h_lo, int ldh, LnStats * st0, LnStats * st1, int M, int D, cudaStream_t st);
@@ -100,6 +106,8 @@ struct BlockBwdArgs {
     int M, D;
     float eps0, eps1;
 };
+// Every operand but gh is read before the dependency wait: it must have been written at least two kernels
+// earlier in the stream (gh may come from the kernel right before).
 void block_bwd(const BlockBwdArgs & a, cudaStream_t st);
 
 // ------------------------------------------------------------------------------------------

@@ -242,18 +242,22 @@ k_block_pre_v(const float * __restrict__ x, int ldx, const float * __restrict__ 
               const float * __restrict__ ln_w, const float * __restrict__ ln_b, float eps0, float eps1,
               float * __restrict__ h_hi, float * __restrict__ h_lo, int ldh, LnStats * __restrict__ st0,
               LnStats * __restrict__ st1, int M, int D) {
-    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
-    if (row >= M) return;
+    // the modulation and the norm weights come from kernels that finished before this grid was launched:
+    // they are read while the preceding kernel (the producer of x) still runs
     float xv[V], sc[V], sh[V], lw[V], lb[V];
-    load_row<V>(x + (size_t) row * ldx, D, lane, xv);
-    load_row<V>(mod + (size_t) row * ld_mod + sc_off, D, lane, sc);
-    load_row<V>(mod + (size_t) row * ld_mod + sh_off, D, lane, sh);
-    if (ln_w) load_row<V>(ln_w, D, lane, lw);
 #pragma unroll
     for (int k = 0; k < V; k++) lb[k] = 0.0f;
-    if (ln_b) load_row<V>(ln_b, D, lane, lb);
+    if (row < M) {
+        load_row<V>(mod + (size_t) row * ld_mod + sc_off, D, lane, sc);
+        load_row<V>(mod + (size_t) row * ld_mod + sh_off, D, lane, sh);
+        if (ln_w) load_row<V>(ln_w, D, lane, lw);
+        if (ln_b) load_row<V>(ln_b, D, lane, lb);
+    }
+    pdl_enter();
+    if (row >= M) return;
+    load_row<V>(x + (size_t) row * ldx, D, lane, xv);
     double mean0; float inv0;
     stats_of<V>(xv, D, lane, eps0, mean0, inv0);
     if (lane == 0) st0[row] = LnStats{mean0, inv0, 0.0f};
@@ -353,31 +357,37 @@ k_layer_norm_bwd_v(const float * __restrict__ gy, int ldgy, const float * __rest
 
 template <int V>
 __global__ void __launch_bounds__(32 * FAST_ROWS) k_block_bwd_v(BlockBwdArgs a) {
-    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
-    if (row >= a.M) return;
     const int D = a.D;
-    const LnStats s0 = a.st0[row];
-    // every load of the row up front (the struct's pointers may alias as far as the compiler knows)
+    // every load of the row up front (the struct's pointers may alias as far as the compiler knows). All but
+    // gh were written at least two kernels earlier in the stream (the forward pass, the modulation, the
+    // residual gradient of the half above), by grids that finished before this one was launched: they are
+    // read while the preceding kernel (the producer of gh) still runs.
     float gz[V], xh[V], sc[V], z[V], lw[V], gr[V], av[V], gt[V];
+    LnStats s0{}, s1{};
+    if (row < a.M) {
+        s0 = a.st0[row];
+        if (a.ln_w) s1 = a.st1[row];
+        load_row<V>(a.x + (size_t) row * a.ldx, D, lane, xh);
+        load_row<V>(a.mod + (size_t) row * a.ld_mod + a.sc_off, D, lane, sc);
+        load_row<V>(a.gres + (size_t) row * a.ldres, D, lane, gr);
+        if (a.ln_w) {
+            load_row<V>(a.mod + (size_t) row * a.ld_mod + a.sh_off, D, lane, z);
+            load_row<V>(a.ln_w, D, lane, lw);
+        }
+        if (a.a2) {
+            load_row<V>(a.a2 + (size_t) row * a.lda2, D, lane, av);
+            load_row<V>(a.mod2 + (size_t) row * a.ld_mod2 + a.gate2_off, D, lane, gt);
+        }
+    }
+    pdl_enter();
+    if (row >= a.M) return;
     load_row<V>(a.gh + (size_t) row * a.ldgh, D, lane, gz);
-    load_row<V>(a.x + (size_t) row * a.ldx, D, lane, xh);
-    load_row<V>(a.mod + (size_t) row * a.ld_mod + a.sc_off, D, lane, sc);
-    load_row<V>(a.gres + (size_t) row * a.ldres, D, lane, gr);
-    if (a.ln_w) {
-        load_row<V>(a.mod + (size_t) row * a.ld_mod + a.sh_off, D, lane, z);
-        load_row<V>(a.ln_w, D, lane, lw);
-    }
-    if (a.a2) {
-        load_row<V>(a.a2 + (size_t) row * a.lda2, D, lane, av);
-        load_row<V>(a.mod2 + (size_t) row * a.ld_mod2 + a.gate2_off, D, lane, gt);
-    }
 #pragma unroll
     for (int k = 0; k < V; k++) xh[k] = xhat_of(xh[k], s0.mean, s0.inv);
     if (a.ln_w) {
         // inner ln backward: gz = ln_bwd(gh) over the ln's normalised input
-        const LnStats s1 = a.st1[row];
         double n1 = 0, n2 = 0;
 #pragma unroll
         for (int k = 0; k < V; k++) {

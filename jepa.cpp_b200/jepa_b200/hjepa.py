@@ -67,6 +67,11 @@ class Planner:
         if self.lib.jepa_b200_hjepa_set_streams(self.ctx, int(n)) != 0:
             raise RuntimeError(f"jepa_b200_hjepa_set_streams failed: {jlib.error_text()}")
 
+    def set_step_modulation(self, mode: int) -> None:
+        """0: every step's adaLN modulation kept when it fits (automatic); 1: one step at a time."""
+        if self.lib.jepa_b200_hjepa_set_step_modulation(self.ctx, int(mode)) != 0:
+            raise RuntimeError(f"jepa_b200_hjepa_set_step_modulation failed: {jlib.error_text()}")
+
     def last_ms(self) -> float:
         return self.lib.jepa_b200_last_plan_ms(self.ctx)
 

@@ -40,6 +40,7 @@ def load() -> C.CDLL:
         "jepa_b200_context_set_shard": (C.c_int, [vp, C.c_int, C.c_int, vp]),
         "jepa_b200_last_plan_ms": (C.c_double, [vp]),
         "jepa_b200_hjepa_set_streams": (C.c_int, [vp, C.c_int]),
+        "jepa_b200_hjepa_set_step_modulation": (C.c_int, [vp, C.c_int]),
         "jepa_b200_last_plan_launches": (C.c_longlong, [vp]),
         "jepa_b200_context_new": (vp, [vp, C.c_int]),
     }

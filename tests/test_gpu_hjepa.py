@@ -135,6 +135,27 @@ def test_solve_does_not_depend_on_the_stream_count(tmpdir_mod, opts):
     P.set_streams(0)
 
 
+def test_step_at_a_time_modulation_is_bit_identical(tmpdir_mod):
+    # the memory-lean mode (modulation per step, recomputed in the backward) against every step's at once:
+    # the same costs, gradients and plan, bit for bit
+    path = forged(tmpdir_mod, "q8_0")
+    P = Planner(path)
+    rng = np.random.default_rng(23)
+    s0 = rng.normal(size=64).astype(np.float32)
+    goal = rng.normal(size=(2, 64)).astype(np.float32)
+    acts = rng.uniform(-1, 1, (37, 6, 2)).astype(np.float32)
+    draws = rng.normal(size=200000).astype(np.float32)
+    plan = solve_plan(T=6, S=70, steps=6, early_stop_patience=0, cost_last_n=2)
+    out = []
+    for mode in (0, 1):
+        P.set_step_modulation(mode)
+        c, g = P.plan_cost(1, s0, goal, acts, goal_level=2, plan=dict(plan, cost_last_n=2))
+        out.append((c, g) + tuple(P.solve(1, s0, goal[:1], dict(plan, cost_last_n=1), noise=draws)[:4]))
+    for a, b in zip(out[0], out[1]):
+        assert np.array_equal(np.asarray(a), np.asarray(b))
+    P.set_step_modulation(0)
+
+
 def test_hierarchy_matches_oracle(tmpdir_mod):
     path = forged(tmpdir_mod, "f32")
     m = O.Model(path)
