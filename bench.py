@@ -180,6 +180,19 @@ def cpu_reference(path, spec, plans, S, steps, warmup, threads):
     return dt / steps   # seconds per (one grad-step of every level)
 
 
+def cpu_sample_rows(cfg: int, S: int) -> int:
+    """Candidates the host baseline evaluates per level (its cost is linear in them; the time is scaled to S):
+    the whole batch for the small configs, a slice for the large ones so that a step stays within seconds."""
+    return {3: 128, 5: 8}.get(cfg, S)
+
+
+def describe(cfg: int, spec, plans, S_gpu: int) -> str:
+    lv = spec.levels[0]
+    hz = "/".join(str(p["horizon"]) for p in plans)
+    return (f"hjepa-config{cfg}: {len(spec.levels)}-level {spec.ftype}, D{lv.embed_dim} L{lv.n_layer} F{lv.ffn_dim}, "
+            f"horizons {hz}, {S_gpu} candidates per GPU, {plans[0]['n_steps']} Adam steps per level")
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -210,18 +223,23 @@ def run_reference(args):
     with tempfile.TemporaryDirectory() as tmp:
         path, spec, plans = setup_model(args.config, os.environ.get("JEPA_BENCH_DIR", tmp))
         S = plans[0]["n_samples"]
-        per = cpu_reference(path, spec, plans, S, args.steps, args.warmup, threads)
+        Sc = cpu_sample_rows(args.config, S)
+        per = cpu_reference(path, spec, plans, Sc, args.steps, args.warmup, threads)
+        if per is not None:
+            per *= S / Sc
     base = {"metric": METRIC, "unit": UNIT, "impl": "reference", "higher_is_better": True, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "dtype": "f32", "data": "synthetic", "scaling": "weak",
-            "config": {"workload": f"hjepa-config{args.config}", "levels": len(spec.levels), "candidates": S}}
+            "steps": args.steps, "warmup": args.warmup, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong" if args.config == 5 else "weak",
+            "config": {"workload": describe(args.config, spec, plans, S), "levels": len(spec.levels), "candidates": S}}
     if per is None:
         base["unavailable"] = "oracle/_ref/libhjepa_ref.so is not built (needs the reference tree at build time)"
         print(json.dumps(base))
         return
     n_levels = len(plans)
     value = n_levels / per          # grad-steps of the config's candidates per second
-    sample = (f"{args.steps} step(s) x one gradient evaluation of each of the {n_levels} levels at S={S} "
-              f"(one Adam iteration per level), reference src/hjepa-plan.cpp via oracle/_ref, {threads} threads")
+    sample = (f"{args.steps} step(s) x one gradient evaluation of each of the {n_levels} levels at S={Sc} "
+              f"(one Adam iteration per level; time scaled to the config's {S} candidates), reference "
+              f"src/hjepa-plan.cpp via oracle/_ref, {threads} threads")
     base.update({"value": value, "ms_per_step": per * 1e3,
                  "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
                  "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -436,7 +454,10 @@ def run_ours(args):
         os.replace(path + ".tmp", path)
     if dist:
         dist.barrier()
-    S1 = plans[0]["n_samples"]
+    # configs[4] (config 5) is the strong-scaling case: the config's candidates over the GPUs; the others are
+    # weak-scaling: the config's candidates per GPU
+    strong = args.config == 5
+    S1 = plans[0]["n_samples"] // (world if strong else 1)
     S = S1 * world
     plans = [dict(p, n_samples=S) for p in plans]
     P = Planner(path, device=local)
@@ -478,7 +499,8 @@ def run_ours(args):
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dev_ms, wall = float(t[0]), float(t[1])
-    grad_steps = sum(p["n_steps"] for p in plans) * args.steps * world   # in units of the config's 256 candidates
+    # in units of the config's candidates (256 for config 2): N of them per step under weak scaling
+    grad_steps = sum(p["n_steps"] for p in plans) * args.steps * (1 if strong else world)
     value = grad_steps / (dev_ms / 1e3)
     e2e = grad_steps / wall
     peak_tf, peak_hbm, peak_kind = peaks()
@@ -492,10 +514,10 @@ def run_ours(args):
     if rank == 0:
         res = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded random-init q8_0 GGUF, N(0,1) latents, U[-1,1] candidates)",
-            "config": {"workload": f"hjepa-config{args.config}: 2-level q8_0, D384 L6 F1536, horizons 16/4, "
-                                   f"{S1} candidates per GPU, 50 Adam steps per level",
+            "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None,
+            "dtype": "f32", "data": f"synthetic (seeded random-init {spec.ftype} GGUF, N(0,1) latents, U[-1,1] candidates)",
+            "config": {"workload": describe(args.config, spec, plans, S1),
                        "candidates_total": S, "parallelism": f"candidates sharded over {world} GPU(s)",
                        "l2": "flushed (256 MiB write) before every timed step; working set > L2",
                        "arith": "3xTF32 tensor-core GEMMs (tcgen05), f32 element-wise"},
@@ -509,15 +531,19 @@ def run_ours(args):
         }
         if world == 1 and not args.no_cpu_baseline:
             try:
-                per = cpu_reference(path, spec, [dict(p, n_samples=S1) for p in plans], S1, 1, 0, os.cpu_count() or 1)
+                Sc = cpu_sample_rows(args.config, S1)
+                per = cpu_reference(path, spec, [dict(p, n_samples=Sc) for p in plans], Sc, 1, 0, os.cpu_count() or 1)
+                if per is not None:
+                    per *= S1 / Sc
             except Exception as e:   # the baseline is reported, never required
                 per = None
                 res["cpu_baseline_error"] = str(e)
             if per is not None:
                 res["cpu_baseline"] = {"value": len(plans) / per, "unit": UNIT, "cores": os.cpu_count() or 1,
                                        "kind": "reference",
-                                       "sample": "one gradient evaluation of each level at S=256 (one Adam iteration per "
-                                                 "level) with the reference's src/hjepa-plan.cpp via oracle/_ref"}
+                                       "sample": f"one gradient evaluation of each level at S={Sc} (one Adam iteration "
+                                                 f"per level; time scaled to {S1} candidates) with the reference's "
+                                                 f"src/hjepa-plan.cpp via oracle/_ref"}
     del flush
     P.close()
     if not args.no_ac:

@@ -401,9 +401,14 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
     auto count = [&](auto ** p, size_t n) { (void) p; ap.add<float>(n); };
     plan_all(count);
     {
-        // the modulation of every step at once (one GEMM each way) when it fits; else one step at a time
+        // the modulation of every step at once (one GEMM each way) when it fits; else one step at a time.
+        // Other levels' cached workspaces are released first when memory is short (a solve uses one level's).
         size_t free_b = 0, total_b = 0;
         cudaMemGetInfo(&free_b, &total_b);
+        if (ap.bytes > free_b / 10 * 9) {
+            for (auto e = ws.begin(); e != ws.end();) e = e->first / 16 != level ? ws.erase(e) : std::next(e);
+            cudaMemGetInfo(&free_b, &total_b);
+        }
         if ((force_step_mod || ap.bytes > free_b / 10 * 9) && T > 1) {
             w->step_mod = true;
             mod_rows = (size_t) S;
