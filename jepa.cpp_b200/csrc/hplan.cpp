@@ -268,7 +268,7 @@ bool HPlanner::build(const jepa_model & m) {
 // ---------------------------------------------------------------------------------------------
 // workspace
 // ---------------------------------------------------------------------------------------------
-Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, int chunk) {
+Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, int chunk, int n_chunks) {
     const int Wa = pooled_chunks(cs);
     const std::string key = std::to_string(S) + "/" + std::to_string(T) + "/" + std::to_string(cs.goal_level) + "/" +
                             std::to_string(cs.dense) + "/" + std::to_string(cs.n_goal) + "/" + std::to_string(cs.cost_last_n) +
@@ -399,38 +399,52 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
         }
     };
     auto count = [&](auto ** p, size_t n) { (void) p; ap.add<float>(n); };
-    plan_all(count);
-    {
-        // the modulation of every step at once (one GEMM each way) when it fits; else one step at a time.
-        // Other levels' cached workspaces are released first when memory is short (a solve uses one level's).
-        size_t free_b = 0, total_b = 0;
-        cudaMemGetInfo(&free_b, &total_b);
-        if (ap.bytes > free_b / 10 * 9) {
-            for (auto e = ws.begin(); e != ws.end();) e = e->first / 16 != level ? ws.erase(e) : std::next(e);
-            cudaMemGetInfo(&free_b, &total_b);
-        }
-        if ((force_step_mod || ap.bytes > free_b / 10 * 9) && T > 1) {
-            w->step_mod = true;
-            mod_rows = (size_t) S;
-            ap = ArenaPlan();
-            plan_all(count);
-        }
-    }
-    ap.add<LnStats>((size_t) T * NL * S * 4 + (size_t) T * S);
-    for (size_t i = 0; i < w->enc.size(); i++) ap.add<LnStats>((size_t) w->enc[i].n * S * 2);
-    ap.add<float>((size_t) 2 * 4096);      // Adam schedule
-    ap.add<int>(4);
-    ap.add<void *>((size_t) 2 * (T + 1));  // cost pointer tables
-    if (ae) {   // carved in this order below
-        const size_t n = (size_t) Wa * S;
-        ap.add<LnStats>(n);
-        if (ae->kind == 2) {
+    auto plan_total = [&]() -> size_t {   // bytes of the whole carve, in the order it is carved below
+        ap = ArenaPlan();
+        plan_all(count);
+        ap.add<LnStats>((size_t) T * NL * S * 4 + (size_t) T * S);
+        for (size_t i = 0; i < w->enc.size(); i++) ap.add<LnStats>((size_t) w->enc[i].n * S * 2);
+        ap.add<float>((size_t) 2 * 4096);      // Adam schedule
+        ap.add<int>(4);
+        ap.add<void *>((size_t) 2 * (T + 1));  // cost pointer tables
+        if (ae) {
+            const size_t n = (size_t) Wa * S;
             ap.add<LnStats>(n);
-            for (size_t b = 0; b < 2 * ae->blocks.size(); b++) ap.add<LnStats>(n * (size_t) pw.G);
+            if (ae->kind == 2) {
+                ap.add<LnStats>(n);
+                for (size_t b = 0; b < 2 * ae->blocks.size(); b++) ap.add<LnStats>(n * (size_t) pw.G);
+            }
+            ap.add<void *>((size_t) Wa); ap.add<void *>((size_t) Wa);
         }
-        ap.add<void *>((size_t) Wa); ap.add<void *>((size_t) Wa);
+        return ap.bytes + 65536;
+    };
+    auto evict_other_levels = [&]() {   // a solve uses one level's workspaces at a time
+        for (auto e = ws.begin(); e != ws.end();) e = e->first / 16 != level ? ws.erase(e) : std::next(e);
+    };
+    auto to_step_mod = [&]() {
+        w->step_mod = true;
+        mod_rows = (size_t) S;
+        return plan_total();
+    };
+    // The modulation of every step at once (one GEMM each way) when it fits -- this workspace and the ones of
+    // the level's candidate streams still to be planned (about the same size each) -- else one step at a time.
+    // Other levels' cached workspaces are released first when memory is short.
+    const size_t left = (size_t) std::max(1, n_chunks - chunk);
+    size_t need = plan_total();
+    size_t free_b = 0, total_b = 0;
+    cudaMemGetInfo(&free_b, &total_b);
+    if (need * left > free_b / 10 * 9) {
+        evict_other_levels();
+        cudaMemGetInfo(&free_b, &total_b);
     }
-    if (!w->arena.reserve(ap.bytes + 65536, ctx->device)) return nullptr;
+    if ((force_step_mod || need * left > free_b / 10 * 9) && T > 1) need = to_step_mod();
+    bool got = w->arena.reserve(need, ctx->device);
+    if (!got) {   // the free figure is not one allocatable block: release, then fall back to one step at a time
+        evict_other_levels();
+        got = w->arena.reserve(need, ctx->device);
+        if (!got && !w->step_mod && T > 1) got = w->arena.reserve(to_step_mod(), ctx->device);
+    }
+    if (!got) return nullptr;
     auto take = [&](auto ** p, size_t n) { *p = (std::remove_pointer_t<decltype(p)>) w->arena.take<float>(n); };
     plan_all(take);
     w->sta0 = w->arena.take<LnStats>((size_t) T * NL * S);

@@ -184,7 +184,8 @@ struct HPlanner {
 
     ~HPlanner();
     bool build(const jepa_model & m);
-    Workspace * workspace(int level, int S, int T, const CostSpec & cs, int chunk = 0);
+    // chunk c of n_chunks candidate streams of one level (created in order; n_chunks sizes the memory decision)
+    Workspace * workspace(int level, int S, int T, const CostSpec & cs, int chunk = 0, int n_chunks = 1);
     int streams_for(int S) const;
     bool ensure_streams(int n);
     // costs [S] and (optionally) grad [S][T][A] of host actions; all host buffers

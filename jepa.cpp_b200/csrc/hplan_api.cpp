@@ -237,7 +237,7 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
     std::vector<Workspace *> wc((size_t) nc);
     std::string gens;
     for (int c = 0; c < nc; c++) {
-        wc[(size_t) c] = workspace(cs.level, cr[(size_t) c + 1] - cr[(size_t) c], T, cs, c);
+        wc[(size_t) c] = workspace(cs.level, cr[(size_t) c + 1] - cr[(size_t) c], T, cs, c, nc);
         if (!wc[(size_t) c] || !cost_tables(*wc[(size_t) c], cs)) return -1;
         gens += std::to_string(wc[(size_t) c]->gen) + ",";
     }
