@@ -91,7 +91,5 @@ int jepa_hjepa_embed(jepa_context *, const float *, const float *, int, jepa_out
 int jepa_hjepa_lift(jepa_context *, int, const float *, int, jepa_output *) { return unsupported("jepa_hjepa_lift"); }
 int jepa_hjepa_action_embed(jepa_context *, int, const float *, int, jepa_output *) { return unsupported("jepa_hjepa_action_embed"); }
 int jepa_hjepa_action_encode(jepa_context *, int, const float *, int, jepa_output *) { return unsupported("jepa_hjepa_action_encode"); }
-int jepa_hjepa_predict(jepa_context *, int, const float *, const float *, int, jepa_output *) { return unsupported("jepa_hjepa_predict"); }
-int jepa_hjepa_rollout(jepa_context *, int, const float *, int, const float *, int, int, float *) { return unsupported("jepa_hjepa_rollout"); }
 
 }  // extern "C"

@@ -110,6 +110,18 @@ struct Uploader {
         finish(L);
         return L;
     }
+    // rows [row0, row0 + rows) of a linear as f32 w (+ bias) only, for the SIMT products of a handful of rows
+    DLin lin_plain(const std::string & name, int64_t row0, int64_t rows) {
+        DLin L;
+        const gguf_tensor * t = m.get(name + ".weight");
+        if (!t || !ok) return L;
+        L.in = (int) t->ne[0];
+        L.out = (int) rows;
+        L.w = alloc<float>((size_t) L.in * L.out);
+        if (!L.w || !dequant_into(t, row0, rows, L.w)) return DLin();
+        if (m.get(name + ".bias")) L.b = vec(name + ".bias", row0, rows);
+        return L;
+    }
     DLin lin(const std::string & name, int64_t row0 = 0, int64_t rows = -1) {
         DLin L;
         const gguf_tensor * t = m.get(name + ".weight");
@@ -165,6 +177,46 @@ bool HPlanner::ensure_streams(int n) {
 Workspace::~Workspace() {
     if (g_iter) cudaGraphExecDestroy(g_iter);
     if (g_fwd) cudaGraphExecDestroy(g_fwd);
+}
+
+// the multi-frame predictor's extra weights (the query / key rows of every block, every position row), and
+// its buffers, on first use
+bool HPlanner::ensure_predict(int level) {
+    DLevel & L = levels[(size_t) level - 1];
+    if (!L.pos_all) {
+        Uploader up{*this, *ctx->model, ctx->stream};
+        const std::string p = "lvl." + std::to_string(level) + ".";
+        L.pos_all = up.vec(p + "pred.pos_embed");
+        for (int i = 0; i < L.L && up.ok; i++)
+            L.blocks[(size_t) i].qk = up.lin_plain(p + "pred.blk." + std::to_string(i) + ".attn_qkv", 0, 2 * (int64_t) L.I);
+        if (!up.ok || !L.pos_all) { L.pos_all = nullptr; log("jepa: hjepa predictor: could not place its weights on the device\n"); return false; }
+    }
+    int rows = 1, heads = 1;
+    size_t width = 1;
+    for (const DLevel & V : levels) {
+        rows = std::max(rows, V.hp.pred_n_frames);
+        heads = std::max(heads, V.hp.pred_n_head);
+        width = std::max({width, (size_t) V.D, (size_t) V.P, (size_t) V.F, (size_t) 3 * V.I, (size_t) 6 * V.P,
+                          (size_t) V.A, (size_t) V.E, (size_t) V.C});
+        for (const DLin * l : {&V.act0, &V.pact0, &V.proj0, &V.out_proj}) if (*l) width = std::max(width, (size_t) l->out);
+    }
+    if (pred.rows >= rows && pred.width >= width && pred.heads >= heads) return true;
+    ArenaPlan ap;
+    for (int i = 0; i < 18; i++) ap.add<float>((size_t) rows * width);
+    ap.add<float>((size_t) rows * rows * heads);   // attention probabilities [T][heads][T]
+    ap.add<LnStats>((size_t) rows); ap.add<LnStats>((size_t) rows);
+    if (!pred.arena.reserve(ap.bytes + 4096, ctx->device)) return false;
+    float ** bufs[] = {&pred.xa, &pred.x, &pred.xm, &pred.c, &pred.cc, &pred.cs, &pred.t1, &pred.t2, &pred.mod,
+                       &pred.hhi, &pred.hlo, &pred.qkv, &pred.o, &pred.a, &pred.u, &pred.g, &pred.y};
+    for (float ** b : bufs) *b = pred.arena.take<float>((size_t) rows * width);
+    (void) pred.arena.take<float>((size_t) rows * width);
+    pred.probs = pred.arena.take<float>((size_t) rows * rows * heads);
+    pred.st0 = pred.arena.take<LnStats>((size_t) rows);
+    pred.st1 = pred.arena.take<LnStats>((size_t) rows);
+    pred.rows = rows;
+    pred.width = width;
+    pred.heads = heads;
+    return pred.st1 != nullptr;
 }
 
 bool HPlanner::build(const jepa_model & m) {

@@ -26,6 +26,7 @@ struct DLin {
 
 struct DBlock {
     DLin v, out, up, down;
+    DLin qk;    // the query and key rows of the fused qkv, f32 only: the multi-frame predictor (loaded on first use)
     DLin ov;    // out(V(h)) composed: W_out W_v, W_out b_v + b_out (one query over one key: attention is V)
     float * ln1_w = nullptr, * ln1_b = nullptr, * ln2_w = nullptr, * ln2_b = nullptr;
 };
@@ -63,6 +64,19 @@ struct DLevel {
     float * enc_in_w = nullptr, * enc_in_b = nullptr, * enc_out_w = nullptr, * enc_out_b = nullptr;
     DLin enc_fc1, enc_fc2;
     std::vector<float> queue;         // host: recorded latent actions [n][A]
+    float * pos_all = nullptr;        // every row of pred.pos_embed [n_frames][D] (multi-frame predictor, on first use)
+};
+
+// Device buffers of the multi-frame predictor (jepa_hjepa_predict / _rollout): T <= the largest
+// pred_n_frames rows, each buffer as wide as the widest activation of any level.
+struct PredWs {
+    Arena arena;
+    int rows = 0, heads = 0;
+    size_t width = 0;
+    float * xa = nullptr, * x = nullptr, * xm = nullptr, * c = nullptr, * cc = nullptr, * cs = nullptr;
+    float * t1 = nullptr, * t2 = nullptr, * mod = nullptr, * hhi = nullptr, * hlo = nullptr, * qkv = nullptr;
+    float * o = nullptr, * a = nullptr, * u = nullptr, * g = nullptr, * y = nullptr, * probs = nullptr;
+    LnStats * st0 = nullptr, * st1 = nullptr;
 };
 
 // Device buffers of one encoder application in the goal-projection chain.
@@ -196,6 +210,10 @@ struct HPlanner {
     int forward(Workspace & w, const CostSpec & cs, bool want_grad);
     int backward(Workspace & w, const CostSpec & cs);
     bool cost_tables(Workspace & w, const CostSpec & cs);
+    // the multi-frame predictor: causal attention over T <= pred_n_frames frames of one sequence
+    PredWs pred;
+    bool ensure_predict(int level);
+    int predict_dev(int level, const float * states, const float * actions, int T, float * out, cudaStream_t st);
     int step_modulation(Workspace & w, int t0, int nt);       // mod of steps [t0, t0 + nt)
     int step_modulation_bwd(Workspace & w, int t0, int nt);   // dcs of steps [t0, t0 + nt) from dmod
     int pooled_chunks(const CostSpec & cs) const;     // Wa: chunks the action cost compares (0 = no action cost)
@@ -206,5 +224,8 @@ struct HPlanner {
     int lin_bwd(const DLin & L, const float * dy, int lddy, const float * dy_hi, const float * dy_lo, int M, float * dx, int lddx,
                 Workspace & w);
 };
+
+// the context's H-JEPA planner, built on first use (weights on the device); null after logging
+HPlanner * hplanner_of(jepa_context * ctx, const char * fn);
 
 }  // namespace jb

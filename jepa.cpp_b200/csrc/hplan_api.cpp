@@ -166,24 +166,6 @@ CostSpec spec_from(int level, int horizon, const float * state, const jepa_hjepa
     return cs;
 }
 
-HPlanner * planner_of(jepa_context * ctx, const char * fn) {
-    if (!ctx->model->hj.present) {
-        log("jepa: %s: '%s' is not an H-JEPA model (jepa.family = '%s')\n", fn, ctx->model->name.c_str(), ctx->model->family.c_str());
-        return nullptr;
-    }
-    if (!ctx->hplan) {
-        cudaSetDevice(ctx->device);
-        auto p = std::make_unique<HPlanner>();
-        p->ctx = ctx;
-        if (!p->build(*ctx->model)) {
-            log("jepa: %s: could not place the planner's weights on CUDA device %d\n", fn, ctx->device);
-            return nullptr;
-        }
-        ctx->hplan = std::move(p);
-    }
-    cudaSetDevice(ctx->device);
-    return ctx->hplan.get();
-}
 
 // stable_worldmodel.solver.decreasing_horizon_schedule (reference: src/hjepa-plan.cpp:1042-1059)
 std::vector<int> decreasing_schedule(int num_calls, int horizon) {
@@ -206,6 +188,26 @@ std::vector<int> decreasing_schedule(int num_calls, int horizon) {
 }
 
 }  // namespace
+
+// the context's planner, built on first use (weights on the device)
+HPlanner * hplanner_of(jepa_context * ctx, const char * fn) {
+    if (!ctx->model->hj.present) {
+        log("jepa: %s: '%s' is not an H-JEPA model (jepa.family = '%s')\n", fn, ctx->model->name.c_str(), ctx->model->family.c_str());
+        return nullptr;
+    }
+    if (!ctx->hplan) {
+        cudaSetDevice(ctx->device);
+        auto p = std::make_unique<HPlanner>();
+        p->ctx = ctx;
+        if (!p->build(*ctx->model)) {
+            log("jepa: %s: could not place the planner's weights on CUDA device %d\n", fn, ctx->device);
+            return nullptr;
+        }
+        ctx->hplan = std::move(p);
+    }
+    cudaSetDevice(ctx->device);
+    return ctx->hplan.get();
+}
 
 // ---------------------------------------------------------------------------------------------
 // one level's solve
@@ -444,7 +446,7 @@ extern "C" {
 
 int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n) {
     if (!ctx || n < 0 || n > 8) { log("jepa: jepa_b200_hjepa_set_streams: a context and 0..8 streams are required\n"); return -1; }
-    HPlanner * pm = planner_of(ctx, "jepa_b200_hjepa_set_streams");
+    HPlanner * pm = hplanner_of(ctx, "jepa_b200_hjepa_set_streams");
     if (!pm) return -1;
     pm->n_streams = n;
     return 0;
@@ -452,7 +454,7 @@ int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n) {
 
 int jepa_b200_hjepa_set_step_modulation(jepa_context * ctx, int mode) {
     if (!ctx || mode < 0 || mode > 1) { log("jepa: jepa_b200_hjepa_set_step_modulation: a context and mode 0 or 1 are required\n"); return -1; }
-    HPlanner * pm = planner_of(ctx, "jepa_b200_hjepa_set_step_modulation");
+    HPlanner * pm = hplanner_of(ctx, "jepa_b200_hjepa_set_step_modulation");
     if (!pm) return -1;
     if (pm->force_step_mod != (mode == 1)) pm->ws.clear();   // workspaces are planned for one mode
     pm->force_step_mod = mode == 1;
@@ -485,7 +487,7 @@ int jepa_hjepa_plan_cost(jepa_context * ctx, int level, const float * state, con
                          const jepa_hjepa_level_plan * plan, const float * actions, int n_samples, int horizon,
                          float * costs, float * grad) {
     if (!ctx || !state || !goal || !actions || !costs || n_samples < 1) return -1;
-    HPlanner * pm = planner_of(ctx, "jepa_hjepa_plan_cost");
+    HPlanner * pm = hplanner_of(ctx, "jepa_hjepa_plan_cost");
     if (!pm) return -1;
     const CostSpec cs = spec_from(level, horizon, state, goal, plan);
     if (!check_spec(*pm, cs, "jepa_hjepa_plan_cost")) return -1;
@@ -496,7 +498,7 @@ int jepa_hjepa_solve(jepa_context * ctx, int level, const float * state, const j
                      const jepa_hjepa_level_plan * plan, jepa_randn_fn randn, void * randn_user, float * actions,
                      float * states, float * cost, int * iters) {
     if (!ctx || !state || !goal || !plan || !actions) return -1;
-    HPlanner * pm = planner_of(ctx, "jepa_hjepa_solve");
+    HPlanner * pm = hplanner_of(ctx, "jepa_hjepa_solve");
     if (!pm) return -1;
     const CostSpec cs = spec_from(level, plan->horizon, state, goal, plan);
     if (!check_spec(*pm, cs, "jepa_hjepa_solve")) return -1;
@@ -566,7 +568,7 @@ int jepa_hjepa_plan(jepa_context * ctx, const float * const * states, const floa
                     const jepa_hjepa_level_plan * levels, int n_levels, jepa_randn_fn randn, void * randn_user,
                     float * actions, jepa_hjepa_plan_info * info) {
     if (!ctx || !states || !goals || !levels || !actions) return -1;
-    HPlanner * pm = planner_of(ctx, "jepa_hjepa_plan");
+    HPlanner * pm = hplanner_of(ctx, "jepa_hjepa_plan");
     if (!pm) return -1;
     if (n_levels != (int) pm->levels.size()) {
         log("jepa: jepa_hjepa_plan: %d level plans for a model with %zu levels\n", n_levels, pm->levels.size());

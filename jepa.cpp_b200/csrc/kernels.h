@@ -140,7 +140,11 @@ void pool_chunks(float * e, float * x, int Wa, int S, int stride, int E, bool ba
 void pool_tokens(float * z, const float * pos, float * X, int Wa, int S, int stride, int d, bool back, cudaStream_t st);
 size_t group_mha_smem(int G, int d, int H, bool backward);
 bool group_mha_prepare(int G, int d, int H);   // false: the group does not fit one CTA's shared memory
-void group_mha_fwd(const float * qkv, float * o, float * probs, int n_groups, int G, int d, int H, cudaStream_t st);
+void group_mha_fwd(const float * qkv, float * o, float * probs, int n_groups, int G, int d, int H, cudaStream_t st,
+                   bool causal = false);
+// y = x + a * gate (the adaLN gated residual), element-wise over M rows of N
+void gated_add(const float * x, int ldx, const float * a, int lda, const float * gate, int ld_gate, float * y, int ldy,
+               int M, int N, cudaStream_t st);
 void group_mha_bwd(const float * go, const float * qkv, const float * probs, float * gqkv, int n_groups, int G, int d, int H,
                    cudaStream_t st);
 

@@ -60,7 +60,7 @@ __global__ void k_pool_tokens(float * __restrict__ z, const float * __restrict__
 
 // One CTA per group of G token rows. qkv [rows][3 d] = [q | k | v]; o [rows][d]; probs [rows][H][G].
 __global__ void k_group_mha_fwd(const float * __restrict__ qkv, float * __restrict__ o, float * __restrict__ probs, int G,
-                                int d, int H, float scale) {
+                                int d, int H, float scale, int causal) {
     extern __shared__ float sm[];
     float * sq = sm;                              // [G][3 d]
     float * sp = sm + (size_t) G * 3 * d;         // [G][H][G]
@@ -72,8 +72,9 @@ __global__ void k_group_mha_fwd(const float * __restrict__ qkv, float * __restri
         const int h = pr / G, i = pr % G;
         const float * q = sq + (size_t) i * 3 * d + h * hd;
         float * p = sp + ((size_t) i * H + h) * G;
+        const int nk = causal ? i + 1 : G;   // causal: query i sees keys 0..i (a masked key has probability 0)
         float mx = -INFINITY;
-        for (int j = 0; j < G; j++) {
+        for (int j = 0; j < nk; j++) {
             const float * k = sq + (size_t) j * 3 * d + d + h * hd;
             float s = 0.0f;
             for (int c = 0; c < hd; c++) s += q[c] * k[c];
@@ -81,8 +82,9 @@ __global__ void k_group_mha_fwd(const float * __restrict__ qkv, float * __restri
             mx = fmaxf(mx, p[j]);
         }
         float sum = 0.0f;
-        for (int j = 0; j < G; j++) { p[j] = expf(p[j] - mx); sum += p[j]; }
-        for (int j = 0; j < G; j++) p[j] = p[j] / sum;
+        for (int j = 0; j < nk; j++) { p[j] = expf(p[j] - mx); sum += p[j]; }
+        for (int j = 0; j < nk; j++) p[j] = p[j] / sum;
+        for (int j = nk; j < G; j++) p[j] = 0.0f;
         float * out = o + (g0 + i) * d + h * hd;
         for (int c = 0; c < hd; c++) {
             float acc = 0.0f;
@@ -172,14 +174,26 @@ size_t group_mha_smem(int G, int d, int H, bool backward) {
 bool group_mha_prepare(int G, int d, int H) {
     const size_t f = group_mha_smem(G, d, H, false), b = group_mha_smem(G, d, H, true);
     if (b > 227 * 1024) return false;
-    return cudaFuncSetAttribute(k_group_mha_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) f) == cudaSuccess &&
-           cudaFuncSetAttribute(k_group_mha_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) b) == cudaSuccess;
+    // the opt-in limit only ever grows (per device), so a smaller group never lowers it under a larger one
+    static size_t set_f[64] = {}, set_b[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return false;
+    if (f > set_f[dev]) {
+        if (cudaFuncSetAttribute(k_group_mha_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) f) != cudaSuccess) return false;
+        set_f[dev] = f;
+    }
+    if (b > set_b[dev]) {
+        if (cudaFuncSetAttribute(k_group_mha_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) b) != cudaSuccess) return false;
+        set_b[dev] = b;
+    }
+    return true;
 }
 
-void group_mha_fwd(const float * qkv, float * o, float * probs, int n_groups, int G, int d, int H, cudaStream_t st) {
+void group_mha_fwd(const float * qkv, float * o, float * probs, int n_groups, int G, int d, int H, cudaStream_t st, bool causal) {
     if (n_groups <= 0) return;
     const float scale = 1.0f / std::sqrt((float) (d / H));
-    k_group_mha_fwd<<<n_groups, 128, group_mha_smem(G, d, H, false), st>>>(qkv, o, probs, G, d, H, scale);
+    k_group_mha_fwd<<<n_groups, 128, group_mha_smem(G, d, H, false), st>>>(qkv, o, probs, G, d, H, scale, causal ? 1 : 0);
 }
 
 void group_mha_bwd(const float * go, const float * qkv, const float * probs, float * gqkv, int n_groups, int G, int d, int H,

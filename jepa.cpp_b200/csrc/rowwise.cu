@@ -507,6 +507,14 @@ __global__ void k_act_bwd(const float * __restrict__ gy, int ldgy, const float *
     *o = accumulate ? *o + v : v;
 }
 
+__global__ void k_gated_add(const float * __restrict__ x, int ldx, const float * __restrict__ a, int lda,
+                            const float * __restrict__ gate, int ld_gate, float * __restrict__ y, int ldy, int M, int N) {
+    const size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t) M * N) return;
+    const int r = (int) (idx / N), c = (int) (idx % N);
+    y[(size_t) r * ldy + c] = x[(size_t) r * ldx + c] + a[(size_t) r * lda + c] * gate[(size_t) r * ld_gate + c];
+}
+
 __global__ void k_add_inplace(float * __restrict__ y, int ldy, const float * __restrict__ x, int ldx, int M, int N) {
     const size_t idx = (size_t) blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (size_t) M * N) return;
@@ -726,6 +734,12 @@ void act_bwd(const float * gy, int ldgy, const float * x, int ldx, float * gx, i
              bool accumulate, cudaStream_t st) {
     const size_t n = (size_t) M * N;
     if (n) k_act_bwd<<<blocks_for(n), 256, 0, st>>>(gy, ldgy, x, ldx, gx, ldgx, M, N, act, accumulate ? 1 : 0);
+}
+
+void gated_add(const float * x, int ldx, const float * a, int lda, const float * gate, int ld_gate, float * y, int ldy,
+               int M, int N, cudaStream_t st) {
+    const size_t n = (size_t) M * N;
+    if (n) k_gated_add<<<blocks_for(n), 256, 0, st>>>(x, ldx, a, lda, gate, ld_gate, y, ldy, M, N);
 }
 
 void add_inplace(float * y, int ldy, const float * x, int ldx, int M, int N, cudaStream_t st) {

@@ -13,6 +13,10 @@ from . import capi
 from . import lib as jlib
 
 
+class _Output(C.Structure):
+    _fields_ = [("data", capi.FP), ("n_tokens", C.c_int64), ("dim", C.c_int64)]
+
+
 class Planner:
     def __init__(self, path: str, device: int = -1, verbose: bool = False):
         self.lib = L = jlib.load()
@@ -61,6 +65,33 @@ class Planner:
         buf = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
         if self.lib.jepa_b200_context_set_shard(self.ctx, rank, world, buf) != 0:
             raise RuntimeError(f"jepa_b200_context_set_shard failed: {jlib.error_text()}")
+
+    def predict(self, level: int, states, actions) -> np.ndarray:
+        """jepa_hjepa_predict: states [T, D], actions [T, A] -> [T, D_out], row t predicted after frames 0..t."""
+        states = np.ascontiguousarray(states, np.float32)
+        actions = np.ascontiguousarray(actions, np.float32)
+        out = _Output()
+        fn = self.lib.jepa_hjepa_predict
+        fn.argtypes = [C.c_void_p, C.c_int, capi.FP, capi.FP, C.c_int, C.POINTER(_Output)]
+        if fn(self.ctx, level, capi.fptr(states), capi.fptr(actions), states.shape[0], C.byref(out)) != 0:
+            raise RuntimeError(f"jepa_hjepa_predict failed: {jlib.error_text()}")
+        try:
+            res = np.ctypeslib.as_array(out.data, shape=(out.n_tokens * out.dim,)).copy()
+        finally:
+            self.lib.jepa_free.argtypes = [C.c_void_p]
+            self.lib.jepa_free(C.cast(out.data, C.c_void_p))
+        return res.reshape(out.n_tokens, out.dim)
+
+    def rollout(self, level: int, seeds, actions, n_steps: int, history: int) -> np.ndarray:
+        """jepa_hjepa_rollout: seeds [n_seed, D], actions [n_seed + n_steps - 1, A] -> [n_steps, D]."""
+        seeds = np.ascontiguousarray(np.atleast_2d(seeds), np.float32)
+        actions = np.ascontiguousarray(actions, np.float32)
+        out = np.zeros((n_steps, seeds.shape[1]), np.float32)
+        fn = self.lib.jepa_hjepa_rollout
+        fn.argtypes = [C.c_void_p, C.c_int, capi.FP, C.c_int, capi.FP, C.c_int, C.c_int, capi.FP]
+        if fn(self.ctx, level, capi.fptr(seeds), seeds.shape[0], capi.fptr(actions), n_steps, history, capi.fptr(out)) != 0:
+            raise RuntimeError(f"jepa_hjepa_rollout failed: {jlib.error_text()}")
+        return out
 
     def set_streams(self, n: int) -> None:
         """Candidate streams of the solves (0 = automatic); results do not depend on it."""

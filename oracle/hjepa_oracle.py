@@ -94,6 +94,7 @@ class LevelW:
     ae_headln_w: Optional[np.ndarray] = None
     ae_headln_b: Optional[np.ndarray] = None
     queue: Optional[np.ndarray] = None
+    pos_all: Optional[np.ndarray] = None        # every row of pred.pos_embed (the multi-frame predictor)
 
 
 class Model:
@@ -116,6 +117,7 @@ class Model:
             p = f"lvl.{li + 1}."
             inner = hp["pred_n_head"] * hp["pred_head_dim"]
             L = LevelW(hp=hp, pos0=T[p + "pred.pos_embed"][0].copy())
+            L.pos_all = T[p + "pred.pos_embed"].copy()
             L.act0, L.act2 = self.lin(p + "act_embed.0"), self.lin(p + "act_embed.2")
             L.pact0, L.pact2 = self.lin(p + "pred.act_embed.0"), self.lin(p + "pred.act_embed.2")
             L.in_proj, L.cond_proj = self.lin(p + "pred.in_proj"), self.lin(p + "pred.cond_proj")
@@ -127,6 +129,7 @@ class Model:
                 L.blocks.append(dict(
                     adaln=self.lin(q + "adaln"),
                     v=self.lin(q + "attn_qkv", 2 * inner, inner),      # the value third (hjepa-plan.cpp:170-171)
+                    qk=self.lin(q + "attn_qkv", 0, 2 * inner),        # query / key rows (the multi-frame predictor)
                     out=self.lin(q + "attn_out"), up=self.lin(q + "ffn_up"), down=self.lin(q + "ffn_down"),
                     ln1_w=T.get(q + "ln1.weight"), ln1_b=T.get(q + "ln1.bias"),
                     ln2_w=T.get(q + "ln2.weight"), ln2_b=T.get(q + "ln2.bias")))
@@ -705,3 +708,72 @@ def replay(draws):
         pos[0] += k
         return out
     return fn
+
+
+# ---------------------------------------------------------------------------------------------
+# the multi-frame predictor: jepa_hjepa_predict / jepa_hjepa_rollout (src/hjepa.cpp:566-667) over the
+# adaLN-zero transformer jepa_build_adaln (src/lewm.cpp:33-95): causal softmax attention across frames
+# ---------------------------------------------------------------------------------------------
+def causal_attention(q, k, v, n_head):
+    """Per head softmax(q k^T / sqrt(hd)) v with keys 0..t for query t (jepa_causal_mask_f16, src/lewm.cpp:97-103)."""
+    T_, inner = q.shape
+    hd = inner // n_head
+    split = lambda x: x.reshape(T_, n_head, hd).transpose(1, 0, 2)
+    qh, kh, vh = split(q), split(k), split(v)
+    s = (qh @ kh.transpose(0, 2, 1)).astype(f32) * f32(1.0 / math.sqrt(hd))
+    s = np.where(np.triu(np.ones((T_, T_), bool), 1)[None], -np.inf, s).astype(f32)
+    e = np.exp((s - s.max(-1, keepdims=True)).astype(f32)).astype(f32)
+    p = (e / e.sum(-1, keepdims=True, dtype=f32)).astype(f32)
+    return (p @ vh).astype(f32).transpose(1, 0, 2).reshape(T_, inner)
+
+
+def predict(m: Model, level: int, states, actions):
+    """states [T][D], actions [T][A] -> [T][D_out]; row t is the state predicted after frames 0..t."""
+    L = m.levels[level - 1]
+    T_ = states.shape[0]
+    D = L.hp["pred_dim"] or L.hp["embed_dim"]
+    c, _ = act_embed_fwd(L, np.asarray(actions, f32))
+    if L.pact0 is not None:
+        c = L.pact2(act_fwd(L.pact0(c), "silu"))
+    x = (np.asarray(states, f32) + L.pos_all[:T_]).astype(f32)
+    if L.in_proj is not None:
+        x = L.in_proj(x)
+    if L.cond_proj is not None:
+        c = L.cond_proj(c)
+    cs = act_fwd(c, "silu")
+    P = x.shape[1]
+    for B in L.blocks:
+        mod = B["adaln"](cs)
+        z, _ = ln_fwd(x, None, None, m.adaln_eps)
+        h = (z * (f32(1) + mod[:, P:2 * P]) + mod[:, 0:P]).astype(f32)
+        if B["ln1_w"] is not None:
+            h, _ = ln_fwd(h, B["ln1_w"], B["ln1_b"], m.ln_eps)
+        qk = B["qk"](h)
+        inner = qk.shape[1] // 2
+        o = causal_attention(qk[:, :inner], qk[:, inner:], B["v"](h), L.hp["pred_n_head"])
+        x = (x + B["out"](o) * mod[:, 2 * P:3 * P]).astype(f32)
+        z, _ = ln_fwd(x, None, None, m.adaln_eps)
+        h = (z * (f32(1) + mod[:, 4 * P:5 * P]) + mod[:, 3 * P:4 * P]).astype(f32)
+        if B["ln2_w"] is not None:
+            h, _ = ln_fwd(h, B["ln2_w"], B["ln2_b"], m.ln_eps)
+        x = (x + B["down"](act_fwd(B["up"](h), "gelu")) * mod[:, 5 * P:6 * P]).astype(f32)
+    x, _ = ln_fwd(x, L.norm_w, L.norm_b, m.ln_eps)
+    if L.out_proj is not None:
+        x = L.out_proj(x)
+    if L.proj0 is not None:
+        x = L.proj2(act_fwd(L.proj0(x), "gelu"))
+    return x
+
+
+def rollout(m: Model, level: int, seeds, actions, n_steps: int, history: int):
+    """seeds [n_seed][D], actions [n_seed + n_steps - 1][A] -> the n_steps predicted states: step j reads the
+    last `history` frames of the growing sequence (seeds, then predictions) and their actions."""
+    seq = [np.asarray(s, f32) for s in seeds]
+    out = []
+    for _ in range(n_steps):
+        have = len(seq)
+        w = min(history, have)
+        nxt = predict(m, level, np.stack(seq[have - w:have]), actions[have - w:have])[-1]
+        seq.append(nxt)
+        out.append(nxt)
+    return np.stack(out)
