@@ -87,9 +87,5 @@ int jepa_lewm_action_dim(const jepa_model *) { return 0; }
 int jepa_lewm_predict(jepa_context *, const float *, const float *, int, jepa_output *) { return unsupported("jepa_lewm_predict"); }
 int jepa_lewm_rollout(jepa_context *, const float *, int, const float *, int, float *) { return unsupported("jepa_lewm_rollout"); }
 
-int jepa_hjepa_embed(jepa_context *, const float *, const float *, int, jepa_output *) { return unsupported("jepa_hjepa_embed"); }
-int jepa_hjepa_lift(jepa_context *, int, const float *, int, jepa_output *) { return unsupported("jepa_hjepa_lift"); }
-int jepa_hjepa_action_embed(jepa_context *, int, const float *, int, jepa_output *) { return unsupported("jepa_hjepa_action_embed"); }
-int jepa_hjepa_action_encode(jepa_context *, int, const float *, int, jepa_output *) { return unsupported("jepa_hjepa_action_encode"); }
 
 }  // extern "C"

@@ -179,6 +179,18 @@ Workspace::~Workspace() {
     if (g_fwd) cudaGraphExecDestroy(g_fwd);
 }
 
+DLin HPlanner::upload_plain(const std::string & name, int64_t row0, int64_t rows) {
+    Uploader up{*this, *ctx->model, ctx->stream};
+    DLin L = up.lin_plain(name, row0, rows);
+    return up.ok ? L : DLin();
+}
+
+float * HPlanner::upload_vec(const std::string & name) {
+    Uploader up{*this, *ctx->model, ctx->stream};
+    float * v = up.vec(name);
+    return up.ok ? v : nullptr;
+}
+
 // the multi-frame predictor's extra weights (the query / key rows of every block, every position row), and
 // its buffers, on first use
 bool HPlanner::ensure_predict(int level) {

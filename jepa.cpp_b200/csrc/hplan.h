@@ -212,6 +212,15 @@ struct HPlanner {
     bool cost_tables(Workspace & w, const CostSpec & cs);
     // the multi-frame predictor: causal attention over T <= pred_n_frames frames of one sequence
     PredWs pred;
+    // the level-1 projector of the encoder's CLS row and the proprio stream (jepa_hjepa_embed), on first use
+    struct EmbedW {
+        bool loaded = false;
+        DLin proj0, proj2, pro0, pro2;
+        float * proj_ln_w = nullptr, * proj_ln_b = nullptr, * pro_ln_w = nullptr, * pro_ln_b = nullptr;
+    } emb;
+    bool ensure_embed();
+    DLin upload_plain(const std::string & name, int64_t row0, int64_t rows);   // f32 weight (+ bias) only
+    float * upload_vec(const std::string & name);
     bool ensure_predict(int level);
     int predict_dev(int level, const float * states, const float * actions, int T, float * out, cudaStream_t st);
     int step_modulation(Workspace & w, int t0, int nt);       // mod of steps [t0, t0 + nt)

@@ -82,6 +82,35 @@ class Planner:
             self.lib.jepa_free(C.cast(out.data, C.c_void_p))
         return res.reshape(out.n_tokens, out.dim)
 
+    def _output(self, fn_name: str, call) -> np.ndarray:
+        out = _Output()
+        if call(C.byref(out)) != 0:
+            raise RuntimeError(f"{fn_name} failed: {jlib.error_text()}")
+        try:
+            res = np.ctypeslib.as_array(out.data, shape=(out.n_tokens * out.dim,)).copy()
+        finally:
+            self.lib.jepa_free.argtypes = [C.c_void_p]
+            self.lib.jepa_free(C.cast(out.data, C.c_void_p))
+        return res.reshape(out.n_tokens, out.dim)
+
+    def encode_states(self, cls_rows, proprio=None) -> np.ndarray:
+        """jepa_hjepa_embed: the encoder's CLS rows [n, Dv] (and the proprio stream [n, P]) -> level-1 states."""
+        cls_rows = np.ascontiguousarray(cls_rows, np.float32)
+        pr = None if proprio is None else np.ascontiguousarray(proprio, np.float32)
+        fn = self.lib.jepa_hjepa_embed
+        fn.argtypes = [C.c_void_p, capi.FP, capi.FP, C.c_int, C.POINTER(_Output)]
+        return self._output("jepa_hjepa_embed",
+                            lambda o: fn(self.ctx, capi.fptr(cls_rows), capi.fptr(pr), cls_rows.shape[0], o))
+
+    def encoder(self, kind: str, level: int, rows) -> np.ndarray:
+        """jepa_hjepa_lift / _action_embed / _action_encode ('lift', 'action_embed', 'action_encode') of rows [n, *]."""
+        rows = np.ascontiguousarray(rows, np.float32)
+        name = {"lift": "jepa_hjepa_lift", "action_embed": "jepa_hjepa_action_embed",
+                "action_encode": "jepa_hjepa_action_encode"}[kind]
+        fn = getattr(self.lib, name)
+        fn.argtypes = [C.c_void_p, C.c_int, capi.FP, C.c_int, C.POINTER(_Output)]
+        return self._output(name, lambda o: fn(self.ctx, level, capi.fptr(rows), rows.shape[0], o))
+
     def rollout(self, level: int, seeds, actions, n_steps: int, history: int) -> np.ndarray:
         """jepa_hjepa_rollout: seeds [n_seed, D], actions [n_seed + n_steps - 1, A] -> [n_steps, D]."""
         seeds = np.ascontiguousarray(np.atleast_2d(seeds), np.float32)

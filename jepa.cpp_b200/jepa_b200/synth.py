@@ -70,6 +70,11 @@ class HJepaSpec:
     w_std: float = 0.02
     cond_std: float = 0.02         # cond_proj / adaln / act_embed init std
     name: str = "synthetic-hjepa"
+    proj_kind: str = "identity"    # level-1 projector of the encoder's CLS row: identity | mlp | layernorm
+    proj_hidden: int = 0           # mlp projector hidden width (0 = 2 enc_dim)
+    proprio_dim: int = 0           # > 0: level 1 is 'vit_proprio' (set its enc_kind), a proprio stream fused in
+    proprio_hidden: int = 32
+    proprio_out: int = 16          # width of the proprio part of the level-1 state
 
 
 def _quantizable(name: str) -> bool:
@@ -123,7 +128,9 @@ def write_hjepa(path: str, spec: HJepaSpec, seed: int = 0) -> None:
     g = _Gen(spec, seed)
     w = g.w
     L = spec.levels
-    Dv = spec.enc_dim or L[0].embed_dim
+    q_pro = spec.proprio_out if spec.proprio_dim else 0
+    pixel = L[0].embed_dim - q_pro     # the pixel part of the level-1 state
+    Dv = spec.enc_dim or pixel
     eh = spec.enc_heads or max(1, Dv // 64)
     ef = spec.enc_ffn or 4 * Dv
     w.add_kv("general.architecture", "jepa")
@@ -144,9 +151,9 @@ def write_hjepa(path: str, spec: HJepaSpec, seed: int = 0) -> None:
     w.add_kv("jepa.hjepa.n_levels", len(L))
     w.add_kv("jepa.hjepa.ln_eps", 1e-5)
     w.add_kv("jepa.hjepa.adaln_eps", 1e-6)
-    w.add_kv("jepa.hjepa.proj_kind", "identity")
-    w.add_kv("jepa.hjepa.pixel_dim", Dv)
-    w.add_kv("jepa.hjepa.proprio_dim", 0)
+    w.add_kv("jepa.hjepa.proj_kind", spec.proj_kind)
+    w.add_kv("jepa.hjepa.pixel_dim", pixel)
+    w.add_kv("jepa.hjepa.proprio_dim", spec.proprio_dim)
     w.add_kv("jepa.hjepa.raw_action_dim", L[0].action_dim)
     w.add_kv("jepa.hjepa.frameskip", 1)
     arr = {
@@ -187,6 +194,17 @@ def write_hjepa(path: str, spec: HJepaSpec, seed: int = 0) -> None:
         k = li + 1
         p = f"lvl.{k}."
         D, P, A, E = l.embed_dim, l.P(), l.action_dim, l.E()
+        if k == 1:   # the projector of the encoder's CLS row (and the proprio stream) into the level-1 state
+            if spec.proj_kind == "mlp":
+                ph = spec.proj_hidden or 2 * Dv
+                g.lin(p + "enc.proj.0", Dv, ph)
+                g.lin(p + "enc.proj.2", ph, pixel)
+            elif spec.proj_kind == "layernorm":
+                g.norm(p + "enc.proj_ln", Dv)
+            if spec.proprio_dim:
+                g.lin(p + "enc.proprio.0", spec.proprio_dim, spec.proprio_hidden)
+                g.norm(p + "enc.proprio.ln", spec.proprio_hidden)
+                g.lin(p + "enc.proprio.2", spec.proprio_hidden, q_pro)
         if k > 1:
             below = L[li - 1]
             if l.enc_kind == "latent_mlp":

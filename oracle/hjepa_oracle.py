@@ -109,6 +109,12 @@ class Model:
         n = int(g("n_levels"))
         keys = ["embed_dim", "stride", "action_dim", "act_embed_dim", "pred_dim", "pred_n_layer", "pred_n_head",
                 "pred_head_dim", "pred_ffn_dim", "pred_n_frames"]
+        # the level-1 projector of the encoder's CLS row and the proprio stream (jepa_hjepa_embed)
+        self.proj_kind = str(g("proj_kind", "identity"))
+        self.proj0, self.proj2 = self.lin("lvl.1.enc.proj.0"), self.lin("lvl.1.enc.proj.2")
+        self.proj_ln = (T.get("lvl.1.enc.proj_ln.weight"), T.get("lvl.1.enc.proj_ln.bias"))
+        self.pro0, self.pro2 = self.lin("lvl.1.enc.proprio.0"), self.lin("lvl.1.enc.proprio.2")
+        self.pro_ln = (T.get("lvl.1.enc.proprio.ln.weight"), T.get("lvl.1.enc.proprio.ln.bias"))
         self.levels = []
         for li in range(n):
             hp = {k: int(g(k)[li]) for k in keys}
@@ -777,3 +783,57 @@ def rollout(m: Model, level: int, seeds, actions, n_steps: int, history: int):
         seq.append(nxt)
         out.append(nxt)
     return np.stack(out)
+
+
+# ---------------------------------------------------------------------------------------------
+# the state and action encoders of the API: jepa_hjepa_embed / _lift / _action_embed / _action_encode
+# (src/hjepa.cpp:374-561)
+# ---------------------------------------------------------------------------------------------
+def embed(m: Model, cls, proprio=None):
+    """Level-1 states from the encoder's CLS rows [n][Dv] (and the proprio stream [n][P]): the projector
+    (mlp with GELU / layernorm / identity), then [pixel | proprio] for 'vit_proprio' (hjepa.cpp:374-414)."""
+    x = np.asarray(cls, f32)
+    if m.proj_kind == "mlp":
+        x = m.proj2(act_fwd(m.proj0(x), "gelu"))
+    elif m.proj_kind == "layernorm":
+        x, _ = ln_fwd(x, m.proj_ln[0], m.proj_ln[1], m.ln_eps)
+    if m.levels[0].hp["enc_kind"] == "vit_proprio":
+        h, _ = ln_fwd(m.pro0(np.asarray(proprio, f32)), m.pro_ln[0], m.pro_ln[1], m.ln_eps)
+        x = np.concatenate([x, m.pro2(act_fwd(h, "gelu"))], axis=1).astype(f32)
+    return x
+
+
+def lift(m: Model, level: int, below):
+    """Level-k states: the state encoder on every stride-th state of level k-1 (hjepa.cpp:416-448)."""
+    up = m.levels[level - 1]
+    x = np.ascontiguousarray(np.asarray(below, f32)[::up.hp["stride"]])
+    y, _ = encode_up_fwd(m, up, x)
+    return y
+
+
+def action_embed(m: Model, level: int, actions):
+    """The level's actions through act_embed (identity when absent) (hjepa.cpp:454-467)."""
+    e, _ = act_embed_fwd(m.levels[level - 1], np.asarray(actions, f32))
+    return e
+
+
+def action_encode(m: Model, level: int, below_emb):
+    """Latent actions of level k from the level below's action embeddings [n][E]: chunks of `stride` rows,
+    a short trailing chunk zero-padded for 'mlp' and run at its own length for 'seq' (hjepa.cpp:508-561)."""
+    up = m.levels[level - 1]
+    S = up.hp["stride"]
+    emb = np.asarray(below_emb, f32)
+    n = emb.shape[0]
+    n_out = (n + S - 1) // S
+    if up.hp["act_enc_kind"] == "mlp":
+        pad = np.zeros((n_out * S, emb.shape[1]), f32)
+        pad[:n] = emb
+        chunks = [np.ascontiguousarray(pad[i::S]) for i in range(S)]   # step i of every chunk
+        y, _ = action_pool_fwd(m, up, chunks)
+        return y
+    out = []
+    for c in range(n_out):
+        rows = emb[c * S:min(n, (c + 1) * S)]
+        y, _ = action_pool_fwd(m, up, [rows[i:i + 1] for i in range(rows.shape[0])])
+        out.append(y[0])
+    return np.stack(out).astype(f32)

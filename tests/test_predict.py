@@ -1,7 +1,8 @@
-"""The H-JEPA multi-frame predictor (jepa_hjepa_predict / jepa_hjepa_rollout) against the reference.
+"""The H-JEPA multi-frame predictor (jepa_hjepa_predict / jepa_hjepa_rollout) and the state / action encoders
+(jepa_hjepa_embed / _lift / _action_embed / _action_encode) against the reference.
 
 tests/golden/hjepa_predict_ref.npz holds outputs of the reference's executable numpy specification of these
-two entry points (scripts/jepa_convert/hjepa_numpy_ref.py, which mirrors src/hjepa.cpp:566-667) on seeded
+entry points (scripts/jepa_convert/hjepa_numpy_ref.py, which mirrors src/hjepa.cpp:566-667) on seeded
 forged models; tests/golden/make_golden_predict.py wrote it.
 
 CPU (always): the models rebuild byte for byte; the oracle restatement reproduces every case.
@@ -57,7 +58,10 @@ def oracles(models):
     return {k: O.Model(p) for k, p in models.items()}
 
 
-@pytest.mark.parametrize("case", CASES, ids=lambda c: c["key"])
+PRED = [c for c in CASES if c["kind"] in ("predict", "rollout")]
+
+
+@pytest.mark.parametrize("case", PRED, ids=lambda c: c["key"])
 def test_oracle_matches_reference(oracles, case):
     m, k = oracles[case["model"]], case["key"]
     if case["kind"] == "predict":
@@ -74,7 +78,7 @@ def planners(models):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", CASES, ids=lambda c: c["key"])
+@pytest.mark.parametrize("case", PRED, ids=lambda c: c["key"])
 def test_gpu_matches_reference(planners, case):
     P, k = planners[case["model"]], case["key"]
     if case["kind"] == "predict":
@@ -111,3 +115,34 @@ def test_gpu_predict_refuses_out_of_range(planners):
         P.rollout(1, s[:1], a[:4], 4, 5)
     with pytest.raises(RuntimeError, match="out of range"):
         P.predict(3, s[:1], a[:1])              # the model has 2 levels
+
+
+# ---------------------------------------------------------------------------------------------
+# the state and action encoders (jepa_hjepa_embed / _lift / _action_embed / _action_encode)
+# ---------------------------------------------------------------------------------------------
+ENC = [c for c in CASES if c["kind"] in ("embed", "lift", "action_embed", "action_encode")]
+
+
+def _oracle_encode(m, case):
+    k = case["key"]
+    if case["kind"] == "embed":
+        return O.embed(m, g(k, "cls"), g(k, "proprio") if case["proprio"] else None)
+    fn = {"lift": O.lift, "action_embed": O.action_embed, "action_encode": O.action_encode}[case["kind"]]
+    return fn(m, case["level"], g(k, "in"))
+
+
+@pytest.mark.parametrize("case", ENC, ids=lambda c: c["key"])
+def test_oracle_encoders_match_reference(oracles, case):
+    assert rel(_oracle_encode(oracles[case["model"]], case), g(case["key"], "out")) < 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ENC, ids=lambda c: c["key"])
+def test_gpu_encoders_match_reference(planners, case):
+    P, k = planners[case["model"]], case["key"]
+    if case["kind"] == "embed":
+        y = P.encode_states(g(k, "cls"), g(k, "proprio") if case["proprio"] else None)
+    else:
+        y = P.encoder(case["kind"], case["level"], g(k, "in"))
+    assert y.shape == g(k, "out").shape
+    assert rel(y, g(k, "out")) < 1e-4
