@@ -71,6 +71,7 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap * map, uint3
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // bias, activation and RoPE on 32 consecutive columns [col0, col0 + 32) of one output row
@@ -291,8 +292,13 @@ k_gemm_f16(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUten
                     if (row < M) epi_store_direct(ep, row, col0, N, v);
                     continue;
                 }
-                // the staging block is free once the previous store has read it
-                if (lane == 0) bulk_wait_read0();
+                // f16 blocks (2 KB) alternate between the two halves of the staging buffer, so a block is
+                // written while the previous one's store is still reading; an f32 block (4 KB) takes it whole
+                const uint32_t half_off = f16_out ? (uint32_t) ((c0 >> 5) & 1) * 2048u : 0u;
+                if (lane == 0) {
+                    if (f16_out) bulk_wait_read1();   // the store that used this half (two blocks ago) has read it
+                    else bulk_wait_read0();
+                }
                 __syncwarp();
                 if (f16_out) {
                     // 32 rows x 64 B, 64-byte swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3)
@@ -303,7 +309,7 @@ k_gemm_f16(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUten
                         u.y = pack2h(v[8 * c + 2], v[8 * c + 3]);
                         u.z = pack2h(v[8 * c + 4], v[8 * c + 5]);
                         u.w = pack2h(v[8 * c + 6], v[8 * c + 7]);
-                        *(uint4 *) (stage + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) = u;
+                        *(uint4 *) (stage + half_off + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) = u;
                     }
                 } else {
                     // 32 rows x 128 B, 128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7)
@@ -316,13 +322,14 @@ k_gemm_f16(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUten
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
+                    const uint32_t src = stage_u + half_off;
                     switch (ep.mode) {
-                        case AEPI_ADD_F32: tma_reduce_add_2d(&tO, stage_u, col0, row0); break;
-                        case AEPI_F32: tma_store_2d(&tO, stage_u, col0, remap_row(ep, row0)); break;
-                        case AEPI_GELU_F16: tma_store_2d(&tO, stage_u, col0, row0); break;
+                        case AEPI_ADD_F32: tma_reduce_add_2d(&tO, src, col0, row0); break;
+                        case AEPI_F32: tma_store_2d(&tO, src, col0, remap_row(ep, row0)); break;
+                        case AEPI_GELU_F16: tma_store_2d(&tO, src, col0, row0); break;
                         default:
-                            if (col0 < ep.D) tma_store_2d(&tO, stage_u, col0, row0);
-                            else tma_store_2d(&tKV, stage_u, col0 - ep.D, row0);
+                            if (col0 < ep.D) tma_store_2d(&tO, src, col0, row0);
+                            else tma_store_2d(&tKV, src, col0 - ep.D, row0);
                             break;
                     }
                     bulk_commit();
