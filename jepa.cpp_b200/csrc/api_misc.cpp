@@ -71,9 +71,6 @@ float * jepa_preprocess_frames_rgb_ex(const jepa_preprocess_params *, const uint
 uint8_t * jepa_load_image_rgb(const char *, int *, int *) { return unsupported_ptr<uint8_t>("jepa_load_image_rgb"); }
 void jepa_resize_antialias_u8(const uint8_t *, int, int, int, uint8_t *, int, int, int) { unsupported("jepa_resize_antialias_u8"); }
 
-int jepa_encode(jepa_context *, const jepa_input *, jepa_output *) { return unsupported("jepa_encode"); }
-int jepa_pool_mean(const jepa_model *, const jepa_output *, jepa_output *) { return unsupported("jepa_pool_mean"); }
-int jepa_pool_cls(const jepa_model *, const jepa_output *, jepa_output *) { return unsupported("jepa_pool_cls"); }
 int jepa_lewm_project(jepa_context *, const jepa_output *, jepa_output *) { return unsupported("jepa_lewm_project"); }
 int jepa_lewm_project_rows(jepa_context *, const float *, int, jepa_output *) { return unsupported("jepa_lewm_project_rows"); }
 int jepa_head(jepa_context *, const jepa_output *, jepa_output *) { return unsupported("jepa_head"); }

@@ -1,0 +1,273 @@
+// jepa_encode for the image families (hfvit, ijepa, lewm, and the encoder of an H-JEPA file), and the
+// pooling helpers of the API (reference: src/jepa.cpp:586-720, :1183-1270).
+//
+//   x = patch_embed(patches) ; tokens = [CLS][registers][patches] + pos_embed
+//   per block: x += ls1 * out(attention(qkv(LN1(x)))) ; x += ls2 * down(act(up(LN2(x))))
+//   y = LN(x)
+//
+// Every (batch, frame) slice is one sequence; a call's slices run as one batch of rows through the 3xTF32
+// tensor-core GEMMs of the planner (the residual add and the layer scale in the gated epilogue, GELU in
+// the up product's epilogue) and a float32 attention kernel. Patchifying (C-H-W inside a patch row,
+// patches h-major) happens on the host as the reference does it.
+#include "encoder.h"
+#include "upload.h"
+#include "common.h"
+
+#include "../../include/jepa.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+namespace jb {
+
+EncEngine::~EncEngine() {
+    for (void * p : allocations) cudaFree(p);
+}
+
+bool EncEngine::build(const jepa_model & m, cudaStream_t st) {
+    Uploader up{allocations, m, st};
+    const EncParams & e = m.enc;
+    const int D = e.embed_dim;
+    patch = up.lin_fwd_only("enc.patch_embed");
+    if (e.cls_token) cls = up.vec("enc.cls_token");
+    if (e.n_registers > 0) reg = up.vec("enc.reg_tokens");
+    pos = up.vec("enc.pos_embed");
+    if (const gguf_tensor * t = m.get("enc.pos_embed")) pos_rows = t->nelements() / D;
+    norm_w = up.vec("enc.norm.weight");
+    norm_b = up.vec("enc.norm.bias");
+    std::vector<float> one((size_t) D, 1.0f);
+    ones = up.alloc<float>((size_t) D);
+    if (ones) up.ok = cuda_ok(cudaMemcpy(ones, one.data(), (size_t) D * 4, cudaMemcpyHostToDevice), "encoder") && up.ok;
+    for (int i = 0; i < e.n_layer && up.ok; i++) {
+        const std::string p = "enc.blk." + std::to_string(i) + ".";
+        EncLayer L;
+        L.qkv = up.lin_fwd_only(p + "attn_qkv");
+        L.out = up.lin_fwd_only(p + "attn_out");
+        L.up = up.lin_fwd_only(p + "ffn_up");
+        L.down = up.lin_fwd_only(p + "ffn_down");
+        L.ln1_w = up.vec(p + "ln1.weight"); L.ln1_b = up.vec(p + "ln1.bias");
+        L.ln2_w = up.vec(p + "ln2.weight"); L.ln2_b = up.vec(p + "ln2.bias");
+        L.ls1 = m.get(p + "ls1") ? up.vec(p + "ls1") : ones;
+        L.ls2 = m.get(p + "ls2") ? up.vec(p + "ls2") : ones;
+        if (!(L.qkv && L.out && L.up && L.down) || L.qkv.out != 3 * D || L.qkv.in != D || L.out.out != D || L.up.in != D ||
+            L.down.out != D || L.down.in != L.up.out) {
+            log("jepa: jepa_encode: block %d is not a fused-qkv pre-norm block of width %d\n", i, D);
+            return false;
+        }
+        layers.push_back(L);
+    }
+    if (!up.ok || !patch || !pos || (e.cls_token && !cls) || (e.n_registers > 0 && !reg)) {
+        log("jepa: jepa_encode: the encoder's weights are incomplete or could not be placed on the device\n");
+        return false;
+    }
+    return true;
+}
+
+namespace {
+
+struct DevBuf {
+    void * p = nullptr;
+    ~DevBuf() { if (p) cudaFree(p); }
+    bool alloc(size_t floats) { return cuda_ok(cudaMalloc(&p, std::max<size_t>(floats, 1) * 4), "encoder buffer"); }
+    float * f() const { return (float *) p; }
+};
+
+int lin_tc(const DLin & L, const float * x_hi, const float * x_lo, int ldx, int M, GemmEpi ep, cudaStream_t st) {
+    return gemm_tc({x_hi, x_lo, ldx}, {L.w_hi, L.w_lo, L.in}, M, L.out, L.in, ep, st);
+}
+
+}  // namespace
+
+}  // namespace jb
+
+using namespace jb;
+
+extern "C" {
+
+int jepa_encode(jepa_context * ctx, const jepa_input * in, jepa_output * out) {
+    if (!ctx || !in || !out || !in->data) return -1;
+    const jepa_model & m = *ctx->model;
+    const EncParams & e = m.enc;
+    static const char * image_families[] = {"hfvit", "ijepa", "lewm", "hjepa"};
+    bool image = false;
+    for (const char * f : image_families) image = image || m.family == f;
+    if (!image) {
+        log("jepa: jepa_encode: the '%s' video encoders are not part of this engine (image families: hfvit, ijepa, lewm, hjepa)\n",
+            m.family.c_str());
+        return -1;
+    }
+    if (in->n_chans != e.in_chans) {
+        log("jepa: input has %d channels, model expects %d\n", in->n_chans, e.in_chans);
+        return -1;
+    }
+    if (in->n_batch < 1 || in->n_frames < 1 || in->height < 1 || in->width < 1) {
+        log("jepa: bad input shape [%d, %d, %d, %d, %d]\n", in->n_batch, in->n_chans, in->n_frames, in->height, in->width);
+        return -1;
+    }
+    const int P = e.patch_size;
+    if (in->height % P != 0 || in->width % P != 0) {
+        log("jepa: input %dx%d is not a multiple of the patch size %d\n", in->height, in->width, P);
+        return -1;
+    }
+    const int gh = in->height / P, gw = in->width / P, C = in->n_chans;
+    const int n_patches = gh * gw, n_cls = e.cls_token ? 1 : 0, n_reg = e.n_registers;
+    const int N = n_patches + n_cls + n_reg, D = e.embed_dim, K = C * P * P;
+    const int items = in->n_batch * in->n_frames;
+    const int64_t rows = (int64_t) items * N;
+    if (rows * (int64_t) std::max(3 * D, e.ffn_dim) >= ((int64_t) 1 << 40)) { log("jepa: jepa_encode: the input is too large\n"); return -1; }
+    if (e.act != "gelu_erf" && e.act != "silu" && e.act != "relu") {
+        log("jepa: jepa_encode: encoder activation '%s' is not supported by this engine\n", e.act.c_str());
+        return -1;
+    }
+    cudaSetDevice(ctx->device);
+    if (!ctx->enc) {
+        auto eng = std::make_unique<EncEngine>();
+        if (!eng->build(m, ctx->stream)) return -1;
+        ctx->enc = std::move(eng);
+    }
+    EncEngine & E = *ctx->enc;
+    if (E.pos_rows != N) {
+        log("jepa: token grid %dx%d (+%d prefix) = %d tokens does not match enc.pos_embed (%lld rows); "
+            "position-table interpolation is not implemented yet -- feed a %dx%d input\n",
+            gh, gw, n_cls + n_reg, N, (long long) E.pos_rows, e.img_size, e.img_size);
+        return -1;
+    }
+    if (!enc_attention_supported(D, e.n_head)) {
+        log("jepa: jepa_encode: head width %d is not supported by this engine (32, 48, 64, 80, 88, 96, 128)\n",
+            e.n_head > 0 ? D / e.n_head : 0);
+        return -1;
+    }
+    // patch rows on the host: per item, per patch (h-major), C x P x P
+    std::vector<float> pr((size_t) items * n_patches * K);
+    const size_t plane = (size_t) in->height * in->width;
+    for (int b = 0; b < in->n_batch; b++) {
+        for (int t = 0; t < in->n_frames; t++) {
+            const int item = b * in->n_frames + t;
+            for (int c = 0; c < C; c++) {
+                const float * src = in->data + (((size_t) b * C + c) * in->n_frames + t) * plane;
+                for (int y = 0; y < gh; y++)
+                    for (int x = 0; x < gw; x++) {
+                        float * dst = pr.data() + ((size_t) item * n_patches + (size_t) y * gw + x) * K + (size_t) c * P * P;
+                        for (int py = 0; py < P; py++)
+                            memcpy(dst + (size_t) py * P, src + (size_t) (y * P + py) * in->width + (size_t) x * P, (size_t) P * 4);
+                    }
+            }
+        }
+    }
+    int F = 1;
+    for (const EncLayer & L : E.layers) F = std::max(F, L.up.out);
+    cudaStream_t st = ctx->stream;
+    const size_t R = (size_t) rows, wide = (size_t) std::max({3 * D, F, K});
+    DevBuf patches, p_hi, p_lo, pe, X, X2, h_hi, h_lo, qkv, o, o_hi, o_lo, a, u, g_hi, g_lo, y;
+    if (!patches.alloc(pr.size()) || !p_hi.alloc(pr.size()) || !p_lo.alloc(pr.size()) || !pe.alloc((size_t) items * n_patches * D) ||
+        !X.alloc(R * D) || !X2.alloc(R * D) || !h_hi.alloc(R * D) || !h_lo.alloc(R * D) || !qkv.alloc(R * 3 * D) || !o.alloc(R * D) ||
+        !o_hi.alloc(R * D) || !o_lo.alloc(R * D) || !a.alloc(R * wide) || !u.alloc(R * F) || !g_hi.alloc(R * F) ||
+        !g_lo.alloc(R * F) || !y.alloc(R * D))
+        return -1;
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, st);
+    JB_CUDA(cudaMemcpyAsync(patches.p, pr.data(), pr.size() * 4, cudaMemcpyHostToDevice, st));
+    split_f32(patches.f(), K, p_hi.f(), p_lo.f(), K, items * n_patches, K, st);
+    {
+        GemmEpi ep;
+        ep.bias = E.patch.b; ep.out0 = pe.f(); ep.ld0 = D;
+        if (lin_tc(E.patch, p_hi.f(), p_lo.f(), K, items * n_patches, ep, st)) return -1;
+    }
+    enc_tokens(pe.f(), E.cls, E.reg, E.pos, X.f(), items, N, n_cls, n_reg, D, st);
+    const int M = (int) rows;
+    for (const EncLayer & L : E.layers) {
+        // attention half: X2 = X + ls1 * out(attention(qkv(LN1(X))))
+        layer_norm(X.f(), D, L.ln1_w, L.ln1_b, e.ln_eps, nullptr, D, h_hi.f(), h_lo.f(), nullptr, M, D, st);
+        GemmEpi e1;
+        e1.bias = L.qkv.b; e1.out0 = qkv.f(); e1.ld0 = 3 * D;
+        if (lin_tc(L.qkv, h_hi.f(), h_lo.f(), D, M, e1, st)) return -1;
+        enc_attention(qkv.f(), o.f(), items, N, D, e.n_head, st);
+        split_f32(o.f(), D, o_hi.f(), o_lo.f(), D, M, D, st);
+        GemmEpi e2;
+        e2.mode = EPI_GATED; e2.bias = L.out.b; e2.out0 = a.f(); e2.ld0 = D; e2.aux = X.f(); e2.ld_aux = D;
+        e2.gate = L.ls1; e2.ld_gate = 0; e2.out1 = X2.f(); e2.ld1 = D;
+        if (lin_tc(L.out, o_hi.f(), o_lo.f(), D, M, e2, st)) return -1;
+        // MLP half: X = X2 + ls2 * down(act(up(LN2(X2))))
+        layer_norm(X2.f(), D, L.ln2_w, L.ln2_b, e.ln_eps, nullptr, D, h_hi.f(), h_lo.f(), nullptr, M, D, st);
+        const int Fl = L.up.out;
+        GemmEpi e3;
+        e3.bias = L.up.b;
+        if (e.act == "gelu_erf") {
+            e3.mode = EPI_GELU_SPLIT; e3.out0 = u.f(); e3.ld0 = Fl; e3.out_hi = g_hi.f(); e3.out_lo = g_lo.f(); e3.ld_split = Fl;
+            if (lin_tc(L.up, h_hi.f(), h_lo.f(), D, M, e3, st)) return -1;
+        } else {
+            e3.out0 = u.f(); e3.ld0 = Fl;
+            if (lin_tc(L.up, h_hi.f(), h_lo.f(), D, M, e3, st)) return -1;
+            act_fwd(u.f(), Fl, a.f(), Fl, M, Fl, e.act == "silu" ? 2 : 3, st);
+            split_f32(a.f(), Fl, g_hi.f(), g_lo.f(), Fl, M, Fl, st);
+        }
+        GemmEpi e4;
+        e4.mode = EPI_GATED; e4.bias = L.down.b; e4.out0 = a.f(); e4.ld0 = D; e4.aux = X2.f(); e4.ld_aux = D;
+        e4.gate = L.ls2; e4.ld_gate = 0; e4.out1 = X.f(); e4.ld1 = D;
+        if (lin_tc(L.down, g_hi.f(), g_lo.f(), Fl, M, e4, st)) return -1;
+    }
+    layer_norm(X.f(), D, E.norm_w, E.norm_b, e.ln_eps, y.f(), D, nullptr, nullptr, nullptr, M, D, st);
+    float * data = (float *) malloc(R * D * sizeof(float));
+    if (!data) { log("jepa: jepa_encode: out of host memory for %lld rows\n", (long long) rows); return -1; }
+    if (!cuda_ok(cudaMemcpyAsync(data, y.p, R * D * 4, cudaMemcpyDeviceToHost, st), "encoder output") ||
+        !cuda_ok(cudaStreamSynchronize(st), "jepa_encode")) {
+        free(data);
+        return -1;
+    }
+    cudaEventRecord(e1, st);
+    cudaEventSynchronize(e1);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    ctx->last_ms = ms;
+    if (gemm_error_flag(st)) { free(data); log("jepa: a tensor-core kernel gave up waiting on its pipeline\n"); return -1; }
+    out->data = data;
+    out->n_tokens = rows;
+    out->dim = D;
+    return 0;
+}
+
+// mean over the patch tokens (the prefix tokens excluded), double accumulation (src/jepa.cpp:1227-1252)
+int jepa_pool_mean(const jepa_model * model, const jepa_output * enc, jepa_output * out) {
+    if (!model || !enc || !out || !enc->data) return -1;
+    const int64_t skip = (model->enc.cls_token ? 1 : 0) + model->enc.n_registers;
+    const int64_t D = enc->dim, n = enc->n_tokens - skip;
+    if (D <= 0 || enc->n_tokens <= 0) {
+        log("jepa: jepa_pool_mean: encoder output is [%lld tokens, %lld dims]\n", (long long) enc->n_tokens, (long long) D);
+        return -1;
+    }
+    if (n <= 0) return -1;
+    out->n_tokens = 1;
+    out->dim = D;
+    out->data = (float *) calloc((size_t) D, sizeof(float));
+    if (!out->data) return -1;
+    std::vector<double> acc((size_t) D, 0.0);
+    for (int64_t i = skip; i < enc->n_tokens; i++)
+        for (int64_t d = 0; d < D; d++) acc[(size_t) d] += enc->data[i * D + d];
+    for (int64_t d = 0; d < D; d++) out->data[d] = (float) (acc[(size_t) d] / (double) n);
+    return 0;
+}
+
+// the CLS row (row 0, after the final norm) (src/jepa.cpp:1254-1270)
+int jepa_pool_cls(const jepa_model * model, const jepa_output * enc, jepa_output * out) {
+    if (!model || !enc || !out || !enc->data) return -1;
+    if (!model->enc.cls_token) { log("jepa: jepa_pool_cls: model has no CLS token\n"); return -1; }
+    if (enc->dim <= 0 || enc->n_tokens < 1) {
+        log("jepa: jepa_pool_cls: encoder output is [%lld tokens, %lld dims]\n", (long long) enc->n_tokens, (long long) enc->dim);
+        return -1;
+    }
+    out->n_tokens = 1;
+    out->dim = enc->dim;
+    out->data = (float *) malloc((size_t) enc->dim * sizeof(float));
+    if (!out->data) return -1;
+    memcpy(out->data, enc->data, (size_t) enc->dim * sizeof(float));
+    return 0;
+}
+
+}  // extern "C"

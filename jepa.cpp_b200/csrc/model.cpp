@@ -9,6 +9,7 @@
 #include "hplan.h"
 #include "shard.h"
 #include "ac.h"
+#include "encoder.h"
 
 #include "../../include/jepa_b200.h"
 
@@ -54,6 +55,9 @@ bool parse(jepa_model & m) {
     e.n_frames = g.geti("jepa.enc.n_frames", 1);
     e.n_registers = g.geti("jepa.enc.n_registers", 0);
     e.cls_token = g.getb("jepa.enc.cls_token", false);
+    e.in_chans = g.geti("jepa.enc.in_chans", 3);
+    e.ln_eps = g.getf("jepa.enc.ln_eps", 1e-6f);
+    e.act = g.gets("jepa.enc.act", "gelu_erf");
     if (!in_range("jepa.enc.embed_dim", e.embed_dim, 1, 65536) || !in_range("jepa.enc.n_layer", e.n_layer, 1, 1024) ||
         !in_range("jepa.enc.n_head", e.n_head, 1, 1024) || !in_range("jepa.enc.ffn_dim", e.ffn_dim, 1, 1048576) ||
         !in_range("jepa.enc.patch_size", e.patch_size, 1, 1024)) {

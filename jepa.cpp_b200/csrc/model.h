@@ -45,8 +45,10 @@ struct ACParams {
 
 struct EncParams {
     int embed_dim = 0, n_layer = 0, n_head = 0, ffn_dim = 0, patch_size = 16, tubelet_size = 1, img_size = 224;
-    int n_frames = 1, n_registers = 0;
+    int n_frames = 1, n_registers = 0, in_chans = 3;
     bool cls_token = false;
+    float ln_eps = 1e-6f;               // jepa.enc.ln_eps
+    std::string act = "gelu_erf";       // jepa.enc.act
 };
 
 }  // namespace jb
@@ -69,6 +71,8 @@ struct jepa_model {
 
 namespace jb { struct HPlanner; struct Shard; struct ACEngine; }
 
+namespace jb { struct EncEngine; }
+
 struct jepa_context {
     jepa_model * model = nullptr;
     jepa_context_params params{};
@@ -78,6 +82,7 @@ struct jepa_context {
     std::unique_ptr<jb::HPlanner> hplan;
     std::unique_ptr<jb::Shard> shard;
     std::unique_ptr<jb::ACEngine> ac;
+    std::unique_ptr<jb::EncEngine> enc;   // the image encoder's weights on the device (jepa_encode), on first use
     double last_ms = 0.0;
     long long last_launches = 0;
     int max_batch = 32;

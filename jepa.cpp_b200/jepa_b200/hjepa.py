@@ -17,6 +17,11 @@ class _Output(C.Structure):
     _fields_ = [("data", capi.FP), ("n_tokens", C.c_int64), ("dim", C.c_int64)]
 
 
+class _Input(C.Structure):
+    _fields_ = [("data", capi.FP), ("n_batch", C.c_int), ("n_chans", C.c_int), ("n_frames", C.c_int),
+                ("height", C.c_int), ("width", C.c_int)]
+
+
 class Planner:
     def __init__(self, path: str, device: int = -1, verbose: bool = False):
         self.lib = L = jlib.load()
@@ -92,6 +97,24 @@ class Planner:
             self.lib.jepa_free.argtypes = [C.c_void_p]
             self.lib.jepa_free(C.cast(out.data, C.c_void_p))
         return res.reshape(out.n_tokens, out.dim)
+
+    def encode(self, images) -> np.ndarray:
+        """jepa_encode: images [B, C, H, W] (or [B, C, T, H, W]) -> [B (T) N, D], final norm applied."""
+        x = np.ascontiguousarray(images, np.float32)
+        if x.ndim == 4:
+            x = x[:, :, None]
+        inp = _Input(capi.fptr(x), x.shape[0], x.shape[1], x.shape[2], x.shape[3], x.shape[4])
+        fn = self.lib.jepa_encode
+        fn.argtypes = [C.c_void_p, C.POINTER(_Input), C.POINTER(_Output)]
+        return self._output("jepa_encode", lambda o: fn(self.ctx, C.byref(inp), o))
+
+    def pool(self, kind: str, enc: np.ndarray) -> np.ndarray:
+        """jepa_pool_cls / jepa_pool_mean of one item's encoder rows [N, D]."""
+        enc = np.ascontiguousarray(enc, np.float32)
+        src = _Output(capi.fptr(enc), enc.shape[0], enc.shape[1])
+        fn = getattr(self.lib, "jepa_pool_" + kind)
+        fn.argtypes = [C.c_void_p, C.POINTER(_Output), C.POINTER(_Output)]
+        return self._output("jepa_pool_" + kind, lambda o: fn(self.model, C.byref(src), o))[0]
 
     def encode_states(self, cls_rows, proprio=None) -> np.ndarray:
         """jepa_hjepa_embed: the encoder's CLS rows [n, Dv] (and the proprio stream [n, P]) -> level-1 states."""
