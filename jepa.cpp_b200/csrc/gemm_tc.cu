@@ -23,6 +23,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 namespace jb {
@@ -31,6 +32,10 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 32;                  // 32 f32 = one 128-byte swizzle row
+// warp 0: TMA producer, warp 1: MMA issuer, warps 2-5: accumulator readers (TMEM lane quadrant = warp % 4);
+// warps 6-11 join the split-K reduction and the fused epilogue, latency-bound per-thread work (a GELU per
+// element) that twelve warps finish in half the time six do
+constexpr int GEMM_THREADS = 384;
 
 __device__ int g_gemm_error = 0;
 
@@ -46,10 +51,14 @@ __device__ __forceinline__ float gelu_grad(float v) {
     return 0.5f * (1.0f + erff(v * 0.70710678118654752f)) + v * 0.39894228040143268f * expf(-0.5f * v * v);
 }
 
-// the fused epilogue of one output element (v = the accumulated product, before the bias)
-__device__ __forceinline__ void apply_epi(const GemmEpi & ep, int row, int col, float v) {
-    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) v = v + ep.bias[col];
-    switch (ep.mode) {
+// The fused epilogue of one output element (v = the accumulated product, before the bias). The mode is a
+// template parameter throughout, so that a kernel holds the code of its own epilogue only: these kernels
+// are latency-bound, and every instruction fetched on the way from the accumulator to the stores is time.
+// The element-wise path (unaligned operands, the ragged last columns) stays out of line.
+template <int MODE>
+__device__ __noinline__ void apply_epi(const GemmEpi & ep, int row, int col, float v) {
+    if (MODE != EPI_DGELU_SPLIT && ep.bias) v = v + ep.bias[col];
+    switch (MODE) {
         case EPI_F32:
             ep.out0[(size_t) row * ep.ld0 + col] = v;
             break;
@@ -98,19 +107,21 @@ struct Epi4In {
     float4 bias, aux, gate;
 };
 
+template <int MODE>
 __device__ __forceinline__ Epi4In epi_load4(const GemmEpi & ep, int row, int col) {
     const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     Epi4In in{z, z, z};
-    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) in.bias = ld4(ep.bias + col);
-    if (ep.mode == EPI_GATED || ep.mode == EPI_DGELU_SPLIT) in.aux = ld4(ep.aux + (size_t) row * ep.ld_aux + col);
-    if (ep.mode == EPI_GATED) in.gate = ld4(ep.gate + (size_t) row * ep.ld_gate + col);
+    if (MODE != EPI_DGELU_SPLIT && ep.bias) in.bias = ld4(ep.bias + col);
+    if (MODE == EPI_GATED || MODE == EPI_DGELU_SPLIT) in.aux = ld4(ep.aux + (size_t) row * ep.ld_aux + col);
+    if (MODE == EPI_GATED) in.gate = ld4(ep.gate + (size_t) row * ep.ld_gate + col);
     return in;
 }
 
 // four consecutive columns of the fused epilogue, vector path (ep.vec and col + 3 < N)
+template <int MODE>
 __device__ __forceinline__ void epi_store4(const GemmEpi & ep, int row, int col, float4 v, const Epi4In & in) {
-    if (ep.mode != EPI_DGELU_SPLIT && ep.bias) v = f4_add(v, in.bias);
-    switch (ep.mode) {
+    if (MODE != EPI_DGELU_SPLIT && ep.bias) v = f4_add(v, in.bias);
+    switch (MODE) {
         case EPI_F32: st4(ep.out0 + (size_t) row * ep.ld0 + col, v); break;
         case EPI_SPLIT: {
             const float4 h = f4_hi(v);
@@ -147,13 +158,14 @@ __device__ __forceinline__ void epi_store4(const GemmEpi & ep, int row, int col,
 
 // four consecutive columns of the fused epilogue: vector loads / stores when the operands allow it
 // (ep.vec: every pointer 16-byte aligned, every leading dimension a multiple of 4), else element-wise
+template <int MODE>
 __device__ __forceinline__ void apply_epi4(const GemmEpi & ep, int row, int col, int N, float4 v) {
     if (!ep.vec || col + 3 >= N) {
         const float e[4] = {v.x, v.y, v.z, v.w};
-        for (int j = 0; j < 4; j++) if (col + j < N) apply_epi(ep, row, col + j, e[j]);
+        for (int j = 0; j < 4; j++) if (col + j < N) apply_epi<MODE>(ep, row, col + j, e[j]);
         return;
     }
-    epi_store4(ep, row, col, v, epi_load4(ep, row, col));
+    epi_store4<MODE>(ep, row, col, v, epi_load4<MODE>(ep, row, col));
 }
 
 __device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
@@ -198,31 +210,41 @@ __host__ __device__ constexpr int split_rows(int splits) { return (BM + splits -
 // partial tile in shared memory and one thread sends each peer its rows with one bulk copy into the peer's
 // receive buffer (completing on the peer's mbarrier); the owner waits for its bytes, sums the splits in rank
 // order (a fixed order: the bits do not depend on timing) from its own shared memory and applies the fused
-// epilogue with all six warps. The epilogue's operands (bias, residual, gate) are loaded right after the dependency wait, so
-// their latency hides behind the mainloop. Cluster barriers: one arrive at the start (the receive
+// epilogue with all twelve warps, in one pass. The epilogue's operands (bias, residual, gate) are requested
+// before the mainloop (before the dependency wait when they come from earlier kernels), so their latency
+// hides behind it. Cluster barriers: one arrive at the start (the receive
 // barriers are initialised) waited on before the first push, one after the receive completes waited on
 // before exit (no CTA leaves while a push to or from it may be in flight).
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, int STAGES, int MODE>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
               const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
-              int M, int N, int K, int splits, GemmEpi ep) {
+              int M, int N, int K, int splits, const __grid_constant__ GemmEpi ep) {
     constexpr uint32_t A_BYTES = BM * BK * 4;
     constexpr uint32_t B_BYTES = BN * BK * 4;
     constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     // two accumulators: hi*hi in columns [0, BN), the small cross terms hi*lo + lo*hi in [BN, 2 BN).
     // The tensor core's float32 accumulation rounds toward zero per instruction; keeping the small terms
     // apart cuts the number of truncations the large partial sum sees by three.
+    //
+    // A stage holds B_hi's BN rows directly followed by B_lo's (the same 128-byte swizzle, 8-row groups
+    // 1024 bytes apart), so the two read as one operand of 2 BN rows: one MMA of width 2 BN computes
+    // [hi*hi | hi*lo] into both accumulators at once and a second of width BN adds lo*hi to the cross
+    // terms -- two instructions per K-step instead of three, and A_hi is read from shared memory once.
     constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
     // instruction descriptor: D f32 (bit 4), A/B tf32 (2 << 7, 2 << 10), K-major both, N >> 3, M >> 4
     constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
-    constexpr int C4 = BN / 4, NT = 192, PER = 2;
+    constexpr uint32_t IDESC2 = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) ((2 * BN) >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
+    static_assert(2 * BN <= 256 && B_BYTES % 1024 == 0, "the stacked B operand is one MMA's N (at most 256) in whole swizzle groups");
+    // every thread reduces and stores PER float4 of the CTA's rows in one pass (at most 64 rows x BN at 2 splits)
+    constexpr int C4 = BN / 4, NT = GEMM_THREADS, PER = (split_rows(2) * C4 + NT - 1) / NT;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     constexpr int PLD = BN + 4;            // padded row of the staged partial tile (conflict-free float4 row writes)
     float * tile = (float *) smem;         // split-K: this CTA's partial tile [BM][PLD], in the idle pipeline buffers
-    float * recv = (float *) (smem + (size_t) STAGES * STAGE_BYTES);   // split-K: the peers' partials [splits][R][PLD]
+    // split-K: the peers' partials [splits - 1][R][PLD]; peer q's rows go to slot q (q < this rank) or q - 1
+    float * recv = (float *) (smem + (size_t) STAGES * STAGE_BYTES);
     static_assert((size_t) BM * PLD * 4 <= (size_t) STAGES * STAGE_BYTES, "staged tile must fit in the pipeline buffers");
     __shared__ __align__(8) uint64_t full_bar[STAGES];
     __shared__ __align__(8) uint64_t empty_bar[STAGES];
@@ -280,23 +302,23 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     }
     // split-K: the first round of this thread's epilogue items, and their operands
     const int n_items = splits > 1 && re > rs ? (re - rs) * C4 : 0;
-    const int rounds = (n_items + NT * PER - 1) / (NT * PER);
+    const bool items = n_items > 0;
     Epi4In in[PER];
-    auto prefetch = [&](int rd) {
+    auto prefetch = [&]() {
 #pragma unroll
         for (int j = 0; j < PER; j++) {
-            const int idx = rd * NT * PER + j * NT + (int) threadIdx.x;
+            const int idx = j * NT + (int) threadIdx.x;
             if (idx >= n_items) continue;
             const int row = m0 + rs + idx / C4, col = n0 + (idx % C4) * 4;
-            if (row < M && ep.vec && col + 3 < N) in[j] = epi_load4(ep, row, col);
+            if (row < M && ep.vec && col + 3 < N) in[j] = epi_load4<MODE>(ep, row, col);
         }
     };
-    if (ep.pre_epi && rounds > 0) prefetch(0);
+    if (ep.pre_epi && items) prefetch();
     // the setup above overlapped the previous kernel (programmatic dependent launch); its outputs are
     // read from here on
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (!ep.pre_epi && rounds > 0) prefetch(0);
+    if (!ep.pre_epi && items) prefetch();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -335,15 +357,14 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error)) { abort_sh = 1; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t a_hi = smem_u32(smem + (size_t) s * STAGE_BYTES);
-                const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
+                const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES;   // B_lo follows B_hi
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; kk++) {
                     const uint32_t off = (uint32_t) kk * 32;   // 8 tf32 = 32 bytes along K
                     const uint64_t dah = sw128_desc(a_hi + off), dal = sw128_desc(a_lo + off);
-                    const uint64_t dbh = sw128_desc(b_hi + off), dbl = sw128_desc(b_lo + off);
-                    mma_kind_tf32(tmem + BN, dal, dbh, IDESC, (i | kk) != 0);
-                    mma_kind_tf32(tmem + BN, dah, dbl, IDESC, 1);
-                    mma_kind_tf32(tmem, dah, dbh, IDESC, (i | kk) != 0);
+                    const uint64_t dbh = sw128_desc(b_hi + off);
+                    mma_kind_tf32(tmem, dah, dbh, IDESC2, (i | kk) != 0);   // [hi*hi | hi*lo], 2 BN wide
+                    mma_kind_tf32(tmem + BN, dal, dbh, IDESC, 1);          // + lo*hi (B_hi rows only)
                 }
                 mma_commit(&empty_bar[s]);
             }
@@ -351,6 +372,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
         }
         __syncwarp();
         if (splits > 1) cluster_wait();
+    } else if (warp >= 6) {
+        if (splits > 1) cluster_wait();   // (the start's arrive; these warps join at the reduction)
     } else {
         // epilogue warps 2..5 (TMEM lane quadrant = warp % 4)
         const int q = warp & 3;
@@ -358,12 +381,40 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int r = q * 32 + lane;
         const bool have = ok && nkt > 0 && !*(volatile int *) &abort_sh;
+        const uint32_t trow = tmem + ((uint32_t) (q * 32) << 16);
+        if constexpr (BN == 64) {
+            if (splits > 1) {
+                // both accumulators' 64 columns in flight at once, then this thread's row of the partial tile
+                uint32_t a0[32], a1[32], b0[32], b1[32];
+                tmem_ld32_async(trow, a0);
+                tmem_ld32_async(trow + 32, a1);
+                tmem_ld32_async(trow + BN, b0);
+                tmem_ld32_async(trow + BN + 32, b1);
+                tmem_ld_wait(a0);
+                tmem_ld_wait(a1);
+                tmem_ld_wait(b0);
+                tmem_ld_wait(b1);
+                auto stage = [&](const uint32_t (&x)[32], const uint32_t (&y)[32], int c0) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 v = have ? make_float4(__uint_as_float(x[j]) + __uint_as_float(y[j]),
+                                                            __uint_as_float(x[j + 1]) + __uint_as_float(y[j + 1]),
+                                                            __uint_as_float(x[j + 2]) + __uint_as_float(y[j + 2]),
+                                                            __uint_as_float(x[j + 3]) + __uint_as_float(y[j + 3]))
+                                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        *(float4 *) &tile[r * PLD + c0 + j] = v;
+                    }
+                };
+                stage(a0, b0, 0);
+                stage(a1, b1, 32);
+            }
+        }
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 0; c0 < BN && splits == 1; c0 += 32) {
             uint32_t a[32], b[32];
-            tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) c0, a);
-            tmem_ld32(tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) (BN + c0), b);
-            if (splits == 1) {
+            tmem_ld32(trow + (uint32_t) c0, a);
+            tmem_ld32(trow + (uint32_t) (BN + c0), b);
+            {
                 // one CTA per tile: straight from the accumulator to the fused epilogue, a row per thread
                 const int row = m0 + r;
                 if (have && row < M) {
@@ -373,18 +424,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                                                      __uint_as_float(a[j + 1]) + __uint_as_float(b[j + 1]),
                                                      __uint_as_float(a[j + 2]) + __uint_as_float(b[j + 2]),
                                                      __uint_as_float(a[j + 3]) + __uint_as_float(b[j + 3]));
-                        apply_epi4(ep, row, n0 + c0 + j, N, v);
+                        apply_epi4<MODE>(ep, row, n0 + c0 + j, N, v);
                     }
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    const float4 v = have ? make_float4(__uint_as_float(a[j]) + __uint_as_float(b[j]),
-                                                        __uint_as_float(a[j + 1]) + __uint_as_float(b[j + 1]),
-                                                        __uint_as_float(a[j + 2]) + __uint_as_float(b[j + 2]),
-                                                        __uint_as_float(a[j + 3]) + __uint_as_float(b[j + 3]))
-                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    *(float4 *) &tile[r * PLD + c0 + j] = v;
                 }
             }
         }
@@ -397,7 +438,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 for (int p = 0; p < splits; p++) {
                     const int prs = p * R, pre = min(BM, prs + R);
                     if (p == split || pre <= prs) continue;
-                    const uint32_t dst = peer_addr(smem_u32(recv + (size_t) split * R * PLD), (uint32_t) p);
+                    const int slot = split < p ? split : split - 1;   // this CTA's slot in peer p's receive buffer
+                    const uint32_t dst = peer_addr(smem_u32(recv + (size_t) slot * R * PLD), (uint32_t) p);
                     bulk_to_peer(dst, smem_u32(tile + (size_t) prs * PLD), (uint32_t) ((pre - prs) * PLD * 4),
                                  peer_addr(smem_u32(&recv_bar), (uint32_t) p));
                 }
@@ -406,26 +448,20 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();   // the accumulator has been read (and this CTA's own partial rows are staged)
-    if (warp == 1) {
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
-    }
     if (splits > 1) {
         const bool got = mbar_wait(&recv_bar, 0, 4, &g_gemm_error);   // the peers' partial rows have landed
-        cluster_arrive_relaxed();
         if (got && !*(volatile int *) &abort_sh) {
-            for (int rd = 0; rd < rounds; rd++) {
-                if (rd > 0) prefetch(rd);
+            {
 #pragma unroll
                 for (int j = 0; j < PER; j++) {
-                    const int idx = rd * NT * PER + j * NT + (int) threadIdx.x;
+                    const int idx = j * NT + (int) threadIdx.x;
                     if (idx >= n_items) continue;
                     const int i = idx / C4, cc = (idx % C4) * 4;
                     const int row = m0 + rs + i, col = n0 + cc;
                     // split p's partial: this CTA's own from the staged tile, the others from the receive buffer
                     auto part = [&](int p) -> float4 {
                         return p == split ? *(const float4 *) &tile[(size_t) (rs + i) * PLD + cc]
-                                          : *(const float4 *) &recv[((size_t) p * R + i) * PLD + cc];
+                                          : *(const float4 *) &recv[((size_t) (p < split ? p : p - 1) * R + i) * PLD + cc];
                     };
                     float4 v = part(0);
 #pragma unroll
@@ -436,12 +472,17 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                         }
                     }
                     if (row >= M) continue;
-                    if (ep.vec && col + 3 < N) epi_store4(ep, row, col, v, in[j]);
-                    else apply_epi4(ep, row, col, N, v);
+                    if (ep.vec && col + 3 < N) epi_store4<MODE>(ep, row, col, v, in[j]);
+                    else apply_epi4<MODE>(ep, row, col, N, v);
                 }
             }
         }
-        cluster_wait();   // every CTA has received everything: no push to or from this CTA is in flight
+        cluster_arrive_relaxed();   // this CTA has received everything
+        cluster_wait();             // every CTA has: no push to or from this CTA is in flight
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
     }
 }
 
@@ -475,7 +516,73 @@ bool make_map(CUtensorMap * map, const float * base, int rows, int cols, int ld,
     return r == CUDA_SUCCESS;
 }
 
+// rows of the split-K receive buffer: (splits - 1) x ceil(128 / splits), at most 114 (7 splits)
+constexpr int recv_rows() {
+    int r = 0;
+    for (int s = 2; s <= 8; s++) r = (s - 1) * split_rows(s) > r ? (s - 1) * split_rows(s) : r;
+    return r;
+}
+
 template <int BN, int STAGES>
+constexpr size_t smem_bytes() {
+    // pipeline stages, the split-K receive buffer and alignment
+    return (size_t) STAGES * (2 * BM * BK * 4 + 2 * BN * BK * 4) + (BN == 64 ? (size_t) recv_rows() * (BN + 4) * 4 : 0) + 1024;
+}
+static_assert(smem_bytes<64, 4>() + 256 <= 227 * 1024, "four 64-wide stages and the receive buffer fit in shared memory");
+
+// the kernel's shared-memory and cluster attributes, once per device
+template <int BN, int STAGES, int MODE>
+bool set_attrs() {
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+        if (cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int) smem_bytes<BN, STAGES>()) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES, MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+            return false;
+        }
+        done[dev] = true;
+    }
+    return true;
+}
+
+// How many split-K clusters of s CTAs of the 64-wide kernel the device holds at once. Clusters are
+// placed inside one GPC, so this is below (SMs / s) when a GPC's SM count is not a multiple of s
+// (on a 148-SM B200, 45 clusters of 3 rather than 49). Cached per device.
+int resident_clusters(int s) {
+    static std::mutex mu;
+    static int cache[64][9] = {};
+    int dev = 0;
+    if (s < 1 || s > 8 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cache[dev][s]) {
+        int n = 0;
+        if (s == 1) {
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        } else if (set_attrs<64, 4, EPI_F32>()) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(1, 1, (unsigned) s);
+            cfg.blockDim = dim3(GEMM_THREADS);
+            cfg.dynamicSmemBytes = smem_bytes<64, 4>();
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 1;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = (unsigned) s;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&n, k_gemm_tf32x3<64, 4, EPI_F32>, &cfg) != cudaSuccess) n = 0;
+        }
+        cudaGetLastError();
+        cache[dev][s] = n > 0 ? n : -1;
+    }
+    return cache[dev][s] > 0 ? cache[dev][s] : 0;
+}
+
+template <int BN, int STAGES, int MODE>
 int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
     if (BN != 64 && splits > 1) { log("jepa: gemm: split-K needs the 64-wide tile\n"); return -1; }
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
@@ -484,17 +591,11 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
         log("jepa: gemm: cuTensorMapEncodeTiled refused an operand (M %d N %d K %d, ld %d / %d)\n", M, N, K, A.ld, B.ld);
         return -1;
     }
-    // pipeline stages, the split-K receive buffer (at most splits x ceil(128 / splits) <= 135 rows) and alignment
-    constexpr size_t smem = (size_t) STAGES * (2 * BM * BK * 4 + 2 * BN * BK * 4) + (BN == 64 ? (size_t) (BM + 7) * (BN + 4) * 4 : 0) + 1024;
-    static bool attr_set = false;
-    if (!attr_set) {
-        JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem));
-        JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        attr_set = true;
-    }
+    constexpr size_t smem = smem_bytes<BN, STAGES>();
+    if (!set_attrs<BN, STAGES, MODE>()) { log("jepa: gemm: cudaFuncSetAttribute failed\n"); return -1; }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) ((M + BM - 1) / BM), (unsigned) ((N + BN - 1) / BN), (unsigned) splits);
-    cfg.blockDim = dim3(192);
+    cfg.blockDim = dim3(GEMM_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -506,8 +607,22 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
     attr[1].val.clusterDim.z = (unsigned) splits;
     cfg.attrs = attr;
     cfg.numAttrs = splits > 1 ? 2 : 1;
-    JB_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tf32x3<BN, STAGES>, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, splits, ep));
+    JB_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tf32x3<BN, STAGES, MODE>, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, splits, ep));
     return 0;
+}
+
+// one kernel per epilogue mode
+template <int BN, int STAGES>
+int launch_mode(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
+    switch (ep.mode) {
+        case EPI_F32: return launch<BN, STAGES, EPI_F32>(A, B, M, N, K, splits, ep, st);
+        case EPI_SPLIT: return launch<BN, STAGES, EPI_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_GELU_SPLIT: return launch<BN, STAGES, EPI_GELU_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_GATED: return launch<BN, STAGES, EPI_GATED>(A, B, M, N, K, splits, ep, st);
+        case EPI_DGELU_SPLIT: return launch<BN, STAGES, EPI_DGELU_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_F32_SPLIT: return launch<BN, STAGES, EPI_F32_SPLIT>(A, B, M, N, K, splits, ep, st);
+        default: log("jepa: gemm: unknown epilogue mode %d\n", ep.mode); return -1;
+    }
 }
 
 bool aligned16(const void * p) { return ((uintptr_t) p & 15) == 0; }
@@ -525,8 +640,10 @@ bool vec_ok(const GemmEpi & ep, int N) {
 }  // namespace
 
 // Tile / split choice: wide outputs (the time-batched adaLN modulation) take 128-wide tiles, one CTA
-// per tile; the per-step products take 64-wide tiles and split K over a cluster of up to 8 CTAs, so
-// that at most one CTA per SM (a single wave) streams a K-slice instead of a dozen CTAs streaming everything.
+// per tile; the per-step products take 64-wide tiles and split K over a cluster of up to 8 CTAs, the
+// largest split at which two rows of tiles (256 rows, or two candidate chains of 128 side by side) are
+// resident at once: one wave, each CTA streaming a K-slice, instead of a dozen CTAs streaming everything
+// or a second wave of the clusters that did not fit.
 int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     if (!load_encode()) {
@@ -542,16 +659,16 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
     e.vec = vec_ok(ep, N) ? 1 : 0;
     // The tile shape and the K split depend on (N, K) only, never on M: a row's arithmetic (and so its
     // bits) is then the same whatever batch of rows it is computed in.
-    if (N >= 4096) return launch<128, 3>(A, B, M, N, K, 1, e, st);
+    if (N >= 4096) return launch_mode<128, 3>(A, B, M, N, K, 1, e, st);
     const int num_k = (K + BK - 1) / BK;
-    long s = 148 / (2L * ((N + 63) / 64));   // at most one CTA per SM (one wave) at 256 rows
-    if (s > 8) s = 8;
-    if (s > num_k) s = num_k;
-    if (s < 1) s = 1;
-    int splits = (int) s;
+    const int tiles2 = 2 * ((N + 63) / 64);
+    int splits = 1;
+    for (int s = std::min(8, num_k); s > 1; s--) {
+        if (tiles2 <= resident_clusters(s)) { splits = s; break; }
+    }
     const int kt_per = (num_k + splits - 1) / splits;
     splits = (num_k + kt_per - 1) / kt_per;   // no empty K-slices
-    return launch<64, 3>(A, B, M, N, K, splits, e, st);
+    return launch_mode<64, 4>(A, B, M, N, K, splits, e, st);
 }
 
 int gemm_error_flag(cudaStream_t st) {
