@@ -50,6 +50,13 @@ __device__ __forceinline__ float gelu_f(float x) {
 __device__ __forceinline__ float gelu_grad(float v) {
     return 0.5f * (1.0f + erff(v * 0.70710678118654752f)) + v * 0.39894228040143268f * expf(-0.5f * v * v);
 }
+// gelu(u) and gelu'(u) from one erf: the same expressions as gelu_f and gelu_grad, so the same bits
+__device__ __forceinline__ void gelu_and_grad(float u, float & g, float & d) {
+    const float e = erff(u * 0.70710678118654752f);
+    g = 0.5f * u * (1.0f + e);
+    d = 0.5f * (1.0f + e) + u * 0.39894228040143268f * expf(-0.5f * u * u);
+}
+template <int MODE> constexpr bool has_bias() { return MODE != EPI_DGELU_SPLIT && MODE != EPI_MUL_SPLIT; }
 
 // The fused epilogue of one output element (v = the accumulated product, before the bias). The mode is a
 // template parameter throughout, so that a kernel holds the code of its own epilogue only: these kernels
@@ -57,7 +64,7 @@ __device__ __forceinline__ float gelu_grad(float v) {
 // The element-wise path (unaligned operands, the ragged last columns) stays out of line.
 template <int MODE>
 __device__ __noinline__ void apply_epi(const GemmEpi & ep, int row, int col, float v) {
-    if (MODE != EPI_DGELU_SPLIT && ep.bias) v = v + ep.bias[col];
+    if (has_bias<MODE>() && ep.bias) v = v + ep.bias[col];
     switch (MODE) {
         case EPI_F32:
             ep.out0[(size_t) row * ep.ld0 + col] = v;
@@ -91,6 +98,20 @@ __device__ __noinline__ void apply_epi(const GemmEpi & ep, int row, int col, flo
             ep.out_hi[(size_t) row * ep.ld_split + col] = h;
             ep.out_lo[(size_t) row * ep.ld_split + col] = d - h;
         } break;
+        case EPI_GELU_D_SPLIT: {
+            float gv, dv;
+            gelu_and_grad(v, gv, dv);
+            ep.out0[(size_t) row * ep.ld0 + col] = dv;
+            const float h = split_hi(gv);
+            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+            ep.out_lo[(size_t) row * ep.ld_split + col] = gv - h;
+        } break;
+        case EPI_MUL_SPLIT: {
+            const float d = v * ep.aux[(size_t) row * ep.ld_aux + col];
+            const float h = split_hi(d);
+            ep.out_hi[(size_t) row * ep.ld_split + col] = h;
+            ep.out_lo[(size_t) row * ep.ld_split + col] = d - h;
+        } break;
         default: break;
     }
 }
@@ -111,8 +132,8 @@ template <int MODE>
 __device__ __forceinline__ Epi4In epi_load4(const GemmEpi & ep, int row, int col) {
     const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     Epi4In in{z, z, z};
-    if (MODE != EPI_DGELU_SPLIT && ep.bias) in.bias = ld4(ep.bias + col);
-    if (MODE == EPI_GATED || MODE == EPI_DGELU_SPLIT) in.aux = ld4(ep.aux + (size_t) row * ep.ld_aux + col);
+    if (has_bias<MODE>() && ep.bias) in.bias = ld4(ep.bias + col);
+    if (MODE == EPI_GATED || MODE == EPI_DGELU_SPLIT || MODE == EPI_MUL_SPLIT) in.aux = ld4(ep.aux + (size_t) row * ep.ld_aux + col);
     if (MODE == EPI_GATED) in.gate = ld4(ep.gate + (size_t) row * ep.ld_gate + col);
     return in;
 }
@@ -120,7 +141,7 @@ __device__ __forceinline__ Epi4In epi_load4(const GemmEpi & ep, int row, int col
 // four consecutive columns of the fused epilogue, vector path (ep.vec and col + 3 < N)
 template <int MODE>
 __device__ __forceinline__ void epi_store4(const GemmEpi & ep, int row, int col, float4 v, const Epi4In & in) {
-    if (MODE != EPI_DGELU_SPLIT && ep.bias) v = f4_add(v, in.bias);
+    if (has_bias<MODE>() && ep.bias) v = f4_add(v, in.bias);
     switch (MODE) {
         case EPI_F32: st4(ep.out0 + (size_t) row * ep.ld0 + col, v); break;
         case EPI_SPLIT: {
@@ -148,6 +169,23 @@ __device__ __forceinline__ void epi_store4(const GemmEpi & ep, int row, int col,
         case EPI_DGELU_SPLIT: {
             const float4 u = in.aux;
             const float4 d = f4_mul(v, make_float4(gelu_grad(u.x), gelu_grad(u.y), gelu_grad(u.z), gelu_grad(u.w)));
+            const float4 h = f4_hi(d);
+            st4(ep.out_hi + (size_t) row * ep.ld_split + col, h);
+            st4(ep.out_lo + (size_t) row * ep.ld_split + col, f4_sub(d, h));
+        } break;
+        case EPI_GELU_D_SPLIT: {
+            float4 g, d;
+            gelu_and_grad(v.x, g.x, d.x);
+            gelu_and_grad(v.y, g.y, d.y);
+            gelu_and_grad(v.z, g.z, d.z);
+            gelu_and_grad(v.w, g.w, d.w);
+            st4(ep.out0 + (size_t) row * ep.ld0 + col, d);
+            const float4 h = f4_hi(g);
+            st4(ep.out_hi + (size_t) row * ep.ld_split + col, h);
+            st4(ep.out_lo + (size_t) row * ep.ld_split + col, f4_sub(g, h));
+        } break;
+        case EPI_MUL_SPLIT: {
+            const float4 d = f4_mul(v, in.aux);
             const float4 h = f4_hi(d);
             st4(ep.out_hi + (size_t) row * ep.ld_split + col, h);
             st4(ep.out_lo + (size_t) row * ep.ld_split + col, f4_sub(d, h));
@@ -450,6 +488,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     __syncthreads();   // the accumulator has been read (and this CTA's own partial rows are staged)
     if (splits > 1) {
         const bool got = mbar_wait(&recv_bar, 0, 4, &g_gemm_error);   // the peers' partial rows have landed
+        cluster_arrive_relaxed();   // this CTA has received everything
         if (got && !*(volatile int *) &abort_sh) {
             {
 #pragma unroll
@@ -477,8 +516,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 }
             }
         }
-        cluster_arrive_relaxed();   // this CTA has received everything
-        cluster_wait();             // every CTA has: no push to or from this CTA is in flight
+        cluster_wait();   // every CTA has received everything: no push to or from this CTA is in flight
     }
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -621,6 +659,8 @@ int launch_mode(const SplitMat & A, const SplitMat & B, int M, int N, int K, int
         case EPI_GATED: return launch<BN, STAGES, EPI_GATED>(A, B, M, N, K, splits, ep, st);
         case EPI_DGELU_SPLIT: return launch<BN, STAGES, EPI_DGELU_SPLIT>(A, B, M, N, K, splits, ep, st);
         case EPI_F32_SPLIT: return launch<BN, STAGES, EPI_F32_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_GELU_D_SPLIT: return launch<BN, STAGES, EPI_GELU_D_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_MUL_SPLIT: return launch<BN, STAGES, EPI_MUL_SPLIT>(A, B, M, N, K, splits, ep, st);
         default: log("jepa: gemm: unknown epilogue mode %d\n", ep.mode); return -1;
     }
 }

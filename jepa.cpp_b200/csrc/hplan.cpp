@@ -576,7 +576,8 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
             block_pre(xm, P, mod_l, ldm, 3 * P, 4 * P, B.ln2_w, B.ln2_b, adaln_eps, ln_eps, w.h_hi, w.h_lo, P,
                       w.stm0 + tl * S, w.stm1 + tl * S, S, P, st);
             GemmEpi e3;
-            e3.mode = EPI_GELU_SPLIT; e3.bias = B.up.b; e3.out0 = u; e3.ld0 = F; e3.out_hi = w.g_hi; e3.out_lo = w.g_lo; e3.ld_split = F;
+            // (u keeps gelu'(pre-activation) for the backward's EPI_MUL_SPLIT)
+            e3.mode = EPI_GELU_D_SPLIT; e3.bias = B.up.b; e3.out0 = u; e3.ld0 = F; e3.out_hi = w.g_hi; e3.out_lo = w.g_lo; e3.ld_split = F;
             if (wgemm({w.h_hi, w.h_lo, P}, {B.up.w_hi, B.up.w_lo, P}, S, F, P, e3, st)) return -1;
             GemmEpi e4;
             e4.mode = EPI_GATED; e4.bias = B.down.b; e4.out0 = dn; e4.ld0 = P; e4.aux = xm; e4.ld_aux = P;
@@ -809,7 +810,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             const float * xin = x0 + (size_t) l * S * P;
             // MLP half
             GemmEpi e1;
-            e1.mode = EPI_DGELU_SPLIT; e1.aux = w.u + tl * S * F; e1.ld_aux = F; e1.out_hi = w.du_hi; e1.out_lo = w.du_lo; e1.ld_split = F;
+            e1.mode = EPI_MUL_SPLIT; e1.aux = w.u + tl * S * F; e1.ld_aux = F; e1.out_hi = w.du_hi; e1.out_lo = w.du_lo; e1.ld_split = F;
             if (wgemm({w.d_hi, w.d_lo, P}, {B.down.wt_hi, B.down.wt_lo, P}, S, F, P, e1, st)) return -1;
             GemmEpi e2;
             e2.out0 = w.gh; e2.ld0 = P;

@@ -137,7 +137,7 @@ struct Workspace {
     float * gstate = nullptr;         // [(T+1) S][D] cost gradients wrt the states
     float * xs = nullptr;             // [T][L+1][S][P]
     float * xmid = nullptr, * o = nullptr, * dn = nullptr;   // [T][L][S][P]
-    float * u = nullptr;              // [T][L][S][F]
+    float * u = nullptr;              // [T][L][S][F] gelu' at the up projection's pre-activation
     LnStats * sta0 = nullptr, * sta1 = nullptr, * stm0 = nullptr, * stm1 = nullptr;   // [T][L][S]
     LnStats * stn = nullptr;          // [T][S]
     float * yn = nullptr;             // final-norm output when a projection follows [T][S][P]

@@ -23,6 +23,8 @@ enum EpiMode : int {
     EPI_GATED = 3,       // out0 = o = acc + bias ; out1 = aux + o * gate
     EPI_DGELU_SPLIT = 4, // (out_hi, out_lo) = split(acc * gelu'(aux))
     EPI_F32_SPLIT = 5,   // out0 = acc + bias and (out_hi, out_lo) = split(acc + bias)
+    EPI_GELU_D_SPLIT = 6, // u = acc + bias: out0 = gelu'(u) ; (out_hi, out_lo) = split(gelu(u)) (one erf for both)
+    EPI_MUL_SPLIT = 7,   // (out_hi, out_lo) = split(acc * aux): EPI_DGELU_SPLIT with gelu' stored by EPI_GELU_D_SPLIT
 };
 
 struct GemmEpi {
