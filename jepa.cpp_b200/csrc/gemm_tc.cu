@@ -56,7 +56,7 @@ __device__ __forceinline__ void gelu_and_grad(float u, float & g, float & d) {
     g = 0.5f * u * (1.0f + e);
     d = 0.5f * (1.0f + e) + u * 0.39894228040143268f * expf(-0.5f * u * u);
 }
-template <int MODE> constexpr bool has_bias() { return MODE != EPI_DGELU_SPLIT && MODE != EPI_MUL_SPLIT; }
+template <int MODE> __host__ __device__ constexpr bool has_bias() { return MODE != EPI_DGELU_SPLIT && MODE != EPI_MUL_SPLIT; }
 
 // The fused epilogue of one output element (v = the accumulated product, before the bias). The mode is a
 // template parameter throughout, so that a kernel holds the code of its own epilogue only: these kernels
@@ -447,23 +447,23 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 stage(a1, b1, 32);
             }
         }
+        if (splits == 1) {
+            // one CTA per tile: the accumulator goes to shared memory a row per thread, and all twelve warps
+            // apply the fused epilogue from there row-major (coalesced loads and stores, after the sync below)
+            if (!have) abort_sh = 1;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN && splits == 1; c0 += 32) {
-            uint32_t a[32], b[32];
-            tmem_ld32(trow + (uint32_t) c0, a);
-            tmem_ld32(trow + (uint32_t) (BN + c0), b);
-            {
-                // one CTA per tile: straight from the accumulator to the fused epilogue, a row per thread
-                const int row = m0 + r;
-                if (have && row < M) {
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t a[32], b[32];
+                tmem_ld32_async(trow + (uint32_t) c0, a);
+                tmem_ld32_async(trow + (uint32_t) (BN + c0), b);
+                tmem_ld_wait(a);
+                tmem_ld_wait(b);
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        const float4 v = make_float4(__uint_as_float(a[j]) + __uint_as_float(b[j]),
-                                                     __uint_as_float(a[j + 1]) + __uint_as_float(b[j + 1]),
-                                                     __uint_as_float(a[j + 2]) + __uint_as_float(b[j + 2]),
-                                                     __uint_as_float(a[j + 3]) + __uint_as_float(b[j + 3]));
-                        apply_epi4<MODE>(ep, row, n0 + c0 + j, N, v);
-                    }
+                for (int j = 0; j < 32; j += 4) {
+                    *(float4 *) &tile[r * PLD + c0 + j] = make_float4(__uint_as_float(a[j]) + __uint_as_float(b[j]),
+                                                                      __uint_as_float(a[j + 1]) + __uint_as_float(b[j + 1]),
+                                                                      __uint_as_float(a[j + 2]) + __uint_as_float(b[j + 2]),
+                                                                      __uint_as_float(a[j + 3]) + __uint_as_float(b[j + 3]));
                 }
             }
         }
@@ -486,6 +486,14 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();   // the accumulator has been read (and this CTA's own partial rows are staged)
+    if (splits == 1 && nkt > 0 && !*(volatile int *) &abort_sh) {
+#pragma unroll 2
+        for (int idx = (int) threadIdx.x; idx < BM * C4; idx += NT) {
+            const int i = idx / C4, cc = (idx % C4) * 4;
+            const int row = m0 + i;
+            if (row < M) apply_epi4<MODE>(ep, row, n0 + cc, N, *(const float4 *) &tile[(size_t) i * PLD + cc]);
+        }
+    }
     if (splits > 1) {
         const bool got = mbar_wait(&recv_bar, 0, 4, &g_gemm_error);   // the peers' partial rows have landed
         cluster_arrive_relaxed();   // this CTA has received everything
@@ -679,8 +687,8 @@ bool vec_ok(const GemmEpi & ep, int N) {
 
 }  // namespace
 
-// Tile / split choice: wide outputs (the time-batched adaLN modulation) take 128-wide tiles, one CTA
-// per tile; the per-step products take 64-wide tiles and split K over a cluster of up to 8 CTAs, the
+// Tile / split choice: wide outputs and wide products take 128-wide tiles, one CTA per tile; the
+// per-step products of the narrower predictors take 64-wide tiles and split K over a cluster of up to 8 CTAs, the
 // largest split at which two rows of tiles (256 rows, or two candidate chains of 128 side by side) are
 // resident at once: one wave, each CTA streaming a K-slice, instead of a dozen CTAs streaming everything
 // or a second wave of the clusters that did not fit.
@@ -699,7 +707,10 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
     e.vec = vec_ok(ep, N) ? 1 : 0;
     // The tile shape and the K split depend on (N, K) only, never on M: a row's arithmetic (and so its
     // bits) is then the same whatever batch of rows it is computed in.
-    if (N >= 4096) return launch_mode<128, 3>(A, B, M, N, K, 1, e, st);
+    // Wide outputs (the adaLN modulation of every step at once) and wide products (output and reduction both
+    // at least 768: the widest predictors, which plan thousands of candidates, so there are tiles enough to
+    // fill the device) take 128-wide tiles and no K split: twice the columns per A tile read, no exchange.
+    if (N >= 4096 || (N >= 768 && K >= 768)) return launch_mode<128, 3>(A, B, M, N, K, 1, e, st);
     const int num_k = (K + BK - 1) / BK;
     const int tiles2 = 2 * ((N + 63) / 64);
     int splits = 1;
