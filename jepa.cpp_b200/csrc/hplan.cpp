@@ -49,8 +49,11 @@ HPlanner::~HPlanner() {
     for (cudaEvent_t e : ev) cudaEventDestroy(e);
 }
 
-int HPlanner::streams_for(int S) const {
-    const int n = n_streams > 0 ? n_streams : (S >= 256 ? 2 : 1);
+// Automatic chain count (measured on one B200): the narrow predictors, whose per-step products split K
+// over clusters, run best in chains of about 256 candidates (up to four side by side); the wide ones
+// (width >= 768, one CTA per 128 x 128 tile) in two chains once there are 512 candidates.
+int HPlanner::streams_for(int S, int width) const {
+    const int n = n_streams > 0 ? n_streams : width >= 768 ? (S >= 512 ? 2 : 1) : std::min(4, S / 256);
     return std::max(1, std::min({n, S, 8}));
 }
 

@@ -200,7 +200,7 @@ struct HPlanner {
     bool build(const jepa_model & m);
     // chunk c of n_chunks candidate streams of one level (created in order; n_chunks sizes the memory decision)
     Workspace * workspace(int level, int S, int T, const CostSpec & cs, int chunk = 0, int n_chunks = 1);
-    int streams_for(int S) const;
+    int streams_for(int S, int width) const;   // candidate chains for S candidates of a level of this predictor width
     bool ensure_streams(int n);
     // costs [S] and (optionally) grad [S][T][A] of host actions; all host buffers
     int plan_cost(const CostSpec & cs, const float * actions, int S, float * costs, float * grad);

@@ -233,7 +233,7 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, Noise
     out.iters = 0;
     if (Sl < 1) { log("jepa: hjepa solve: %d candidates over %d GPUs leaves rank %d without any\n", S, world, rank); return -1; }
     // the rank's candidates as nc streams of consecutive rows: stream c holds rows [cr[c], cr[c + 1])
-    const int nc = streams_for(Sl);
+    const int nc = streams_for(Sl, L.P);
     std::vector<int> cr((size_t) nc + 1);
     for (int c = 0; c <= nc; c++) cr[(size_t) c] = (int) ((int64_t) Sl * c / nc);
     std::vector<Workspace *> wc((size_t) nc);
