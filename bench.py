@@ -69,6 +69,32 @@ def plan_flops(spec: synth.HJepaSpec, plans: list, S: int) -> float:
     return total
 
 
+def chains_for(S: int, width: int) -> int:
+    """The planner's automatic candidate-chain count (HPlanner::streams_for, csrc/hplan.cpp)."""
+    n = (2 if S >= 512 else 1) if width >= 768 else min(4, S // 256)
+    return max(1, min(n, S, 8))
+
+
+def step_gemm_roofline(L, lv, S1: int, reps: int = 50):
+    """The planner's dominant kernel (k_gemm_tf32x3) at the lowest level's per-step shapes -- M x P x P (value /
+    output), M x F x P (up), M x P x F (down), M = the candidates of one chain -- each timed live with CUDA events
+    over `reps` back-to-back launches through jepa_b200_gemm_bench. Returns (TFLOP/s, [(M, N, K, us)])."""
+    P = lv.pred_dim or lv.embed_dim
+    M = S1 // chains_for(S1, P)
+    fn = L.jepa_b200_gemm_bench
+    fn.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
+    fl = ms_tot = 0.0
+    shapes = []
+    for (N, K) in ((P, P), (lv.ffn_dim, P), (P, lv.ffn_dim)):
+        ms = C.c_double()
+        if fn(M, N, K, reps, C.byref(ms)) != 0:
+            return None, []
+        fl += 2.0 * M * N * K
+        ms_tot += ms.value
+        shapes.append((M, N, K, round(ms.value * 1e3, 2)))
+    return fl / (ms_tot / 1e3) / 1e12, shapes
+
+
 def peaks(sustained: bool = False):
     try:
         with open(PEAKS_PATH) as f:
@@ -253,6 +279,7 @@ def run_reference(args):
 AC_UNIT = "CEM candidates/s"
 AC_K, AC_H, AC_ITERS, AC_TOPK, AC_SEED_FRAMES = 800, 2, 10, 10, 2
 AC_GEMM_TRAFFIC = 2.06e9     # DRAM bytes per k_gemm_f16 launch at the benchmark's rows (profiles/gemm_f16_ac128.md)
+GEMM_SMALL_TRAFFIC = 2.01e6   # DRAM bytes of one 256 x 384 x 384 k_gemm_tf32x3 launch (profiles/gemm_small_256x384x384.md)
 
 
 def ac_spec() -> synth.ACSpec:
@@ -498,6 +525,7 @@ def run_ours(args):
     t = torch.tensor([dev_ms, wall], dtype=torch.float64)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    gemm_tf, gemm_shapes = step_gemm_roofline(jlib.load(), spec.levels[0], S1) if rank == 0 else (None, [])
     dev_ms, wall = float(t[0]), float(t[1])
     # in units of the config's candidates (256 for config 2): N of them per step under weak scaling
     grad_steps = sum(p["n_steps"] for p in plans) * args.steps * (1 if strong else world)
@@ -523,10 +551,15 @@ def run_ours(args):
                        "arith": "3xTF32 tensor-core GEMMs (tcgen05), f32 element-wise"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved_tf / peak_tf, "traffic": None,
-                         "scope": "whole plan: algorithmic GEMM FLOPs / device time of the jepa_hjepa_plan call",
-                         "peak_kind": f"bf16 dense, {peak_kind}"},
+            "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": (gemm_tf / peak_tf) if gemm_tf else None, "traffic": GEMM_SMALL_TRAFFIC,
+                         "traffic_note": "DRAM read + write of one 256 x 384 x 384 launch from ncu "
+                                         "(profiles/gemm_small_256x384x384.md); algorithmic 1.97 MB",
+                         "kernel": "k_gemm_tf32x3 (tcgen05 kind::tf32, 3xTF32)",
+                         "scope": "2 M N K / CUDA-event duration per launch at the lowest level's per-step shapes "
+                                  "(M, N, K, us per launch): " + ", ".join(f"{m}x{n}x{k} {u}" for m, n, k, u in gemm_shapes),
+                         "peak_kind": f"bf16 dense, {peak_kind}",
+                         "whole_plan_tflops": achieved_tf, "whole_plan_frac": achieved_tf / peak_tf},
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
