@@ -66,6 +66,35 @@ def test_plan_cost_matches_oracle(tmpdir_mod, ftype, level, goal_level, T, dense
     assert np.array_equal(c2, costs)
 
 
+def wide(tmp, ftype):
+    """A predictor 768 wide (one block, MLP 768): its per-step products and its adaLN GEMM (6 x 768 outputs)
+    take the 128-wide unsplit tiles, every epilogue mode included."""
+    spec = synth.HJepaSpec(levels=[synth.Level(768, 1, 12, 768, 2)], ftype=ftype, rand_all=True, cond_std=0.3, w_std=0.03)
+    path = os.path.join(tmp, f"wide-{ftype}.gguf")
+    if not os.path.exists(path):
+        synth.write_hjepa(path, spec, seed=9)
+    return path
+
+
+@pytest.mark.parametrize("ftype", ["f32", "q8_0"])
+def test_wide_predictor_matches_oracle(tmpdir_mod, ftype):
+    path = wide(tmpdir_mod, ftype)
+    m = O.Model(path)
+    P = Planner(path)
+    rng = np.random.default_rng(31)
+    s0 = rng.normal(size=768).astype(np.float32)
+    goal = rng.normal(size=(1, 768)).astype(np.float32)
+    acts = rng.uniform(-1, 1, (37, 3, 2)).astype(np.float32)
+    costs, grad = P.plan_cost(1, s0, goal, acts)
+    oc, og, _ = O.batch_cost(m, O.CostSpec(level=1, horizon=3, s0=s0, goal=goal), acts)
+    assert rel_err(costs, oc) < REL, rel_err(costs, oc)
+    assert rel_err(grad, og) < REL, rel_err(grad, og)
+    # unsplit tiles: a row's bits do not depend on the batch either
+    c_sub, g_sub = P.plan_cost(1, s0, goal, np.ascontiguousarray(acts[5:20]))
+    assert np.array_equal(costs[5:20], c_sub)
+    assert np.array_equal(grad[5:20], g_sub)
+
+
 def test_rows_do_not_depend_on_the_batch(tmpdir_mod):
     """A candidate's cost and gradient are the same bits whatever batch it is evaluated in (what makes the
     candidate sharding across GPUs exact)."""

@@ -11,8 +11,11 @@ from jepa_b200.gguf_write import quantize_q4_0, quantize_q8_0
 pytestmark = pytest.mark.gpu
 
 
+# split-K 64-wide tiles (N or K < 768), and the 128-wide unsplit tiles (N, K >= 768, or N >= 4096) with ragged
+# M and N edges
 @pytest.mark.parametrize("M,N,K", [(128, 64, 32), (256, 384, 384), (200, 130, 100), (1, 8, 4), (512, 2304, 384),
-                                   (256, 384, 1536), (4096, 1152, 384)])
+                                   (256, 384, 1536), (4096, 1152, 384), (300, 768, 768), (257, 800, 1000),
+                                   (130, 4100, 64), (33, 3072, 768)])
 def test_gemm_3xtf32_matches_f64(M, N, K):
     L = jlib.load()
     rng = np.random.default_rng(M * 7 + N + K)
