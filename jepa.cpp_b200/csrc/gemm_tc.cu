@@ -242,7 +242,8 @@ __host__ __device__ constexpr int split_rows(int splits) { return (BM + splits -
 
 // One 128 x BN tile of C per CTA, or -- split-K -- one K-slice of it per CTA of a (1, 1, splits) cluster.
 //
-// splits == 1: the epilogue warps go from TMEM straight to the fused epilogue, a row per thread.
+// splits == 1: the four accumulator warps stage the tile in shared memory (a row per thread, from TMEM),
+// and all twelve warps apply the fused epilogue from there row-major: coalesced loads and stores.
 // splits > 1 (a reduce-scatter over distributed shared memory): CTA p of the cluster owns rows
 // [p R, p R + R) of the tile (R = ceil(128 / splits)). After the mainloop the epilogue warps stage the
 // partial tile in shared memory and one thread sends each peer its rows with one bulk copy into the peer's
@@ -274,13 +275,13 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) (BN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
     constexpr uint32_t IDESC2 = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) ((2 * BN) >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
     static_assert(2 * BN <= 256 && B_BYTES % 1024 == 0, "the stacked B operand is one MMA's N (at most 256) in whole swizzle groups");
-    // every thread reduces and stores PER float4 of the CTA's rows in one pass (at most 64 rows x BN at 2 splits)
+    // split-K: every thread reduces and stores PER float4 of the CTA's rows in one pass (at most 64 rows x BN at 2 splits)
     constexpr int C4 = BN / 4, NT = GEMM_THREADS, PER = (split_rows(2) * C4 + NT - 1) / NT;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     constexpr int PLD = BN + 4;            // padded row of the staged partial tile (conflict-free float4 row writes)
-    float * tile = (float *) smem;         // split-K: this CTA's partial tile [BM][PLD], in the idle pipeline buffers
+    float * tile = (float *) smem;         // the staged accumulator tile [BM][PLD], in the idle pipeline buffers
     // split-K: the peers' partials [splits - 1][R][PLD]; peer q's rows go to slot q (q < this rank) or q - 1
     float * recv = (float *) (smem + (size_t) STAGES * STAGE_BYTES);
     static_assert((size_t) BM * PLD * 4 <= (size_t) STAGES * STAGE_BYTES, "staged tile must fit in the pipeline buffers");
