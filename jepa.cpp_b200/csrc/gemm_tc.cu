@@ -473,10 +473,11 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             asm volatile("bar.sync 1, 128;" ::: "memory");
             cluster_wait();   // every peer's receive barrier is initialised
-            if (threadIdx.x == 64) {
-                for (int p = 0; p < splits; p++) {
-                    const int prs = p * R, pre = min(BM, prs + R);
-                    if (p == split || pre <= prs) continue;
+            if (warp == 2 && lane < splits) {
+                // one copy per lane: lane p sends peer p its rows (the copies are issued side by side)
+                const int p = lane;
+                const int prs = p * R, pre = min(BM, prs + R);
+                if (p != split && pre > prs) {
                     const int slot = split < p ? split : split - 1;   // this CTA's slot in peer p's receive buffer
                     const uint32_t dst = peer_addr(smem_u32(recv + (size_t) slot * R * PLD), (uint32_t) p);
                     bulk_to_peer(dst, smem_u32(tile + (size_t) prs * PLD), (uint32_t) ((pre - prs) * PLD * 4),
@@ -533,6 +534,177 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     }
 }
 
+
+// Wide products (N, K >= 768) and wide outputs (N >= 4096): persistent, one CTA per SM walking 128 x 128
+// tiles (n fastest, so CTAs that run side by side share A rows), no K split. Warp 0 issues the TMA loads
+// (A_hi, A_lo, B_hi, B_lo; 64 KB a stage, 3 stages), one thread of warp 1 the MMAs -- per K-step one of
+// N = 256 over the stacked B_hi|B_lo operand and one of N = 128 (the same two as the split kernel) -- into one
+// of two 256-column TMEM accumulator pairs, so that warps 2..9 drain tile i (two warps per lane quadrant,
+// 64 columns each) while tile i+1's products run. A draining warp stages 32 rows x 32 columns in its own
+// 4 KB shared buffer (16-byte chunk c of row r at c ^ (r & 7)) and applies the fused epilogue from there
+// four rows per instruction: coalesced loads and stores. A tile's arithmetic is the split kernel's at
+// one split (the same MMAs in the same order), so a row's bits do not depend on the batch.
+constexpr int PBN = 128, PSTAGES = 3, PEPI_WARPS = 8, PTHREADS = 64 + 32 * PEPI_WARPS;
+constexpr uint32_t PSTAGE_BYTES = 2 * BM * BK * 4 + 2 * PBN * BK * 4;
+constexpr size_t PSMEM_BYTES = (size_t) PSTAGES * PSTAGE_BYTES + (size_t) PEPI_WARPS * 32 * 32 * 4 + 1024;
+static_assert(PSMEM_BYTES + 256 <= 227 * 1024, "persistent tf32x3 GEMM: stages and staging buffers fit");
+
+template <int MODE>
+__global__ void __launch_bounds__(PTHREADS, 1)
+k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
+                const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
+                int M, int N, int K, const __grid_constant__ GemmEpi ep) {
+    constexpr uint32_t A_BYTES = BM * BK * 4;
+    constexpr uint32_t B_BYTES = PBN * BK * 4;
+    constexpr uint32_t TMEM_COLS = 4 * PBN;   // two accumulator pairs [hi*hi | cross terms], 256 columns each
+    constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) (PBN >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
+    constexpr uint32_t IDESC2 = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t) ((2 * PBN) >> 3) << 17) | ((uint32_t) (BM >> 4) << 24);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    __shared__ __align__(8) uint64_t full_bar[PSTAGES];
+    __shared__ __align__(8) uint64_t empty_bar[PSTAGES];
+    __shared__ __align__(8) uint64_t accf_bar[2];   // MMA -> epilogue: accumulator pair b holds a finished tile
+    __shared__ __align__(8) uint64_t acce_bar[2];   // epilogue -> MMA: accumulator pair b has been read
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_k = (K + BK - 1) / BK;
+    const int tiles_n = (N + PBN - 1) / PBN;
+    const int total = ((M + BM - 1) / BM) * tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PSTAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(&accf_bar[b], 1); mbar_init(&acce_bar[b], PEPI_WARPS); }
+        abort_sh = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(&tmem_base_sh)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (threadIdx.x == 32) {
+        asm volatile("prefetch.tensormap [%0];" :: "l"((uint64_t) &tA_hi) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"((uint64_t) &tA_lo) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"((uint64_t) &tB_hi) : "memory");
+        asm volatile("prefetch.tensormap [%0];" :: "l"((uint64_t) &tB_lo) : "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_sh;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int kt = 0;
+            for (int t = blockIdx.x; t < total && !*(volatile int *) &abort_sh; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * PBN;
+                for (int k = 0; k < num_k; k++, kt++) {
+                    const int s = kt % PSTAGES;
+                    const uint32_t ph = (uint32_t) (kt / PSTAGES) & 1u;
+                    if (kt >= PSTAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1, &g_gemm_error)) { abort_sh = 1; break; }
+                    if (*(volatile int *) &abort_sh) break;
+                    uint8_t * st = smem + (size_t) s * PSTAGE_BYTES;
+                    mbar_expect_tx(&full_bar[s], PSTAGE_BYTES);
+                    tma_load_2d(st, &tA_hi, k * BK, m0, &full_bar[s]);
+                    tma_load_2d(st + A_BYTES, &tA_lo, k * BK, m0, &full_bar[s]);
+                    tma_load_2d(st + 2 * A_BYTES, &tB_hi, k * BK, n0, &full_bar[s]);
+                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, k * BK, n0, &full_bar[s]);
+                }
+            }
+            if (*(volatile int *) &abort_sh) {
+                // let the copies already issued land before the CTA exits
+                for (int j = kt - PSTAGES < 0 ? 0 : kt - PSTAGES; j < kt; j++) {
+                    mbar_wait(&full_bar[j % PSTAGES], (uint32_t) (j / PSTAGES) & 1u, 5, &g_gemm_error);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int kt = 0, i = 0;
+            for (int t = blockIdx.x; t < total && !*(volatile int *) &abort_sh; t += gridDim.x, i++) {
+                const int b = i & 1;
+                if (i >= 2 && !mbar_wait(&acce_bar[b], (uint32_t) ((i >> 1) - 1) & 1u, 4, &g_gemm_error)) { abort_sh = 1; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t d = tmem + (uint32_t) (b * 2 * PBN);
+                for (int k = 0; k < num_k; k++, kt++) {
+                    const int s = kt % PSTAGES;
+                    const uint32_t ph = (uint32_t) (kt / PSTAGES) & 1u;
+                    if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error)) { abort_sh = 1; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t a_hi = smem_u32(smem + (size_t) s * PSTAGE_BYTES);
+                    const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES;   // B_lo follows B_hi
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; kk++) {
+                        const uint32_t off = (uint32_t) kk * 32;
+                        const uint64_t dbh = sw128_desc(b_hi + off);
+                        mma_kind_tf32(d, sw128_desc(a_hi + off), dbh, IDESC2, (k | kk) != 0);   // [hi*hi | hi*lo]
+                        mma_kind_tf32(d + PBN, sw128_desc(a_lo + off), dbh, IDESC, 1);           // + lo*hi
+                    }
+                    mma_commit(&empty_bar[s]);
+                }
+                if (*(volatile int *) &abort_sh) break;
+                mma_commit(&accf_bar[b]);
+            }
+        }
+    } else {
+        const int q = warp & 3;                 // TMEM lane quadrant this warp may read
+        const int half = (warp - 2) >> 2;       // which 64 of the tile's 128 columns
+        float * stage = (float *) (smem + (size_t) PSTAGES * PSTAGE_BYTES + (size_t) (warp - 2) * 32 * 32 * 4);
+        const uint32_t trow = tmem + ((uint32_t) (q * 32) << 16);
+        int i = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, i++) {
+            const int b = i & 1;
+            const bool ok = mbar_wait(&accf_bar[b], (uint32_t) (i >> 1) & 1u, 3, &g_gemm_error);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (!ok || *(volatile int *) &abort_sh) { abort_sh = 1; break; }
+            const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * PBN;
+            const int row0 = m0 + q * 32;
+#pragma unroll 1
+            for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+                uint32_t x[32], y[32];
+                tmem_ld32_async(trow + (uint32_t) (b * 2 * PBN + c0), x);
+                tmem_ld32_async(trow + (uint32_t) (b * 2 * PBN + PBN + c0), y);
+                tmem_ld_wait(x);
+                tmem_ld_wait(y);
+                if (c0 == half * 64 + 32) {
+                    // the tile's last accumulator read by this warp: the MMA warp may refill the pair
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acce_bar[b]);
+                }
+                __syncwarp();   // the previous block's reads of the staging buffer are done
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    *(float4 *) &stage[lane * 32 + ((c ^ (lane & 7)) << 2)] =
+                        make_float4(__uint_as_float(x[4 * c]) + __uint_as_float(y[4 * c]),
+                                    __uint_as_float(x[4 * c + 1]) + __uint_as_float(y[4 * c + 1]),
+                                    __uint_as_float(x[4 * c + 2]) + __uint_as_float(y[4 * c + 2]),
+                                    __uint_as_float(x[4 * c + 3]) + __uint_as_float(y[4 * c + 3]));
+                }
+                __syncwarp();
+                if (row0 >= M || n0 + c0 >= N) continue;   // warp-uniform
+#pragma unroll 4
+                for (int j = 0; j < 8; j++) {
+                    const int idx = j * 32 + lane, r = idx >> 3, c = idx & 7;
+                    const int row = row0 + r;
+                    if (row < M) apply_epi4<MODE>(ep, row, n0 + c0 + 4 * c, N, *(const float4 *) &stage[r * 32 + ((c ^ (r & 7)) << 2)]);
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
 
 // ---------------------------------------------------------------------------------------------
 // host side: tensor maps and launch
@@ -658,6 +830,47 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
     return 0;
 }
 
+template <int MODE>
+int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
+    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+    if (!make_map(&ta_hi, A.hi, M, K, A.ld, BM) || !make_map(&ta_lo, A.lo, M, K, A.ld, BM) ||
+        !make_map(&tb_hi, B.hi, N, K, B.ld, PBN) || !make_map(&tb_lo, B.lo, N, K, B.ld, PBN)) {
+        log("jepa: gemm: cuTensorMapEncodeTiled refused an operand (M %d N %d K %d, ld %d / %d)\n", M, N, K, A.ld, B.ld);
+        return -1;
+    }
+    static std::mutex mu;
+    static bool done[64] = {};
+    static int sms[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!done[dev]) {
+            JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_p<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) PSMEM_BYTES));
+            JB_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+            done[dev] = true;
+        }
+    }
+    const long tiles = (long) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN);
+    const unsigned grid = (unsigned) std::max(1L, std::min<long>(tiles, sms[dev]));
+    JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE>, dim3(grid), dim3(PTHREADS), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep));
+    return 0;
+}
+
+int launch_p_mode(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
+    switch (ep.mode) {
+        case EPI_F32: return launch_p<EPI_F32>(A, B, M, N, K, ep, st);
+        case EPI_SPLIT: return launch_p<EPI_SPLIT>(A, B, M, N, K, ep, st);
+        case EPI_GELU_SPLIT: return launch_p<EPI_GELU_SPLIT>(A, B, M, N, K, ep, st);
+        case EPI_GATED: return launch_p<EPI_GATED>(A, B, M, N, K, ep, st);
+        case EPI_DGELU_SPLIT: return launch_p<EPI_DGELU_SPLIT>(A, B, M, N, K, ep, st);
+        case EPI_F32_SPLIT: return launch_p<EPI_F32_SPLIT>(A, B, M, N, K, ep, st);
+        case EPI_GELU_D_SPLIT: return launch_p<EPI_GELU_D_SPLIT>(A, B, M, N, K, ep, st);
+        case EPI_MUL_SPLIT: return launch_p<EPI_MUL_SPLIT>(A, B, M, N, K, ep, st);
+        default: log("jepa: gemm: unknown epilogue mode %d\n", ep.mode); return -1;
+    }
+}
+
 // one kernel per epilogue mode
 template <int BN, int STAGES>
 int launch_mode(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
@@ -710,8 +923,9 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
     // bits) is then the same whatever batch of rows it is computed in.
     // Wide outputs (the adaLN modulation of every step at once) and wide products (output and reduction both
     // at least 768: the widest predictors, which plan thousands of candidates, so there are tiles enough to
-    // fill the device) take 128-wide tiles and no K split: twice the columns per A tile read, no exchange.
-    if (N >= 4096 || (N >= 768 && K >= 768)) return launch_mode<128, 3>(A, B, M, N, K, 1, e, st);
+    // fill the device) take the persistent kernel's 128 x 128 tiles and no K split: twice the columns per A
+    // tile read, no exchange, and each tile's epilogue overlapping the next tile's products.
+    if (N >= 4096 || (N >= 768 && K >= 768)) return launch_p_mode(A, B, M, N, K, e, st);
     const int num_k = (K + BK - 1) / BK;
     const int tiles2 = 2 * ((N + 63) / 64);
     int splits = 1;
