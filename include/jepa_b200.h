@@ -63,8 +63,9 @@ double jepa_b200_last_plan_ms(const jepa_context * ctx);
 long long jepa_b200_last_plan_launches(const jepa_context * ctx);
 
 // Candidate streams of the H-JEPA solves on this context: a level's candidates (this GPU's share) run as
-// n independent chains of consecutive rows side by side on the GPU (1..8; 0 = automatic: 2 from 256
-// candidates up, else 1). Results do not depend on n (rows never interact), as the reference's results do
+// n independent chains of consecutive rows side by side on the GPU (1..8; 0 = automatic: for predictors
+// narrower than 768 one chain per 256 candidates, at most 4; for wider ones 2 from 512 candidates up, else 1).
+// Results do not depend on n (rows never interact), as the reference's results do
 // not depend on its thread count (its jepa_context_params.n_threads). Returns 0, or -1 for a non-H-JEPA
 // context or n out of range.
 int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n);
