@@ -6,7 +6,7 @@
   tests/golden/rope3d_hf.npz   the reference's RoPE golden vectors for the tiled layout the AC predictor
                                uses (tests/vectors/rope3d/hd64_*_hf_*), copied so the GPU box has them
 
-    python tests/golden/make_golden_ac.py        (needs the reference tree; run in the build container)
+    JEPA_REF=/path/to/jepa.cpp python tests/golden/make_golden_ac.py     (needs the reference checkout)
 
 The model is not stored: tests rebuild it from MODEL (synth spec + seed) and check its sha256.
 """
@@ -22,7 +22,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = "/root/reference"
+REF = os.environ.get("JEPA_REF", "")
 sys.path.insert(0, os.path.join(ROOT, "jepa.cpp_b200"))
 
 from jepa_b200 import synth  # noqa: E402
@@ -42,6 +42,8 @@ def build_model(workdir: str) -> tuple[str, str]:
 
 
 def main() -> None:
+    if not REF:
+        sys.exit("set JEPA_REF to the reference checkout (its scripts/jepa_convert is imported)")
     sys.path.insert(0, os.path.join(REF, "scripts", "jepa_convert"))
     import selftest   # the reference's numpy spec (read-only import from the reference tree)
     out = {}
