@@ -45,6 +45,19 @@ int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms);
 #define JEPA_B200_NOALLOC_MAX_FLOATS (4u * 1024u * 1024u)
 int jepa_b200_gemm_noalloc(const float * A, const float * B, int M, int N, int K, float * C);
 
+// The failure path of the engine's bounded device waits, run on purpose without a fault: one CTA takes
+// tensor memory as the GEMM does, waits on an mbarrier that nothing arrives on with a bound of
+// `limit_cycles` SM clock cycles (1 .. 4e9; the kernels' own bound is 4e9, about 2 s), raises the GEMM's
+// error flag when the bound runs out, frees its tensor memory and returns. *code receives the flag as
+// the engine reads it after a call (9 for this check, 0 if the wait did not run out); the read resets
+// it. Returns 0 when the flag could be read and was reset, -1 otherwise. No counterpart in the reference
+// (its planners run on the host and have no device waits).
+int jepa_b200_check_wait_timeout(long long limit_cycles, int * code);
+
+// The same rows decoded on the host by the loader's CPU decoder (no GPU needed): the decoder the engine
+// uses for host-side tensors (recorded actions, the oracle's weights), checkable without a device.
+int jepa_b200_host_dequant(uint32_t ggml_type, const void * src, int64_t rows, int64_t ne0, float * dst);
+
 // Dequantise `rows` GGUF rows of `ne0` values of ggml type `ggml_type` (0 f32, 1 f16, 2 q4_0, 8 q8_0,
 // 30 bf16) from the host bytes `src` into host float32 `dst` by the device kernel the weight loader uses.
 int jepa_b200_dequant(uint32_t ggml_type, const void * src, int64_t rows, int64_t ne0, float * dst);

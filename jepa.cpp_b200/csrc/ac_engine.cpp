@@ -373,6 +373,7 @@ ACEngine * ac_engine_of(jepa_context * ctx, const char * fn) {
         }
         ctx->ac = std::move(e);
     }
+    if (device_flags_clear(ctx->stream)) return nullptr;
     return ctx->ac.get();
 }
 
@@ -566,8 +567,8 @@ int rollout(ACEngine & e, jepa_context * ctx, const RolloutReq & q, const char *
         }
     }
     JB_CUDA(cudaStreamSynchronize(st));
-    if (gemm_f16_error_flag(st) != 0) {
-        log("jepa: %s: a tensor-core GEMM timed out waiting on its pipeline; results are invalid\n", fn);
+    if (gemm_f16_error_flag(st) != 0 || attention_tc_error_flag(st) != 0) {
+        log("jepa: %s: a tensor-core kernel timed out waiting on its pipeline; results are invalid\n", fn);
         return -1;
     }
     return 0;
@@ -700,7 +701,10 @@ int predict(jepa_context * ctx, const float * context, int T, int B, const float
     }
     cudaEventRecord(ev.b, st);
     if (!cuda_ok(cudaStreamSynchronize(st), fn)) return fail();
-    if (gemm_f16_error_flag(st) != 0) { log("jepa: %s: a tensor-core GEMM timed out\n", fn); return fail(); }
+    if (gemm_f16_error_flag(st) != 0 || attention_tc_error_flag(st) != 0) {
+        log("jepa: %s: a tensor-core kernel timed out waiting on its pipeline\n", fn);
+        return fail();
+    }
     float ms = 0;
     cudaEventElapsedTime(&ms, ev.a, ev.b);
     ctx->last_ms = ms;

@@ -443,9 +443,19 @@ int attention_tc(const AttnArgs & a, cudaStream_t st) {
 
 int attention_tc_error_flag(cudaStream_t st) {
     int v = 0;
-    cudaMemcpyFromSymbolAsync(&v, g_attn_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
-    cudaStreamSynchronize(st);
+    static const int zero = 0;
+    if (!cuda_ok(cudaMemcpyFromSymbolAsync(&v, g_attn_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st), "reading the attention error flag") ||
+        !cuda_ok(cudaMemcpyToSymbolAsync(g_attn_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st), "resetting the attention error flag") ||
+        !cuda_ok(cudaStreamSynchronize(st), "reading the attention error flag")) {
+        return -1;
+    }
     return v;
+}
+
+int attention_tc_error_clear(cudaStream_t st) {
+    static const int zero = 0;
+    return cuda_ok(cudaMemcpyToSymbolAsync(g_attn_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st),
+                   "clearing the attention error flag") ? 0 : -1;
 }
 
 }  // namespace jb

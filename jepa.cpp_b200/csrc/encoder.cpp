@@ -160,6 +160,7 @@ int jepa_encode(jepa_context * ctx, const jepa_input * in, jepa_output * out) {
     int F = 1;
     for (const EncLayer & L : E.layers) F = std::max(F, L.up.out);
     cudaStream_t st = ctx->stream;
+    if (device_flags_clear(st)) return -1;
     const size_t R = (size_t) rows, wide = (size_t) std::max({3 * D, F, K});
     DevBuf patches, p_hi, p_lo, pe, X, X2, h_hi, h_lo, qkv, o, o_hi, o_lo, a, u, g_hi, g_lo, y;
     if (!patches.alloc(pr.size()) || !p_hi.alloc(pr.size()) || !p_lo.alloc(pr.size()) || !pe.alloc((size_t) items * n_patches * D) ||

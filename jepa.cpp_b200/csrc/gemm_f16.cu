@@ -445,9 +445,19 @@ int gemm_f16(const __half * A, int lda, const __half * B, int ldb, int M, int N,
 
 int gemm_f16_error_flag(cudaStream_t st) {
     int v = 0;
-    cudaMemcpyFromSymbolAsync(&v, g_f16_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
-    cudaStreamSynchronize(st);
+    static const int zero = 0;
+    if (!cuda_ok(cudaMemcpyFromSymbolAsync(&v, g_f16_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st), "reading the f16 GEMM error flag") ||
+        !cuda_ok(cudaMemcpyToSymbolAsync(g_f16_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st), "resetting the f16 GEMM error flag") ||
+        !cuda_ok(cudaStreamSynchronize(st), "reading the f16 GEMM error flag")) {
+        return -1;
+    }
     return v;
+}
+
+int gemm_f16_error_clear(cudaStream_t st) {
+    static const int zero = 0;
+    return cuda_ok(cudaMemcpyToSymbolAsync(g_f16_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st),
+                   "clearing the f16 GEMM error flag") ? 0 : -1;
 }
 
 }  // namespace jb

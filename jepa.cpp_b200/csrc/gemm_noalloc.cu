@@ -55,12 +55,17 @@ extern "C" int jepa_b200_gemm_noalloc(const float * A, const float * B, int M, i
     float * b = a_lo + mk, * b_hi = b + nk, * b_lo = b_hi + nk;
     float * c = b_lo + nk;
     cudaStream_t st = 0;   // the legacy default stream: no stream object to create
+    // a timeout flag left by an earlier call that failed before reading it must not fail this one
+    if (jb::gemm_error_clear(st) != 0) return -1;
     JB_CUDA(cudaMemcpyAsync(a, A, (size_t) M * K * 4, cudaMemcpyHostToDevice, st));
     JB_CUDA(cudaMemcpyAsync(b, B, (size_t) N * K * 4, cudaMemcpyHostToDevice, st));
     // every element the kernels read is written first (the split planes, then C in full), so stale
     // contents left by an earlier call need no clearing
     jb::split_f32(a, K, a_hi, a_lo, K, M, K, st);
     jb::split_f32(b, K, b_hi, b_lo, K, N, K, st);
+    // a launch that failed (configuration errors are not sticky, so the synchronise below would not
+    // report it) would leave the GEMM reading the split planes of the previous call
+    JB_CUDA(cudaGetLastError());
     jb::GemmEpi ep;
     ep.mode = jb::EPI_F32;
     ep.out0 = c;
@@ -69,7 +74,7 @@ extern "C" int jepa_b200_gemm_noalloc(const float * A, const float * B, int M, i
     JB_CUDA(cudaMemcpyAsync(C, c, (size_t) M * N * 4, cudaMemcpyDeviceToHost, st));
     JB_CUDA(cudaStreamSynchronize(st));
     if (jb::gemm_error_flag(st) != 0) {
-        jb::log("jepa: jepa_b200_gemm_noalloc: the tensor-core kernel timed out waiting on its pipeline\n");
+        jb::log("jepa: jepa_b200_gemm_noalloc: the tensor-core kernel timed out waiting on its pipeline (or its flag could not be read)\n");
         return -1;
     }
     return 0;

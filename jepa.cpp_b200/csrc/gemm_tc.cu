@@ -939,9 +939,55 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
 
 int gemm_error_flag(cudaStream_t st) {
     int v = 0;
-    cudaMemcpyFromSymbolAsync(&v, g_gemm_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
-    cudaStreamSynchronize(st);
+    static const int zero = 0;
+    // read, then reset on the same stream: a timeout is reported once, to the call that saw it
+    if (!cuda_ok(cudaMemcpyFromSymbolAsync(&v, g_gemm_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st), "reading the GEMM error flag") ||
+        !cuda_ok(cudaMemcpyToSymbolAsync(g_gemm_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st), "resetting the GEMM error flag") ||
+        !cuda_ok(cudaStreamSynchronize(st), "reading the GEMM error flag")) {
+        return -1;
+    }
     return v;
+}
+
+// The failure path of the bounded waits, exercised on purpose: one CTA takes TMEM like the GEMM does,
+// initialises an mbarrier that nothing will ever arrive on, and waits on it with a short limit. The wait
+// gives up, raises g_gemm_error with `code`, and the CTA releases its TMEM and returns: the same steps a
+// GEMM takes when its pipeline stalls, with nothing in flight.
+__global__ void k_wait_timeout_check(long long limit, int code) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t tmem_base_sh;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(&tmem_base_sh)), "r"(32) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_sh;
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, code, &g_gemm_error, limit);   // nobody arrives: runs out
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(32) : "memory");
+    }
+}
+
+int wait_timeout_check(long long limit_cycles, int code, cudaStream_t st) {
+    k_wait_timeout_check<<<1, 64, 0, st>>>(limit_cycles, code);
+    return cuda_ok(cudaGetLastError(), "k_wait_timeout_check") ? 0 : -1;
+}
+
+int gemm_error_clear(cudaStream_t st) {
+    static const int zero = 0;
+    return cuda_ok(cudaMemcpyToSymbolAsync(g_gemm_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st),
+                   "clearing the GEMM error flag") ? 0 : -1;
 }
 
 }  // namespace jb

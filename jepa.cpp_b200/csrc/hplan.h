@@ -160,7 +160,8 @@ struct Workspace {
     ~Workspace();
 };
 
-// What one batch_cost evaluates (reference: cost_spec, src/hjepa-plan.cpp:689-701)
+// One cost evaluation: which level plans how far, scored against which goal (the reference's cost
+// specification, src/hjepa-plan.cpp:689-701)
 struct CostSpec {
     int level = 1, horizon = 1;
     const float * s0 = nullptr;
@@ -178,7 +179,7 @@ struct SolveOut {
     int iters = 0;
 };
 
-struct NoiseSource;
+class DrawSource;
 
 struct HPlanner {
     jepa_context * ctx = nullptr;
@@ -204,7 +205,7 @@ struct HPlanner {
     bool ensure_streams(int n);
     // costs [S] and (optionally) grad [S][T][A] of host actions; all host buffers
     int plan_cost(const CostSpec & cs, const float * actions, int S, float * costs, float * grad);
-    int solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, NoiseSource & noise, SolveOut & out);
+    int solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, DrawSource & draws, SolveOut & out);
 
     // pieces
     int forward(Workspace & w, const CostSpec & cs, bool want_grad);

@@ -174,6 +174,7 @@ int jepa_hjepa_predict(jepa_context * ctx, int level, const float * states, cons
     cudaEventDestroy(e1);
     ctx->last_ms = ms;
     ctx->last_launches = pm->launches;
+    if (gemm_error_flag(st)) { free(data); log("jepa: jepa_hjepa_predict: a tensor-core kernel gave up waiting on its pipeline\n"); return -1; }
     out->data = data;
     out->n_tokens = T;
     out->dim = Do;
@@ -227,6 +228,7 @@ int jepa_hjepa_rollout(jepa_context * ctx, int level, const float * states, int 
     cudaEventDestroy(e1);
     ctx->last_ms = ms;
     ctx->last_launches = pm->launches;
+    if (gemm_error_flag(st)) { log("jepa: jepa_hjepa_rollout: a tensor-core kernel gave up waiting on its pipeline\n"); return -1; }
     return 0;
 }
 

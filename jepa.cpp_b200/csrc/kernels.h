@@ -51,8 +51,15 @@ struct SplitMat {                    // a split operand: two float32 planes with
 // Returns 0, or -1 after logging (unsupported shape / a CUDA error).
 int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st);
 
-// Error flag the tensor-core kernels raise when a bounded wait gives up (0 = fine). Host reads it.
+// Error flag the tensor-core kernels raise when a bounded wait gives up. gemm_error_flag returns it
+// (0 = fine, the waiter's code otherwise, -1 when the flag could not be read) and resets it to 0 on the
+// stream; gemm_error_clear only resets it (at the start of an API call, so that a flag left by an
+// earlier call that failed for another reason does not fail this one).
 int gemm_error_flag(cudaStream_t st);
+int gemm_error_clear(cudaStream_t st);
+// Launches one CTA that takes TMEM, waits on an mbarrier nothing arrives on with a bound of limit_cycles
+// (clock64), raises the GEMM error flag with `code` when the bound runs out, frees its TMEM and returns.
+int wait_timeout_check(long long limit_cycles, int code, cudaStream_t st);
 
 // ------------------------------------------------------------------------------------------
 // SIMT linear for shapes the tensor-core path does not take (tiny K or N):
@@ -191,7 +198,8 @@ struct AcGemmEpi {
 
 // C[M,N] = A[M,K] * B[N,K]^T, A and B f16 row-major (K contiguous), tcgen05 kind::f16, f32 accumulate
 int gemm_f16(const __half * A, int lda, const __half * B, int ldb, int M, int N, int K, const AcGemmEpi & ep, cudaStream_t st);
-int gemm_f16_error_flag(cudaStream_t st);
+int gemm_f16_error_flag(cudaStream_t st);   // as gemm_error_flag, for the f16 GEMM
+int gemm_f16_error_clear(cudaStream_t st);
 
 // Attention of the rows of `n_qframes` consecutive frames over their key frames. Frames are whole blocks
 // (block-causal across frames: a frame sees every row of the frames up to its own), so no mask is needed
@@ -216,7 +224,12 @@ int attention_f16(const AttnArgs & a, cudaStream_t st);
 // the tcgen05 attention (attention_tc.cu): head width 64, at most 288 query rows per frame
 bool attention_tc_supported(const AttnArgs & a);
 int attention_tc(const AttnArgs & a, cudaStream_t st);
-int attention_tc_error_flag(cudaStream_t st);
+int attention_tc_error_flag(cudaStream_t st);   // as gemm_error_flag, for the tcgen05 attention
+int attention_tc_error_clear(cudaStream_t st);
+// resets all three flags on the stream (0 = done)
+inline int device_flags_clear(cudaStream_t st) {
+    return (gemm_error_clear(st) | gemm_f16_error_clear(st) | attention_tc_error_clear(st)) ? -1 : 0;
+}
 
 // Two-level row gather: in = (r / (g1 g2)) * s2 + ((r / g1) % g2) * s1 + off + r % g1  (g1 = 0: in = r)
 struct RowMap {

@@ -7,8 +7,11 @@
 
 #include "../../include/jepa_b200.h"
 
+#include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 namespace jb {
@@ -19,32 +22,116 @@ bool nccl_ok(ncclResult_t r, const char * what) {
     log("jepa: NCCL error in %s: %s\n", what, ncclGetErrorString(r));
     return false;
 }
+
+using Clock = std::chrono::steady_clock;
+
+long long env_timeout_ms() {
+    const char * v = getenv("JEPA_B200_NCCL_TIMEOUT_MS");
+    if (!v || !*v) return 120000;
+    const long long t = atoll(v);
+    return t > 0 ? t : 120000;
+}
 }  // namespace
 
 Shard::~Shard() {
-    if (comm) ncclCommDestroy(comm);
+    if (comm) {
+        if (aborted || ncclCommDestroy(comm) != ncclSuccess) ncclCommAbort(comm);
+    }
     if (dbuf) cudaFree(dbuf);
 }
 
-float Shard::min_f32(float v, cudaStream_t st) {
-    float * d = (float *) dbuf;
-    cudaMemcpyAsync(d, &v, 4, cudaMemcpyHostToDevice, st);
-    nccl_ok(ncclAllReduce(d, d, 1, ncclFloat, ncclMin, comm, st), "ncclAllReduce(min)");
-    float out = v;
-    cudaMemcpyAsync(&out, d, 4, cudaMemcpyDeviceToHost, st);
-    cudaStreamSynchronize(st);
-    return out;
+void Shard::abort(const char * why) {
+    log("jepa: shard rank %d of %d: %s; aborting the NCCL communicator\n", rank, world, why);
+    if (comm && !aborted) ncclCommAbort(comm);
+    comm = nullptr;
+    aborted = true;
 }
 
-void Shard::argmin_global(float cost, int gidx, float * cost_out, int * gidx_out, int * owner, cudaStream_t st) {
+bool Shard::settle(ncclResult_t r, const char * what) {
+    if (aborted || !comm) { log("jepa: %s: the NCCL communicator was aborted earlier\n", what); return false; }
+    if (r != ncclSuccess && r != ncclInProgress) {
+        log("jepa: NCCL error in %s: %s\n", what, ncclGetErrorString(r));
+        abort(what);
+        return false;
+    }
+    const auto t0 = Clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        if (ncclCommGetAsyncError(comm, &st) != ncclSuccess) st = ncclSystemError;
+        if (st == ncclSuccess) return true;
+        if (st != ncclInProgress) {
+            log("jepa: NCCL error in %s: %s\n", what, ncclGetErrorString(st));
+            abort(what);
+            return false;
+        }
+        if (std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0).count() > timeout_ms) {
+            log("jepa: %s did not complete within %lld ms (a rank that never joined or stopped?)\n", what, timeout_ms);
+            abort(what);
+            return false;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+bool Shard::finish(cudaStream_t st, const char * what) {
+    if (aborted || !comm) { log("jepa: %s: the NCCL communicator was aborted earlier\n", what); return false; }
+    const auto t0 = Clock::now();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(st);
+        if (q == cudaSuccess) return true;
+        if (q != cudaErrorNotReady) { cuda_ok(q, what); abort(what); return false; }
+        ncclResult_t ae = ncclSuccess;
+        if (ncclCommGetAsyncError(comm, &ae) == ncclSuccess && ae != ncclSuccess && ae != ncclInProgress) {
+            log("jepa: NCCL error in %s: %s\n", what, ncclGetErrorString(ae));
+            abort(what);
+            return false;
+        }
+        if (std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0).count() > timeout_ms) {
+            log("jepa: %s did not finish within %lld ms (a peer that stopped?)\n", what, timeout_ms);
+            abort(what);
+            return false;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+bool Shard::init(const void * nccl_id128) {
+    timeout_ms = env_timeout_ms();
+    ncclUniqueId id;
+    memcpy(&id, nccl_id128, sizeof(id));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        log("jepa: NCCL error in ncclCommInitRankConfig: %s\n", ncclGetErrorString(r));
+        if (comm) ncclCommAbort(comm);
+        comm = nullptr;
+        aborted = true;
+        return false;
+    }
+    if (!comm) { log("jepa: ncclCommInitRankConfig returned no communicator\n"); aborted = true; return false; }
+    if (!settle(ncclSuccess, "joining the NCCL communicator")) return false;
+    return cuda_ok(cudaMalloc(&dbuf, sizeof(int) * (size_t) (2 + 2 * world)), "shard buffer");
+}
+
+bool Shard::min_f32(float v, float * out, cudaStream_t st) {
+    float * d = (float *) dbuf;
+    *out = v;
+    if (!cuda_ok(cudaMemcpyAsync(d, &v, 4, cudaMemcpyHostToDevice, st), "min_f32")) return false;
+    if (!settle(ncclAllReduce(d, d, 1, ncclFloat, ncclMin, comm, st), "ncclAllReduce(min)")) return false;
+    if (!cuda_ok(cudaMemcpyAsync(out, d, 4, cudaMemcpyDeviceToHost, st), "min_f32")) return false;
+    return finish(st, "ncclAllReduce(min)");
+}
+
+bool Shard::argmin_global(float cost, int gidx, float * cost_out, int * gidx_out, int * owner, cudaStream_t st) {
     int mine[2];
     memcpy(&mine[0], &cost, 4);
     mine[1] = gidx;
     std::vector<int> all((size_t) 2 * world);
-    cudaMemcpyAsync(dbuf, mine, 8, cudaMemcpyHostToDevice, st);
-    nccl_ok(ncclAllGather(dbuf, dbuf + 2, 2, ncclInt32, comm, st), "ncclAllGather(argmin)");
-    cudaMemcpyAsync(all.data(), dbuf + 2, (size_t) 8 * world, cudaMemcpyDeviceToHost, st);
-    cudaStreamSynchronize(st);
+    if (!cuda_ok(cudaMemcpyAsync(dbuf, mine, 8, cudaMemcpyHostToDevice, st), "argmin")) return false;
+    if (!settle(ncclAllGather(dbuf, dbuf + 2, 2, ncclInt32, comm, st), "ncclAllGather(argmin)")) return false;
+    if (!cuda_ok(cudaMemcpyAsync(all.data(), dbuf + 2, (size_t) 8 * world, cudaMemcpyDeviceToHost, st), "argmin")) return false;
+    if (!finish(st, "ncclAllGather(argmin)")) return false;
     float best = INFINITY;
     int bi = -1, br = 0;
     for (int r = 0; r < world; r++) {
@@ -56,21 +143,22 @@ void Shard::argmin_global(float cost, int gidx, float * cost_out, int * gidx_out
     *cost_out = best;
     *gidx_out = bi;
     *owner = br;
+    return true;
 }
 
 bool Shard::bcast_host(float * host, size_t n, int root, cudaStream_t st) {
     float * d = nullptr;
     if (!cuda_ok(cudaMalloc(&d, n * 4), "broadcast buffer")) return false;
     bool ok = cuda_ok(cudaMemcpyAsync(d, host, n * 4, cudaMemcpyHostToDevice, st), "broadcast") &&
-              nccl_ok(ncclBroadcast(d, d, n, ncclFloat, root, comm, st), "ncclBroadcast") &&
+              settle(ncclBroadcast(d, d, n, ncclFloat, root, comm, st), "ncclBroadcast") &&
               cuda_ok(cudaMemcpyAsync(host, d, n * 4, cudaMemcpyDeviceToHost, st), "broadcast") &&
-              cuda_ok(cudaStreamSynchronize(st), "broadcast");
-    cudaFree(d);
+              finish(st, "ncclBroadcast");
+    if (ok) cudaFree(d);   // an aborted exchange may leave the buffer in use: kept then
     return ok;
 }
 
 bool Shard::allgather_f32(const float * send, float * recv, size_t n, cudaStream_t st) {
-    return nccl_ok(ncclAllGather(send, recv, n, ncclFloat, comm, st), "ncclAllGather(energy)");
+    return settle(ncclAllGather(send, recv, n, ncclFloat, comm, st), "ncclAllGather(energy)");
 }
 
 }  // namespace jb
@@ -96,10 +184,7 @@ extern "C" int jepa_b200_context_set_shard(jepa_context * ctx, int rank, int wor
     sh->rank = rank;
     sh->world = world;
     sh->device = ctx->device;
-    ncclUniqueId id;
-    memcpy(&id, nccl_id, sizeof(id));
-    if (!jb::nccl_ok(ncclCommInitRank(&sh->comm, world, id, rank), "ncclCommInitRank")) return -1;
-    if (!jb::cuda_ok(cudaMalloc(&sh->dbuf, sizeof(int) * (size_t) (2 + 2 * world)), "shard buffer")) return -1;
+    if (!sh->init(nccl_id)) return -1;
     ctx->shard = std::move(sh);
     return 0;
 }

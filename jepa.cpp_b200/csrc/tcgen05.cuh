@@ -40,7 +40,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
 // bounded wait; false = gave up (the error flag is raised). try_wait suspends the thread in hardware for a
 // while before it reports "not yet", so the loop polls gently; the clock is read once per 256 polls (a
 // clock read on every poll costs issue slots that the waiting warps' neighbours need).
-__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int code, int * err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int code, int * err,
+                                          long long limit = WAIT_LIMIT) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     for (;;) {
@@ -48,7 +49,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, int c
         for (int i = 0; i < 256; i++) {
             if (mbar_try_wait(bar, parity)) return true;
         }
-        if (clock64() - t0 > WAIT_LIMIT) {
+        if (clock64() - t0 > limit) {
             atomicExch(err, code);
             return false;
         }

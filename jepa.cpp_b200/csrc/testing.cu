@@ -2,6 +2,7 @@
 // reached through the C ABI with host buffers, for parity tests and isolated timing.
 #include "kernels.h"
 #include "common.h"
+#include "gguf.h"
 #include "../../include/jepa_b200.h"
 
 #include <vector>
@@ -46,6 +47,7 @@ extern "C" int jepa_b200_gemm(const float * A, const float * B, int M, int N, in
     }
     cudaStream_t st;
     JB_CUDA(cudaStreamCreate(&st));
+    if (jb::gemm_error_clear(st) != 0) { cudaStreamDestroy(st); return -1; }
     DevBuf ar, ah, al, br, bh, bl, c;
     int rc = -1;
     if (upload_split(A, (size_t) M * K, ar, ah, al, M, K, st) && upload_split(B, (size_t) N * K, br, bh, bl, N, K, st) &&
@@ -276,4 +278,39 @@ extern "C" int jepa_b200_dequant(uint32_t type, const void * src, int64_t rows, 
     }
     cudaStreamDestroy(st);
     return rc;
+}
+
+extern "C" int jepa_b200_check_wait_timeout(long long limit_cycles, int * code) {
+    if (!code || limit_cycles < 1 || limit_cycles > 4000000000LL) {
+        jb::log("jepa: jepa_b200_check_wait_timeout: need an output and 1 <= limit_cycles <= 4e9\n");
+        return -1;
+    }
+    constexpr int CODE = 9;   // the code this check's wait reports (the GEMM's own waits use 1..5)
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    int rc = -1;
+    if (jb::gemm_error_clear(st) == 0 && jb::wait_timeout_check(limit_cycles, CODE, st) == 0 &&
+        jb::cuda_ok(cudaStreamSynchronize(st), "jepa_b200_check_wait_timeout")) {
+        *code = jb::gemm_error_flag(st);            // the timeout, read once ...
+        const int after = jb::gemm_error_flag(st);   // ... and reset by that read
+        rc = (*code >= 0 && after == 0) ? 0 : -1;
+        if (after != 0) jb::log("jepa: jepa_b200_check_wait_timeout: the flag was not reset by its read (%d)\n", after);
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+extern "C" int jepa_b200_host_dequant(uint32_t type, const void * src, int64_t rows, int64_t ne0, float * dst) {
+    if (!src || !dst || rows < 1 || ne0 < 1) return -1;
+    size_t row_bytes = 0;
+    switch (type) {
+        case 0: row_bytes = (size_t) ne0 * 4; break;
+        case 1: case 30: row_bytes = (size_t) ne0 * 2; break;
+        case 8: row_bytes = (size_t) (ne0 / 32) * 34; break;
+        case 2: row_bytes = (size_t) (ne0 / 32) * 18; break;
+        default: jb::log("jepa: jepa_b200_host_dequant: unsupported ggml type %u\n", type); return -1;
+    }
+    if ((type == 8 || type == 2) && ne0 % 32) { jb::log("jepa: jepa_b200_host_dequant: block rows need ne0 %% 32 == 0\n"); return -1; }
+    for (int64_t r = 0; r < rows; r++) jb::dequant_row(type, (const uint8_t *) src + (size_t) r * row_bytes, dst + r * ne0, ne0);
+    return 0;
 }

@@ -1,0 +1,43 @@
+"""Failure detection without a GPU fault.
+
+Device side: every wait of the tensor-core kernels on an mbarrier is bounded; when the bound runs out the
+kernel raises an error flag, frees its tensor memory and returns, the host reads the flag after the call
+and the call returns -1. jepa_b200_check_wait_timeout runs that path on purpose (a wait on a barrier that
+nothing arrives on, with a bound of about a millisecond), and the context has to stay usable after it.
+
+Host side (no GPU): the reference's contract is 0 / -1 with the reason in jepa_error_text() for every
+failure (reference: src/jepa.cpp:16-36); the NCCL set-up of the candidate sharding must return -1 instead
+of hanging when a rank never joins."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from jepa_b200 import capi, lib as jlib
+
+
+@pytest.mark.gpu
+def test_bounded_wait_runs_out_reports_and_leaves_the_context_usable():
+    L = jlib.load()
+    L.jepa_b200_check_wait_timeout.argtypes = [C.c_longlong, C.POINTER(C.c_int)]
+    code = C.c_int(-5)
+    assert L.jepa_b200_check_wait_timeout(2_000_000, C.byref(code)) == 0, jlib.error_text()
+    assert code.value == 9
+    # the flag was reset by its read: a GEMM right after runs and is correct
+    rng = np.random.default_rng(1)
+    A = rng.normal(size=(130, 96)).astype(np.float32)
+    B = rng.normal(size=(70, 96)).astype(np.float32)
+    Cm = np.zeros((130, 70), np.float32)
+    assert L.jepa_b200_gemm(capi.fptr(A), capi.fptr(B), 130, 70, 96, capi.fptr(Cm)) == 0, jlib.error_text()
+    ref = A.astype(np.float64) @ B.astype(np.float64).T
+    assert np.abs(Cm - ref).max() / np.abs(ref).max() < 1e-5
+    # and the check itself repeats
+    assert L.jepa_b200_check_wait_timeout(2_000_000, C.byref(code)) == 0 and code.value == 9
+
+
+def test_timeout_check_refuses_bad_arguments():
+    L = jlib.load()
+    L.jepa_b200_check_wait_timeout.argtypes = [C.c_longlong, C.POINTER(C.c_int)]
+    L.jepa_error_reset()
+    assert L.jepa_b200_check_wait_timeout(0, C.byref(C.c_int())) == -1
+    assert b"limit_cycles" in L.jepa_error_text()
