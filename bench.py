@@ -1,23 +1,34 @@
-"""Benchmark of the H-JEPA gradient planner on B200, and the reference arm.
+"""Benchmark of the two planners on B200: H-JEPA plan grad-steps/s (headline) and V-JEPA 2-AC CEM
+candidates/s, and the reference arm.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 5|1|2|3|4]
 
-Workload (N = 1): BASELINE configs[1] -- a 2-level H-JEPA hierarchy, q8_0 GGUF, seeded random init
-(weights N(0, 0.02), biases 0, LayerNorm gamma 1), each level's predictor 6 layers x 384 wide, 6 heads,
-MLP 1536; level 2 plans 4 steps over 384-d subgoal latents, level 1 plans 16 steps of 2-d actions
-scored against level 2's subgoals; 256 candidates, 50 Adam steps per level (early stopping off,
-weight decay 0). Start and goal latents N(0, 1); candidates initialised U[-1, 1] through the
-jepa_randn_fn hook (prior mean 0, std 1, candidate 0 at the mean), as the measurement rule maps it.
+Headline workload (N = 1 and the scaling runs): BASELINE configs[4] ("config 5"), the largest H-JEPA
+configuration, which fits one GPU -- a 4-level hierarchy, q8_0 GGUF, seeded random init (weights
+N(0, 0.02), biases 0, LayerNorm gamma 1), every level's predictor 12 layers x 768 wide, 12 heads, MLP 3072,
+horizons 64 / 16 / 8 / 4 from the bottom up, 4096 candidates. Start and goal latents N(0, 1); candidates
+initialised U[-1, 1] through the jepa_randn_fn hook (prior mean 0, std 1, candidate 0 at the mean), as the
+measurement rule maps the configs' prose onto the reference's planner. Early stopping off, weight decay 0.
 
-A step is one jepa_hjepa_plan call (both levels: 100 grad-steps). The metric is grad-steps/s, where a
-grad-step is one Adam iteration of one level over the config's 256 candidates. With N GPUs the plan
-holds 256 N candidates sharded 256 per GPU (candidate sharding, one NCCL exchange per level): weak
-scaling, value = N * 100 * K / (max over ranks of the device time).
+A step is one Adam iteration of every level over all 4096 candidates. The timed region is ONE
+jepa_hjepa_plan call with n_steps = K on every level (the warm-up: one call with n_steps = W): K steps,
+plus each level's closing no-gradient evaluation and argmin, which are timed but not counted. The metric
+unit, a grad-step, is one Adam iteration of one level (4 per step). With N GPUs the 4096 candidates are
+split over the N ranks (strong scaling; one NCCL exchange per level); value = 4 K / (max over ranks of the
+device time).
 
-`value` is device time (CUDA events on the planner's stream around each call, weights resident);
-`e2e` is host wall-clock around the same C-ABI calls with host buffers in and out. The reference arm
-runs the reference's own planner source (src/hjepa-plan.cpp, compiled against the ggml shim, oracle/)
-on the host cores, one level-1 and one level-2 gradient evaluation per step.
+`value` is device time (CUDA events on the planner's stream around the call, weights resident); `e2e` is
+the same call timed on the host, with host buffers in and out through the C ABI. The working set (weights
+as f32 planes, activations of 2048-row chains) is far above the 126 MB L2, so no flush is needed between
+timed iterations.
+
+The reference arm runs the reference's own planner source (src/hjepa-plan.cpp, compiled unmodified against
+the ggml shim, oracle/) on the host cores: each step is one gradient evaluation of one level, the levels in
+rotation, over 8 candidates per host thread (the reference evaluates candidates 8 per thread), scaled to
+the config's candidates.
+
+The default run also measures the metric's second half, V-JEPA 2-AC CEM candidates/s (BASELINE
+configs[3]), as the `ac_cem` object of the same line.
 """
 from __future__ import annotations
 
@@ -34,7 +45,10 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-os.environ["NCCL_DEBUG"] = "WARN"     # rank 0 prints exactly one JSON line: no NCCL banner on stdout
+# NCCL's communicator log goes to stderr, so that stdout holds exactly one JSON line
+os.environ.setdefault("NCCL_DEBUG", "INFO")
+os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 sys.path.insert(0, os.path.join(ROOT, "jepa.cpp_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
@@ -43,6 +57,12 @@ from jepa_b200 import capi, synth  # noqa: E402
 METRIC = "H-JEPA plan grad-steps/s & V-JEPA2-AC CEM candidates/s at 1/2/4/8 B200"
 UNIT = "grad-steps/s"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+DEFAULT_CONFIG = 5
+# DRAM read + write of one k_gemm_tf32x3_p launch at 2048 x 3072 x 768 (ncu, dram__bytes_read.sum +
+# dram__bytes_write.sum, one capture of that kernel at that shape): 31.5 MB read (the A and B hi / lo
+# planes, once) + 0.3 MB written (the 25.2 MB output is still in L2 when the kernel ends)
+GEMM_WIDE_TRAFFIC = 31.8e6
+GEMM_WIDE_SHAPE = (2048, 3072, 768)
 
 
 def row_step_flops(lv: synth.Level) -> float:
@@ -75,17 +95,19 @@ def chains_for(S: int, width: int) -> int:
     return max(1, min(n, S, 8))
 
 
-def step_gemm_roofline(L, lv, S1: int, reps: int = 50):
-    """The planner's dominant kernel (k_gemm_tf32x3) at the lowest level's per-step shapes -- M x P x P (value /
-    output), M x F x P (up), M x P x F (down), M = the candidates of one chain -- each timed live with CUDA events
-    over `reps` back-to-back launches through jepa_b200_gemm_bench. Returns (TFLOP/s, [(M, N, K, us)])."""
+def gemm_roofline(L, lv, S_rank: int, reps: int = 20):
+    """The planner's dominant kernel at the lowest level's per-step shapes, M = the rows of one candidate chain:
+    the composed value/output product (M x P x P), up (M x F x P), down (M x P x F), and the adaLN modulation
+    of one step (M x 6PL x P) with its transposed backward (M x P x 6PL). Each is timed live with CUDA events on
+    its launch stream over `reps` back-to-back launches (jepa_b200_gemm_bench). Returns (TFLOP/s over the set,
+    [(M, N, K, us per launch)])."""
     P = lv.pred_dim or lv.embed_dim
-    M = S1 // chains_for(S1, P)
+    M = S_rank // chains_for(S_rank, P)
     fn = L.jepa_b200_gemm_bench
     fn.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
     fl = ms_tot = 0.0
     shapes = []
-    for (N, K) in ((P, P), (lv.ffn_dim, P), (P, lv.ffn_dim)):
+    for (N, K) in ((P, P), (lv.ffn_dim, P), (P, lv.ffn_dim), (6 * P * lv.n_layer, P), (P, 6 * P * lv.n_layer)):
         ms = C.c_double()
         if fn(M, N, K, reps, C.byref(ms)) != 0:
             return None, []
@@ -144,11 +166,16 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def setup_model(cfg: int, workdir: str) -> tuple[str, synth.HJepaSpec, list]:
+def model_path(cfg: int, rank: int, dist) -> tuple[str, synth.HJepaSpec, list]:
+    """The config's synthetic GGUF (written once per box by rank 0, seed = config index)."""
     spec, plans = synth.hjepa_config(cfg)
+    workdir = os.environ.get("JEPA_BENCH_DIR", tempfile.gettempdir())
     path = os.path.join(workdir, f"bench-cfg{cfg}.gguf")
-    if not os.path.exists(path):
-        synth.write_hjepa(path, spec, seed=cfg)
+    if rank == 0 and not os.path.exists(path):
+        synth.write_hjepa(path + ".tmp", spec, seed=cfg)
+        os.replace(path + ".tmp", path)
+    if dist:
+        dist.barrier()
     return path, spec, plans
 
 
@@ -165,67 +192,110 @@ def uniform_draws(spec, plans, S):
     return np.random.default_rng(7).uniform(-1.0, 1.0, n).astype(np.float32)
 
 
-# ---------------------------------------------------------------------------------------------
-def cpu_reference(path, spec, plans, S, steps, warmup, threads):
-    """The reference planner (oracle/_ref) on the host: one gradient evaluation of every level per step."""
-    import ref
-    if not ref.available():
-        return None
-    P = ref.RefPlanner(path, n_threads=threads)
-    states, goals = inputs(spec)
-    rng = np.random.default_rng(3)
-    levels = []
-    for k, (lv, p) in enumerate(zip(spec.levels, plans)):
-        level = k + 1
-        T, A = p["horizon"], lv.action_dim
-        acts = rng.uniform(-1, 1, (S, T, A)).astype(np.float32)
-        if level < len(spec.levels):
-            up = spec.levels[level]
-            n_goal = p["cost_last_n"]
-            goal = rng.normal(size=(n_goal, up.embed_dim)).astype(np.float32)
-            g = capi.Goal(capi.fptr(goal), n_goal, level + 1, 0, capi.fptr(None))
-        else:
-            goal = goals[k].reshape(1, -1)
-            g = capi.Goal(capi.fptr(goal), 1, 0, 0, capi.fptr(None))
-        lp = capi.LevelPlan.of(**p)
-        levels.append((level, acts, goal, g, lp, np.zeros(S, np.float32), np.zeros_like(acts)))
-
-    def one():
-        for level, acts, goal, g, lp, costs, grad in levels:
-            s0 = states[level - 1]
-            rc = P.lib.jepa_hjepa_plan_cost(P.ctx, level, capi.fptr(s0), C.byref(g), C.byref(lp), capi.fptr(acts),
-                                            S, acts.shape[1], capi.fptr(costs), capi.fptr(grad))
-            assert rc == 0
-    for _ in range(warmup):
-        one()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        one()
-    dt = time.perf_counter() - t0
-    P.close()
-    return dt / steps   # seconds per (one grad-step of every level)
+def strong_scaling(cfg: int) -> bool:
+    return cfg == 5
 
 
-def cpu_sample_rows(cfg: int, S: int) -> int:
-    """Candidates the host baseline evaluates per level (its cost is linear in them; the time is scaled to S):
-    the whole batch for the small configs, a slice for the large ones so that a step stays within seconds."""
-    return {3: 128, 5: 8}.get(cfg, S)
+def total_candidates(cfg: int, plans, world: int) -> int:
+    """configs[4] (config 5) splits its candidates over the GPUs; the others plan their candidates per GPU."""
+    S = plans[0]["n_samples"]
+    return S if strong_scaling(cfg) else S * world
 
 
-def describe(cfg: int, spec, plans, S_gpu: int) -> str:
+def hjepa_config_dict(cfg: int, spec, plans, world: int) -> dict:
+    """The `config` object of the H-JEPA line, the same in both arms."""
+    S = total_candidates(cfg, plans, world)
     lv = spec.levels[0]
     hz = "/".join(str(p["horizon"]) for p in plans)
-    return (f"hjepa-config{cfg}: {len(spec.levels)}-level {spec.ftype}, D{lv.embed_dim} L{lv.n_layer} F{lv.ffn_dim}, "
-            f"horizons {hz}, {S_gpu} candidates per GPU, {plans[0]['n_steps']} Adam steps per level")
+    return {"workload": f"hjepa-config{cfg}: {len(spec.levels)}-level {spec.ftype}, D{lv.embed_dim} L{lv.n_layer} "
+                        f"F{lv.ffn_dim}, horizons {hz}, {S} candidates in all",
+            "levels": len(spec.levels), "candidates_total": S,
+            "step": "one Adam iteration of every level over all candidates",
+            "parallelism": f"candidates split over {world} GPU(s) ({'strong' if strong_scaling(cfg) else 'weak'} scaling)",
+            "l2": "no flush: the working set (f32 weight planes, 2048-row activations) is far above L2"}
+
+
+# ---------------------------------------------------------------------------------------------
+# the reference planner on the host (oracle/_ref)
+# ---------------------------------------------------------------------------------------------
+class RefLevels:
+    """One gradient evaluation of one level of the reference planner per call, the levels in rotation,
+    over S candidates (actions U[-1, 1], the level above's states as goals, the top level's goal)."""
+
+    def __init__(self, path, spec, plans, S, threads):
+        import ref
+        self.ok = ref.available()
+        if not self.ok:
+            return
+        self.P = ref.RefPlanner(path, n_threads=threads)
+        states, goals = inputs(spec)
+        rng = np.random.default_rng(3)
+        self.levels = []
+        for k, (lv, p) in enumerate(zip(spec.levels, plans)):
+            level = k + 1
+            T, A = p["horizon"], lv.action_dim
+            acts = rng.uniform(-1, 1, (S, T, A)).astype(np.float32)
+            if level < len(spec.levels):
+                up = spec.levels[level]
+                n_goal = p["cost_last_n"]
+                goal = rng.normal(size=(n_goal, up.embed_dim)).astype(np.float32)
+                g = capi.Goal(capi.fptr(goal), n_goal, level + 1, 0, capi.fptr(None))
+            else:
+                goal = goals[k].reshape(1, -1)
+                g = capi.Goal(capi.fptr(goal), 1, 0, 0, capi.fptr(None))
+            lp = capi.LevelPlan.of(**p)
+            self.levels.append((level, states[k], acts, goal, g, lp, np.zeros(S, np.float32), np.zeros_like(acts)))
+        self.S = S
+        self.turn = len(self.levels) - 1   # the cheapest level (the top) first
+
+    def step(self) -> float:
+        """Seconds of one gradient evaluation of the next level in the rotation."""
+        level, s0, acts, goal, g, lp, costs, grad = self.levels[self.turn]
+        self.turn = (self.turn - 1) % len(self.levels)
+        t0 = time.perf_counter()
+        rc = self.P.lib.jepa_hjepa_plan_cost(self.P.ctx, level, capi.fptr(s0), C.byref(g), C.byref(lp), capi.fptr(acts),
+                                             self.S, acts.shape[1], capi.fptr(costs), capi.fptr(grad))
+        assert rc == 0
+        return time.perf_counter() - t0
+
+    def close(self):
+        if self.ok:
+            self.P.close()
+
+
+def ref_sample_rows(S_total: int, threads: int) -> int:
+    """Candidates per reference evaluation: 8 per host thread (the reference hands each thread chunks of 8),
+    at most the config's."""
+    return max(1, min(S_total, 8 * threads))
+
+
+def reference_rate(path, spec, plans, S_total, threads, steps, warmup):
+    """(grad-steps/s of the config's S_total candidates, seconds measured, sample description) of the
+    reference planner: `warmup` + `steps` evaluations in the level rotation, the timed ones summed; each
+    evaluation counts as S / S_total of a grad-step."""
+    S = ref_sample_rows(S_total, threads)
+    R = RefLevels(path, spec, plans, S, threads)
+    if not R.ok:
+        return None, 0.0, ""
+    for _ in range(warmup):
+        R.step()
+    secs = sum(R.step() for _ in range(steps))
+    R.close()
+    grad_steps = steps * S / S_total
+    sample = (f"{steps} gradient evaluation(s) of one level each, the {len(plans)} levels in rotation, {S} candidates "
+              f"per evaluation ({threads} threads x 8), counted as {S}/{S_total} of a grad-step each, after {warmup} "
+              f"warm-up evaluation(s); reference src/hjepa-plan.cpp via oracle/_ref")
+    return grad_steps / secs, secs, sample
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     if args.config == 4:
-        # the reference's AC path is ggml CPU code that cannot be built here; its numpy restatement stands in
+        # the reference's AC path is ggml CPU graph code that cannot be built here; its numpy restatement stands in
         spec = ac_spec()
         with tempfile.TemporaryDirectory() as tmp:
             path = os.path.join(os.environ.get("JEPA_BENCH_DIR", tmp), "bench-cfg4.gguf")
@@ -239,34 +309,27 @@ def run_reference(args):
                   "whole context, plus its energy), numpy restatement oracle/ac_oracle.py, f32, BLAS threads")
         print(json.dumps({"metric": METRIC, "unit": AC_UNIT, "impl": "reference", "higher_is_better": True,
                           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "dtype": "f32",
-                          "data": "synthetic", "scaling": "weak", "value": value, "ms_per_step": sec * 1e3,
-                          "config": {"workload": "vjepa2-ac-config4", "candidates": 1},
+                          "data": "synthetic", "scaling": "strong", "value": value, "ms_per_step": sec * 1e3,
+                          "config": ac_config_dict(spec, world),
                           "cpu_baseline": {"value": value, "unit": AC_UNIT, "cores": threads, "kind": "port",
                                            "sample": sample},
                           "e2e": {"value": value, "unit": AC_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                           "vs_baseline": None}))
         return
-    with tempfile.TemporaryDirectory() as tmp:
-        path, spec, plans = setup_model(args.config, os.environ.get("JEPA_BENCH_DIR", tmp))
-        S = plans[0]["n_samples"]
-        Sc = cpu_sample_rows(args.config, S)
-        per = cpu_reference(path, spec, plans, Sc, args.steps, args.warmup, threads)
-        if per is not None:
-            per *= S / Sc
+    path, spec, plans = model_path(args.config, 0, None)
+    S_total = total_candidates(args.config, plans, world)
     base = {"metric": METRIC, "unit": UNIT, "impl": "reference", "higher_is_better": True, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "dtype": "f32", "data": "synthetic",
-            "scaling": "strong" if args.config == 5 else "weak",
-            "config": {"workload": describe(args.config, spec, plans, S), "levels": len(spec.levels), "candidates": S}}
-    if per is None:
+            "scaling": "strong" if strong_scaling(args.config) else "weak",
+            "config": hjepa_config_dict(args.config, spec, plans, world)}
+    value, secs, sample = reference_rate(path, spec, plans, S_total, threads, args.steps, args.warmup)
+    if value is None:
         base["unavailable"] = "oracle/_ref/libhjepa_ref.so is not built (needs the reference tree at build time)"
         print(json.dumps(base))
         return
-    n_levels = len(plans)
-    value = n_levels / per          # grad-steps of the config's candidates per second
-    sample = (f"{args.steps} step(s) x one gradient evaluation of each of the {n_levels} levels at S={Sc} "
-              f"(one Adam iteration per level; time scaled to the config's {S} candidates), reference "
-              f"src/hjepa-plan.cpp via oracle/_ref, {threads} threads")
-    base.update({"value": value, "ms_per_step": per * 1e3,
+    # one bench step is one Adam iteration of every level: len(plans) grad-steps
+    ms_per_step = len(plans) / value * 1e3
+    base.update({"value": value, "ms_per_step": ms_per_step,
                  "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
                  "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                  "vs_baseline": None})
@@ -278,8 +341,9 @@ def run_reference(args):
 # ---------------------------------------------------------------------------------------------
 AC_UNIT = "CEM candidates/s"
 AC_K, AC_H, AC_ITERS, AC_TOPK, AC_SEED_FRAMES = 800, 2, 10, 10, 2
-AC_GEMM_TRAFFIC = 2.06e9     # DRAM bytes per k_gemm_f16 launch at the benchmark's rows (profiles/gemm_f16_ac128.md)
-GEMM_SMALL_TRAFFIC = 2.01e6   # DRAM bytes of one 256 x 384 x 384 k_gemm_tf32x3 launch (profiles/gemm_small_256x384x384.md)
+# DRAM read + write per k_gemm_f16 launch at the benchmark's rows: ncu capture at M = 33,024 rows, scaled
+# by rows to the 206,400 of the plan's passes (every operand but the weights grows with M)
+AC_GEMM_TRAFFIC = 2.06e9
 
 
 def ac_spec() -> synth.ACSpec:
@@ -287,6 +351,15 @@ def ac_spec() -> synth.ACSpec:
     q8_0, weights N(0, 0.02), biases 0, LayerNorm gamma 1."""
     return synth.ACSpec(enc_dim=1408, pred_dim=1024, n_layer=24, n_head=16, ffn_dim=4096, grid=16, n_frames=4,
                         ftype="q8_0", name="bench-vjepa2-ac")
+
+
+def ac_config_dict(spec, world: int) -> dict:
+    return {"workload": f"vjepa2-ac-config4: CEM {AC_K} samples in all x {AC_ITERS} iterations, horizon {AC_H}, "
+                        f"top-{AC_TOPK}, {AC_SEED_FRAMES} observed frames x 256 x 1408, predictor 24 x 1024 "
+                        f"(16 heads, MLP 4096), q8_0",
+            "candidates_total": AC_K,
+            "parallelism": f"candidates split over {world} GPU(s) (strong scaling), one NCCL all-gather of energies "
+                           f"per CEM iteration"}
 
 
 def ac_inputs(spec: synth.ACSpec, K: int):
@@ -315,7 +388,7 @@ def ac_flops(spec: synth.ACSpec):
     return alg / 1e9, ex / 1e9
 
 
-def ac_cpu_port(path, spec, seconds_cap=60.0):
+def ac_cpu_port(path, spec):
     """The numpy restatement (oracle/ac_oracle.py) of the reference's rollout, the way the reference runs
     it: one candidate carried through both horizon steps, each step re-evaluating the whole context
     (predict_all over T = 2 then 3 frames), then its L1 energy. Returns seconds per candidate-iteration."""
@@ -347,6 +420,16 @@ def kernel_profile(L, call, last_ms):
     return kinds, total
 
 
+def nccl_id(rank, dist):
+    from jepa_b200 import lib as jlib
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        assert jlib.load().jepa_b200_nccl_unique_id(uid) == 0
+    obj = [bytes(uid.raw)] if rank == 0 else [None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
 def run_ac(args, rank, world, local, dist, primary: bool):
     from jepa_b200.ac import ACWorldModel
     from jepa_b200 import lib as jlib
@@ -359,16 +442,11 @@ def run_ac(args, rank, world, local, dist, primary: bool):
         os.replace(path + ".tmp", path)
     if dist:
         dist.barrier()
-    K = AC_K * world
+    K = AC_K                       # in all: each rank rolls out ceil(K / world) of them
     latents, seed_action, states, goal, noise = ac_inputs(spec, K)
     wm = ACWorldModel(path, device=local)
     if world > 1:
-        uid = C.create_string_buffer(128)
-        if rank == 0:
-            assert jlib.load().jepa_b200_nccl_unique_id(uid) == 0
-        obj = [bytes(uid.raw)] if rank == 0 else [None]
-        dist.broadcast_object_list(obj, src=0)
-        wm.set_shard(rank, world, obj[0])
+        wm.set_shard(rank, world, nccl_id(rank, dist))
     h = wm.context_new(latents, AC_SEED_FRAMES, seed_action, states)
     params = wm.cem_params(samples=K, topk=AC_TOPK, cem_steps=AC_ITERS, horizon=AC_H)
     L = jlib.load()
@@ -404,33 +482,29 @@ def run_ac(args, rank, world, local, dist, primary: bool):
         if k.startswith("gemm_f16"):
             g = {"n": g["n"] + v["n"], "ms": g["ms"] + v["ms"], "flops": g["flops"] + v["flops"]}
     gemm_tf = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else None
-    per_gpu_k = AC_K
+    Kr = -(-K // world)
     n_seq = AC_SEED_FRAMES + AC_H - 1
-    h2d = goal.nbytes + noise.nbytes + AC_ITERS * per_gpu_k * n_seq * (spec.action_dim + spec.state_dim) * 4
-    d2h = AC_ITERS * K * 4 + AC_H * spec.action_dim * 4 + AC_ITERS * 4
+    h2d = goal.nbytes + noise.nbytes + AC_ITERS * Kr * n_seq * (spec.action_dim + spec.state_dim) * 4
+    d2h = AC_H * spec.action_dim * 4 + AC_ITERS * 4
     res = {
         "metric": METRIC, "value": value, "unit": AC_UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f16", "data": "synthetic (seeded random-init q8_0 GGUF, N(0,1) context / goal latents, N(0,1) CEM noise)",
-        "config": {"workload": f"vjepa2-ac-config4: CEM {AC_K} samples per GPU x {AC_ITERS} iterations, horizon {AC_H}, "
-                               f"top-{AC_TOPK}, {AC_SEED_FRAMES} observed frames x 256 x 1408, predictor 24 x 1024 "
-                               f"(16 heads, MLP 4096), q8_0 weights held as f16",
-                   "candidates_total": K, "parallelism": f"candidates sharded over {world} GPU(s), one NCCL all-gather "
-                                                         f"of energies per CEM iteration",
-                   "l2": "working set (keys / values 40 GB, activations 4 GB per GPU) far above L2",
-                   "arith": "f16 operands, f32 accumulate (tcgen05 kind::f16), f32 residual stream",
-                   "gflop_per_candidate_iteration": {"algorithmic": round(alg, 1), "executed": round(ex, 1)}},
+        "config": dict(ac_config_dict(spec, world),
+                       l2="working set (keys / values 40 GB, activations 4 GB at one GPU) far above L2",
+                       arith="f16 operands, f32 accumulate (tcgen05 kind::f16), f32 residual stream",
+                       gflop_per_candidate_iteration={"algorithmic": round(alg, 1), "executed": round(ex, 1)}),
         "e2e": {"value": e2e, "unit": AC_UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": (gemm_tf / peak_tf) if gemm_tf else None, "traffic": AC_GEMM_TRAFFIC,
-                     "traffic_note": "bytes per GEMM launch (mean of a layer's four): ncu DRAM read + write at M = 33,024 rows "
-                                     "scaled by rows to M = 206,400 (profiles/gemm_f16_ac128.md); algorithmic 2.34 GB",
+                     "traffic_note": "DRAM bytes per GEMM launch (mean of a layer's four), ncu at M = 33,024 rows scaled "
+                                     "by rows to M = 206,400; algorithmic 2.34 GB",
                      "kernel": "k_gemm_f16 (tcgen05 kind::f16)",
                      "scope": f"2 M N K per launch / CUDA-event duration per launch, summed over the {g['n']} GEMM "
                               f"launches of one plan ({g['ms']:.1f} of {plan_ms_prof:.1f} ms)",
                      "peak_kind": f"bf16/f16 dense sustained, {peak_kind}",
-                     "whole_plan_executed_tflops": ex * 1e9 * K / world * AC_ITERS / (plan_ms_prof / 1e3) / 1e12},
+                     "whole_plan_executed_tflops": ex * 1e9 * Kr * AC_ITERS / (plan_ms_prof / 1e3) / 1e12},
         "clocks": clocks,
         "kernels": {k: {"launches": v["n"], "ms": round(v["ms"], 3), "share": round(v["ms"] / plan_ms_prof, 4),
                         **({"tflops": round(v["flops"] / v["ms"] / 1e9, 1)} if v["flops"] else {}),
@@ -439,11 +513,13 @@ def run_ac(args, rank, world, local, dist, primary: bool):
     }
     if world == 1 and not args.no_cpu_baseline and rank == 0:
         try:
+            ac_cpu_port(path, spec)                  # warm-up, as the reference arm takes
             sec = ac_cpu_port(path, spec)
             res["cpu_baseline"] = {"value": 1.0 / sec, "unit": AC_UNIT, "cores": os.cpu_count() or 1, "kind": "port",
                                    "sample": "one candidate-iteration (one candidate through both horizon steps, each "
                                              "re-evaluating the whole context as the reference does, plus its energy) "
-                                             "with the numpy restatement oracle/ac_oracle.py (f32, BLAS threads)"}
+                                             "with the numpy restatement oracle/ac_oracle.py (f32, BLAS threads), after "
+                                             "one warm-up"}
         except Exception as e:
             res["cpu_baseline_error"] = str(e)
     wm.close()
@@ -453,6 +529,96 @@ def run_ac(args, rank, world, local, dist, primary: bool):
 
 
 # ---------------------------------------------------------------------------------------------
+# H-JEPA (headline)
+# ---------------------------------------------------------------------------------------------
+def run_hjepa(args, rank, world, local, dist):
+    import torch
+    from jepa_b200.hjepa import Planner
+    from jepa_b200 import lib as jlib
+    cfg = args.config
+    path, spec, plans = model_path(cfg, rank, dist)
+    S = total_candidates(cfg, plans, world)
+    if S % world:
+        raise SystemExit(f"{S} candidates do not split evenly over {world} GPUs")
+    S_rank = S // world
+    P = Planner(path, device=local)
+    if world > 1:
+        P.set_shard(rank, world, nccl_id(rank, dist))
+    states, goals = inputs(spec)
+    draws = uniform_draws(spec, plans, S)
+    K, W = args.steps, max(3, args.warmup)
+
+    def plan(n_steps):
+        p = [dict(q, n_samples=S, n_steps=n_steps) for q in plans]
+        t0 = time.perf_counter()
+        P.plan(states, goals, p, noise=draws)
+        return P.last_ms(), P.last_launches(), time.perf_counter() - t0
+
+    plan(W)                                   # warm-up: W steps, workspaces built and graphs captured
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = Clocks(local)
+    dev_ms, launches, wall = plan(K)          # the timed region: K steps in one call
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = clk.stop()
+    t = torch.tensor([dev_ms, wall], dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms, wall = float(t[0]), float(t[1])
+    res = None
+    if rank == 0:
+        gemm_tf, shapes = gemm_roofline(jlib.load(), spec.levels[0], S_rank)
+        grad_steps = len(plans) * K
+        value = grad_steps / (dev_ms / 1e3)
+        peak_tf, _, peak_kind = peaks()
+        flops = plan_flops(spec, [dict(p, n_steps=K) for p in plans], S)
+        achieved_tf = flops / (dev_ms / 1e3) / 1e12
+        draws_bytes = draws.nbytes
+        h2d = sum(l.embed_dim * 4 * 2 for l in spec.levels) + draws_bytes
+        d2h = plans[0]["horizon"] * spec.levels[0].action_dim * 4 + \
+            sum((p["horizon"] + 1) * l.embed_dim * 4 + p["horizon"] * l.action_dim * 4 + 8 for l, p in zip(spec.levels, plans))
+        Mw, Nw, Kw = GEMM_WIDE_SHAPE
+        res = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": dev_ms / K, "higher_is_better": True,
+            "scaling": "strong" if strong_scaling(cfg) else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": f"synthetic (seeded random-init {spec.ftype} GGUF, N(0,1) latents, U[-1,1] candidates)",
+            "config": dict(hjepa_config_dict(cfg, spec, plans, world),
+                           arith="3xTF32 tensor-core GEMMs (tcgen05 kind::tf32, f32 accuracy), f32 element-wise"),
+            "e2e": {"value": grad_steps / wall, "unit": UNIT, "h2d_bytes_per_step": int(h2d / K),
+                    "d2h_bytes_per_step": int(d2h / K)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": (gemm_tf / peak_tf) if gemm_tf else None,
+                         "traffic": GEMM_WIDE_TRAFFIC * (shapes[1][0] / Mw) if shapes else None,
+                         "traffic_note": f"DRAM read + write of one launch at {Mw} x {Nw} x {Kw} from an ncu capture of the "
+                                         f"same kernel, scaled by rows to M = {shapes[1][0] if shapes else '?'} (the up "
+                                         f"product); algorithmic {(4 * 2 * (Mw * Kw + Nw * Kw) + 4 * Mw * Nw) / 1e6:.1f} MB "
+                                         f"at {Mw} rows",
+                         "kernel": "k_gemm_tf32x3_p (tcgen05 kind::tf32, 3xTF32, persistent)",
+                         "scope": "2 M N K / CUDA-event duration per launch at the lowest level's per-step shapes "
+                                  "(M, N, K, us per launch): " + ", ".join(f"{m}x{n}x{k} {u}" for m, n, k, u in shapes),
+                         "peak_kind": f"bf16 dense, {peak_kind}; the kernel runs tf32 (half the bf16 rate) three products "
+                                      f"per output (hi x hi, hi x lo, lo x hi), so its own ceiling is 1/6 of this peak",
+                         "whole_plan_tflops": achieved_tf, "whole_plan_frac": achieved_tf / peak_tf},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                threads = os.cpu_count() or 1
+                rate, secs, sample = reference_rate(path, spec, plans, S, threads, len(plans), 1)
+                if rate is not None:
+                    res["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": threads, "kind": "reference",
+                                           "sample": sample}
+            except Exception as e:   # the baseline is reported, never required
+                res["cpu_baseline_error"] = str(e)
+    P.close()
+    return res
+
+
 def run_ours(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -462,131 +628,21 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
         import datetime
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
     torch.cuda.set_device(local)
-    from jepa_b200.hjepa import Planner
-    from jepa_b200 import lib as jlib
     if args.config == 4:
         run_ac(args, rank, world, local, dist, primary=True)
-        if dist:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
-
-    workdir = os.environ.get("JEPA_BENCH_DIR", tempfile.gettempdir())
-    path = os.path.join(workdir, f"bench-cfg{args.config}.gguf")
-    spec, plans = synth.hjepa_config(args.config)
-    if rank == 0 and not os.path.exists(path):
-        synth.write_hjepa(path + ".tmp", spec, seed=args.config)
-        os.replace(path + ".tmp", path)
-    if dist:
-        dist.barrier()
-    # configs[4] (config 5) is the strong-scaling case: the config's candidates over the GPUs; the others are
-    # weak-scaling: the config's candidates per GPU
-    strong = args.config == 5
-    S1 = plans[0]["n_samples"] // (world if strong else 1)
-    S = S1 * world
-    plans = [dict(p, n_samples=S) for p in plans]
-    P = Planner(path, device=local)
-    if world > 1:
-        uid = C.create_string_buffer(128)
+    else:
+        res = run_hjepa(args, rank, world, local, dist)
+        if not args.no_ac:
+            # the metric's second half: V-JEPA 2-AC CEM candidates/s on the same GPUs
+            ac = run_ac(args, rank, world, local, dist, primary=False)
+            if rank == 0:
+                res["ac_cem"] = {k: ac[k] for k in ("value", "unit", "ms_per_step", "scaling", "dtype", "config", "e2e",
+                                                     "gpu_launches", "roofline", "clocks", "cpu_baseline",
+                                                     "cpu_baseline_error") if k in ac}
         if rank == 0:
-            assert jlib.load().jepa_b200_nccl_unique_id(uid) == 0
-        obj = [bytes(uid.raw)] if rank == 0 else [None]
-        dist.broadcast_object_list(obj, src=0)
-        P.set_shard(rank, world, obj[0])
-    states, goals = inputs(spec)
-    draws = uniform_draws(spec, plans, S)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")   # 256 MiB > L2
-
-    def step():
-        out, info, used = P.plan(states, goals, plans, noise=draws)
-        return P.last_ms(), P.last_launches(), out, info
-
-    for _ in range(max(3, args.warmup)):
-        step()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clk = Clocks(local)
-    dev_ms, launches, wall = 0.0, 0, 0.0
-    for _ in range(args.steps):
-        flush.fill_(1.0)                       # L2 flushed between timed iterations
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        ms, nl, out, info = step()
-        wall += time.perf_counter() - t0
-        dev_ms += ms
-        launches += nl
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    clocks = clk.stop()
-    t = torch.tensor([dev_ms, wall], dtype=torch.float64)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    gemm_tf, gemm_shapes = step_gemm_roofline(jlib.load(), spec.levels[0], S1) if rank == 0 else (None, [])
-    dev_ms, wall = float(t[0]), float(t[1])
-    # in units of the config's candidates (256 for config 2): N of them per step under weak scaling
-    grad_steps = sum(p["n_steps"] for p in plans) * args.steps * (1 if strong else world)
-    value = grad_steps / (dev_ms / 1e3)
-    e2e = grad_steps / wall
-    peak_tf, peak_hbm, peak_kind = peaks()
-    flops = plan_flops(spec, plans, S) * args.steps
-    achieved_tf = flops / (dev_ms / 1e3) / 1e12
-    A = spec.levels[0].action_dim
-    h2d = sum(l.embed_dim * 4 * 2 for l in spec.levels) + draws.nbytes + \
-        sum(S1 * p["horizon"] * l.action_dim * 4 for l, p in zip(spec.levels, plans))
-    d2h = plans[0]["horizon"] * A * 4 + sum((p["horizon"] + 1) * l.embed_dim * 4 + p["horizon"] * l.action_dim * 4 + 8
-                                            for l, p in zip(spec.levels, plans))
-    if rank == 0:
-        res = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "strong" if strong else "weak",
-            "vs_baseline": None,
-            "dtype": "f32", "data": f"synthetic (seeded random-init {spec.ftype} GGUF, N(0,1) latents, U[-1,1] candidates)",
-            "config": {"workload": describe(args.config, spec, plans, S1),
-                       "candidates_total": S, "parallelism": f"candidates sharded over {world} GPU(s)",
-                       "l2": "flushed (256 MiB write) before every timed step; working set > L2",
-                       "arith": "3xTF32 tensor-core GEMMs (tcgen05), f32 element-wise"},
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": (gemm_tf / peak_tf) if gemm_tf else None, "traffic": GEMM_SMALL_TRAFFIC,
-                         "traffic_note": "DRAM read + write of one 256 x 384 x 384 launch from ncu "
-                                         "(profiles/gemm_small_256x384x384.md); algorithmic 1.97 MB",
-                         "kernel": "k_gemm_tf32x3 (tcgen05 kind::tf32, 3xTF32)",
-                         "scope": "2 M N K / CUDA-event duration per launch at the lowest level's per-step shapes "
-                                  "(M, N, K, us per launch): " + ", ".join(f"{m}x{n}x{k} {u}" for m, n, k, u in gemm_shapes),
-                         "peak_kind": f"bf16 dense, {peak_kind}",
-                         "whole_plan_tflops": achieved_tf, "whole_plan_frac": achieved_tf / peak_tf},
-            "clocks": clocks,
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            try:
-                Sc = cpu_sample_rows(args.config, S1)
-                per = cpu_reference(path, spec, [dict(p, n_samples=Sc) for p in plans], Sc, 1, 0, os.cpu_count() or 1)
-                if per is not None:
-                    per *= S1 / Sc
-            except Exception as e:   # the baseline is reported, never required
-                per = None
-                res["cpu_baseline_error"] = str(e)
-            if per is not None:
-                res["cpu_baseline"] = {"value": len(plans) / per, "unit": UNIT, "cores": os.cpu_count() or 1,
-                                       "kind": "reference",
-                                       "sample": f"one gradient evaluation of each level at S={Sc} (one Adam iteration "
-                                                 f"per level; time scaled to {S1} candidates) with the reference's "
-                                                 f"src/hjepa-plan.cpp via oracle/_ref"}
-    del flush
-    P.close()
-    if not args.no_ac:
-        # the metric's second half: V-JEPA 2-AC CEM candidates/s on the same GPUs
-        ac = run_ac(args, rank, world, local, dist, primary=False)
-        if rank == 0:
-            res["ac_cem"] = {k: ac[k] for k in ("value", "unit", "ms_per_step", "dtype", "config", "e2e", "gpu_launches",
-                                                 "roofline", "clocks", "cpu_baseline", "cpu_baseline_error") if k in ac}
-    if rank == 0:
-        print(json.dumps(res))
+            print(json.dumps(res))
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -595,12 +651,12 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--config", type=int, default=DEFAULT_CONFIG, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-ac", action="store_true", help="skip the V-JEPA 2-AC CEM leg of the default (config 2) run")
+    ap.add_argument("--no-ac", action="store_true", help="skip the V-JEPA 2-AC CEM leg of an H-JEPA run")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -600,26 +600,34 @@ bool ac_ok(jepa_context * ctx, const char * fn) {
     return true;
 }
 
-// xorshift128+ with Box-Muller: the CEM draws when the caller passes no noise (the reference's own
-// generator, src/vjepa2_ac.cpp:807-826 -- kept identical so seeded plans agree)
-struct CemRng {
-    uint64_t s0, s1;
-    explicit CemRng(uint32_t seed) : s0(0x9E3779B97F4A7C15ull ^ seed), s1(0xBF58476D1CE4E5B9ull + seed) {
-        for (int i = 0; i < 8; i++) next();
+// The draws a plan uses when the caller passes no noise: xorshift128+ (shifts 23, 17, 26) seeded from
+// `seed` and advanced 8 outputs, the top 53 bits of an output scaled into (0, 1], and one normal from two
+// such uniforms by Box-Muller's cosine branch -- the generator of the reference planner
+// (src/vjepa2_ac.cpp:807-826), so that a seeded plan samples what the reference samples.
+class CemDraws {
+  public:
+    explicit CemDraws(uint32_t seed) : s0_(0x9E3779B97F4A7C15ull ^ seed), s1_(0xBF58476D1CE4E5B9ull + seed) {
+        for (int i = 0; i < 8; i++) advance();
     }
-    uint64_t next() {
-        uint64_t x = s0;
-        const uint64_t y = s1;
-        s0 = y;
-        x ^= x << 23;
-        s1 = x ^ y ^ (x >> 17) ^ (y >> 26);
-        return s1 + y;
+    void fill(float * out, size_t n) {
+        for (size_t i = 0; i < n; i++) out[i] = normal();
     }
-    float uniform() { return (float) (((next() >> 11) + 1) * (1.0 / 9007199254740993.0)); }
+
+  private:
+    uint64_t advance() {
+        uint64_t t = s0_;
+        const uint64_t u = s1_;
+        s0_ = u;
+        t ^= t << 23;
+        s1_ = t ^ u ^ (t >> 17) ^ (u >> 26);
+        return s1_ + u;
+    }
+    float unit() { return (float) (((advance() >> 11) + 1) * (1.0 / 9007199254740993.0)); }
     float normal() {
-        const float u1 = uniform(), u2 = uniform();
-        return sqrtf(-2.0f * logf(u1)) * cosf(6.2831853071795864769f * u2);
+        const float r = unit(), phase = unit();
+        return sqrtf(-2.0f * logf(r)) * cosf(6.2831853071795864769f * phase);
     }
+    uint64_t s0_, s1_;
 };
 
 int predict(jepa_context * ctx, const float * context, int T, int B, const float * actions, const float * states, bool all,
@@ -894,81 +902,100 @@ int jepa_ac_rollout_cached(jepa_context * ctx, jepa_ac_context * h, const float 
     return rc;
 }
 
-// CEM (reference: src/vjepa2_ac.cpp:829-946, a port of Meta's mpc_utils.py::cem): sample in the 4-d space
-// (dx, dy, dz, gripper) in the order (iteration, horizon step, candidate, lane), clamp, roll every candidate
-// out through the cached context, L1 energy of the final frame, stable sort, top-k mean and unbiased std,
-// momentum. With a shard set, each rank rolls out a contiguous slice of the candidates and one NCCL
-// all-gather of the energies per iteration gives every rank the same sort and the same refit.
+// CEM planning (reference interface: include/jepa.h:471-510; the loop of Meta's mpc_utils.py::cem as the
+// reference runs it). The sampling distribution (mean and std per horizon step over translation and the
+// gripper) and the whole draw stream live on the device; per iteration:
+//   k_cem_sample  -> every candidate's actions (all K on every rank, so all ranks hold the same elites)
+//   rollout       -> the rank's candidates through the cached context, L1 energy of the final frame
+//   ncclAllGather -> every rank's energies (sharded only)
+//   k_cem_refit   -> stable top-k elites, their mean and unbiased std, the momentum update
+// The host copies each iteration's actions back (the rollout derives the poses from them with the double
+// precision pose update) and, at the end, the mean: the plan is the mean with the rotation lanes zero and
+// gripper commands below round_gripper dropped.
 int jepa_ac_plan(jepa_context * ctx, jepa_ac_context * handle, const float * goal, const jepa_ac_cem_params * params,
                  const float * noise, float * out_actions, float * out_energy) {
     if (!ctx || !handle || !goal || !params || !out_actions) return -1;
     if (!ac_ok(ctx, "jepa_ac_plan")) return -1;
     const jepa_ac_cem_params & q = *params;
-    if (q.samples <= 0 || q.topk <= 0 || q.topk > q.samples || q.cem_steps <= 0 || q.horizon <= 0) {
-        log("jepa: jepa_ac_plan: need samples > 0, 0 < topk <= samples, cem_steps > 0 and horizon > 0 (got %d / %d / %d / %d)\n",
+    if (q.samples < 1 || q.topk < 1 || q.topk > q.samples || q.cem_steps < 1 || q.horizon < 1) {
+        log("jepa: jepa_ac_plan: samples %d, topk %d, cem_steps %d, horizon %d: all must be positive and topk <= samples\n",
             q.samples, q.topk, q.cem_steps, q.horizon);
         return -1;
     }
     const int A = ctx->model->ac.action_dim;
     if (A < 7) {
-        log("jepa: jepa_ac_plan: this CEM samples translation (0..2) and the gripper (6), so it needs action_dim >= 7; the "
-            "model's is %d\n", A);
+        log("jepa: jepa_ac_plan: CEM moves action lanes 0-2 (translation) and 6 (gripper); this model's actions have %d lanes\n", A);
         return -1;
     }
     if (handle->owner != ctx) {
-        log("jepa: jepa_ac_plan: the handle was built for a different jepa_context\n");
+        log("jepa: jepa_ac_plan: this context handle belongs to another jepa_context\n");
         return -1;
     }
     ACEngine * e = ac_engine_of(ctx, "jepa_ac_plan");
     if (!e) return -1;
     cudaStream_t st = ctx->stream;
-    const int K = q.samples, H = q.horizon;
-    const int world = ctx->shard ? ctx->shard->world : 1, rank = ctx->shard ? ctx->shard->rank : 0;
+    const int K = q.samples, H = q.horizon, iters = q.cem_steps;
+    Shard * sh = ctx->shard.get();
+    const int world = sh ? sh->world : 1, rank = sh ? sh->rank : 0;
     const int Kr = (K + world - 1) / world;
     const int lo = std::min(K, rank * Kr), hi = std::min(K, lo + Kr);
 
-    std::vector<float> mean((size_t) H * 4, 0.0f), sd((size_t) H * 4, 0.0f);
-    for (int h = 0; h < H; h++) {
-        sd[(size_t) h * 4 + 0] = sd[(size_t) h * 4 + 1] = sd[(size_t) h * 4 + 2] = q.maxnorm;
-        sd[(size_t) h * 4 + 3] = 1.0f;
+    // the draws of every iteration, in the order (iteration, horizon step, candidate, lane)
+    const size_t per_iter = (size_t) H * K * 4;
+    std::vector<float> own;
+    const float * draws = noise;
+    if (!draws) {
+        own.resize(per_iter * iters);
+        CemDraws(q.seed).fill(own.data(), own.size());
+        draws = own.data();
     }
-    std::vector<float> acts((size_t) K * H * A, 0.0f), energy((size_t) K), gathered((size_t) Kr * world);
-    std::vector<int> order((size_t) K);
-    CemRng rng(q.seed);
-
-    // device: goal, this rank's energies (padded to Kr), the gathered energies, the seed latents
+    // the starting distribution: mean 0, std maxnorm on translation and 1 on the gripper
+    std::vector<float> dist((size_t) 8 * H, 0.0f);
+    for (int h = 0; h < H; h++) {
+        float * sd = dist.data() + (size_t) 4 * H + (size_t) 4 * h;
+        sd[0] = sd[1] = sd[2] = q.maxnorm;
+        sd[3] = 1.0f;
+    }
+    // device: goal, draws, distribution, actions, energies (the rank's, padded to Kr; all ranks'), per-iteration
+    // best energies, elite indices
     const size_t goal_n = (size_t) e->HW * e->OUT;
+    const size_t sizes[] = {goal_n * 4, per_iter * iters * 4, dist.size() * 4, (size_t) K * H * A * 4, (size_t) Kr * 4,
+                            (size_t) Kr * world * 4, (size_t) iters * 4, (size_t) q.topk * 4};
+    size_t total = 0;
+    for (size_t b : sizes) total += round256(b);
     ScratchBuf dev, seed;
-    if (!e->grow(dev.b, round256(goal_n * 4) + round256((size_t) Kr * 4) + round256((size_t) Kr * world * 4), "the plan buffers")) return -1;
-    float * goal_d = (float *) dev.b.p;
-    float * en_d = (float *) ((char *) dev.b.p + round256(goal_n * 4));
-    float * all_d = (float *) ((char *) en_d + round256((size_t) Kr * 4));
+    if (!e->grow(dev.b, total, "the plan buffers")) return -1;
+    char * cur = (char *) dev.b.p;
+    auto carve = [&](size_t b) { char * p = cur; cur += round256(b); return p; };
+    float * goal_d = (float *) carve(sizes[0]);
+    float * draws_d = (float *) carve(sizes[1]);
+    float * dist_d = (float *) carve(sizes[2]);
+    float * acts_d = (float *) carve(sizes[3]);
+    float * en_d = (float *) carve(sizes[4]);
+    float * all_d = (float *) carve(sizes[5]);
+    float * best_d = (float *) carve(sizes[6]);
+    int * elite_d = (int *) carve(sizes[7]);
+    float * mean_d = dist_d, * sd_d = dist_d + (size_t) 4 * H;
+
     Events ev;
     const long long l0 = e->launches;
     cudaEventRecord(ev.a, st);
     JB_CUDA(cudaMemcpyAsync(goal_d, goal, goal_n * 4, cudaMemcpyHostToDevice, st));
+    JB_CUDA(cudaMemcpyAsync(draws_d, draws, per_iter * iters * 4, cudaMemcpyHostToDevice, st));
+    JB_CUDA(cudaMemcpyAsync(dist_d, dist.data(), dist.size() * 4, cudaMemcpyHostToDevice, st));
     JB_CUDA(cudaMemsetAsync(en_d, 0, (size_t) Kr * 4, st));
     const size_t n_seed_el = (size_t) handle->n_frames * e->HW * e->E;
     if (!e->grow(seed.b, n_seed_el * 2, "the context latents")) return -1;
     to_f16(handle->slab, e->E, (__half *) seed.b.p, e->E, handle->n_frames * e->HW, e->E, RowMap{}, st);
     e->launches++;
+    auto wait = [&](const char * what) { return world > 1 ? sh->finish(st, what) : cuda_ok(cudaStreamSynchronize(st), what); };
 
-    for (int it = 0; it < q.cem_steps; it++) {
-        for (int h = 0; h < H; h++) {
-            for (int c = 0; c < K; c++) {
-                float v[4];
-                for (int j = 0; j < 4; j++) {
-                    const float z = noise ? noise[(((size_t) it * H + h) * K + c) * 4 + j] : rng.normal();
-                    v[j] = z * sd[(size_t) h * 4 + j] + mean[(size_t) h * 4 + j];
-                }
-                for (int j = 0; j < 3; j++) v[j] = std::min(std::max(v[j], -q.maxnorm), q.maxnorm);
-                v[3] = std::min(std::max(v[3], -q.gripper_clamp), q.gripper_clamp);
-                float * a = acts.data() + ((size_t) c * H + h) * A;
-                for (int j = 0; j < A; j++) a[j] = 0.0f;
-                a[0] = v[0]; a[1] = v[1]; a[2] = v[2];
-                a[6] = v[3];
-            }
-        }
+    std::vector<float> acts((size_t) K * H * A);
+    for (int it = 0; it < iters; it++) {
+        cem_sample(draws_d + per_iter * it, mean_d, sd_d, K, H, A, q.maxnorm, q.gripper_clamp, acts_d, st);
+        e->launches++;
+        JB_CUDA(cudaMemcpyAsync(acts.data(), acts_d, acts.size() * 4, cudaMemcpyDeviceToHost, st));
+        if (!wait("jepa_ac_plan")) return -1;
         if (hi > lo) {
             RolloutReq rq;
             rq.seed16 = (const __half *) seed.b.p; rq.n_seed = handle->n_frames;
@@ -978,57 +1005,31 @@ int jepa_ac_plan(jepa_context * ctx, jepa_ac_context * handle, const float * goa
             rq.cache_owner = handle; rq.cache_gen = handle->gen;
             if (rollout(*e, ctx, rq, "jepa_ac_plan") != 0) return -1;
         }
+        // all ranks' energies in candidate order: rank r's slots [r Kr, r Kr + Kr) hold candidates r Kr ..
+        const float * energies = en_d;
         if (world > 1) {
-            if (!ctx->shard->allgather_f32(en_d, all_d, (size_t) Kr, st)) return -1;
-            JB_CUDA(cudaMemcpyAsync(gathered.data(), all_d, (size_t) Kr * world * 4, cudaMemcpyDeviceToHost, st));
-            JB_CUDA(cudaStreamSynchronize(st));
-            for (int r = 0; r < world; r++) {
-                const int rl = std::min(K, r * Kr), rh = std::min(K, rl + Kr);
-                for (int c = rl; c < rh; c++) energy[(size_t) c] = gathered[(size_t) r * Kr + (c - rl)];
-            }
-        } else {
-            JB_CUDA(cudaMemcpyAsync(energy.data(), en_d, (size_t) K * 4, cudaMemcpyDeviceToHost, st));
-            JB_CUDA(cudaStreamSynchronize(st));
+            if (!sh->allgather_f32(en_d, all_d, (size_t) Kr, st)) return -1;
+            energies = all_d;
         }
-        for (int c = 0; c < K; c++) order[(size_t) c] = c;
-        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return energy[(size_t) a] < energy[(size_t) b]; });
-        if (out_energy) out_energy[it] = energy[(size_t) order[0]];
-        for (int h = 0; h < H; h++) {
-            double mu[4] = {0, 0, 0, 0};
-            for (int k = 0; k < q.topk; k++) {
-                const float * a = acts.data() + ((size_t) order[(size_t) k] * H + h) * A;
-                mu[0] += a[0]; mu[1] += a[1]; mu[2] += a[2]; mu[3] += a[6];
-            }
-            for (int j = 0; j < 4; j++) mu[j] /= (double) q.topk;
-            double var[4] = {0, 0, 0, 0};
-            for (int k = 0; k < q.topk; k++) {
-                const float * a = acts.data() + ((size_t) order[(size_t) k] * H + h) * A;
-                const double d[4] = {a[0] - mu[0], a[1] - mu[1], a[2] - mu[2], a[6] - mu[3]};
-                for (int j = 0; j < 4; j++) var[j] += d[j] * d[j];
-            }
-            const double denom = q.topk > 1 ? (double) (q.topk - 1) : 1.0;
-            for (int j = 0; j < 4; j++) var[j] = sqrt(var[j] / denom);
-            float * mn = mean.data() + (size_t) h * 4;
-            float * sv = sd.data() + (size_t) h * 4;
-            for (int j = 0; j < 3; j++) {
-                mn[j] = (float) (mu[j] * (1.0 - q.momentum_mean) + mn[j] * q.momentum_mean);
-                sv[j] = (float) (var[j] * (1.0 - q.momentum_std) + sv[j] * q.momentum_std);
-            }
-            mn[3] = (float) (mu[3] * (1.0 - q.momentum_mean_gripper) + mn[3] * q.momentum_mean_gripper);
-            sv[3] = (float) (var[3] * (1.0 - q.momentum_std_gripper) + sv[3] * q.momentum_std_gripper);
-        }
+        cem_refit(energies, acts_d, mean_d, sd_d, best_d + it, elite_d, K, H, A, q.topk, q.momentum_mean, q.momentum_std,
+                  q.momentum_mean_gripper, q.momentum_std_gripper, st);
+        e->launches++;
     }
-    for (int h = 0; h < H; h++) {
-        float * a = out_actions + (size_t) h * A;
-        for (int j = 0; j < A; j++) a[j] = 0.0f;
-        a[0] = mean[(size_t) h * 4 + 0];
-        a[1] = mean[(size_t) h * 4 + 1];
-        a[2] = mean[(size_t) h * 4 + 2];
-        const float g = mean[(size_t) h * 4 + 3];
-        a[6] = fabsf(g) < q.round_gripper ? 0.0f : g;
-    }
+    std::vector<float> best((size_t) iters);
+    JB_CUDA(cudaMemcpyAsync(dist.data(), dist_d, dist.size() * 4, cudaMemcpyDeviceToHost, st));
+    JB_CUDA(cudaMemcpyAsync(best.data(), best_d, best.size() * 4, cudaMemcpyDeviceToHost, st));
     cudaEventRecord(ev.b, st);
-    cudaStreamSynchronize(st);
+    if (!wait("jepa_ac_plan")) return -1;
+    if (out_energy) std::copy(best.begin(), best.end(), out_energy);
+    for (int h = 0; h < H; h++) {
+        const float * m = dist.data() + (size_t) 4 * h;
+        float * a = out_actions + (size_t) h * A;
+        std::fill(a, a + A, 0.0f);
+        a[0] = m[0];
+        a[1] = m[1];
+        a[2] = m[2];
+        a[6] = fabsf(m[3]) < q.round_gripper ? 0.0f : m[3];
+    }
     float ms = 0;
     cudaEventElapsedTime(&ms, ev.a, ev.b);
     ctx->last_ms = ms;

@@ -249,6 +249,15 @@ void ac_cond_rows(const float * acts, long long act_cand, const float * states, 
                   int n_cand, int n_frames, int rows_per_frame, int D, cudaStream_t st);
 // copy rows [row0, row0 + rows) of candidate 0's block to the same rows of candidates 1 .. n_cand-1
 void ac_broadcast_rows(float * x, int ld, long long cand_rows, int row0, int rows, int n_cand, int D, cudaStream_t st);
+// CEM on the device (cem.cu). cem_sample: acts [K][H][A] from noise [H][K][4] and the distribution mean / sd
+// [H][4] (translation lanes 0..2 and the gripper lane 6; rotation 0). cem_refit: the topk lowest of energy [K]
+// (ties to the lower index), best[0] = the lowest, then mean / sd moved to the elites' mean and unbiased std
+// with the given momenta (translation, gripper). elite: [topk] ints of device scratch.
+void cem_sample(const float * noise, const float * mean, const float * sd, int K, int H, int A, float maxnorm,
+                float gripper_clamp, float * acts, cudaStream_t st);
+void cem_refit(const float * energy, const float * acts, float * mean, float * sd, float * best, int * elite, int K, int H,
+               int A, int topk, float m_mean, float m_std, float m_mean_grip, float m_std_grip, cudaStream_t st);
+
 // energy[c] = mean |pred[c] - goal| over n values, double accumulation (jepa_ac_energy)
 void ac_energy(const float * pred, long long cand_stride, const float * goal, long long n, int n_cand, float * energy,
                cudaStream_t st);

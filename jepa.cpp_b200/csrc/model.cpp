@@ -1,10 +1,9 @@
 // Model loading (GGUF -> hyper-parameters + host tensors), load-time validation of the H-JEPA tensors,
 // and the lifecycle / introspection / device entry points of the C API.
 //
-// Key parsing follows the jepa.* schema the reference loader implements (src/jepa-gguf.cpp:254-550:
-// required encoder keys, range checks on every integer taken from the file, the per-level jepa.hjepa.*
-// arrays with one entry per level); a file that fails a check is refused with a message naming the key
-// or tensor, never loaded half-way.
+// The keys are the jepa.* GGUF schema (the reference's docs/gguf-schema.md): required encoder keys, a range
+// on the integers a file supplies, the per-level jepa.hjepa.* arrays with one entry per level. A file that
+// fails a check is refused with a message naming the key or tensor, never loaded half-way.
 #include "model.h"
 #include "hplan.h"
 #include "shard.h"
@@ -13,7 +12,10 @@
 
 #include "../../include/jepa_b200.h"
 
+#include <algorithm>
 #include <cinttypes>
+#include <climits>
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 
@@ -21,129 +23,183 @@ namespace jb {
 
 namespace {
 
-bool in_range(const char * key, int64_t v, int64_t lo, int64_t hi) {
-    if (v >= lo && v <= hi) return true;
-    log("jepa: %s = %" PRId64 " is out of range [%" PRId64 ", %" PRId64 "]\n", key, v, lo, hi);
-    return false;
-}
+// Reads jepa.* metadata into the hyper-parameter structs. Each call names a key, its destination, its
+// default and, for integers, the range a file may hold; the first key that is missing (when required),
+// out of range or, for a per-level array, not one value per level, is logged and makes ok() false --
+// later calls then do nothing, so a file is refused at its first bad key.
+class KeyReader {
+  public:
+    explicit KeyReader(const gguf_file & g) : g_(g) {}
+    bool ok() const { return ok_; }
+
+    KeyReader & need(std::initializer_list<const char *> keys) {
+        for (const char * k : keys) {
+            if (ok_ && !g_.has(k)) fail("the file lacks the key %s\n", k);
+        }
+        return *this;
+    }
+    KeyReader & num(const char * key, int & dst, int def, int64_t lo = INT32_MIN, int64_t hi = INT32_MAX) {
+        if (!ok_) return *this;
+        dst = g_.geti(key, def);
+        if (dst < lo || dst > hi) fail("%s holds %d, outside %lld..%lld\n", key, dst, (long long) lo, (long long) hi);
+        return *this;
+    }
+    KeyReader & real(const char * key, float & dst, float def, float lo = -INFINITY, float hi = INFINITY) {
+        if (!ok_) return *this;
+        dst = g_.getf(key, def);
+        if (!(dst >= lo && dst <= hi)) fail("%s holds %g, outside [%g, %g]\n", key, (double) dst, (double) lo, (double) hi);
+        return *this;
+    }
+    KeyReader & flag(const char * key, bool & dst, bool def) {
+        if (ok_) dst = g_.getb(key, def);
+        return *this;
+    }
+    KeyReader & text(const char * key, std::string & dst, const char * def) {
+        if (ok_) dst = g_.gets(key, def);
+        return *this;
+    }
+    // an integer array with one value per level, each in lo..hi, into member `field` of every level
+    KeyReader & per_level(const char * key, std::vector<HLevel> & levels, int HLevel::* field, int lo, int hi) {
+        if (!ok_) return *this;
+        const std::vector<int> v = g_.get_iarr(key);
+        if (!same_count(key, v.size(), levels.size())) return *this;
+        for (size_t i = 0; i < v.size() && ok_; i++) {
+            if (v[i] < lo || v[i] > hi) fail("%s[%zu] holds %d, outside %d..%d\n", key, i, v[i], lo, hi);
+            else levels[i].*field = v[i];
+        }
+        return *this;
+    }
+    KeyReader & per_level(const char * key, std::vector<HLevel> & levels, std::string HLevel::* field) {
+        if (!ok_) return *this;
+        const std::vector<std::string> v = g_.get_sarr(key);
+        if (!same_count(key, v.size(), levels.size())) return *this;
+        for (size_t i = 0; i < v.size(); i++) levels[i].*field = v[i];
+        return *this;
+    }
+    template <class... Args> void fail(const char * fmt, Args... args) {
+        std::string f = std::string("jepa: ") + fmt;
+        log(f.c_str(), args...);
+        ok_ = false;
+    }
+
+  private:
+    bool same_count(const char * key, size_t have, size_t levels) {
+        if (have == levels) return true;
+        fail("%s has %zu entries for %zu levels (one per level is required)\n", key, have, levels);
+        return false;
+    }
+    const gguf_file & g_;
+    bool ok_ = true;
+};
+
+constexpr int MAX_WIDTH = 65536, MAX_DEPTH = 1024, MAX_FFN = 1048576, MAX_FRAMES = 65536;
 
 bool parse(jepa_model & m) {
     const gguf_file & g = *m.file;
     if (g.gets("general.architecture", "") != "jepa") {
-        log("jepa: general.architecture is '%s', expected 'jepa'\n", g.gets("general.architecture", "").c_str());
+        log("jepa: general.architecture is '%s'; this loader reads 'jepa' files only\n", g.gets("general.architecture", "").c_str());
         return false;
     }
     m.name = g.gets("general.name", "");
     m.family = g.gets("jepa.family", "");
     m.modality = g.gets("jepa.modality", "image");
     m.file_type = (uint32_t) g.geti("general.file_type", 0);
-    static const char * families[] = {"ijepa", "vjepa", "vjepa2", "vjepa2_1", "levjepa", "hfvit", "lewm", "hjepa"};
-    bool known = false;
-    for (const char * f : families) known = known || m.family == f;
-    if (!known) { log("jepa: unknown jepa.family '%s'\n", m.family.c_str()); return false; }
-    for (const char * k : {"jepa.enc.embed_dim", "jepa.enc.n_layer", "jepa.enc.n_head", "jepa.enc.ffn_dim", "jepa.enc.patch_size"}) {
-        if (!g.has(k)) { log("jepa: missing required key %s\n", k); return false; }
-    }
-    EncParams & e = m.enc;
-    e.embed_dim = g.geti("jepa.enc.embed_dim", 0);
-    e.n_layer = g.geti("jepa.enc.n_layer", 0);
-    e.n_head = g.geti("jepa.enc.n_head", 0);
-    e.ffn_dim = g.geti("jepa.enc.ffn_dim", 0);
-    e.patch_size = g.geti("jepa.enc.patch_size", 16);
-    e.tubelet_size = g.geti("jepa.enc.tubelet_size", 1);
-    e.img_size = g.geti("jepa.enc.img_size", 224);
-    e.n_frames = g.geti("jepa.enc.n_frames", 1);
-    e.n_registers = g.geti("jepa.enc.n_registers", 0);
-    e.cls_token = g.getb("jepa.enc.cls_token", false);
-    e.in_chans = g.geti("jepa.enc.in_chans", 3);
-    e.ln_eps = g.getf("jepa.enc.ln_eps", 1e-6f);
-    e.act = g.gets("jepa.enc.act", "gelu_erf");
-    if (!in_range("jepa.enc.embed_dim", e.embed_dim, 1, 65536) || !in_range("jepa.enc.n_layer", e.n_layer, 1, 1024) ||
-        !in_range("jepa.enc.n_head", e.n_head, 1, 1024) || !in_range("jepa.enc.ffn_dim", e.ffn_dim, 1, 1048576) ||
-        !in_range("jepa.enc.patch_size", e.patch_size, 1, 1024)) {
+    static const char * const families[] = {"ijepa", "vjepa", "vjepa2", "vjepa2_1", "levjepa", "hfvit", "lewm", "hjepa"};
+    if (std::none_of(std::begin(families), std::end(families), [&](const char * f) { return m.family == f; })) {
+        log("jepa: jepa.family '%s' is not one this loader knows\n", m.family.c_str());
         return false;
     }
+    KeyReader r(g);
+    EncParams & e = m.enc;
+    r.need({"jepa.enc.embed_dim", "jepa.enc.n_layer", "jepa.enc.n_head", "jepa.enc.ffn_dim", "jepa.enc.patch_size"})
+        .num("jepa.enc.embed_dim", e.embed_dim, 0, 1, MAX_WIDTH)
+        .num("jepa.enc.n_layer", e.n_layer, 0, 1, MAX_DEPTH)
+        .num("jepa.enc.n_head", e.n_head, 0, 1, MAX_DEPTH)
+        .num("jepa.enc.ffn_dim", e.ffn_dim, 0, 1, MAX_FFN)
+        .num("jepa.enc.patch_size", e.patch_size, 16, 1, 1024)
+        .num("jepa.enc.tubelet_size", e.tubelet_size, 1)
+        .num("jepa.enc.img_size", e.img_size, 224)
+        .num("jepa.enc.n_frames", e.n_frames, 1)
+        .num("jepa.enc.n_registers", e.n_registers, 0)
+        .num("jepa.enc.in_chans", e.in_chans, 3)
+        .flag("jepa.enc.cls_token", e.cls_token, false)
+        .real("jepa.enc.ln_eps", e.ln_eps, 1e-6f)
+        .text("jepa.enc.act", e.act, "gelu_erf");
+    if (!r.ok()) return false;
+
     m.pred_kind = g.has("jepa.pred.kind") ? g.gets("jepa.pred.kind", "none") : "";
     if (m.pred_kind == "none") m.pred_kind = "";
     if (m.pred_kind == "ac") {
         ACParams & a = m.ac;
         a.present = true;
-        a.embed_dim = g.geti("jepa.pred.embed_dim", 0);
-        a.n_layer = g.geti("jepa.pred.n_layer", 0);
-        a.n_head = g.geti("jepa.pred.n_head", 0);
-        a.ffn_dim = g.geti("jepa.pred.ffn_dim", 0);
-        a.head_dim = g.geti("jepa.pred.head_dim", 0);
-        a.action_dim = g.geti("jepa.pred.action_dim", 0);
-        a.state_dim = g.geti("jepa.pred.state_dim", 0);
-        a.n_cond_tokens = g.geti("jepa.pred.n_cond_tokens", 0);
-        a.grid_size = g.geti("jepa.pred.grid_size", 0);
-        a.n_frames = g.geti("jepa.pred.n_frames", 0);
-        a.normalize_reps = g.getb("jepa.pred.normalize_reps", false);
-        a.norm_reps_eps = g.getf("jepa.pred.norm_reps_eps", 1e-5f);
-        a.ln_eps = g.getf("jepa.pred.ln_eps", 1e-6f);
-        a.frame_causal = g.getb("jepa.pred.frame_causal", false);
-        a.rope_interleaved = g.gets("jepa.pred.rope_freq_layout", "") == "interleaved";
-        a.rope_theta = g.getf("jepa.enc.rope_theta", 10000.0f);
-        a.out_dim = g.geti("jepa.pred.out_dim", e.embed_dim);
-        a.act = g.gets("jepa.pred.act", "gelu_erf");
-        if (!(a.rope_theta >= 1e-6f && a.rope_theta <= 1e12f)) { log("jepa: jepa.enc.rope_theta is out of range\n"); return false; }
-        if (!in_range("jepa.pred.embed_dim", a.embed_dim, 1, 65536) || !in_range("jepa.pred.n_layer", a.n_layer, 1, 1024) ||
-            !in_range("jepa.pred.n_head", a.n_head, 1, 1024) || !in_range("jepa.pred.ffn_dim", a.ffn_dim, 1, 1048576) ||
-            !in_range("jepa.pred.action_dim", a.action_dim, 1, 65536) || !in_range("jepa.pred.state_dim", a.state_dim, 1, 65536) ||
-            !in_range("jepa.pred.n_cond_tokens", a.n_cond_tokens, 1, 1024) || !in_range("jepa.pred.grid_size", a.grid_size, 1, 65536) ||
-            !in_range("jepa.pred.n_frames", a.n_frames, 1, 65536)) {
-            return false;
-        }
+        std::string layout;
+        r.num("jepa.pred.embed_dim", a.embed_dim, 0, 1, MAX_WIDTH)
+            .num("jepa.pred.n_layer", a.n_layer, 0, 1, MAX_DEPTH)
+            .num("jepa.pred.n_head", a.n_head, 0, 1, MAX_DEPTH)
+            .num("jepa.pred.ffn_dim", a.ffn_dim, 0, 1, MAX_FFN)
+            .num("jepa.pred.head_dim", a.head_dim, 0)
+            .num("jepa.pred.action_dim", a.action_dim, 0, 1, MAX_WIDTH)
+            .num("jepa.pred.state_dim", a.state_dim, 0, 1, MAX_WIDTH)
+            .num("jepa.pred.n_cond_tokens", a.n_cond_tokens, 0, 1, MAX_DEPTH)
+            .num("jepa.pred.grid_size", a.grid_size, 0, 1, MAX_WIDTH)
+            .num("jepa.pred.n_frames", a.n_frames, 0, 1, MAX_FRAMES)
+            .num("jepa.pred.out_dim", a.out_dim, e.embed_dim)
+            .flag("jepa.pred.normalize_reps", a.normalize_reps, false)
+            .flag("jepa.pred.frame_causal", a.frame_causal, false)
+            .real("jepa.pred.norm_reps_eps", a.norm_reps_eps, 1e-5f)
+            .real("jepa.pred.ln_eps", a.ln_eps, 1e-6f)
+            .real("jepa.enc.rope_theta", a.rope_theta, 10000.0f, 1e-6f, 1e12f)
+            .text("jepa.pred.rope_freq_layout", layout, "")
+            .text("jepa.pred.act", a.act, "gelu_erf");
+        if (!r.ok()) return false;
+        a.rope_interleaved = layout == "interleaved";
         if (a.head_dim == 0) {
-            if (a.embed_dim % a.n_head) { log("jepa: jepa.pred.embed_dim %d is not divisible by n_head %d\n", a.embed_dim, a.n_head); return false; }
+            if (a.embed_dim % a.n_head) {
+                log("jepa: jepa.pred.embed_dim %d does not split into %d heads\n", a.embed_dim, a.n_head);
+                return false;
+            }
             a.head_dim = a.embed_dim / a.n_head;
         }
-        if (a.head_dim % 2) { log("jepa: the ac predictor rotates pairs with 3-D RoPE, so its head width has to be even\n"); return false; }
+        if (a.head_dim % 2) {
+            log("jepa: the ac predictor's head width %d is odd; its 3-D RoPE rotates pairs of lanes\n", a.head_dim);
+            return false;
+        }
     }
     if (m.family == "hjepa") {
         HParams & hj = m.hj;
-        const int n = g.geti("jepa.hjepa.n_levels", 0);
-        if (!in_range("jepa.hjepa.n_levels", n, 1, 64)) return false;
+        int n = 0;
+        r.num("jepa.hjepa.n_levels", n, 0, 1, 64);
+        if (!r.ok()) return false;
         hj.present = true;
-        hj.ln_eps = g.getf("jepa.hjepa.ln_eps", 1e-5f);
-        hj.adaln_eps = g.getf("jepa.hjepa.adaln_eps", 1e-6f);
-        if (!(hj.ln_eps >= 0.0f && hj.ln_eps <= 1.0f) || !(hj.adaln_eps >= 0.0f && hj.adaln_eps <= 1.0f)) {
-            log("jepa: jepa.hjepa.ln_eps / adaln_eps must be finite values in [0, 1]\n");
-            return false;
-        }
-        hj.proj_kind = g.gets("jepa.hjepa.proj_kind", "identity");
-        hj.pixel_dim = g.geti("jepa.hjepa.pixel_dim", 0);
-        hj.proprio_dim = g.geti("jepa.hjepa.proprio_dim", 0);
-        hj.raw_action_dim = g.geti("jepa.hjepa.raw_action_dim", 0);
-        hj.frameskip = g.geti("jepa.hjepa.frameskip", 0);
         hj.levels.resize((size_t) n);
-        struct ik { const char * key; int HLevel::* f; int lo, hi; };
-        const ik ints[] = {
-            {"jepa.hjepa.embed_dim", &HLevel::embed_dim, 1, 65536}, {"jepa.hjepa.stride", &HLevel::stride, 1, 65536},
-            {"jepa.hjepa.window", &HLevel::window, 1, 1}, {"jepa.hjepa.target_length", &HLevel::target_length, 0, 65536},
-            {"jepa.hjepa.action_dim", &HLevel::action_dim, 1, 65536}, {"jepa.hjepa.act_embed_dim", &HLevel::act_embed_dim, 1, 65536},
-            {"jepa.hjepa.act_enc_dim", &HLevel::act_enc_dim, 0, 65536}, {"jepa.hjepa.act_enc_n_layer", &HLevel::act_enc_n_layer, 0, 1024},
-            {"jepa.hjepa.act_enc_n_head", &HLevel::act_enc_n_head, 0, 1024}, {"jepa.hjepa.act_enc_max_chunk", &HLevel::act_enc_max_chunk, 0, 65536},
-            {"jepa.hjepa.pred_dim", &HLevel::pred_dim, 1, 65536}, {"jepa.hjepa.pred_n_layer", &HLevel::pred_n_layer, 1, 1024},
-            {"jepa.hjepa.pred_n_head", &HLevel::pred_n_head, 1, 1024}, {"jepa.hjepa.pred_head_dim", &HLevel::pred_head_dim, 1, 65536},
-            {"jepa.hjepa.pred_ffn_dim", &HLevel::pred_ffn_dim, 1, 1048576}, {"jepa.hjepa.pred_n_frames", &HLevel::pred_n_frames, 1, 65536},
-        };
-        for (const ik & k : ints) {
-            const std::vector<int> v = g.get_iarr(k.key);
-            if ((int) v.size() != n) { log("jepa: %s holds %zu values, expected one per level (%d)\n", k.key, v.size(), n); return false; }
-            for (int i = 0; i < n; i++) {
-                if (!in_range(k.key, v[(size_t) i], k.lo, k.hi)) return false;
-                hj.levels[(size_t) i].*k.f = v[(size_t) i];
-            }
-        }
-        struct sk { const char * key; std::string HLevel::* f; };
-        const sk strs[] = {{"jepa.hjepa.enc_kind", &HLevel::enc_kind}, {"jepa.hjepa.act_enc_kind", &HLevel::act_enc_kind},
-                           {"jepa.hjepa.pred_kind", &HLevel::pred_kind}};
-        for (const sk & k : strs) {
-            const std::vector<std::string> v = g.get_sarr(k.key);
-            if ((int) v.size() != n) { log("jepa: %s holds %zu values, expected one per level (%d)\n", k.key, v.size(), n); return false; }
-            for (int i = 0; i < n; i++) hj.levels[(size_t) i].*k.f = v[(size_t) i];
-        }
+        auto & lv = hj.levels;
+        r.real("jepa.hjepa.ln_eps", hj.ln_eps, 1e-5f, 0.0f, 1.0f)
+            .real("jepa.hjepa.adaln_eps", hj.adaln_eps, 1e-6f, 0.0f, 1.0f)
+            .text("jepa.hjepa.proj_kind", hj.proj_kind, "identity")
+            .num("jepa.hjepa.pixel_dim", hj.pixel_dim, 0)
+            .num("jepa.hjepa.proprio_dim", hj.proprio_dim, 0)
+            .num("jepa.hjepa.raw_action_dim", hj.raw_action_dim, 0)
+            .num("jepa.hjepa.frameskip", hj.frameskip, 0)
+            .per_level("jepa.hjepa.embed_dim", lv, &HLevel::embed_dim, 1, MAX_WIDTH)
+            .per_level("jepa.hjepa.stride", lv, &HLevel::stride, 1, MAX_FRAMES)
+            .per_level("jepa.hjepa.window", lv, &HLevel::window, 1, 1)
+            .per_level("jepa.hjepa.target_length", lv, &HLevel::target_length, 0, MAX_FRAMES)
+            .per_level("jepa.hjepa.action_dim", lv, &HLevel::action_dim, 1, MAX_WIDTH)
+            .per_level("jepa.hjepa.act_embed_dim", lv, &HLevel::act_embed_dim, 1, MAX_WIDTH)
+            .per_level("jepa.hjepa.act_enc_dim", lv, &HLevel::act_enc_dim, 0, MAX_WIDTH)
+            .per_level("jepa.hjepa.act_enc_n_layer", lv, &HLevel::act_enc_n_layer, 0, MAX_DEPTH)
+            .per_level("jepa.hjepa.act_enc_n_head", lv, &HLevel::act_enc_n_head, 0, MAX_DEPTH)
+            .per_level("jepa.hjepa.act_enc_max_chunk", lv, &HLevel::act_enc_max_chunk, 0, MAX_FRAMES)
+            .per_level("jepa.hjepa.pred_dim", lv, &HLevel::pred_dim, 1, MAX_WIDTH)
+            .per_level("jepa.hjepa.pred_n_layer", lv, &HLevel::pred_n_layer, 1, MAX_DEPTH)
+            .per_level("jepa.hjepa.pred_n_head", lv, &HLevel::pred_n_head, 1, MAX_DEPTH)
+            .per_level("jepa.hjepa.pred_head_dim", lv, &HLevel::pred_head_dim, 1, MAX_WIDTH)
+            .per_level("jepa.hjepa.pred_ffn_dim", lv, &HLevel::pred_ffn_dim, 1, MAX_FFN)
+            .per_level("jepa.hjepa.pred_n_frames", lv, &HLevel::pred_n_frames, 1, MAX_FRAMES)
+            .per_level("jepa.hjepa.enc_kind", lv, &HLevel::enc_kind)
+            .per_level("jepa.hjepa.act_enc_kind", lv, &HLevel::act_enc_kind)
+            .per_level("jepa.hjepa.pred_kind", lv, &HLevel::pred_kind);
+        if (!r.ok()) return false;
     }
     return true;
 }

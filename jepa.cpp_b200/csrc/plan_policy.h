@@ -14,6 +14,7 @@
 #pragma once
 
 #include "hplan.h"
+#include "stats.h"
 
 #include <cstdint>
 #include <random>
@@ -23,21 +24,6 @@
 namespace jb {
 
 // ---- statistics --------------------------------------------------------------------------------
-// Mean and population variance of n values, two passes in double (first the mean, then the squared
-// deviations of each value from it, in index order).
-template <class At>
-inline void two_pass_moments(int64_t n, At at, double & mean, double & var) {
-    double s = 0.0;
-    for (int64_t i = 0; i < n; i++) s += (double) at(i);
-    mean = s / (double) n;
-    double q = 0.0;
-    for (int64_t i = 0; i < n; i++) {
-        const double d = (double) at(i) - mean;
-        q += d * d;
-    }
-    var = q / (double) n;
-}
-
 // The q-quantile of ascending values by linear interpolation between the two order statistics that
 // bracket position q (n - 1), computed in double and rounded once to float.
 float interpolated_quantile(const std::vector<float> & ascending, double q);

@@ -237,6 +237,39 @@ def energy(pred, goal):
     return (d.sum(1) / d.shape[1]).astype(f32)
 
 
+def cem_draws(seed: int, n: int) -> np.ndarray:
+    """The normal draws jepa_ac_plan makes when it is given no noise (src/vjepa2_ac.cpp:804-826): xorshift128+
+    with shifts 23 / 17 / 26, state (0x9E3779B97F4A7C15 ^ seed, 0xBF58476D1CE4E5B9 + seed) advanced by 8
+    outputs; a uniform in (0, 1] from the top 53 bits of an output, ((x >> 11) + 1) / (2^53 + 1) in double
+    rounded to float; one normal from two uniforms, sqrtf(-2 logf(u1)) * cosf(2 pi u2) in float. The float
+    functions are the C library's own (logf, cosf, sqrtf through ctypes), as in the reference's host code."""
+    import ctypes
+    libm = ctypes.CDLL("libm.so.6")
+    for fn in ("logf", "cosf", "sqrtf"):
+        getattr(libm, fn).restype = ctypes.c_float
+        getattr(libm, fn).argtypes = [ctypes.c_float]
+    mask = (1 << 64) - 1
+    s = [(0x9E3779B97F4A7C15 ^ seed) & mask, (0xBF58476D1CE4E5B9 + seed) & mask]
+
+    def advance():
+        x, y = s
+        s[0] = y
+        x ^= (x << 23) & mask
+        s[1] = x ^ y ^ (x >> 17) ^ (y >> 26)
+        return (s[1] + y) & mask
+
+    for _ in range(8):
+        advance()
+    two_pi = f32(6.2831853071795864769)
+    out = np.empty(n, f32)
+    for i in range(n):
+        u1 = f32(((advance() >> 11) + 1) * (1.0 / 9007199254740993.0))
+        u2 = f32(((advance() >> 11) + 1) * (1.0 / 9007199254740993.0))
+        r = f32(libm.sqrtf(float(f32(-2.0) * f32(libm.logf(float(u1))))))
+        out[i] = r * f32(libm.cosf(float(two_pi * u2)))
+    return out
+
+
 def cem(m: ACModel, latents, n_seed, seed_actions, seed_states, goal, p: dict, noise, rollout_fn=None, A=None,
         energy_fn=None):
     """jepa_ac_plan with explicit noise [cem_steps, H, K, 4] (src/vjepa2_ac.cpp:829-946). Returns

@@ -276,6 +276,39 @@ def test_gpu_cached_context_equals_explicit(golden_model):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("seed", [0, 7])
+def test_gpu_cem_default_draws_match_the_reference_generator(golden_model, seed):
+    """jepa_ac_plan without noise draws from the reference's seeded generator (src/vjepa2_ac.cpp:804-826,
+    restated in oracle/ac_oracle.py cem_draws): the plan equals the oracle's CEM refit fed with those draws
+    and the GPU's own predictions."""
+    wm = _wm(golden_model)
+    m = O.ACModel(golden_model)
+    rng = np.random.default_rng(61)
+    HW, E = wm.HW, 96
+    lat, sa, ss, _ = _rollout_inputs(rng, HW, E, 2, 1, 1)
+    goal = rng.normal(size=(HW, E)).astype(np.float32)
+    h = wm.context_new(lat, 2, sa, ss)
+    p = dict(samples=20, topk=5, cem_steps=3, horizon=2, maxnorm=0.05, gripper_clamp=0.75, momentum_mean=0.25,
+             momentum_std=0.95, momentum_mean_gripper=0.15, momentum_std_gripper=0.15, round_gripper=0.25)
+    plan, best = wm.plan(h, goal, wm.cem_params(seed=seed, **p), noise=None)
+    draws = O.cem_draws(seed, p["cem_steps"] * p["horizon"] * p["samples"] * 4).reshape(
+        p["cem_steps"], p["horizon"], p["samples"], 4)
+    ref, ref_best, _ = O.cem(m, None, 2, None, None, goal, p, draws, rollout_fn=lambda a: wm.rollout_cached(h, a, E=E))
+    np.testing.assert_allclose(plan, ref, rtol=0, atol=1e-6)
+    np.testing.assert_allclose(best, ref_best, rtol=1e-6)
+    # explicit noise equal to those draws gives the same plan bit for bit
+    plan2, best2 = wm.plan(h, goal, wm.cem_params(seed=seed + 1, **p), noise=draws)
+    assert np.array_equal(plan, plan2) and np.array_equal(best, best2)
+
+
+def test_oracle_cem_draws_are_normal_and_seeded():
+    a = O.cem_draws(0, 4000)
+    assert np.array_equal(a[:50], O.cem_draws(0, 50))
+    assert not np.array_equal(a[:50], O.cem_draws(1, 50))
+    assert abs(float(a.mean())) < 0.06 and abs(float(a.std()) - 1.0) < 0.05
+
+
+@pytest.mark.gpu
 def test_gpu_cem_matches_oracle_refit(golden_model):
     wm = _wm(golden_model)
     m = O.ACModel(golden_model)

@@ -210,7 +210,7 @@ def test_errors_are_reported(tmpdir_mod):
     P = Planner(path)
     s0 = np.zeros(64, np.float32)
     goal = np.zeros((1, 64), np.float32)
-    with pytest.raises(RuntimeError, match="level 3 is out of range"):
+    with pytest.raises(RuntimeError, match="no level 3 to plan"):
         P.plan_cost(3, s0, goal, np.zeros((2, 3, 2), np.float32))
-    with pytest.raises(RuntimeError, match="does not reach one state"):
+    with pytest.raises(RuntimeError, match="shorter than one step of level 2"):
         P.plan_cost(1, s0, goal, np.zeros((2, 1, 2), np.float32), goal_level=2)
