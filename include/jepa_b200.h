@@ -83,10 +83,11 @@ long long jepa_b200_last_plan_launches(const jepa_context * ctx);
 // context or n out of range.
 int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n);
 
-// Memory mode of the H-JEPA solves on this context: 0 = automatic (every step's adaLN modulation and its
-// gradient, [T S][6 P L] floats x 3, are kept when they fit the free device memory, else one step's at a time),
-// 1 = always one step at a time (the modulation recomputed in the backward: more GEMM work, far less memory).
-// Results are the same in both modes. Returns 0, or -1 for a non-H-JEPA context or a mode out of range.
+// Memory mode of the H-JEPA solves on this context: 0 = automatic (the first that fits the free device memory
+// of: every step's adaLN modulation and its gradient, [T S][6 P L] floats x 3; every step's modulation kept
+// ([T S][6 P L] x 1) and the gradient folded step by step; one step at a time), 1 = always one step at a time
+// (the modulation recomputed in the backward: more GEMM work, least memory), 2 = always the middle mode.
+// Results are the same in every mode. Returns 0, or -1 for a non-H-JEPA context or a mode out of range.
 int jepa_b200_hjepa_set_step_modulation(jepa_context * ctx, int mode);
 
 // C[M,N] = f16(A)[M,K] * f16(B)[N,K]^T with f32 accumulation through the V-JEPA 2-AC predictor's

@@ -296,7 +296,9 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
         pool_scr = std::max(pool_scr, n * (size_t) wide);
     }
     ArenaPlan ap;
-    size_t mod_rows = R;   // rows of mod / dmod: every step's (R), or one step's (S) in step-at-a-time mode
+    // rows of mod and of dmod: every step's (R), or one step's (S) in the step-at-a-time modes (mod keeps R
+    // rows when the forward modulation is kept)
+    size_t mod_rows = R, dmod_rows = R;
     auto plan_all = [&](auto && add) {
         add((float **) &w->x, (size_t) S * T * A); add(&w->m, (size_t) S * T * A); add(&w->v, (size_t) S * T * A);
         add(&w->grad, (size_t) S * T * A); add(&w->a_all, R * A); add(&w->da_all, R * A);
@@ -304,7 +306,7 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
         if (L.act0) { add(&w->ae_u, R * L.act0.out); add(&w->ae_s, R * L.act0.out); add(&w->e, R * L.E); }
         if (L.pact0) { add(&w->pa_u, R * L.pact0.out); add(&w->pa_s, R * L.pact0.out); add(&w->c0, R * L.C); }
         add(&w->cpre, R * P); add(&w->cs_hi, R * P); add(&w->cs_lo, R * P);
-        add(&w->mod, mod_rows * ldm); add(&w->dmod_hi, mod_rows * ldm); add(&w->dmod_lo, mod_rows * ldm);
+        add(&w->mod, mod_rows * ldm); add(&w->dmod_hi, dmod_rows * ldm); add(&w->dmod_lo, dmod_rows * ldm);
         add(&w->dcs, R * P); add(&w->dc, R * P); add(&w->tmpR, R * maxw); add(&w->tmpR2, R * maxw);
         add(&w->states, (size_t) (T + 1) * S * D); add(&w->gstate, (size_t) (T + 1) * S * D);
         add(&w->xs, (size_t) T * (NL + 1) * S * P);
@@ -382,28 +384,41 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
     auto evict_other_levels = [&]() {   // a solve uses one level's workspaces at a time
         for (auto e = ws.begin(); e != ws.end();) e = e->first / 16 != level ? ws.erase(e) : std::next(e);
     };
-    auto to_step_mod = [&]() {
+    auto to_step_mod = [&](bool keep) {
         w->step_mod = true;
-        mod_rows = (size_t) S;
+        w->keep_mod = keep;
+        mod_rows = keep ? R : (size_t) S;
+        dmod_rows = (size_t) S;
         return plan_total();
     };
-    // The modulation of every step at once (one GEMM each way) when it fits -- this workspace and the ones of
-    // the level's candidate streams still to be planned (about the same size each) -- else one step at a time.
-    // Other levels' cached workspaces are released first when memory is short.
+    // Three memory modes, the first that fits this workspace and the ones of the level's candidate streams
+    // still to be planned (about the same size each): every step's modulation and its gradient (one GEMM
+    // each way); every step's modulation kept and the gradient folded per step; one step at a time (the
+    // modulation recomputed in the backward). Other levels' cached workspaces are released first when
+    // memory is short.
     const size_t left = (size_t) std::max(1, n_chunks - chunk);
     size_t need = plan_total();
     size_t free_b = 0, total_b = 0;
     cudaMemGetInfo(&free_b, &total_b);
-    if (need * left > free_b / 10 * 9) {
+    auto fits = [&](size_t n) { return n * left <= free_b / 10 * 9; };
+    if (!fits(need)) {
         evict_other_levels();
         cudaMemGetInfo(&free_b, &total_b);
     }
-    if ((force_step_mod || need * left > free_b / 10 * 9) && T > 1) need = to_step_mod();
+    if (T > 1) {
+        if (force_mod_mode == 1) need = to_step_mod(false);
+        else if (force_mod_mode == 2) need = to_step_mod(true);
+        else if (!fits(need)) {
+            need = to_step_mod(true);
+            if (!fits(need)) need = to_step_mod(false);
+        }
+    }
     bool got = w->arena.reserve(need, ctx->device);
-    if (!got) {   // the free figure is not one allocatable block: release, then fall back to one step at a time
+    if (!got) {   // the free figure is not one allocatable block: release, then fall back to leaner modes
         evict_other_levels();
         got = w->arena.reserve(need, ctx->device);
-        if (!got && !w->step_mod && T > 1) got = w->arena.reserve(to_step_mod(), ctx->device);
+        if (!got && T > 1 && !w->step_mod) got = w->arena.reserve(to_step_mod(true), ctx->device);
+        if (!got && T > 1 && w->keep_mod) got = w->arena.reserve(to_step_mod(false), ctx->device);
     }
     if (!got) return nullptr;
     auto take = [&](auto ** p, size_t n) { *p = (std::remove_pointer_t<decltype(p)>) w->arena.take<float>(n); };
@@ -496,7 +511,8 @@ int HPlanner::lin_bwd(const DLin & L, const float * dy, int lddy, const float * 
 // dcs = dmod adaln.W for the same rows (every step at once, or one step at a time: mod / dmod then hold
 // one step's rows)
 // ---------------------------------------------------------------------------------------------
-static size_t mod_row0(const Workspace & w, int t) { return w.step_mod ? 0 : (size_t) t * w.S; }
+static size_t mod_row0(const Workspace & w, int t) { return (w.step_mod && !w.keep_mod) ? 0 : (size_t) t * w.S; }
+static size_t dmod_row0(const Workspace & w, int t) { return w.step_mod ? 0 : (size_t) t * w.S; }
 
 int HPlanner::step_modulation(Workspace & w, int t0, int nt) {
     const DLevel & L = levels[(size_t) w.level - 1];
@@ -515,7 +531,7 @@ int HPlanner::step_modulation_bwd(Workspace & w, int t0, int nt) {
     GemmEpi ep;
     ep.out0 = w.dcs + (size_t) t0 * w.S * P; ep.ld0 = P;
     launches++;
-    const size_t m0 = mod_row0(w, t0) * ldm;
+    const size_t m0 = dmod_row0(w, t0) * ldm;
     return wgemm({w.dmod_hi + m0, w.dmod_lo + m0, ldm}, {L.adaln.wt_hi, L.adaln.wt_lo, ldm}, nt * w.S, P, ldm, ep, w.st);
 }
 
@@ -549,13 +565,13 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
     }
     act_fwd(w.cpre, P, w.tmpR, P, R, P, 2, st); launches++;
     split_f32(w.tmpR, P, w.cs_hi, w.cs_lo, P, R, P, st); launches++;
-    if (!w.step_mod && step_modulation(w, 0, T)) return -1;
+    if ((!w.step_mod || w.keep_mod) && step_modulation(w, 0, T)) return -1;
     // ---- rollout
     for (int t = 0; t < T; t++) {
         const float * s_t = w.states + (size_t) t * S * D;
         float * x0 = w.xs + (size_t) t * (NL + 1) * S * P;
         // (step-at-a-time modulation: step t's, at least one kernel ahead of its first reader)
-        if (w.step_mod && step_modulation(w, t, 1)) return -1;
+        if (w.step_mod && !w.keep_mod && step_modulation(w, t, 1)) return -1;
         if (L.in_proj) {
             add_row_vec(s_t, D, L.pos0, w.gtmp, D, S, D, st); launches++;
             if (lin_fwd(L.in_proj, w.gtmp, D, nullptr, nullptr, S, x0, P, nullptr, nullptr, w)) return -1;
@@ -775,7 +791,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
     }
     // ---- rollout, reverse
     for (int t = T - 1; t >= 0; t--) {
-        if (w.step_mod && step_modulation(w, t, 1)) return -1;   // step t's modulation, recomputed
+        if (w.step_mod && !w.keep_mod && step_modulation(w, t, 1)) return -1;   // step t's modulation, recomputed
         const float * g_next = w.gstate + (size_t) (t + 1) * S * D;
         const float * x0 = w.xs + (size_t) t * (NL + 1) * S * P;
         const float * xL = x0 + (size_t) NL * S * P;
@@ -799,8 +815,8 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             const float * mod_l = w.mod + mod_row0(w, t) * ldm + (size_t) (NL - 1) * 6 * P;
             layer_norm_bwd(gy, ldgy, xL, P, w.stn + (size_t) t * S, L.norm_w, nullptr, 0, w.gx, P,
                            w.dn + tl * S * P, P, mod_l + 5 * P, ldm,
-                           w.dmod_hi + mod_row0(w, t) * ldm + (size_t) (NL - 1) * 6 * P + 5 * P,
-                           w.dmod_lo + mod_row0(w, t) * ldm + (size_t) (NL - 1) * 6 * P + 5 * P, ldm,
+                           w.dmod_hi + dmod_row0(w, t) * ldm + (size_t) (NL - 1) * 6 * P + 5 * P,
+                           w.dmod_lo + dmod_row0(w, t) * ldm + (size_t) (NL - 1) * 6 * P + 5 * P, ldm,
                            w.d_hi, w.d_lo, P, S, P, st);
             launches++;
         }
@@ -808,8 +824,8 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             const DBlock & B = L.blocks[(size_t) l];
             const size_t tl = (size_t) t * NL + l;
             const float * mod_l = w.mod + mod_row0(w, t) * ldm + (size_t) l * 6 * P;
-            float * dmh = w.dmod_hi + mod_row0(w, t) * ldm + (size_t) l * 6 * P;
-            float * dml = w.dmod_lo + mod_row0(w, t) * ldm + (size_t) l * 6 * P;
+            float * dmh = w.dmod_hi + dmod_row0(w, t) * ldm + (size_t) l * 6 * P;
+            float * dml = w.dmod_lo + dmod_row0(w, t) * ldm + (size_t) l * 6 * P;
             const float * xin = x0 + (size_t) l * S * P;
             // MLP half
             GemmEpi e1;

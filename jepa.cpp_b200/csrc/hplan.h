@@ -121,6 +121,9 @@ struct Workspace {
     // adaLN GEMM runs per step in the forward and again in the backward, dmod is folded into dcs per step.
     // Bit-identical to the all-steps mode (a GEMM row does not depend on the batch it is in).
     bool step_mod = false;
+    // within step_mod: every step's forward modulation is still kept ([T S][6PL], one copy), so the backward
+    // reads it instead of recomputing it; only the gradient is folded per step (dmod holds one step's rows)
+    bool keep_mod = false;
     cudaStream_t st = nullptr;        // the stream its kernels are launched on
     PoolWs pool;
     Arena arena;
@@ -193,7 +196,7 @@ struct HPlanner {
     // two chains side by side fill the SMs one chain leaves idle. Rows never interact, so the result is
     // the same for any stream count.
     int n_streams = 0;                // 0 = automatic
-    bool force_step_mod = false;      // step-at-a-time modulation even when every step's fits
+    int force_mod_mode = 0;           // 0 automatic, 1 step at a time (recomputed), 2 forward kept, gradient per step
     std::vector<cudaStream_t> side;   // streams of the candidate streams 1..n-1
     std::vector<cudaEvent_t> ev;      // fork / join events of the captures
 

@@ -401,11 +401,11 @@ int jepa_b200_hjepa_set_streams(jepa_context * ctx, int n) {
 }
 
 int jepa_b200_hjepa_set_step_modulation(jepa_context * ctx, int mode) {
-    if (!ctx || mode < 0 || mode > 1) { log("jepa: jepa_b200_hjepa_set_step_modulation: a context and mode 0 or 1 are required\n"); return -1; }
+    if (!ctx || mode < 0 || mode > 2) { log("jepa: jepa_b200_hjepa_set_step_modulation: a context and mode 0, 1 or 2 are required\n"); return -1; }
     HPlanner * pm = hplanner_of(ctx, "jepa_b200_hjepa_set_step_modulation");
     if (!pm) return -1;
-    if (pm->force_step_mod != (mode == 1)) pm->ws.clear();   // workspaces are planned for one mode
-    pm->force_step_mod = mode == 1;
+    if (pm->force_mod_mode != mode) pm->ws.clear();   // workspaces are planned for one mode
+    pm->force_mod_mode = mode;
     return 0;
 }
 

@@ -41,3 +41,41 @@ def test_timeout_check_refuses_bad_arguments():
     L.jepa_error_reset()
     assert L.jepa_b200_check_wait_timeout(0, C.byref(C.c_int())) == -1
     assert b"limit_cycles" in L.jepa_error_text()
+
+
+_LONELY_RANK = r"""
+import ctypes as C, os, sys, time
+sys.path.insert(0, os.path.join(sys.argv[1], "jepa.cpp_b200"))
+from jepa_b200 import lib as jlib
+from jepa_b200.hjepa import Planner
+P = Planner(sys.argv[2], device=0)
+uid = C.create_string_buffer(128)
+assert jlib.load().jepa_b200_nccl_unique_id(uid) == 0
+t0 = time.time()
+L = jlib.load()
+L.jepa_b200_context_set_shard.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+rc = L.jepa_b200_context_set_shard(P.ctx, 0, 2, uid)
+print("RC", rc, "S", round(time.time() - t0, 2), "MSG", jlib.error_text())
+"""
+
+
+@pytest.mark.gpu
+def test_a_rank_that_never_joins_ends_in_an_error_not_a_hang(tmp_path):
+    """Rank 0 of a 2-rank shard whose rank 1 never starts: the non-blocking NCCL set-up gives up after
+    JEPA_B200_NCCL_TIMEOUT_MS, aborts the communicator and returns -1 with a reason (host-side failure; no
+    kernel or collective is in flight). Run as a child process, itself bounded."""
+    import os
+    import subprocess
+    import sys
+    from jepa_b200 import synth
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    path = str(tmp_path / "tiny.gguf")
+    synth.write_hjepa(path, synth.HJepaSpec(levels=[synth.Level(32, 1, 2, 64, 2)], ftype="f32"), seed=1)
+    env = dict(os.environ, JEPA_B200_NCCL_TIMEOUT_MS="3000", NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-c", _LONELY_RANK, root, path], capture_output=True, text=True, timeout=120, env=env)
+    line = [l for l in r.stdout.splitlines() if l.startswith("RC")]
+    assert line, (r.stdout, r.stderr[-2000:])
+    parts = line[0].split()
+    assert parts[1] == "-1", line[0]
+    assert float(parts[3]) < 60.0, line[0]
+    assert "never joined" in line[0] or "did not complete" in line[0], line[0]

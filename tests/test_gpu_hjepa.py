@@ -165,8 +165,8 @@ def test_solve_does_not_depend_on_the_stream_count(tmpdir_mod, opts):
 
 
 def test_step_at_a_time_modulation_is_bit_identical(tmpdir_mod):
-    # the memory-lean mode (modulation per step, recomputed in the backward) against every step's at once:
-    # the same costs, gradients and plan, bit for bit
+    # the memory-lean modes (modulation per step, recomputed in the backward; every step's modulation kept,
+    # its gradient folded per step) against every step's at once: the same costs, gradients and plan, bit for bit
     path = forged(tmpdir_mod, "q8_0")
     P = Planner(path)
     rng = np.random.default_rng(23)
@@ -176,12 +176,13 @@ def test_step_at_a_time_modulation_is_bit_identical(tmpdir_mod):
     draws = rng.normal(size=200000).astype(np.float32)
     plan = solve_plan(T=6, S=70, steps=6, early_stop_patience=0, cost_last_n=2)
     out = []
-    for mode in (0, 1):
+    for mode in (0, 1, 2):
         P.set_step_modulation(mode)
         c, g = P.plan_cost(1, s0, goal, acts, goal_level=2, plan=dict(plan, cost_last_n=2))
         out.append((c, g) + tuple(P.solve(1, s0, goal[:1], dict(plan, cost_last_n=1), noise=draws)[:4]))
-    for a, b in zip(out[0], out[1]):
-        assert np.array_equal(np.asarray(a), np.asarray(b))
+    for other in out[1:]:
+        for a, b in zip(out[0], other):
+            assert np.array_equal(np.asarray(a), np.asarray(b))
     P.set_step_modulation(0)
 
 
