@@ -45,10 +45,21 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-# NCCL's communicator log goes to stderr, so that stdout holds exactly one JSON line
+# NCCL's communicator log (its INIT lines name the rank count) goes to a per-process file that is copied to
+# stderr at exit, so that stdout holds exactly one JSON line
 os.environ.setdefault("NCCL_DEBUG", "INFO")
 os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+NCCL_LOG = os.path.join(tempfile.gettempdir(), f"jepa-bench-nccl.{os.getpid()}.log")
+os.environ.setdefault("NCCL_DEBUG_FILE", NCCL_LOG)
+
+
+def copy_nccl_log() -> None:
+    try:
+        with open(NCCL_LOG) as f:
+            sys.stderr.write(f.read())
+        os.unlink(NCCL_LOG)
+    except OSError:
+        pass
 sys.path.insert(0, os.path.join(ROOT, "jepa.cpp_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
@@ -662,6 +673,7 @@ def main():
         run_reference(args)
     else:
         run_ours(args)
+        copy_nccl_log()
 
 
 if __name__ == "__main__":

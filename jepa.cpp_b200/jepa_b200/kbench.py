@@ -3,6 +3,7 @@
     python -m jepa_b200.kbench M N K [reps] [--f16]
     python -m jepa_b200.kbench --attn n_cand n_frames rows heads hd [reps] [impl: 0 auto, 1 mma.sync, 2 tcgen05]
     python -m jepa_b200.kbench --ac samples cem_steps [model.gguf]
+    python -m jepa_b200.kbench --hjepa config candidates [steps] [model.gguf]
 
 Prints the mean device time per launch (CUDA events) and the algorithmic TFLOP/s (2 M N K per launch).
 Without --f16 it times the H-JEPA planner's 3xTF32 GEMM, with --f16 the V-JEPA 2-AC predictor's f16 GEMM.
@@ -10,7 +11,12 @@ Without --f16 it times the H-JEPA planner's 3xTF32 GEMM, with --f16 the V-JEPA 2
 --ac runs one V-JEPA 2-AC CEM plan (horizon 2, two observed frames) on a model of the benchmark's size
 (24 x 1024, 16 heads, MLP 4096, 16 x 16 patches of 1408-d latents, q8_0; written to the given path, or a
 temporary file, when absent) with `samples` candidates: a small, self-contained case of the real kernels.
-Used for isolated kernel timing and as a small, self-contained target for ncu captures.
+--hjepa solves level 1 of an H-JEPA benchmark configuration (1, 2, 3, 5: the bench's synthetic model) for
+`steps` Adam iterations over `candidates` U[-1, 1] candidates -- every kernel of the level's iterations. Config
+"w" is one level of config 5's width (768, 12 heads, MLP 3072, q8_0) with 2 layers and horizon 4: the same
+per-launch shapes at a fraction of the memory, for profiler captures.
+This module is part of the library's tooling: kernel timing in isolation, and a small, self-contained
+target for ncu captures (the commands in profiles/ run it).
 """
 from __future__ import annotations
 
@@ -67,7 +73,50 @@ def ac_plan(samples: int, cem_steps: int, path: str = "") -> float:
     return ms
 
 
+def hjepa_solve(cfg: str, S: int, steps: int = 2, path: str = "") -> float:
+    import os
+    import tempfile
+
+    import numpy as np
+
+    from . import synth
+    from .hjepa import Planner
+    if cfg == "w":
+        spec = synth.HJepaSpec(levels=[synth.Level(768, 2, 12, 3072, 2)], ftype="q8_0", name="kbench-wide")
+        plans = [dict(synth.hjepa_config(5)[1][0], horizon=4, cost_last_n=1)]
+    else:
+        spec, plans = synth.hjepa_config(int(cfg))
+    if not path:
+        path = os.path.join(tempfile.gettempdir(), f"kbench-cfg{cfg}.gguf")
+    if not os.path.exists(path):
+        synth.write_hjepa(path + ".tmp", spec, seed=cfg)
+        os.replace(path + ".tmp", path)
+    rng = np.random.default_rng(1)
+    lv, p = spec.levels[0], plans[0]
+    P = Planner(path, device=0)
+    s0 = rng.normal(size=lv.embed_dim).astype(np.float32)
+    acts = rng.uniform(-1, 1, (S, p["horizon"], lv.action_dim)).astype(np.float32)
+    if len(spec.levels) > 1:
+        goal = rng.normal(size=(p["cost_last_n"], spec.levels[1].embed_dim)).astype(np.float32)
+        gl = 2
+    else:
+        goal = rng.normal(size=(1, lv.embed_dim)).astype(np.float32)
+        gl = 0
+    draws = rng.uniform(-1, 1, S * p["horizon"] * lv.action_dim).astype(np.float32)
+    P.solve(1, s0, goal, dict(p, n_samples=S, n_steps=steps), noise=draws, goal_level=gl)
+    ms = P.last_ms()
+    P.close()
+    return ms
+
+
 if __name__ == "__main__":
+    if "--hjepa" in sys.argv:
+        a = [x for x in sys.argv[1:] if not x.startswith("--")]
+        cfg, S = a[0], int(a[1])
+        steps = int(a[2]) if len(a) > 2 else 2
+        ms = hjepa_solve(cfg, S, steps, a[3] if len(a) > 3 else "")
+        print(f"hjepa config {cfg} level-1 solve, {S} candidates, {steps} steps: {ms:.2f} ms")
+        sys.exit(0)
     if "--ac" in sys.argv:
         a = [x for x in sys.argv[1:] if not x.startswith("--")]
         ms = ac_plan(int(a[0]), int(a[1]), a[2] if len(a) > 2 else "")
