@@ -23,8 +23,13 @@ const char * jepa_b200_version(void);
 // (host buffers, row-major). A kernel check: the planner's linears all run through this kernel.
 int jepa_b200_gemm(const float * A, const float * B, int M, int N, int K, float * C);
 
-// Same product timed on the device: `reps` launches on device-resident operands, returns the mean
-// milliseconds per launch in *ms (CUDA events around the launches).
+// The same product in the planner's configuration: narrow, long products (at most 8 output column tiles of
+// 128, K >= 768) split their K range in three parts whose partial tiles a fix-up sums in a fixed order (the
+// planner passes that scratch on every such product). Agrees with jepa_b200_gemm to rounding.
+int jepa_b200_gemm_ksplit(const float * A, const float * B, int M, int N, int K, float * C);
+
+// The planner-configuration product timed on the device: `reps` launches on device-resident operands,
+// returns the mean milliseconds per launch in *ms (CUDA events around the launches).
 int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms);
 
 // jepa_b200_gemm for callers that must not allocate device memory. No counterpart in the reference.

@@ -553,7 +553,7 @@ template <int MODE>
 __global__ void __launch_bounds__(PTHREADS, 1)
 k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
                 const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
-                int M, int N, int K, const __grid_constant__ GemmEpi ep) {
+                int M, int N, int K, int splits, const __grid_constant__ GemmEpi ep) {
     constexpr uint32_t A_BYTES = BM * BK * 4;
     constexpr uint32_t B_BYTES = PBN * BK * 4;
     constexpr uint32_t TMEM_COLS = 4 * PBN;   // two accumulator pairs [hi*hi | cross terms], 256 columns each
@@ -568,16 +568,21 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
     __shared__ __align__(8) uint64_t acce_bar[2];   // epilogue -> MMA: accumulator pair b has been read
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
+    __shared__ int epi_stop_sh, last_sh;   // K split: the epilogue warps' common abort decision; "this part sums"
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_k = (K + BK - 1) / BK;
     const int tiles_n = (N + PBN - 1) / PBN;
-    const int total = ((M + BM - 1) / BM) * tiles_n;
+    // work units: unit u is K-part u % splits of output tile u / splits (splits == 1: whole tiles)
+    const int total = ((M + BM - 1) / BM) * tiles_n * splits;
+    const int kq = (num_k + splits - 1) / splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < PSTAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
         for (int b = 0; b < 2; b++) { mbar_init(&accf_bar[b], 1); mbar_init(&acce_bar[b], PEPI_WARPS); }
         abort_sh = 0;
+        epi_stop_sh = 0;
+        last_sh = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -602,9 +607,11 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
     if (warp == 0) {
         if (lane == 0) {
             int kt = 0;
-            for (int t = blockIdx.x; t < total && !*(volatile int *) &abort_sh; t += gridDim.x) {
+            for (int u = blockIdx.x; u < total && !*(volatile int *) &abort_sh; u += gridDim.x) {
+                const int t = u / splits, part = u % splits;
                 const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * PBN;
-                for (int k = 0; k < num_k; k++, kt++) {
+                const int kb = part * kq, ke = min(num_k, kb + kq);
+                for (int k = kb; k < ke; k++, kt++) {
                     const int s = kt % PSTAGES;
                     const uint32_t ph = (uint32_t) (kt / PSTAGES) & 1u;
                     if (kt >= PSTAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1, &g_gemm_error)) { abort_sh = 1; break; }
@@ -627,12 +634,13 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
     } else if (warp == 1) {
         if (lane == 0) {
             int kt = 0, i = 0;
-            for (int t = blockIdx.x; t < total && !*(volatile int *) &abort_sh; t += gridDim.x, i++) {
+            for (int u = blockIdx.x; u < total && !*(volatile int *) &abort_sh; u += gridDim.x, i++) {
                 const int b = i & 1;
+                const int kb = (u % splits) * kq, ke = min(num_k, kb + kq);
                 if (i >= 2 && !mbar_wait(&acce_bar[b], (uint32_t) ((i >> 1) - 1) & 1u, 4, &g_gemm_error)) { abort_sh = 1; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t d = tmem + (uint32_t) (b * 2 * PBN);
-                for (int k = 0; k < num_k; k++, kt++) {
+                for (int k = kb; k < ke; k++, kt++) {
                     const int s = kt % PSTAGES;
                     const uint32_t ph = (uint32_t) (kt / PSTAGES) & 1u;
                     if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error)) { abort_sh = 1; break; }
@@ -643,8 +651,8 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                     for (int kk = 0; kk < BK / 8; kk++) {
                         const uint32_t off = (uint32_t) kk * 32;
                         const uint64_t dbh = sw128_desc(b_hi + off);
-                        mma_kind_tf32(d, sw128_desc(a_hi + off), dbh, IDESC2, (k | kk) != 0);   // [hi*hi | hi*lo]
-                        mma_kind_tf32(d + PBN, sw128_desc(a_lo + off), dbh, IDESC, 1);           // + lo*hi
+                        mma_kind_tf32(d, sw128_desc(a_hi + off), dbh, IDESC2, ((k - kb) | kk) != 0);   // [hi*hi | hi*lo]
+                        mma_kind_tf32(d + PBN, sw128_desc(a_lo + off), dbh, IDESC, 1);                  // + lo*hi
                     }
                     mma_commit(&empty_bar[s]);
                 }
@@ -658,13 +666,79 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
         float * stage = (float *) (smem + (size_t) PSTAGES * PSTAGE_BYTES + (size_t) (warp - 2) * 32 * 32 * 4);
         const uint32_t trow = tmem + ((uint32_t) (q * 32) << 16);
         int i = 0;
-        for (int t = blockIdx.x; t < total; t += gridDim.x, i++) {
+        for (int u = blockIdx.x; u < total; u += gridDim.x, i++) {
             const int b = i & 1;
+            const int t = u / splits, part = u % splits;
             const bool ok = mbar_wait(&accf_bar[b], (uint32_t) (i >> 1) & 1u, 3, &g_gemm_error);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            if (!ok || *(volatile int *) &abort_sh) { abort_sh = 1; break; }
+            if (splits > 1) {
+                // the eight epilogue warps decide together, so that none waits at a barrier another has left
+                if (!ok || *(volatile int *) &abort_sh) epi_stop_sh = 1;
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (*(volatile int *) &epi_stop_sh) { abort_sh = 1; break; }
+            } else if (!ok || *(volatile int *) &abort_sh) {
+                abort_sh = 1;
+                break;
+            }
             const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * PBN;
             const int row0 = m0 + q * 32;
+            if (splits > 1) {
+                // this part's partial tile (hi*hi + cross terms) into its scratch slot, row-major
+                float * slot = ep.fix + ((size_t) t * splits + part) * (size_t) (BM * PBN);
+#pragma unroll 1
+                for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+                    uint32_t x[32], y[32];
+                    tmem_ld32_async(trow + (uint32_t) (b * 2 * PBN + c0), x);
+                    tmem_ld32_async(trow + (uint32_t) (b * 2 * PBN + PBN + c0), y);
+                    tmem_ld_wait(x);
+                    tmem_ld_wait(y);
+                    if (c0 == half * 64 + 32) {
+                        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acce_bar[b]);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        *(float4 *) &stage[lane * 32 + ((c ^ (lane & 7)) << 2)] =
+                            make_float4(__uint_as_float(x[4 * c]) + __uint_as_float(y[4 * c]),
+                                        __uint_as_float(x[4 * c + 1]) + __uint_as_float(y[4 * c + 1]),
+                                        __uint_as_float(x[4 * c + 2]) + __uint_as_float(y[4 * c + 2]),
+                                        __uint_as_float(x[4 * c + 3]) + __uint_as_float(y[4 * c + 3]));
+                    }
+                    __syncwarp();
+#pragma unroll 4
+                    for (int j = 0; j < 8; j++) {
+                        const int idx = j * 32 + lane, r = idx >> 3, c = idx & 7;
+                        __stcg((float4 *) (slot + (size_t) (q * 32 + r) * PBN + c0 + 4 * c),
+                               *(const float4 *) &stage[r * 32 + ((c ^ (r & 7)) << 2)]);
+                    }
+                }
+                __threadfence();
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (warp == 2 && lane == 0) {
+                    const int before = atomicAdd(&ep.fix_count[t], 1);
+                    last_sh = before == splits - 1;
+                    if (last_sh) ep.fix_count[t] = 0;   // every part has counted: ready for the next launch
+                }
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (!last_sh) continue;
+                // the last part to finish: the parts summed in order 0, 1, ..., then the fused epilogue
+                __threadfence();
+                const float * parts = ep.fix + (size_t) t * splits * (size_t) (BM * PBN);
+                if (row0 >= M || n0 + half * 64 >= N) continue;   // warp-uniform
+#pragma unroll 2
+                for (int j = 0; j < 16; j++) {
+                    const int idx = j * 32 + lane, r = idx >> 4, c = idx & 15;
+                    const int row = row0 + r, col = half * 64 + 4 * c;
+                    if (row >= M) continue;
+                    const float * p0 = parts + (size_t) (q * 32 + r) * PBN + col;
+                    float4 v = __ldcg((const float4 *) p0);
+                    for (int p = 1; p < splits; p++) v = f4_add(v, __ldcg((const float4 *) (p0 + (size_t) p * (BM * PBN))));
+                    apply_epi4<MODE>(ep, row, n0 + col, N, v);
+                }
+                continue;
+            }
 #pragma unroll 1
             for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
                 uint32_t x[32], y[32];
@@ -831,7 +905,7 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
 }
 
 template <int MODE>
-int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
+int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
     if (!make_map(&ta_hi, A.hi, M, K, A.ld, BM) || !make_map(&ta_lo, A.lo, M, K, A.ld, BM) ||
         !make_map(&tb_hi, B.hi, N, K, B.ld, PBN) || !make_map(&tb_lo, B.lo, N, K, B.ld, PBN)) {
@@ -851,25 +925,46 @@ int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, const 
             done[dev] = true;
         }
     }
-    const long tiles = (long) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN);
-    const unsigned grid = (unsigned) std::max(1L, std::min<long>(tiles, sms[dev]));
-    JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE>, dim3(grid), dim3(PTHREADS), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep));
+    const long units = (long) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN) * splits;
+    const unsigned grid = (unsigned) std::max(1L, std::min<long>(units, sms[dev]));
+    JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE>, dim3(grid), dim3(PTHREADS), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K,
+                       splits, ep));
     return 0;
 }
 
-int launch_p_mode(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st) {
+int launch_p_mode(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
     switch (ep.mode) {
-        case EPI_F32: return launch_p<EPI_F32>(A, B, M, N, K, ep, st);
-        case EPI_SPLIT: return launch_p<EPI_SPLIT>(A, B, M, N, K, ep, st);
-        case EPI_GELU_SPLIT: return launch_p<EPI_GELU_SPLIT>(A, B, M, N, K, ep, st);
-        case EPI_GATED: return launch_p<EPI_GATED>(A, B, M, N, K, ep, st);
-        case EPI_DGELU_SPLIT: return launch_p<EPI_DGELU_SPLIT>(A, B, M, N, K, ep, st);
-        case EPI_F32_SPLIT: return launch_p<EPI_F32_SPLIT>(A, B, M, N, K, ep, st);
-        case EPI_GELU_D_SPLIT: return launch_p<EPI_GELU_D_SPLIT>(A, B, M, N, K, ep, st);
-        case EPI_MUL_SPLIT: return launch_p<EPI_MUL_SPLIT>(A, B, M, N, K, ep, st);
+        case EPI_F32: return launch_p<EPI_F32>(A, B, M, N, K, splits, ep, st);
+        case EPI_SPLIT: return launch_p<EPI_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_GELU_SPLIT: return launch_p<EPI_GELU_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_GATED: return launch_p<EPI_GATED>(A, B, M, N, K, splits, ep, st);
+        case EPI_DGELU_SPLIT: return launch_p<EPI_DGELU_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_F32_SPLIT: return launch_p<EPI_F32_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_GELU_D_SPLIT: return launch_p<EPI_GELU_D_SPLIT>(A, B, M, N, K, splits, ep, st);
+        case EPI_MUL_SPLIT: return launch_p<EPI_MUL_SPLIT>(A, B, M, N, K, splits, ep, st);
         default: log("jepa: gemm: unknown epilogue mode %d\n", ep.mode); return -1;
     }
 }
+
+// the persistent kernel's K split of a shape (1 = none): narrow (at most 8 column tiles), long (K >= 768)
+// products, which have too few output tiles to fill the device at planner row counts
+int p_splits(int N, int K) {
+    const bool persistent = N >= 4096 || (N >= 768 && K >= 768);
+    return persistent && (N + PBN - 1) / PBN <= 8 && (K + BK - 1) / BK >= 24 ? GEMM_KSPLIT : 1;
+}
+
+}  // namespace
+
+size_t gemm_fixup_floats(int M, int N, int K) {
+    const int s = p_splits(N, K);
+    return s > 1 ? (size_t) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN) * s * (BM * PBN) : 0;
+}
+
+size_t gemm_fixup_counters(int M, int N, int K) {
+    return p_splits(N, K) > 1 ? (size_t) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN) : 0;
+}
+
+namespace {
 
 // one kernel per epilogue mode
 template <int BN, int STAGES>
@@ -925,7 +1020,14 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
     // at least 768: the widest predictors, which plan thousands of candidates, so there are tiles enough to
     // fill the device) take the persistent kernel's 128 x 128 tiles and no K split: twice the columns per A
     // tile read, no exchange, and each tile's epilogue overlapping the next tile's products.
-    if (N >= 4096 || (N >= 768 && K >= 768)) return launch_p_mode(A, B, M, N, K, e, st);
+    if (N >= 4096 || (N >= 768 && K >= 768)) {
+        int splits = p_splits(N, K);
+        if (splits > 1 && (!ep.fix || !ep.fix_count || ep.fix_floats < gemm_fixup_floats(M, N, K) ||
+                           ep.fix_counters < gemm_fixup_counters(M, N, K))) {
+            splits = 1;   // no scratch from the caller: whole tiles
+        }
+        return launch_p_mode(A, B, M, N, K, splits, e, st);
+    }
     const int num_k = (K + BK - 1) / BK;
     const int tiles2 = 2 * ((N + 63) / 64);
     int splits = 1;

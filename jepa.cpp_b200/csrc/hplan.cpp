@@ -36,9 +36,19 @@ namespace jb {
 // Every product of the planner's sweep multiplies by a weight (B never comes from the kernel before), and
 // its epilogue reads only biases and operands written at least two kernels earlier (the modulation, the
 // block's input, the forward pre-activations): both are loaded before the dependency wait.
-static int wgemm(const SplitMat & A, const SplitMat & B, int M, int N, int K, GemmEpi ep, cudaStream_t st) {
+// The planner's GEMM call: operands not produced by the previous kernel are loaded ahead of the dependency
+// wait, and the workspace's fix-up scratch lets narrow, long products split their K range.
+static int wgemm(const Workspace & w, const SplitMat & A, const SplitMat & B, int M, int N, int K, GemmEpi ep, cudaStream_t st) {
     ep.pre_b = 1;
     ep.pre_epi = 1;
+    ep.fix = w.fix;
+    ep.fix_floats = w.fix_floats;
+    ep.fix_count = w.fix_count;
+    ep.fix_counters = w.fix_counters;
+    if (gemm_fixup_floats(M, N, K) > w.fix_floats || gemm_fixup_counters(M, N, K) > w.fix_counters) {
+        log("jepa: hjepa planner: the workspace's GEMM scratch does not cover %d x %d x %d\n", M, N, K);
+        return -1;
+    }
     return gemm_tc(A, B, M, N, K, ep, st);
 }
 
@@ -295,6 +305,32 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
         }
         pool_scr = std::max(pool_scr, n * (size_t) wide);
     }
+    // GEMM fix-up scratch: the largest any product of this workspace can ask for, at the largest row count it
+    // runs (every step at once, the goal-projection encoders, the pooled action chunks)
+    {
+        const size_t rows = std::max({R + (size_t) S, ae ? (size_t) Wa * S * (size_t) pw.G : 0,
+                                      ae ? (size_t) Wa * S * (size_t) pw.stride : 0});
+        const int M_cap = (int) std::min<size_t>(rows, (size_t) INT32_MAX);
+        auto cover = [&](int n_out, int n_in) {
+            w->fix_floats = std::max({w->fix_floats, gemm_fixup_floats(M_cap, n_out, n_in), gemm_fixup_floats(M_cap, n_in, n_out)});
+            w->fix_counters = std::max({w->fix_counters, gemm_fixup_counters(M_cap, n_out, n_in),
+                                        gemm_fixup_counters(M_cap, n_in, n_out)});
+        };
+        auto cover_lin = [&](const DLin & l) { if (l) cover(l.out, l.in); };
+        cover((int) ldm, P);
+        for (const DLin * l : {&L.act0, &L.act2, &L.pact0, &L.pact2, &L.in_proj, &L.cond_proj, &L.out_proj, &L.proj0, &L.proj2})
+            cover_lin(*l);
+        for (const DBlock & B : L.blocks) { cover_lin(B.ov); cover_lin(B.up); cover_lin(B.down); }
+        for (const EncStage & e : w->enc) {
+            const DLevel & U = levels[(size_t) e.lv - 1];
+            cover_lin(U.enc_fc1);
+            cover_lin(U.enc_fc2);
+        }
+        if (ae) {
+            for (const DLin * l : {&ae->fc1, &ae->fc2, &ae->step, &ae->head0, &ae->head2}) cover_lin(*l);
+            for (const DSeqBlock & B : ae->blocks) { cover_lin(B.qkv); cover_lin(B.out); cover_lin(B.up); cover_lin(B.down); }
+        }
+    }
     ArenaPlan ap;
     // rows of mod and of dmod: every step's (R), or one step's (S) in the step-at-a-time modes (mod keeps R
     // rows when the forward modulation is kept)
@@ -347,6 +383,7 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
             add(&pw.goals, (size_t) Wa * Au); add(&pw.weights, (size_t) Wa);
         }
         add(&w->cost, (size_t) S); add(&w->best_val, (size_t) 1);
+        if (w->fix_floats) add(&w->fix, w->fix_floats);
         const int Dg = levels[(size_t) cs.goal_level - 1].D;
         // one goal row per scored prediction (W <= T + 1 of them; a single goal is repeated)
         add(&w->goals, (size_t) (T + 1) * Dg); add(&w->weights, (size_t) (T + 1));
@@ -369,6 +406,7 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
         for (size_t i = 0; i < w->enc.size(); i++) ap.add<LnStats>((size_t) w->enc[i].n * S * 2);
         ap.add<float>((size_t) 2 * 4096);      // Adam schedule
         ap.add<int>(4);
+        ap.add<int>(w->fix_counters);
         ap.add<void *>((size_t) 2 * (T + 1));  // cost pointer tables
         if (ae) {
             const size_t n = (size_t) Wa * S;
@@ -434,6 +472,10 @@ Workspace * HPlanner::workspace(int level, int S, int T, const CostSpec & cs, in
     }
     w->sched = w->arena.take<float>((size_t) 2 * 4096);
     w->step_ctr = w->arena.take<int>(4);
+    if (w->fix_counters) {
+        w->fix_count = w->arena.take<int>(w->fix_counters);
+        if (!w->fix_count || !cuda_ok(cudaMemset(w->fix_count, 0, w->fix_counters * sizeof(int)), "GEMM fix-up counters")) return nullptr;
+    }
     w->pred_ptrs = (const float **) w->arena.take<void *>((size_t) (T + 1));
     w->gpred_ptrs = (float **) w->arena.take<void *>((size_t) (T + 1));
     w->best_idx = w->arena.take<int>(1);
@@ -478,7 +520,7 @@ int HPlanner::lin_fwd(const DLin & L, const float * x, int ldx, const float * x_
         ep.out_hi = y_hi; ep.out_lo = y_lo; ep.ld_split = ldy;
         ep.mode = y_hi ? (y ? EPI_F32_SPLIT : EPI_SPLIT) : EPI_F32;
         launches++;
-        return wgemm({x_hi, x_lo, ld}, {L.w_hi, L.w_lo, L.in}, M, L.out, L.in, ep, st);
+        return wgemm(w, {x_hi, x_lo, ld}, {L.w_hi, L.w_lo, L.in}, M, L.out, L.in, ep, st);
     }
     linear_simt(x, ldx, L.w, L.b, y, ldy, M, L.out, L.in, st);
     launches++;
@@ -499,7 +541,7 @@ int HPlanner::lin_bwd(const DLin & L, const float * dy, int lddy, const float * 
         GemmEpi ep;
         ep.out0 = dx; ep.ld0 = lddx;
         launches++;
-        return wgemm({dy_hi, dy_lo, ld}, {L.wt_hi, L.wt_lo, L.out}, M, L.in, L.out, ep, st);
+        return wgemm(w, {dy_hi, dy_lo, ld}, {L.wt_hi, L.wt_lo, L.out}, M, L.in, L.out, ep, st);
     }
     linear_simt(dy, lddy, L.wt, nullptr, dx, lddx, M, L.in, L.out, st);
     launches++;
@@ -522,7 +564,7 @@ int HPlanner::step_modulation(Workspace & w, int t0, int nt) {
     ep.out0 = w.mod + mod_row0(w, t0) * ldm; ep.ld0 = ldm;
     launches++;
     const size_t r0 = (size_t) t0 * w.S * P;
-    return wgemm({w.cs_hi + r0, w.cs_lo + r0, P}, {L.adaln.w_hi, L.adaln.w_lo, P}, nt * w.S, ldm, P, ep, w.st);
+    return wgemm(w, {w.cs_hi + r0, w.cs_lo + r0, P}, {L.adaln.w_hi, L.adaln.w_lo, P}, nt * w.S, ldm, P, ep, w.st);
 }
 
 int HPlanner::step_modulation_bwd(Workspace & w, int t0, int nt) {
@@ -532,7 +574,7 @@ int HPlanner::step_modulation_bwd(Workspace & w, int t0, int nt) {
     ep.out0 = w.dcs + (size_t) t0 * w.S * P; ep.ld0 = P;
     launches++;
     const size_t m0 = dmod_row0(w, t0) * ldm;
-    return wgemm({w.dmod_hi + m0, w.dmod_lo + m0, ldm}, {L.adaln.wt_hi, L.adaln.wt_lo, ldm}, nt * w.S, P, ldm, ep, w.st);
+    return wgemm(w, {w.dmod_hi + m0, w.dmod_lo + m0, ldm}, {L.adaln.wt_hi, L.adaln.wt_lo, ldm}, nt * w.S, P, ldm, ep, w.st);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -591,17 +633,17 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
             GemmEpi e2;
             e2.mode = EPI_GATED; e2.bias = B.ov.b; e2.out0 = o; e2.ld0 = P; e2.aux = xin; e2.ld_aux = P;
             e2.gate = mod_l + 2 * P; e2.ld_gate = ldm; e2.out1 = xm; e2.ld1 = P;
-            if (wgemm({w.h_hi, w.h_lo, P}, {B.ov.w_hi, B.ov.w_lo, P}, S, P, P, e2, st)) return -1;
+            if (wgemm(w, {w.h_hi, w.h_lo, P}, {B.ov.w_hi, B.ov.w_lo, P}, S, P, P, e2, st)) return -1;
             block_pre(xm, P, mod_l, ldm, 3 * P, 4 * P, B.ln2_w, B.ln2_b, adaln_eps, ln_eps, w.h_hi, w.h_lo, P,
                       w.stm0 + tl * S, w.stm1 + tl * S, S, P, st);
             GemmEpi e3;
             // (u keeps gelu'(pre-activation) for the backward's EPI_MUL_SPLIT)
             e3.mode = EPI_GELU_D_SPLIT; e3.bias = B.up.b; e3.out0 = u; e3.ld0 = F; e3.out_hi = w.g_hi; e3.out_lo = w.g_lo; e3.ld_split = F;
-            if (wgemm({w.h_hi, w.h_lo, P}, {B.up.w_hi, B.up.w_lo, P}, S, F, P, e3, st)) return -1;
+            if (wgemm(w, {w.h_hi, w.h_lo, P}, {B.up.w_hi, B.up.w_lo, P}, S, F, P, e3, st)) return -1;
             GemmEpi e4;
             e4.mode = EPI_GATED; e4.bias = B.down.b; e4.out0 = dn; e4.ld0 = P; e4.aux = xm; e4.ld_aux = P;
             e4.gate = mod_l + 5 * P; e4.ld_gate = ldm; e4.out1 = xout; e4.ld1 = P;
-            if (wgemm({w.g_hi, w.g_lo, F}, {B.down.w_hi, B.down.w_lo, F}, S, P, F, e4, st)) return -1;
+            if (wgemm(w, {w.g_hi, w.g_lo, F}, {B.down.w_hi, B.down.w_lo, F}, S, P, F, e4, st)) return -1;
             launches += 5;
         }
         const float * xL = x0 + (size_t) NL * S * P;
@@ -652,7 +694,7 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
                 GemmEpi ep;
                 ep.mode = EPI_GELU_SPLIT; ep.bias = U.enc_fc1.b; ep.out0 = e.u; ep.ld0 = H; ep.out_hi = e.g_hi; ep.out_lo = e.g_lo; ep.ld_split = H;
                 launches++;
-                if (wgemm({e.h_hi, e.h_lo, Din}, {U.enc_fc1.w_hi, U.enc_fc1.w_lo, Din}, n, H, Din, ep, st)) return -1;
+                if (wgemm(w, {e.h_hi, e.h_lo, Din}, {U.enc_fc1.w_hi, U.enc_fc1.w_lo, Din}, n, H, Din, ep, st)) return -1;
             } else {
                 layer_norm(e.in, Din, U.enc_in_w, U.enc_in_b, ln_eps, w.tmpR2, Din, nullptr, nullptr, nullptr, n, Din, st);
                 linear_simt(w.tmpR2, Din, U.enc_fc1.w, U.enc_fc1.b, e.u, H, n, H, Din, st);
@@ -770,10 +812,10 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             split_f32(gy, Dout, e.d_hi, e.d_lo, Dout, n, Dout, st);
             GemmEpi ep;
             ep.mode = EPI_DGELU_SPLIT; ep.aux = e.u; ep.ld_aux = H; ep.out_hi = e.g_hi; ep.out_lo = e.g_lo; ep.ld_split = H;
-            if (wgemm({e.d_hi, e.d_lo, Dout}, {U.enc_fc2.wt_hi, U.enc_fc2.wt_lo, Dout}, n, H, Dout, ep, st)) return -1;
+            if (wgemm(w, {e.d_hi, e.d_lo, Dout}, {U.enc_fc2.wt_hi, U.enc_fc2.wt_lo, Dout}, n, H, Dout, ep, st)) return -1;
             GemmEpi ep2;
             ep2.out0 = e.gin; ep2.ld0 = Din;
-            if (wgemm({e.g_hi, e.g_lo, H}, {U.enc_fc1.wt_hi, U.enc_fc1.wt_lo, H}, n, Din, H, ep2, st)) return -1;
+            if (wgemm(w, {e.g_hi, e.g_lo, H}, {U.enc_fc1.wt_hi, U.enc_fc1.wt_lo, H}, n, Din, H, ep2, st)) return -1;
             launches += 3;
         } else {
             if (lin_bwd(U.enc_fc2, gy, Dout, nullptr, nullptr, n, w.tmpR2, H, w)) return -1;
@@ -830,10 +872,10 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             // MLP half
             GemmEpi e1;
             e1.mode = EPI_MUL_SPLIT; e1.aux = w.u + tl * S * F; e1.ld_aux = F; e1.out_hi = w.du_hi; e1.out_lo = w.du_lo; e1.ld_split = F;
-            if (wgemm({w.d_hi, w.d_lo, P}, {B.down.wt_hi, B.down.wt_lo, P}, S, F, P, e1, st)) return -1;
+            if (wgemm(w, {w.d_hi, w.d_lo, P}, {B.down.wt_hi, B.down.wt_lo, P}, S, F, P, e1, st)) return -1;
             GemmEpi e2;
             e2.out0 = w.gh; e2.ld0 = P;
-            if (wgemm({w.du_hi, w.du_lo, F}, {B.up.wt_hi, B.up.wt_lo, F}, S, P, F, e2, st)) return -1;
+            if (wgemm(w, {w.du_hi, w.du_lo, F}, {B.up.wt_hi, B.up.wt_lo, F}, S, P, F, e2, st)) return -1;
             BlockBwdArgs a{};
             a.gh = w.gh; a.ldgh = P; a.gres = w.gx; a.ldres = P; a.x = w.xmid + tl * S * P; a.ldx = P;
             a.st0 = w.stm0 + tl * S; a.st1 = w.stm1 + tl * S; a.ln_w = B.ln2_w; a.ln_b = B.ln2_b;
@@ -846,7 +888,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             // attention half (one query over one key: the value path, through the composed linear)
             GemmEpi e4;
             e4.out0 = w.gh; e4.ld0 = P;
-            if (wgemm({w.d_hi, w.d_lo, P}, {B.ov.wt_hi, B.ov.wt_lo, P}, S, P, P, e4, st)) return -1;
+            if (wgemm(w, {w.d_hi, w.d_lo, P}, {B.ov.wt_hi, B.ov.wt_lo, P}, S, P, P, e4, st)) return -1;
             BlockBwdArgs b{};
             b.gh = w.gh; b.ldgh = P; b.gres = w.gmid; b.ldres = P; b.x = xin; b.ldx = P;
             b.st0 = w.sta0 + tl * S; b.st1 = w.sta1 + tl * S; b.ln_w = B.ln1_w; b.ln_b = B.ln1_b;
@@ -921,6 +963,7 @@ int HPlanner::plan_cost(const CostSpec & cs, const float * actions, int S, float
     cudaEventCreate(&e1);
     cudaEventRecord(e0, st);
     JB_CUDA(cudaMemcpyAsync(w->x, actions, (size_t) S * T * A * 4, cudaMemcpyHostToDevice, st));
+    if (w->fix_count) JB_CUDA(cudaMemsetAsync(w->fix_count, 0, w->fix_counters * sizeof(int), st));
     JB_CUDA(cudaMemcpyAsync(w->gtmp, cs.s0, (size_t) D * 4, cudaMemcpyHostToDevice, st));
     copy_rows(w->gtmp, 0, w->states, D, S, D, st);
     gather_actions(w->x, w->a_all, S, T, A, st);

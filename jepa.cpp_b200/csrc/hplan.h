@@ -156,6 +156,10 @@ struct Workspace {
     int * best_idx = nullptr;
     float * best_val = nullptr;
     std::vector<EncStage> enc;
+    // scratch of the GEMM's K-split fix-up (narrow, long products: every such product of this workspace
+    // uses it, so the split never depends on a call's row count); counters zeroed before each call
+    float * fix = nullptr; size_t fix_floats = 0;
+    int * fix_count = nullptr; size_t fix_counters = 0;
     // captured graphs
     cudaGraphExec_t g_iter = nullptr, g_fwd = nullptr;
     std::string graph_key, iter_key, fwd_key;

@@ -102,6 +102,7 @@ int HPlanner::solve(const CostSpec & cs, const jepa_hjepa_level_plan & lp, DrawS
         JB_CUDA(cudaMemsetAsync(w->m, 0, n * 4, st));
         JB_CUDA(cudaMemsetAsync(w->v, 0, n * 4, st));
         JB_CUDA(cudaMemsetAsync(w->step_ctr, 0, 4 * sizeof(int), st));
+        if (w->fix_count) JB_CUDA(cudaMemsetAsync(w->fix_count, 0, w->fix_counters * sizeof(int), st));
         JB_CUDA(cudaMemcpyAsync(w->gtmp, cs.s0, (size_t) D * 4, cudaMemcpyHostToDevice, st));
         copy_rows(w->gtmp, 0, w->states, D, w->S, D, st);
         gather_actions(w->x, w->a_all, w->S, T, A, st);

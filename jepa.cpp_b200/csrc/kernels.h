@@ -40,6 +40,10 @@ struct GemmEpi {
     // least two kernels earlier, or are weights): loaded before the dependency wait, while that kernel
     // still runs. pre_b: the B operand (its first pipeline stages); pre_epi: bias / aux / gate.
     int pre_b = 0, pre_epi = 0;
+    // Scratch of the K-split fix-up (see gemm_fixup_floats): partial tiles and one counter per output tile,
+    // the counters zero before the launch (the kernel leaves them zero). Without it the K split is off.
+    float * fix = nullptr; size_t fix_floats = 0;
+    int * fix_count = nullptr; size_t fix_counters = 0;
 };
 
 struct SplitMat {                    // a split operand: two float32 planes with one leading dimension
@@ -50,6 +54,14 @@ struct SplitMat {                    // a split operand: two float32 planes with
 
 // Returns 0, or -1 after logging (unsupported shape / a CUDA error).
 int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st);
+// The persistent kernel splits the K range of narrow, long products (at most 8 column tiles, K >= 768) in
+// GEMM_KSPLIT parts when the caller passes fix-up scratch: each part's partial tile goes to the scratch and
+// the last part to finish sums the parts in a fixed order and applies the epilogue. The split depends on
+// (N, K) only, so a row's bits still do not depend on the batch. These give the scratch a call needs:
+// partial-tile floats and tile counters (0 when the shape is not split).
+constexpr int GEMM_KSPLIT = 3;
+size_t gemm_fixup_floats(int M, int N, int K);
+size_t gemm_fixup_counters(int M, int N, int K);
 
 // Error flag the tensor-core kernels raise when a bounded wait gives up. gemm_error_flag returns it
 // (0 = fine, the waiter's code otherwise, -1 when the flag could not be read) and resets it to 0 on the

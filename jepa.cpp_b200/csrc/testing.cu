@@ -40,19 +40,34 @@ bool upload_split(const float * h, size_t n, DevBuf & raw, DevBuf & hi, DevBuf &
 
 extern "C" const char * jepa_b200_version(void) { return "jepa-b200 0.1.0"; }
 
-extern "C" int jepa_b200_gemm(const float * A, const float * B, int M, int N, int K, float * C) {
+namespace {
+
+// fix-up scratch for the GEMM's K split (the planner's configuration): partial tiles and zeroed counters
+bool alloc_fixup(DevBuf & fix, DevBuf & cnt, int M, int N, int K, jb::GemmEpi & ep, cudaStream_t st) {
+    const size_t nf = jb::gemm_fixup_floats(M, N, K), nc = jb::gemm_fixup_counters(M, N, K);
+    if (!nf) return true;
+    if (!fix.alloc(nf * 4) || !cnt.alloc(nc * sizeof(int))) return false;
+    if (cudaMemsetAsync(cnt.p, 0, nc * sizeof(int), st) != cudaSuccess) return false;
+    ep.fix = fix.f();
+    ep.fix_floats = nf;
+    ep.fix_count = (int *) cnt.p;
+    ep.fix_counters = nc;
+    return true;
+}
+
+int gemm_host(const float * A, const float * B, int M, int N, int K, float * C, bool ksplit, const char * fn) {
     if (!A || !B || !C || M < 1 || N < 1 || K < 1 || (K & 3)) {
-        jb::log("jepa: jepa_b200_gemm: need host buffers and M, N, K >= 1 with K a multiple of 4\n");
+        jb::log("jepa: %s: need host buffers and M, N, K >= 1 with K a multiple of 4\n", fn);
         return -1;
     }
     cudaStream_t st;
     JB_CUDA(cudaStreamCreate(&st));
     if (jb::gemm_error_clear(st) != 0) { cudaStreamDestroy(st); return -1; }
-    DevBuf ar, ah, al, br, bh, bl, c;
+    DevBuf ar, ah, al, br, bh, bl, c, fix, cnt;
     int rc = -1;
+    jb::GemmEpi ep;
     if (upload_split(A, (size_t) M * K, ar, ah, al, M, K, st) && upload_split(B, (size_t) N * K, br, bh, bl, N, K, st) &&
-        c.alloc((size_t) M * N * 4)) {
-        jb::GemmEpi ep;
+        c.alloc((size_t) M * N * 4) && (!ksplit || alloc_fixup(fix, cnt, M, N, K, ep, st))) {
         ep.mode = jb::EPI_F32;
         ep.out0 = c.f();
         ep.ld0 = N;
@@ -60,29 +75,39 @@ extern "C" int jepa_b200_gemm(const float * A, const float * B, int M, int N, in
         if (rc == 0 && !jb::cuda_ok(cudaMemcpyAsync(C, c.p, (size_t) M * N * 4, cudaMemcpyDeviceToHost, st), "copy C")) rc = -1;
         if (rc == 0 && !jb::cuda_ok(cudaStreamSynchronize(st), "gemm")) rc = -1;
         if (rc == 0 && jb::gemm_error_flag(st) != 0) {
-            jb::log("jepa: jepa_b200_gemm: the tensor-core kernel timed out waiting on its pipeline\n");
+            jb::log("jepa: %s: the tensor-core kernel timed out waiting on its pipeline\n", fn);
             rc = -1;
         }
     } else {
-        jb::log("jepa: jepa_b200_gemm: device allocation or upload failed\n");
+        jb::log("jepa: %s: device allocation or upload failed\n", fn);
     }
     cudaStreamDestroy(st);
     return rc;
+}
+
+}  // namespace
+
+extern "C" int jepa_b200_gemm(const float * A, const float * B, int M, int N, int K, float * C) {
+    return gemm_host(A, B, M, N, K, C, false, "jepa_b200_gemm");
+}
+
+extern "C" int jepa_b200_gemm_ksplit(const float * A, const float * B, int M, int N, int K, float * C) {
+    return gemm_host(A, B, M, N, K, C, true, "jepa_b200_gemm_ksplit");
 }
 
 extern "C" int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms) {
     if (M < 1 || N < 1 || K < 1 || (K & 3) || reps < 1 || !ms) return -1;
     cudaStream_t st;
     JB_CUDA(cudaStreamCreate(&st));
-    DevBuf ah, al, bh, bl, c;
+    DevBuf ah, al, bh, bl, c, fix, cnt;
     int rc = -1;
+    jb::GemmEpi ep;
     if (ah.alloc((size_t) M * K * 4) && al.alloc((size_t) M * K * 4) && bh.alloc((size_t) N * K * 4) &&
-        bl.alloc((size_t) N * K * 4) && c.alloc((size_t) M * N * 4)) {
+        bl.alloc((size_t) N * K * 4) && c.alloc((size_t) M * N * 4) && alloc_fixup(fix, cnt, M, N, K, ep, st)) {
         cudaMemsetAsync(ah.p, 0, (size_t) M * K * 4, st);
         cudaMemsetAsync(al.p, 0, (size_t) M * K * 4, st);
         cudaMemsetAsync(bh.p, 0, (size_t) N * K * 4, st);
         cudaMemsetAsync(bl.p, 0, (size_t) N * K * 4, st);
-        jb::GemmEpi ep;
         ep.out0 = c.f();
         ep.ld0 = N;
         rc = jb::gemm_tc({ah.f(), al.f(), K}, {bh.f(), bl.f(), K}, M, N, K, ep, st);   // warm-up

@@ -86,10 +86,11 @@ def hjepa_solve(cfg: str, S: int, steps: int = 2, path: str = "") -> float:
         plans = [dict(synth.hjepa_config(5)[1][0], horizon=4, cost_last_n=1)]
     else:
         spec, plans = synth.hjepa_config(int(cfg))
+    seed = 99 if cfg == "w" else int(cfg)
     if not path:
         path = os.path.join(tempfile.gettempdir(), f"kbench-cfg{cfg}.gguf")
     if not os.path.exists(path):
-        synth.write_hjepa(path + ".tmp", spec, seed=cfg)
+        synth.write_hjepa(path + ".tmp", spec, seed=seed)
         os.replace(path + ".tmp", path)
     rng = np.random.default_rng(1)
     lv, p = spec.levels[0], plans[0]

@@ -13,6 +13,29 @@ pytestmark = pytest.mark.gpu
 
 # split-K 64-wide tiles (N or K < 768), and the 128-wide unsplit tiles (N, K >= 768, or N >= 4096) with ragged
 # M and N edges
+@pytest.mark.parametrize("M,N,K", [(2048, 768, 768), (1024, 768, 3072), (300, 1000, 5000), (2048, 768, 55296), (130, 900, 772)])
+def test_gemm_ksplit_matches_f64_and_the_unsplit_kernel(M, N, K):
+    """The planner's configuration of the persistent GEMM: K split in three parts, the partial tiles summed
+    in a fixed order by the part that finishes last (ragged M, N and K edges included)."""
+    L = jlib.load()
+    L.jepa_b200_gemm_ksplit.argtypes = [capi.FP, capi.FP, C.c_int, C.c_int, C.c_int, capi.FP]
+    rng = np.random.default_rng(M + 3 * N + K)
+    A = rng.normal(size=(M, K)).astype(np.float32)
+    B = rng.normal(size=(N, K)).astype(np.float32)
+    Cs = np.zeros((M, N), np.float32)
+    Cu = np.zeros((M, N), np.float32)
+    assert L.jepa_b200_gemm_ksplit(capi.fptr(A), capi.fptr(B), M, N, K, capi.fptr(Cs)) == 0, jlib.error_text()
+    assert L.jepa_b200_gemm(capi.fptr(A), capi.fptr(B), M, N, K, capi.fptr(Cu)) == 0, jlib.error_text()
+    ref = A.astype(np.float64) @ B.astype(np.float64).T
+    scale = np.abs(ref).max()
+    assert np.abs(Cs - ref).max() / scale < 1e-5 * max(1.0, K / 1536)
+    assert np.abs(Cs - Cu).max() / scale < 2e-5 * max(1.0, K / 1536)
+    # deterministic: the parts are summed in a fixed order whichever finishes last
+    C2 = np.zeros((M, N), np.float32)
+    assert L.jepa_b200_gemm_ksplit(capi.fptr(A), capi.fptr(B), M, N, K, capi.fptr(C2)) == 0
+    assert np.array_equal(Cs, C2)
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 64, 32), (256, 384, 384), (200, 130, 100), (1, 8, 4), (512, 2304, 384),
                                    (256, 384, 1536), (4096, 1152, 384), (300, 768, 768), (257, 800, 1000),
                                    (130, 4100, 64), (33, 3072, 768)])
