@@ -125,7 +125,21 @@ bool parse(jepa_model & m) {
         .flag("jepa.enc.cls_token", e.cls_token, false)
         .real("jepa.enc.ln_eps", e.ln_eps, 1e-6f)
         .text("jepa.enc.act", e.act, "gelu_erf");
+    std::string enc_layout, attn_mode;
+    r.real("jepa.enc.rope_theta", e.rope_theta, 10000.0f, 1e-6f, 1e12f)
+        .text("jepa.enc.rope_freq_layout", enc_layout, "tiled")
+        .flag("jepa.enc.rope_interpolate", e.rope_interpolate, false)
+        .num("jepa.enc.rope_ref_grid", e.rope_ref_grid, 0, 0, MAX_WIDTH)
+        .flag("jepa.enc.modality_embed", e.modality_embed, false)
+        .flag("jepa.enc.image_patch_embed", e.image_patch_embed, false)
+        .text("jepa.enc.attn_mode", attn_mode, "full");
     if (!r.ok()) return false;
+    e.rope_interleaved = enc_layout == "interleaved";
+    e.block_causal = attn_mode == "block_causal";
+    if (e.rope_interpolate && e.rope_ref_grid < 1) {
+        log("jepa: jepa.enc.rope_interpolate asks for positions rescaled to jepa.enc.rope_ref_grid, which is %d\n", e.rope_ref_grid);
+        return false;
+    }
 
     m.pred_kind = g.has("jepa.pred.kind") ? g.gets("jepa.pred.kind", "none") : "";
     if (m.pred_kind == "none") m.pred_kind = "";

@@ -49,6 +49,15 @@ struct EncParams {
     bool cls_token = false;
     float ln_eps = 1e-6f;               // jepa.enc.ln_eps
     std::string act = "gelu_erf";       // jepa.enc.act
+    // video encoders (V-JEPA 2 / 2.1, LeVJEPA): 3-D RoPE on q / k, optional modality vectors, the 2.1 image
+    // tokenizer, block-causal attention across temporal slots
+    float rope_theta = 10000.0f;        // jepa.enc.rope_theta
+    bool rope_interleaved = false;      // jepa.enc.rope_freq_layout == "interleaved" (else tiled)
+    bool rope_interpolate = false;      // jepa.enc.rope_interpolate: positions rescaled to rope_ref_grid
+    int rope_ref_grid = 0;              // jepa.enc.rope_ref_grid
+    bool modality_embed = false;        // jepa.enc.modality_embed
+    bool image_patch_embed = false;     // jepa.enc.image_patch_embed
+    bool block_causal = false;          // jepa.enc.attn_mode == "block_causal"
 };
 
 }  // namespace jb

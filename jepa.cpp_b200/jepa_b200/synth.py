@@ -337,6 +337,76 @@ def write_ac(path: str, spec: ACSpec, seed: int = 0) -> None:
     w.write(path)
 
 
+@dc.dataclass
+class VideoEncSpec:
+    """A video encoder bundle: V-JEPA 2 (tiled 3-D RoPE, tubelet 2), V-JEPA 2.1 (interleaved RoPE, modality
+    vectors, a one-frame image tokenizer) or LeVJEPA (CLS token, block-causal attention, tubelet 1)."""
+    family: str = "vjepa2"
+    dim: int = 128
+    n_layer: int = 2
+    n_head: int = 2
+    ffn_dim: int = 256
+    patch: int = 16
+    tubelet: int = 2
+    ftype: str = "f32"
+    w_std: float = 0.05
+    rope_layout: str = "tiled"
+    rope_theta: float = 10000.0
+    rope_interpolate: bool = False
+    rope_ref_grid: int = 0
+    modality_embed: bool = False
+    image_patch_embed: bool = False
+    cls_token: bool = False
+    block_causal: bool = False
+    name: str = "synthetic-video-encoder"
+
+
+def write_video_encoder(path: str, spec: VideoEncSpec, seed: int = 0) -> None:
+    """Write an encoder-only video bundle of the given family (every parameter random)."""
+    g = _Gen(HJepaSpec(levels=[], ftype=spec.ftype, rand_all=True, w_std=spec.w_std), seed)
+    w = g.w
+    D, P = spec.dim, spec.patch
+    w.add_kv("general.architecture", "jepa")
+    w.add_kv("general.name", spec.name)
+    w.add_kv("general.file_type", FTYPE[spec.ftype])
+    w.add_kv("jepa.schema_version", 1)
+    w.add_kv("jepa.family", spec.family)
+    w.add_kv("jepa.modality", "video")
+    for k, v in (("embed_dim", D), ("n_layer", spec.n_layer), ("n_head", spec.n_head), ("ffn_dim", spec.ffn_dim),
+                 ("patch_size", P), ("tubelet_size", spec.tubelet), ("img_size", 256), ("n_frames", 16), ("in_chans", 3)):
+        w.add_kv("jepa.enc." + k, v)
+    w.add_kv("jepa.enc.ln_eps", 1e-6)
+    w.add_kv("jepa.enc.act", "gelu_erf")
+    w.add_kv("jepa.enc.pos_type", "rope3d")
+    w.add_kv("jepa.enc.rope_theta", spec.rope_theta)
+    w.add_kv("jepa.enc.rope_freq_layout", spec.rope_layout)
+    if spec.rope_interpolate:
+        w.add_kv("jepa.enc.rope_interpolate", True)
+        w.add_kv("jepa.enc.rope_ref_grid", spec.rope_ref_grid)
+    w.add_kv("jepa.enc.modality_embed", spec.modality_embed)
+    w.add_kv("jepa.enc.image_patch_embed", spec.image_patch_embed)
+    w.add_kv("jepa.enc.cls_token", spec.cls_token)
+    w.add_kv("jepa.enc.attn_mode", "block_causal" if spec.block_causal else "full")
+    g.lin("enc.patch_embed", 3 * spec.tubelet * P * P, D)
+    if spec.image_patch_embed:
+        g.lin("enc.patch_embed_img", 3 * P * P, D)
+    if spec.modality_embed:
+        g.tensor("enc.mod_embed_video", g.rng.normal(0.0, 0.5, D).astype(np.float32))
+        g.tensor("enc.mod_embed_img", g.rng.normal(0.0, 0.5, D).astype(np.float32))
+    if spec.cls_token:
+        g.tensor("enc.cls_token", g.rng.normal(0.0, 0.5, D).astype(np.float32))
+    for i in range(spec.n_layer):
+        q = f"enc.blk.{i}."
+        g.norm(q + "ln1", D)
+        g.lin(q + "attn_qkv", D, 3 * D)
+        g.lin(q + "attn_out", D, D)
+        g.norm(q + "ln2", D)
+        g.lin(q + "ffn_up", D, spec.ffn_dim)
+        g.lin(q + "ffn_down", spec.ffn_dim, D)
+    g.norm("enc.norm", D)
+    w.write(path)
+
+
 # ---------------------------------------------------------------------------------------------
 # benchmark configurations (the BASELINE configs mapped onto the reference architecture)
 # ---------------------------------------------------------------------------------------------
