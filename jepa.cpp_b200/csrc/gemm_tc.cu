@@ -946,11 +946,13 @@ int launch_p_mode(const SplitMat & A, const SplitMat & B, int M, int N, int K, i
     }
 }
 
-// the persistent kernel's K split of a shape (1 = none): narrow (at most 8 column tiles), long (K >= 768)
-// products, which have too few output tiles to fill the device at planner row counts
+// the persistent kernel's K split of a shape (1 = none): narrow (at most 8 column tiles), very long
+// (K >= 8192) products, which have too few output tiles to fill the device at planner row counts and enough
+// K per part that the partial-tile round trip is small beside it (measured on a B200 at 2048 rows: K = 55,296
+// 894 -> 636 us; at K = 768 and 3072 the split lost, 16 -> 36 and 53 -> 56 us)
 int p_splits(int N, int K) {
     const bool persistent = N >= 4096 || (N >= 768 && K >= 768);
-    return persistent && (N + PBN - 1) / PBN <= 8 && (K + BK - 1) / BK >= 24 ? GEMM_KSPLIT : 1;
+    return persistent && (N + PBN - 1) / PBN <= 8 && K >= 8192 ? GEMM_KSPLIT : 1;
 }
 
 }  // namespace

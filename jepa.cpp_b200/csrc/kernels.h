@@ -54,7 +54,7 @@ struct SplitMat {                    // a split operand: two float32 planes with
 
 // Returns 0, or -1 after logging (unsupported shape / a CUDA error).
 int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st);
-// The persistent kernel splits the K range of narrow, long products (at most 8 column tiles, K >= 768) in
+// The persistent kernel splits the K range of narrow, very long products (at most 8 column tiles, K >= 8192) in
 // GEMM_KSPLIT parts when the caller passes fix-up scratch: each part's partial tile goes to the scratch and
 // the last part to finish sums the parts in a fixed order and applies the epilogue. The split depends on
 // (N, K) only, so a row's bits still do not depend on the batch. These give the scratch a call needs:
