@@ -9,8 +9,8 @@
 // -ffp-contract=off) rounds twice; these kernels then agree with the host ops bit for bit except
 // where a transcendental (erff / expf) differs in its last bit.
 //
-// One warp per row for the row-wise kernels (rows are candidates, a few hundred floats wide), the
-// row re-read from L1 for each pass instead of being held in registers.
+// The loop kernels below take one warp per row and re-read the row from L1 for each pass; the register-
+// resident kernels further down (one or four warps per row) serve every row width that is a multiple of 32.
 #include "kernels.h"
 #include "common.h"
 #include "launch.h"
@@ -204,12 +204,18 @@ __global__ void k_block_bwd(BlockBwdArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Register-resident variants for rows of up to 32 V floats: every pass over the row issues all of its
-// loads at once (element i = lane + 32 k, coalesced per warp instruction) and keeps the values in
-// registers, so a pass costs one memory latency instead of one per element. Same arithmetic, same
-// expression order as the loop kernels above (bit-identical results).
+// Register-resident variants: a row of D floats is held by W warps (32 W threads), V values per thread,
+// element i = t + 32 W k for thread t of the row (coalesced per warp instruction). Every pass over the row
+// issues all of its loads at once and keeps the values in registers, so a pass costs one memory latency
+// instead of one per element. Narrow rows take one warp each (W = 1, FAST_ROWS rows per block); rows of 512
+// floats and more take four warps (W = 4, two rows per block): a 768-wide row is then 6 values per thread
+// instead of 24, which keeps the block backward's eight row arrays in ~70 registers rather than 252 and
+// lets an SM hold four times the warps to cover the memory latency. Row sums reduce each warp's lanes by
+// shuffles, then the W warp partials in shared memory in warp order (a fixed order: deterministic). Same
+// element-wise arithmetic and expression order as the loop kernels above.
 // ---------------------------------------------------------------------------------------------
-constexpr int FAST_ROWS = 4;   // warps (= rows) per block
+constexpr int FAST_ROWS = 4;   // rows per block with one warp per row
+constexpr int WIDE_ROWS = 2;   // rows per block with four warps per row
 
 // Programmatic dependent launch: wait for the grid this one depends on (its writes become visible),
 // then let the next grid in the stream begin launching while this one runs.
@@ -218,88 +224,121 @@ __device__ __forceinline__ void pdl_enter() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-template <int V>
-__device__ __forceinline__ void load_row(const float * __restrict__ p, int D, int lane, float (&v)[V]) {
+// where a thread sits: its row in the block, its index t within the row, its warp within the row
+template <int W>
+struct RowPos {
+    int rr, t, wir, lane;
+    __device__ RowPos() {
+        lane = threadIdx.x & 31;
+        t = threadIdx.x % (32 * W);
+        rr = threadIdx.x / (32 * W);
+        wir = t >> 5;
+    }
+};
+
+template <int V, int W>
+__device__ __forceinline__ void load_row(const float * __restrict__ p, int D, int t, float (&v)[V]) {
 #pragma unroll
-    for (int k = 0; k < V; k++) { const int i = lane + 32 * k; v[k] = i < D ? p[i] : 0.0f; }
+    for (int k = 0; k < V; k++) { const int i = t + 32 * W * k; v[k] = i < D ? p[i] : 0.0f; }
 }
 
-template <int V>
-__device__ __forceinline__ void stats_of(const float (&v)[V], int D, int lane, float eps, double & mean, float & inv) {
+// the sum of a row's per-thread partials (every thread of the block calls it, valid row or not)
+template <int W>
+__device__ __forceinline__ double row_sum(double v, const RowPos<W> & p) {
+    v = warp_sum(v);
+    if (W == 1) return v;
+    __shared__ double red[8][W];
+    if (p.lane == 0) red[p.rr][p.wir] = v;
+    __syncthreads();
+    double s = red[p.rr][0];
+#pragma unroll
+    for (int w = 1; w < W; w++) s += red[p.rr][w];
+    __syncthreads();
+    return s;
+}
+
+template <int V, int W>
+__device__ __forceinline__ void stats_of(const float (&v)[V], int D, const RowPos<W> & p, float eps, double & mean, float & inv) {
     double s = 0;
 #pragma unroll
-    for (int k = 0; k < V; k++) if (lane + 32 * k < D) s += (double) v[k];
-    mean = warp_sum(s) / D;
+    for (int k = 0; k < V; k++) if (p.t + 32 * W * k < D) s += (double) v[k];
+    mean = row_sum<W>(s, p) / D;
     double q = 0;
 #pragma unroll
-    for (int k = 0; k < V; k++) if (lane + 32 * k < D) { const double c = (double) v[k] - mean; q += c * c; }
-    inv = (float) (1.0 / sqrt(warp_sum(q) / D + (double) eps));
+    for (int k = 0; k < V; k++) if (p.t + 32 * W * k < D) { const double c = (double) v[k] - mean; q += c * c; }
+    inv = (float) (1.0 / sqrt(row_sum<W>(q, p) / D + (double) eps));
 }
 
-template <int V>
-__global__ void __launch_bounds__(32 * FAST_ROWS)
+template <int W> __host__ __device__ constexpr int rows_per_block() { return W == 1 ? FAST_ROWS : WIDE_ROWS; }
+
+template <int V, int W>
+__global__ void __launch_bounds__(32 * W * rows_per_block<W>())
 k_block_pre_v(const float * __restrict__ x, int ldx, const float * __restrict__ mod, int ld_mod, int sh_off, int sc_off,
               const float * __restrict__ ln_w, const float * __restrict__ ln_b, float eps0, float eps1,
               float * __restrict__ h_hi, float * __restrict__ h_lo, int ldh, LnStats * __restrict__ st0,
               LnStats * __restrict__ st1, int M, int D) {
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
+    const RowPos<W> p;
+    const int row = blockIdx.x * rows_per_block<W>() + p.rr;
+    const bool valid = row < M;
     // the modulation and the norm weights come from kernels that finished before this grid was launched:
     // they are read while the preceding kernel (the producer of x) still runs
     float xv[V], sc[V], sh[V], lw[V], lb[V];
 #pragma unroll
-    for (int k = 0; k < V; k++) lb[k] = 0.0f;
-    if (row < M) {
-        load_row<V>(mod + (size_t) row * ld_mod + sc_off, D, lane, sc);
-        load_row<V>(mod + (size_t) row * ld_mod + sh_off, D, lane, sh);
-        if (ln_w) load_row<V>(ln_w, D, lane, lw);
-        if (ln_b) load_row<V>(ln_b, D, lane, lb);
+    for (int k = 0; k < V; k++) { lb[k] = 0.0f; sc[k] = sh[k] = lw[k] = xv[k] = 0.0f; }
+    if (valid) {
+        load_row<V, W>(mod + (size_t) row * ld_mod + sc_off, D, p.t, sc);
+        load_row<V, W>(mod + (size_t) row * ld_mod + sh_off, D, p.t, sh);
+        if (ln_w) load_row<V, W>(ln_w, D, p.t, lw);
+        if (ln_b) load_row<V, W>(ln_b, D, p.t, lb);
     }
     pdl_enter();
-    if (row >= M) return;
-    load_row<V>(x + (size_t) row * ldx, D, lane, xv);
+    if (valid) load_row<V, W>(x + (size_t) row * ldx, D, p.t, xv);
     double mean0; float inv0;
-    stats_of<V>(xv, D, lane, eps0, mean0, inv0);
-    if (lane == 0) st0[row] = LnStats{mean0, inv0, 0.0f};
+    stats_of<V, W>(xv, D, p, eps0, mean0, inv0);
+    if (valid && p.t == 0) st0[row] = LnStats{mean0, inv0, 0.0f};
 #pragma unroll
     for (int k = 0; k < V; k++) xv[k] = xhat_of(xv[k], mean0, inv0) * (1.0f + sc[k]) + sh[k];   // z, the FiLM output
     if (ln_w) {
         double mean1; float inv1;
-        stats_of<V>(xv, D, lane, eps1, mean1, inv1);
-        if (lane == 0) st1[row] = LnStats{mean1, inv1, 0.0f};
+        stats_of<V, W>(xv, D, p, eps1, mean1, inv1);
+        if (valid && p.t == 0) st1[row] = LnStats{mean1, inv1, 0.0f};
 #pragma unroll
         for (int k = 0; k < V; k++) xv[k] = xhat_of(xv[k], mean1, inv1) * lw[k] + lb[k];
     }
+    if (!valid) return;
     float * hh = h_hi + (size_t) row * ldh;
     float * hl = h_lo + (size_t) row * ldh;
 #pragma unroll
     for (int k = 0; k < V; k++) {
-        const int i = lane + 32 * k;
+        const int i = p.t + 32 * W * k;
         if (i < D) store_split(hh, hl, i, xv[k]);
     }
 }
 
-template <int V>
-__global__ void __launch_bounds__(32 * FAST_ROWS)
+template <int V, int W>
+__global__ void __launch_bounds__(32 * W * rows_per_block<W>())
 k_layer_norm_v(const float * __restrict__ x, int ldx, const float * __restrict__ w, const float * __restrict__ b, float eps,
                float * __restrict__ y, int ldy, float * __restrict__ hi, float * __restrict__ lo, LnStats * __restrict__ stats,
                int M, int D) {
     pdl_enter();
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
-    if (row >= M) return;
+    const RowPos<W> p;
+    const int row = blockIdx.x * rows_per_block<W>() + p.rr;
+    const bool valid = row < M;
     float xv[V], wv[V], bv[V];
-    load_row<V>(x + (size_t) row * ldx, D, lane, xv);
 #pragma unroll
-    for (int k = 0; k < V; k++) { wv[k] = 1.0f; bv[k] = 0.0f; }
-    if (w) load_row<V>(w, D, lane, wv);
-    if (b) load_row<V>(b, D, lane, bv);
+    for (int k = 0; k < V; k++) { wv[k] = 1.0f; bv[k] = 0.0f; xv[k] = 0.0f; }
+    if (valid) {
+        load_row<V, W>(x + (size_t) row * ldx, D, p.t, xv);
+        if (w) load_row<V, W>(w, D, p.t, wv);
+        if (b) load_row<V, W>(b, D, p.t, bv);
+    }
     double mean; float inv;
-    stats_of<V>(xv, D, lane, eps, mean, inv);
-    if (stats && lane == 0) stats[row] = LnStats{mean, inv, 0.0f};
+    stats_of<V, W>(xv, D, p, eps, mean, inv);
+    if (!valid) return;
+    if (stats && p.t == 0) stats[row] = LnStats{mean, inv, 0.0f};
 #pragma unroll
     for (int k = 0; k < V; k++) {
-        const int i = lane + 32 * k;
+        const int i = p.t + 32 * W * k;
         if (i >= D) continue;
         const float v = xhat_of(xv[k], mean, inv) * wv[k] + bv[k];
         if (y) y[(size_t) row * ldy + i] = v;
@@ -307,43 +346,46 @@ k_layer_norm_v(const float * __restrict__ x, int ldx, const float * __restrict__
     }
 }
 
-template <int V>
-__global__ void __launch_bounds__(32 * FAST_ROWS)
+template <int V, int W>
+__global__ void __launch_bounds__(32 * W * rows_per_block<W>())
 k_layer_norm_bwd_v(const float * __restrict__ gy, int ldgy, const float * __restrict__ x, int ldx,
                    const LnStats * __restrict__ stats, const float * __restrict__ w, const float * __restrict__ gres, int ldres,
                    float * __restrict__ gx, int ldgx, const float * __restrict__ dn, int lddn, const float * __restrict__ gate,
                    int ld_gate, float * __restrict__ dmod_hi, float * __restrict__ dmod_lo, int ld_dmod,
                    float * __restrict__ d_hi, float * __restrict__ d_lo, int ldd, int M, int D) {
     pdl_enter();
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
-    if (row >= M) return;
-    const LnStats stt = stats[row];
+    const RowPos<W> p;
+    const int row = blockIdx.x * rows_per_block<W>() + p.rr;
+    const bool valid = row < M;
+    const LnStats stt = valid ? stats[row] : LnStats{0.0, 0.0f, 0.0f};
     float gh[V], xh[V], wv[V], gr[V], dv[V], gt[V];
-    load_row<V>(gy + (size_t) row * ldgy, D, lane, gh);
-    load_row<V>(x + (size_t) row * ldx, D, lane, xh);
 #pragma unroll
-    for (int k = 0; k < V; k++) { wv[k] = 1.0f; gr[k] = 0.0f; }
-    if (w) load_row<V>(w, D, lane, wv);
-    if (gres) load_row<V>(gres + (size_t) row * ldres, D, lane, gr);
-    if (dn) {
-        load_row<V>(dn + (size_t) row * lddn, D, lane, dv);
-        load_row<V>(gate + (size_t) row * ld_gate, D, lane, gt);
+    for (int k = 0; k < V; k++) { wv[k] = 1.0f; gr[k] = 0.0f; gh[k] = xh[k] = dv[k] = gt[k] = 0.0f; }
+    if (valid) {
+        load_row<V, W>(gy + (size_t) row * ldgy, D, p.t, gh);
+        load_row<V, W>(x + (size_t) row * ldx, D, p.t, xh);
+        if (w) load_row<V, W>(w, D, p.t, wv);
+        if (gres) load_row<V, W>(gres + (size_t) row * ldres, D, p.t, gr);
+        if (dn) {
+            load_row<V, W>(dn + (size_t) row * lddn, D, p.t, dv);
+            load_row<V, W>(gate + (size_t) row * ld_gate, D, p.t, gt);
+        }
     }
     double m1 = 0, m2 = 0;
 #pragma unroll
     for (int k = 0; k < V; k++) {
-        if (lane + 32 * k >= D) continue;
+        if (p.t + 32 * W * k >= D) continue;
         gh[k] = gh[k] * wv[k];
         xh[k] = xhat_of(xh[k], stt.mean, stt.inv);
         m1 += gh[k];
         m2 += (double) gh[k] * xh[k];
     }
-    m1 = warp_sum(m1) / D;
-    m2 = warp_sum(m2) / D;
+    m1 = row_sum<W>(m1, p) / D;
+    m2 = row_sum<W>(m2, p) / D;
+    if (!valid) return;
 #pragma unroll
     for (int k = 0; k < V; k++) {
-        const int i = lane + 32 * k;
+        const int i = p.t + 32 * W * k;
         if (i >= D) continue;
         float v = (float) (((double) gh[k] - m1 - (double) xh[k] * m2) * (double) stt.inv);
         if (gres) v = gr[k] + v;
@@ -355,35 +397,37 @@ k_layer_norm_bwd_v(const float * __restrict__ gy, int ldgy, const float * __rest
     }
 }
 
-template <int V>
-__global__ void __launch_bounds__(32 * FAST_ROWS) k_block_bwd_v(BlockBwdArgs a) {
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * FAST_ROWS + (threadIdx.x >> 5);
+template <int V, int W>
+__global__ void __launch_bounds__(32 * W * rows_per_block<W>()) k_block_bwd_v(BlockBwdArgs a) {
+    const RowPos<W> p;
+    const int row = blockIdx.x * rows_per_block<W>() + p.rr;
+    const bool valid = row < a.M;
     const int D = a.D;
     // every load of the row up front (the struct's pointers may alias as far as the compiler knows). All but
     // gh were written at least two kernels earlier in the stream (the forward pass, the modulation, the
     // residual gradient of the half above), by grids that finished before this one was launched: they are
     // read while the preceding kernel (the producer of gh) still runs.
     float gz[V], xh[V], sc[V], z[V], lw[V], gr[V], av[V], gt[V];
+#pragma unroll
+    for (int k = 0; k < V; k++) gz[k] = xh[k] = sc[k] = z[k] = lw[k] = gr[k] = av[k] = gt[k] = 0.0f;
     LnStats s0{}, s1{};
-    if (row < a.M) {
+    if (valid) {
         s0 = a.st0[row];
         if (a.ln_w) s1 = a.st1[row];
-        load_row<V>(a.x + (size_t) row * a.ldx, D, lane, xh);
-        load_row<V>(a.mod + (size_t) row * a.ld_mod + a.sc_off, D, lane, sc);
-        load_row<V>(a.gres + (size_t) row * a.ldres, D, lane, gr);
+        load_row<V, W>(a.x + (size_t) row * a.ldx, D, p.t, xh);
+        load_row<V, W>(a.mod + (size_t) row * a.ld_mod + a.sc_off, D, p.t, sc);
+        load_row<V, W>(a.gres + (size_t) row * a.ldres, D, p.t, gr);
         if (a.ln_w) {
-            load_row<V>(a.mod + (size_t) row * a.ld_mod + a.sh_off, D, lane, z);
-            load_row<V>(a.ln_w, D, lane, lw);
+            load_row<V, W>(a.mod + (size_t) row * a.ld_mod + a.sh_off, D, p.t, z);
+            load_row<V, W>(a.ln_w, D, p.t, lw);
         }
         if (a.a2) {
-            load_row<V>(a.a2 + (size_t) row * a.lda2, D, lane, av);
-            load_row<V>(a.mod2 + (size_t) row * a.ld_mod2 + a.gate2_off, D, lane, gt);
+            load_row<V, W>(a.a2 + (size_t) row * a.lda2, D, p.t, av);
+            load_row<V, W>(a.mod2 + (size_t) row * a.ld_mod2 + a.gate2_off, D, p.t, gt);
         }
     }
     pdl_enter();
-    if (row >= a.M) return;
-    load_row<V>(a.gh + (size_t) row * a.ldgh, D, lane, gz);
+    if (valid) load_row<V, W>(a.gh + (size_t) row * a.ldgh, D, p.t, gz);
 #pragma unroll
     for (int k = 0; k < V; k++) xh[k] = xhat_of(xh[k], s0.mean, s0.inv);
     if (a.ln_w) {
@@ -391,14 +435,14 @@ __global__ void __launch_bounds__(32 * FAST_ROWS) k_block_bwd_v(BlockBwdArgs a) 
         double n1 = 0, n2 = 0;
 #pragma unroll
         for (int k = 0; k < V; k++) {
-            if (lane + 32 * k >= D) continue;
+            if (p.t + 32 * W * k >= D) continue;
             z[k] = xhat_of(xh[k] * (1.0f + sc[k]) + z[k], s1.mean, s1.inv);
             gz[k] = gz[k] * lw[k];
             n1 += gz[k];
             n2 += (double) gz[k] * z[k];
         }
-        n1 = warp_sum(n1) / D;
-        n2 = warp_sum(n2) / D;
+        n1 = row_sum<W>(n1, p) / D;
+        n2 = row_sum<W>(n2, p) / D;
 #pragma unroll
         for (int k = 0; k < V; k++) gz[k] = (float) (((double) gz[k] - n1 - (double) z[k] * n2) * (double) s1.inv);
     }
@@ -407,19 +451,22 @@ __global__ void __launch_bounds__(32 * FAST_ROWS) k_block_bwd_v(BlockBwdArgs a) 
     double m1 = 0, m2 = 0;
 #pragma unroll
     for (int k = 0; k < V; k++) {
-        const int i = lane + 32 * k;
+        const int i = p.t + 32 * W * k;
         if (i >= D) continue;
-        store_split(dmh, dml, a.sc_off + i, gz[k] * xh[k]);
-        store_split(dmh, dml, a.sh_off + i, gz[k]);
+        if (valid) {
+            store_split(dmh, dml, a.sc_off + i, gz[k] * xh[k]);
+            store_split(dmh, dml, a.sh_off + i, gz[k]);
+        }
         gz[k] = gz[k] * (1.0f + sc[k]);   // now the gradient into LN0's output
         m1 += gz[k];
         m2 += (double) gz[k] * xh[k];
     }
-    m1 = warp_sum(m1) / D;
-    m2 = warp_sum(m2) / D;
+    m1 = row_sum<W>(m1, p) / D;
+    m2 = row_sum<W>(m2, p) / D;
+    if (!valid) return;
 #pragma unroll
     for (int k = 0; k < V; k++) {
-        const int i = lane + 32 * k;
+        const int i = p.t + 32 * W * k;
         if (i >= D) continue;
         const float v = gr[k] + (float) (((double) gz[k] - m1 - (double) xh[k] * m2) * (double) s0.inv);
         a.gx[(size_t) row * a.ldgx + i] = v;
@@ -431,10 +478,13 @@ __global__ void __launch_bounds__(32 * FAST_ROWS) k_block_bwd_v(BlockBwdArgs a) 
     }
 }
 
-// values per lane of the register kernels for a row of D floats (0 = use the loop kernels)
+// values per thread of the register kernels for a row of D floats at W warps per row (0 = use the loop
+// kernels): four warps per row from 512 floats, one below
+inline int fast_w(int D) { return D >= 512 && D % 128 == 0 ? 4 : 1; }
 inline int fast_v(int D) {
+    const int lanes = 32 * fast_w(D);
     if (D % 32 != 0) return 0;
-    const int v = D / 32;
+    const int v = (D + lanes - 1) / lanes;
     for (int c : {1, 2, 4, 6, 8, 12, 16, 24, 32}) if (v <= c) return c;
     return 0;
 }
@@ -450,6 +500,17 @@ inline int fast_v(int D) {
         case 16: { constexpr int VV = 16; __VA_ARGS__; } break;    \
         case 24: { constexpr int VV = 24; __VA_ARGS__; } break;    \
         default: { constexpr int VV = 32; __VA_ARGS__; } break;    \
+    }
+// one warp per row, or four for rows of 512 floats and more (a multiple of 128, at most 32 x 128)
+#define JB_DISPATCH_VW(D, ...)                                                                      \
+    if (fast_w(D) == 4) {                                                                           \
+        constexpr int WW = 4;                                                                       \
+        const unsigned nb = (unsigned) ((M_ + WIDE_ROWS - 1) / WIDE_ROWS);                          \
+        JB_DISPATCH_V(fast_v(D), __VA_ARGS__);                                                      \
+    } else {                                                                                        \
+        constexpr int WW = 1;                                                                       \
+        const unsigned nb = (unsigned) ((M_ + FAST_ROWS - 1) / FAST_ROWS);                          \
+        JB_DISPATCH_V(fast_v(D), __VA_ARGS__);                                                      \
     }
 
 // ---------------------------------------------------------------------------------------------
@@ -661,10 +722,10 @@ void block_pre(const float * x, int ldx, const float * mod, int ld_mod, int sh_o
                const float * ln_b, float eps0, float eps1, float * h_hi, float * h_lo, int ldh, LnStats * st0,
                LnStats * st1, int M, int D, cudaStream_t st) {
     if (M <= 0) return;
-    if (const int v = fast_v(D)) {
-        const unsigned nb = (unsigned) ((M + FAST_ROWS - 1) / FAST_ROWS);
-        JB_DISPATCH_V(v, (launch_pdl(k_block_pre_v<VV>, nb, 32 * FAST_ROWS, 0, st, x, ldx, mod, ld_mod, sh_off, sc_off, ln_w, ln_b,
-                                                                           eps0, eps1, h_hi, h_lo, ldh, st0, st1, M, D)));
+    if (fast_v(D)) {
+        const int M_ = M;
+        JB_DISPATCH_VW(D, (launch_pdl(k_block_pre_v<VV, WW>, nb, 32 * WW * rows_per_block<WW>(), 0, st, x, ldx, mod, ld_mod,
+                                      sh_off, sc_off, ln_w, ln_b, eps0, eps1, h_hi, h_lo, ldh, st0, st1, M, D)));
         return;
     }
     k_block_pre<<<row_blocks(M), 32 * ROWS_PER_BLOCK, 0, st>>>(x, ldx, mod, ld_mod, sh_off, sc_off, ln_w, ln_b, eps0,
@@ -674,9 +735,10 @@ void block_pre(const float * x, int ldx, const float * mod, int ld_mod, int sh_o
 void layer_norm(const float * x, int ldx, const float * w, const float * b, float eps, float * y, int ldy, float * hi,
                 float * lo, LnStats * stats, int M, int D, cudaStream_t st) {
     if (M <= 0) return;
-    if (const int v = fast_v(D)) {
-        const unsigned nb = (unsigned) ((M + FAST_ROWS - 1) / FAST_ROWS);
-        JB_DISPATCH_V(v, (launch_pdl(k_layer_norm_v<VV>, nb, 32 * FAST_ROWS, 0, st, x, ldx, w, b, eps, y, ldy, hi, lo, stats, M, D)));
+    if (fast_v(D)) {
+        const int M_ = M;
+        JB_DISPATCH_VW(D, (launch_pdl(k_layer_norm_v<VV, WW>, nb, 32 * WW * rows_per_block<WW>(), 0, st, x, ldx, w, b, eps, y,
+                                      ldy, hi, lo, stats, M, D)));
         return;
     }
     k_layer_norm<<<row_blocks(M), 32 * ROWS_PER_BLOCK, 0, st>>>(x, ldx, w, b, eps, y, ldy, hi, lo, stats, M, D);
@@ -687,11 +749,11 @@ void layer_norm_bwd(const float * gy, int ldgy, const float * x, int ldx, const 
                     int ld_gate, float * dmod_hi, float * dmod_lo, int ld_dmod, float * d_hi, float * d_lo, int ldd,
                     int M, int D, cudaStream_t st) {
     if (M <= 0) return;
-    if (const int v = fast_v(D)) {
-        const unsigned nb = (unsigned) ((M + FAST_ROWS - 1) / FAST_ROWS);
-        JB_DISPATCH_V(v, (launch_pdl(k_layer_norm_bwd_v<VV>, nb, 32 * FAST_ROWS, 0, st, gy, ldgy, x, ldx, stats, w, gres, ldres, gx, ldgx,
-                                                                                dn, lddn, gate, ld_gate, dmod_hi, dmod_lo, ld_dmod,
-                                                                                d_hi, d_lo, ldd, M, D)));
+    if (fast_v(D)) {
+        const int M_ = M;
+        JB_DISPATCH_VW(D, (launch_pdl(k_layer_norm_bwd_v<VV, WW>, nb, 32 * WW * rows_per_block<WW>(), 0, st, gy, ldgy, x, ldx,
+                                      stats, w, gres, ldres, gx, ldgx, dn, lddn, gate, ld_gate, dmod_hi, dmod_lo, ld_dmod, d_hi,
+                                      d_lo, ldd, M, D)));
         return;
     }
     k_layer_norm_bwd<<<row_blocks(M), 32 * ROWS_PER_BLOCK, 0, st>>>(gy, ldgy, x, ldx, stats, w, gres, ldres, gx, ldgx, dn,
@@ -701,9 +763,9 @@ void layer_norm_bwd(const float * gy, int ldgy, const float * x, int ldx, const 
 
 void block_bwd(const BlockBwdArgs & a, cudaStream_t st) {
     if (a.M <= 0) return;
-    if (const int v = fast_v(a.D)) {
-        const unsigned nb = (unsigned) ((a.M + FAST_ROWS - 1) / FAST_ROWS);
-        JB_DISPATCH_V(v, (launch_pdl(k_block_bwd_v<VV>, nb, 32 * FAST_ROWS, 0, st, a)));
+    if (fast_v(a.D)) {
+        const int M_ = a.M;
+        JB_DISPATCH_VW(a.D, (launch_pdl(k_block_bwd_v<VV, WW>, nb, 32 * WW * rows_per_block<WW>(), 0, st, a)));
         return;
     }
     k_block_bwd<<<row_blocks(a.M), 32 * ROWS_PER_BLOCK, 0, st>>>(a);
