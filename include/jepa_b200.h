@@ -23,8 +23,8 @@ const char * jepa_b200_version(void);
 // (host buffers, row-major). A kernel check: the planner's linears all run through this kernel.
 int jepa_b200_gemm(const float * A, const float * B, int M, int N, int K, float * C);
 
-// The same product in the planner's configuration: narrow, very long products (at most 8 output column tiles
-// of 128, K >= 8192) split their K range in three parts whose partial tiles a fix-up sums in a fixed order (the
+// The same product in the planner's configuration: narrow, long products (at most 8 output column tiles
+// of 128, K >= 2048) split their K range in three parts whose partial tiles a fix-up sums in a fixed order (the
 // planner passes that scratch on every such product). Agrees with jepa_b200_gemm to rounding.
 int jepa_b200_gemm_ksplit(const float * A, const float * B, int M, int N, int K, float * C);
 

@@ -545,6 +545,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
 // four rows per instruction: coalesced loads and stores. A tile's arithmetic is the split kernel's at
 // one split (the same MMAs in the same order), so a row's bits do not depend on the batch.
 constexpr int PBN = 128, PSTAGES = 3, PEPI_WARPS = 8, PTHREADS = 64 + 32 * PEPI_WARPS;
+constexpr int FIX_ROWS = 4;   // K-split fix-up: row groups of partial tiles loaded at once per lane
 constexpr uint32_t PSTAGE_BYTES = 2 * BM * BK * 4 + 2 * PBN * BK * 4;
 constexpr size_t PSMEM_BYTES = (size_t) PSTAGES * PSTAGE_BYTES + (size_t) PEPI_WARPS * 32 * 32 * 4 + 1024;
 static_assert(PSMEM_BYTES + 256 <= 227 * 1024, "persistent tf32x3 GEMM: stages and staging buffers fit");
@@ -727,15 +728,32 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                 __threadfence();
                 const float * parts = ep.fix + (size_t) t * splits * (size_t) (BM * PBN);
                 if (row0 >= M || n0 + half * 64 >= N) continue;   // warp-uniform
-#pragma unroll 2
-                for (int j = 0; j < 16; j++) {
-                    const int idx = j * 32 + lane, r = idx >> 4, c = idx & 15;
-                    const int row = row0 + r, col = half * 64 + 4 * c;
-                    if (row >= M) continue;
-                    const float * p0 = parts + (size_t) (q * 32 + r) * PBN + col;
-                    float4 v = __ldcg((const float4 *) p0);
-                    for (int p = 1; p < splits; p++) v = f4_add(v, __ldcg((const float4 *) (p0 + (size_t) p * (BM * PBN))));
-                    apply_epi4<MODE>(ep, row, n0 + col, N, v);
+                // FIX_ROWS groups of every part's values are loaded before any is summed, so that a lane waits
+                // out one L2 round trip per group of loads rather than one per load (every slot row exists:
+                // the parts write whole tiles)
+#pragma unroll 1
+                for (int j0 = 0; j0 < 16; j0 += FIX_ROWS) {
+                    float4 v[FIX_ROWS][GEMM_KSPLIT_MAX];
+#pragma unroll
+                    for (int jj = 0; jj < FIX_ROWS; jj++) {
+                        const int idx = (j0 + jj) * 32 + lane, r = idx >> 4, c = idx & 15;
+                        const float * p0 = parts + (size_t) (q * 32 + r) * PBN + half * 64 + 4 * c;
+#pragma unroll
+                        for (int p = 0; p < GEMM_KSPLIT_MAX; p++) {
+                            if (p < splits) v[jj][p] = __ldcg((const float4 *) (p0 + (size_t) p * (BM * PBN)));
+                        }
+                    }
+#pragma unroll
+                    for (int jj = 0; jj < FIX_ROWS; jj++) {
+                        const int idx = (j0 + jj) * 32 + lane, r = idx >> 4, c = idx & 15;
+                        const int row = row0 + r, col = half * 64 + 4 * c;
+                        float4 s = v[jj][0];
+#pragma unroll
+                        for (int p = 1; p < GEMM_KSPLIT_MAX; p++) {
+                            if (p < splits) s = f4_add(s, v[jj][p]);   // parts in order 0, 1, ...
+                        }
+                        if (row < M) apply_epi4<MODE>(ep, row, n0 + col, N, s);
+                    }
                 }
                 continue;
             }
@@ -906,6 +924,7 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
 
 template <int MODE>
 int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
+    if (splits < 1 || splits > GEMM_KSPLIT_MAX) { log("jepa: gemm: %d K parts (at most %d)\n", splits, GEMM_KSPLIT_MAX); return -1; }
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
     if (!make_map(&ta_hi, A.hi, M, K, A.ld, BM) || !make_map(&ta_lo, A.lo, M, K, A.ld, BM) ||
         !make_map(&tb_hi, B.hi, N, K, B.ld, PBN) || !make_map(&tb_lo, B.lo, N, K, B.ld, PBN)) {
@@ -946,13 +965,15 @@ int launch_p_mode(const SplitMat & A, const SplitMat & B, int M, int N, int K, i
     }
 }
 
-// the persistent kernel's K split of a shape (1 = none): narrow (at most 8 column tiles), very long
-// (K >= 8192) products, which have too few output tiles to fill the device at planner row counts and enough
-// K per part that the partial-tile round trip is small beside it (measured on a B200 at 2048 rows: K = 55,296
-// 894 -> 636 us; at K = 768 and 3072 the split lost, 16 -> 36 and 53 -> 56 us)
+// the persistent kernel's K split of a shape (1 = none): narrow (at most 8 column tiles), long (K >= 2048)
+// products, which have too few output tiles to fill the device at planner row counts and enough K per part
+// that the partial-tile round trip is small beside it. Measured on a B200 (us per launch, rows 256 / 1024 /
+// 2048): N 768 K 3072 unsplit 45.8 / 46.1 / 53.7, in three parts 23.1 / 24.5 / 46.0; K 55,296 at 2048 rows
+// 894 -> 629. At K = 768 the split loses at 2048 rows (15.9 -> 22.4), and the 3072-wide products (24 column
+// tiles) lose from 512 rows on, so those keep whole tiles.
 int p_splits(int N, int K) {
     const bool persistent = N >= 4096 || (N >= 768 && K >= 768);
-    return persistent && (N + PBN - 1) / PBN <= 8 && K >= 8192 ? GEMM_KSPLIT : 1;
+    return persistent && (N + PBN - 1) / PBN <= 8 && K >= 2048 ? GEMM_KSPLIT : 1;
 }
 
 }  // namespace
