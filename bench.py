@@ -614,7 +614,9 @@ def run_hjepa(args, rank, world, local, dist):
                                   "(M, N, K, us per launch): " + ", ".join(f"{m}x{n}x{k} {u}" for m, n, k, u in shapes),
                          "peak_kind": f"bf16 dense, {peak_kind}; the kernel runs tf32 (half the bf16 rate) three products "
                                       f"per output (hi x hi, hi x lo, lo x hi), so its own ceiling is 1/6 of this peak",
-                         "whole_plan_tflops": achieved_tf, "whole_plan_frac": achieved_tf / peak_tf},
+                         "whole_plan_tflops": achieved_tf, "whole_plan_frac": achieved_tf / (peak_tf * world),
+                         "whole_plan_note": f"algorithmic FLOPs of the plan over all {world} GPU(s) / device time, "
+                                            f"against {world} x the bf16 peak"},
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
