@@ -32,6 +32,18 @@ int jepa_b200_gemm_ksplit(const float * A, const float * B, int M, int N, int K,
 // returns the mean milliseconds per launch in *ms (CUDA events around the launches).
 int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms);
 
+// The planner's GEMM with its weight operand kept in GGUF block values and dequantised in the mainloop:
+// W [rows][ne0] are the raw rows of a weight of ggml type 8 (q8_0), 2 (q4_0) or 1 (f16), rows and ne0
+// multiples of 32. transposed = 0: C [M][rows] = A [M][ne0] W^T (the forward product); transposed = 1:
+// C [M][ne0] = A [M][rows] W (the backward product against the same weight). ksplit = 1 passes the K-split
+// scratch as the planner does. Equals jepa_b200_gemm on the dequantised weight bit for bit.
+int jepa_b200_gemm_quant(uint32_t ggml_type, const void * w_raw, int rows, int ne0, int transposed, const float * A, int M,
+                         float * C, int ksplit);
+
+// jepa_b200_gemm_quant timed on the device (zero operands of shape M x N x K, `reps` launches); the mean
+// milliseconds per launch in *ms.
+int jepa_b200_gemm_quant_bench(uint32_t ggml_type, int M, int N, int K, int transposed, int reps, double * ms);
+
 // jepa_b200_gemm for callers that must not allocate device memory. No counterpart in the reference.
 // Some hosts cannot call cudaMalloc around a kernel call: a process whose device memory budget is fixed
 // at start-up, a real-time control loop where an allocation (which can synchronise the whole device)

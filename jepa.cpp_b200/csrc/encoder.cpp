@@ -89,7 +89,7 @@ struct DevBuf {
 };
 
 int lin_tc(const DLin & L, const float * x_hi, const float * x_lo, int ldx, int M, GemmEpi ep, cudaStream_t st) {
-    return gemm_tc({x_hi, x_lo, ldx}, {L.w_hi, L.w_lo, L.in}, M, L.out, L.in, ep, st);
+    return gemm_tc({x_hi, x_lo, ldx}, L.fwd(), M, L.out, L.in, ep, st);
 }
 
 }  // namespace

@@ -237,6 +237,163 @@ __device__ __forceinline__ void bulk_to_peer(uint32_t remote_dst, uint32_t local
                  :: "r"(remote_dst), "r"(local_src), "r"(bytes), "r"(remote_bar) : "memory");
 }
 
+// ---------------------------------------------------------------------------------------------
+// Weight operands dequantised in the mainloop (QuantB). The producer's TMA copies a K-step's raw tile --
+// BN rows of 32 block values and their f16 scales -- into the stage's B_lo area; two converter warps read it
+// into registers, meet on the stage's raw barrier (after which the area may be overwritten), and write the
+// split planes B_hi and B_lo in the 128-byte swizzle the TMA would have used (16-byte chunk c of row r at
+// c ^ (r & 7)). The MMA warp waits on the stage's converted barrier instead of the copy barrier.
+// ---------------------------------------------------------------------------------------------
+struct QDesc {
+    int fmt = QF_NONE;
+    int orient = 0;
+};
+// converter warps: four in the split-K cluster kernel (its reduction warps are idle in the mainloop), PCONV_WARPS
+// in the persistent kernel (added warps: its register budget caps them)
+constexpr int CONV_WARPS = 4;
+#ifndef JB_PCONV_WARPS
+#define JB_PCONV_WARPS 2
+#endif
+constexpr int PCONV_WARPS = JB_PCONV_WARPS;
+
+// raw bytes of one row of a K-step (32 values) and of the K-step's scales, for BN rows
+__host__ __device__ constexpr uint32_t raw_row_bytes(int fmt) { return fmt == QF_Q8 ? 32u : fmt == QF_Q4 ? 16u : fmt == QF_F16 ? 64u : 0u; }
+__host__ __device__ constexpr uint32_t raw_scale_bytes(int fmt, int bn) { return fmt == QF_Q8 || fmt == QF_Q4 ? 2u * (uint32_t) bn : 0u; }
+
+__device__ __forceinline__ float half_bits(uint32_t h) { return __half2float(__ushort_as_half((unsigned short) (h & 0xFFFFu))); }
+
+// byte k of x as the float 2^23 + byte (exact): the block values become floats by a byte permute and one
+// exact subtraction instead of an integer conversion
+__device__ __forceinline__ float byte_as_float(uint32_t x, int k) {
+    return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7650u | (uint32_t) k));
+}
+
+// value e (0..15) of a 16-value row segment: the block value times its scale, exact in float32.
+// w: the segment's raw words (q8_0: int8 with the sign bit flipped; q4_0: low and high nibbles in words
+// 0-1 and 2-3; f16: halves); sc: the scale(s) as f16 bits.
+template <int FMT, int ORIENT>
+__device__ __forceinline__ float seg_value(const uint32_t (&w)[8], const uint32_t (&sc)[8], int e) {
+    if (FMT == QF_F16) return half_bits(w[e >> 1] >> ((e & 1) * 16));
+    const float d = ORIENT == 0 ? half_bits(sc[0]) : half_bits(sc[e >> 1] >> ((e & 1) * 16));
+    if (FMT == QF_Q8) return d * (byte_as_float(w[e >> 2], e & 3) - 8388736.0f);            // q
+    return (byte_as_float(w[2 * (e & 1) + (e >> 3)], (e >> 1) & 3) - 8388616.0f) * d;      // q - 8
+}
+
+// The split planes of a converter thread's NSEG row segments (raw words w and scales sc in registers, as
+// seg_value reads them) into a stage's B_hi / B_lo areas (bh, bh + BN * 128): segment g of thread ct is
+// segment ct + CT g of the tile, row (ct + CT g) / 2, values 16 ((ct + CT g) % 2) ..
+template <int BN, int CT, int FMT, int ORIENT, int NSEG>
+__device__ __forceinline__ void write_segments(uint8_t * bh, int ct, const uint32_t (&w)[NSEG][8], const uint32_t (&sc)[NSEG][8]) {
+    uint8_t * bl = bh + BN * 128;
+#pragma unroll
+    for (int g = 0; g < NSEG; g++) {
+        const int seg = ct + CT * g, r = seg >> 1, h = seg & 1;
+        float * hrow = (float *) (bh + r * 128);
+        float * lrow = (float *) (bl + r * 128);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            float hv[4], lv[4];
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const float v = seg_value<FMT, ORIENT>(w[g], sc[g], 4 * c + t);
+                hv[t] = split_hi(v);
+                lv[t] = v - hv[t];
+            }
+            const int pos = ((4 * h + c) ^ (r & 7)) << 2;
+            *(float4 *) (hrow + pos) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+            *(float4 *) (lrow + pos) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+        }
+    }
+    // the planes are read by the tensor core (async proxy) after the converted barrier
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// the raw words of a 16-value segment (q8_0: sign bit flipped; q4_0: low nibbles in words 0-1, high in 2-3)
+template <int FMT>
+__device__ __forceinline__ void raw_words(const uint8_t * src, uint32_t (&w)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) w[i] = 0u;
+    if (FMT == QF_Q4) {
+        const uint2 x = *(const uint2 *) src;
+        w[0] = x.x & 0x0F0F0F0Fu; w[1] = x.y & 0x0F0F0F0Fu;
+        w[2] = (x.x >> 4) & 0x0F0F0F0Fu; w[3] = (x.y >> 4) & 0x0F0F0F0Fu;
+        return;
+    }
+    constexpr int N4 = FMT == QF_F16 ? 2 : 1;
+#pragma unroll
+    for (int i = 0; i < N4; i++) {
+        const uint4 x = ((const uint4 *) src)[i];
+        w[4 * i] = x.x; w[4 * i + 1] = x.y; w[4 * i + 2] = x.z; w[4 * i + 3] = x.w;
+    }
+    if (FMT == QF_Q8) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) w[i] ^= 0x80808080u;   // int8 -> byte + 128
+    }
+}
+
+// 16 consecutive f16 scales (orient 1) into sc[0 .. 7]
+__device__ __forceinline__ void scale_words(const uint16_t * src, uint32_t (&sc)[8]) {
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const uint4 x = ((const uint4 *) src)[i];
+        sc[4 * i] = x.x; sc[4 * i + 1] = x.y; sc[4 * i + 2] = x.z; sc[4 * i + 3] = x.w;
+    }
+}
+
+// Converts one stage's raw tile (in the B_lo area at bh + BN * 128) into B_hi / B_lo. The tile's rows are
+// cut in 16-value segments; converter thread ct of CT owns segments ct, ct + CT, ... (segment g: row g / 2,
+// values 16 (g % 2) ..). The raw area is overwritten by the planes, so the converters first read their
+// segments into registers and meet on the stage's raw barrier. False = that wait gave up.
+template <int BN, int CT, int FMT, int ORIENT>
+__device__ __forceinline__ bool convert_rows(uint8_t * bh, int ct, int lane, uint64_t * raw_bar, uint32_t ph) {
+    constexpr int NSEG = 2 * BN / CT;
+    constexpr int RB = (int) raw_row_bytes(FMT), SB = RB / 2;
+    static_assert(NSEG >= 1 && 2 * BN % CT == 0, "whole segments per converter thread");
+    const uint8_t * bl = bh + BN * 128;
+    uint32_t w[NSEG][8], sc[NSEG][8];
+#pragma unroll
+    for (int g = 0; g < NSEG; g++) {
+        const int seg = ct + CT * g, r = seg >> 1, h = seg & 1;
+        raw_words<FMT>(bl + r * RB + h * SB, w[g]);
+#pragma unroll
+        for (int i = 0; i < 8; i++) sc[g][i] = 0u;
+        if (FMT != QF_F16) {
+            const uint8_t * d = bl + BN * RB;
+            if (ORIENT == 0) sc[g][0] = ((const uint16_t *) d)[r];
+            else scale_words((const uint16_t *) (d + (r >> 5) * 64 + h * 32), sc[g]);
+        }
+    }
+    // every converter thread holds its raw segments: the B_lo area may be overwritten from here on
+    __syncwarp();
+    if (lane == 0) mbar_arrive(raw_bar);
+    if (!mbar_wait_spin(raw_bar, ph, 7, &g_gemm_error)) return false;
+    write_segments<BN, CT, FMT, ORIENT, NSEG>(bh, ct, w, sc);
+    return true;
+}
+
+template <int BN, int CT>
+__device__ __forceinline__ bool convert_stage(uint8_t * bh, const QDesc & qd, int ct, int lane, uint64_t * raw_bar, uint32_t ph) {
+    switch (qd.fmt * 2 + qd.orient) {
+        case QF_Q8 * 2: return convert_rows<BN, CT, QF_Q8, 0>(bh, ct, lane, raw_bar, ph);
+        case QF_Q8 * 2 + 1: return convert_rows<BN, CT, QF_Q8, 1>(bh, ct, lane, raw_bar, ph);
+        case QF_Q4 * 2: return convert_rows<BN, CT, QF_Q4, 0>(bh, ct, lane, raw_bar, ph);
+        case QF_Q4 * 2 + 1: return convert_rows<BN, CT, QF_Q4, 1>(bh, ct, lane, raw_bar, ph);
+        default: return convert_rows<BN, CT, QF_F16, 0>(bh, ct, lane, raw_bar, ph);
+    }
+}
+
+// the TMA copies of one stage's raw B tile (K-step kt of the BN rows from n0) onto `bar`
+template <int BN>
+__device__ __forceinline__ void load_raw_b(uint8_t * b_lo_area, const CUtensorMap * tq, const CUtensorMap * td, const QDesc & qd,
+                                           int kt, int n0, uint64_t * bar) {
+    tma_load_2d(b_lo_area, tq, qd.fmt == QF_Q4 ? kt * 16 : kt * 32, n0, bar);
+    if (qd.fmt == QF_Q8 || qd.fmt == QF_Q4) {
+        uint8_t * ds = b_lo_area + BN * raw_row_bytes(qd.fmt);
+        if (qd.orient == 0) tma_load_2d(ds, td, n0, kt, bar);
+        else tma_load_2d(ds, td, kt * 32, n0 / 32, bar);
+    }
+}
+
 // Rows of the tile each CTA of a split-K cluster reduces and stores.
 __host__ __device__ constexpr int split_rows(int splits) { return (BM + splits - 1) / splits; }
 
@@ -258,10 +415,13 @@ template <int BN, int STAGES, int MODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
               const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
-              int M, int N, int K, int splits, const __grid_constant__ GemmEpi ep) {
+              int M, int N, int K, int splits, const QDesc qd, const __grid_constant__ GemmEpi ep) {
     constexpr uint32_t A_BYTES = BM * BK * 4;
     constexpr uint32_t B_BYTES = BN * BK * 4;
     constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    // bytes a stage's copies deliver: A_hi, A_lo, B_hi, B_lo on the stage's full barrier; with a weight in block
+    // planes, A alone there and the raw B tile on its own barrier (the converters need B only)
+    const uint32_t raw_tx = BN * raw_row_bytes(qd.fmt) + raw_scale_bytes(qd.fmt, BN);
     // two accumulators: hi*hi in columns [0, BN), the small cross terms hi*lo + lo*hi in [BN, 2 BN).
     // The tensor core's float32 accumulation rounds toward zero per instruction; keeping the small terms
     // apart cuts the number of truncations the large partial sum sees by three.
@@ -287,6 +447,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     static_assert((size_t) BM * PLD * 4 <= (size_t) STAGES * STAGE_BYTES, "staged tile must fit in the pipeline buffers");
     __shared__ __align__(8) uint64_t full_bar[STAGES];
     __shared__ __align__(8) uint64_t empty_bar[STAGES];
+    __shared__ __align__(8) uint64_t rawf_bar[STAGES];   // block planes: the raw B tile has landed
+    __shared__ __align__(8) uint64_t raw_bar[STAGES];    // block planes: the converters hold the raw tile
+    __shared__ __align__(8) uint64_t conv_bar[STAGES];   // block planes: B_hi / B_lo written
     __shared__ __align__(8) uint64_t acc_bar;
     __shared__ __align__(8) uint64_t recv_bar;
     __shared__ uint32_t tmem_base_sh;
@@ -303,7 +466,10 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     const int rs = split * R, re = min(BM, rs + R);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1);
+            mbar_init(&rawf_bar[s], 1); mbar_init(&raw_bar[s], CONV_WARPS); mbar_init(&conv_bar[s], CONV_WARPS);
+        }
         mbar_init(&acc_bar, 1);
         mbar_init(&recv_bar, 1);
         abort_sh = 0;
@@ -334,9 +500,14 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     if (warp == 0 && lane == 0) {
         for (int i = 0; i < pre_stages; i++) {
             uint8_t * st = smem + (size_t) i * STAGE_BYTES;
-            mbar_expect_tx(&full_bar[i], STAGE_BYTES);
-            tma_load_2d(st + 2 * A_BYTES, &tB_hi, (kt0 + i) * BK, n0, &full_bar[i]);
-            tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, (kt0 + i) * BK, n0, &full_bar[i]);
+            if (qd.fmt) {
+                mbar_expect_tx(&rawf_bar[i], raw_tx);
+                load_raw_b<BN>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, kt0 + i, n0, &rawf_bar[i]);
+            } else {
+                mbar_expect_tx(&full_bar[i], STAGE_BYTES);
+                tma_load_2d(st + 2 * A_BYTES, &tB_hi, (kt0 + i) * BK, n0, &full_bar[i]);
+                tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, (kt0 + i) * BK, n0, &full_bar[i]);
+            }
         }
     }
     // split-K: the first round of this thread's epilogue items, and their operands
@@ -354,10 +525,17 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     };
     if (ep.pre_epi && items) prefetch();
     // the setup above overlapped the previous kernel (programmatic dependent launch); its outputs are
-    // read from here on
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (!ep.pre_epi && items) prefetch();
+    // read from here on. The converter warps of a weight in block planes read the weight and shared memory
+    // only: they convert the stages whose raw tiles were requested early while that kernel still runs, and
+    // wait for it after their loop (their epilogue items' operands are read from there on). No thread lets
+    // the next kernel launch before it has waited: that kernel's early reads assume this one's predecessor
+    // has finished.
+    const bool conv_early = qd.fmt && warp >= 6 && warp < 6 + CONV_WARPS;
+    if (!conv_early) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        if (!ep.pre_epi && items) prefetch();
+    }
 
     if (warp == 0) {
         if (lane == 0) {
@@ -371,10 +549,16 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 if (i >= pre_stages && *(volatile int *) &abort_sh) break;
                 uint8_t * st = smem + (size_t) s * STAGE_BYTES;
                 if (i >= pre_stages) {
-                    mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-                    tma_load_2d(st + 2 * A_BYTES, &tB_hi, kt * BK, n0, &full_bar[s]);
-                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, kt * BK, n0, &full_bar[s]);
+                    if (qd.fmt) {
+                        mbar_expect_tx(&rawf_bar[s], raw_tx);
+                        load_raw_b<BN>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, kt, n0, &rawf_bar[s]);
+                    } else {
+                        mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+                        tma_load_2d(st + 2 * A_BYTES, &tB_hi, kt * BK, n0, &full_bar[s]);
+                        tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, kt * BK, n0, &full_bar[s]);
+                    }
                 }
+                if (qd.fmt) mbar_expect_tx(&full_bar[s], 2 * A_BYTES);
                 tma_load_2d(st, &tA_hi, kt * BK, m0, &full_bar[s]);
                 tma_load_2d(st + A_BYTES, &tA_lo, kt * BK, m0, &full_bar[s]);
                 issued = i + 1;
@@ -383,6 +567,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 // drain: the copies of the last stages it armed must land before the buffers are reused
                 for (int i = issued - STAGES < 0 ? 0 : issued - STAGES; i < issued; i++) {
                     mbar_wait(&full_bar[i % STAGES], (uint32_t) (i / STAGES) & 1u, 5, &g_gemm_error);
+                    if (qd.fmt) mbar_wait(&rawf_bar[i % STAGES], (uint32_t) (i / STAGES) & 1u, 5, &g_gemm_error);
                 }
             }
         }
@@ -393,7 +578,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
             for (int i = 0; i < nkt; i++) {
                 const int s = i % STAGES;
                 const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
-                if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error)) { abort_sh = 1; break; }
+                if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error) ||
+                    (qd.fmt && !mbar_wait_spin(&conv_bar[s], ph, 2, &g_gemm_error))) { abort_sh = 1; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t a_hi = smem_u32(smem + (size_t) s * STAGE_BYTES);
                 const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES;   // B_lo follows B_hi
@@ -412,6 +598,26 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
         __syncwarp();
         if (splits > 1) cluster_wait();
     } else if (warp >= 6) {
+        if (qd.fmt && warp < 6 + CONV_WARPS) {
+            // converter warps: the raw B tile of every stage into its split planes
+            const int ct = (int) threadIdx.x - 6 * 32;
+            for (int i = 0; i < nkt; i++) {
+                const int s = i % STAGES;
+                const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
+                if (!mbar_wait_spin(&rawf_bar[s], ph, 6, &g_gemm_error) ||
+                    !convert_stage<BN, 32 * CONV_WARPS>(smem + (size_t) s * STAGE_BYTES + 2 * A_BYTES, qd, ct, lane, &raw_bar[s], ph)) {
+                    abort_sh = 1;
+                    break;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&conv_bar[s]);
+            }
+        }
+        if (conv_early) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+            if (!ep.pre_epi && items) prefetch();
+        }
         if (splits > 1) cluster_wait();   // (the start's arrive; these warps join at the reduction)
     } else {
         // epilogue warps 2..5 (TMEM lane quadrant = warp % 4)
@@ -544,7 +750,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
 // 4 KB shared buffer (16-byte chunk c of row r at c ^ (r & 7)) and applies the fused epilogue from there
 // four rows per instruction: coalesced loads and stores. A tile's arithmetic is the split kernel's at
 // one split (the same MMAs in the same order), so a row's bits do not depend on the batch.
-constexpr int PBN = 128, PSTAGES = 3, PEPI_WARPS = 8, PTHREADS = 64 + 32 * PEPI_WARPS;
+constexpr int PBN = 128, PSTAGES = 3, PEPI_WARPS = 8, PTHREADS = 64 + 32 * PEPI_WARPS + 32 * PCONV_WARPS;
 constexpr int FIX_ROWS = 4;   // K-split fix-up: row groups of partial tiles loaded at once per lane
 constexpr uint32_t PSTAGE_BYTES = 2 * BM * BK * 4 + 2 * PBN * BK * 4;
 constexpr size_t PSMEM_BYTES = (size_t) PSTAGES * PSTAGE_BYTES + (size_t) PEPI_WARPS * 32 * 32 * 4 + 1024;
@@ -554,7 +760,7 @@ template <int MODE>
 __global__ void __launch_bounds__(PTHREADS, 1)
 k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
                 const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
-                int M, int N, int K, int splits, const __grid_constant__ GemmEpi ep) {
+                int M, int N, int K, int splits, const QDesc qd, const __grid_constant__ GemmEpi ep) {
     constexpr uint32_t A_BYTES = BM * BK * 4;
     constexpr uint32_t B_BYTES = PBN * BK * 4;
     constexpr uint32_t TMEM_COLS = 4 * PBN;   // two accumulator pairs [hi*hi | cross terms], 256 columns each
@@ -565,6 +771,9 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     __shared__ __align__(8) uint64_t full_bar[PSTAGES];
     __shared__ __align__(8) uint64_t empty_bar[PSTAGES];
+    __shared__ __align__(8) uint64_t rawf_bar[PSTAGES];   // block planes: the raw B tile has landed
+    __shared__ __align__(8) uint64_t raw_bar[PSTAGES];    // block planes: the converters hold the raw tile
+    __shared__ __align__(8) uint64_t conv_bar[PSTAGES];   // block planes: B_hi / B_lo written
     __shared__ __align__(8) uint64_t accf_bar[2];   // MMA -> epilogue: accumulator pair b holds a finished tile
     __shared__ __align__(8) uint64_t acce_bar[2];   // epilogue -> MMA: accumulator pair b has been read
     __shared__ uint32_t tmem_base_sh;
@@ -579,7 +788,10 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
     const int kq = (num_k + splits - 1) / splits;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < PSTAGES; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        for (int s = 0; s < PSTAGES; s++) {
+            mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1);
+            mbar_init(&rawf_bar[s], 1); mbar_init(&raw_bar[s], PCONV_WARPS); mbar_init(&conv_bar[s], PCONV_WARPS);
+        }
         for (int b = 0; b < 2; b++) { mbar_init(&accf_bar[b], 1); mbar_init(&acce_bar[b], PEPI_WARPS); }
         abort_sh = 0;
         epi_stop_sh = 0;
@@ -618,17 +830,25 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                     if (kt >= PSTAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1, &g_gemm_error)) { abort_sh = 1; break; }
                     if (*(volatile int *) &abort_sh) break;
                     uint8_t * st = smem + (size_t) s * PSTAGE_BYTES;
-                    mbar_expect_tx(&full_bar[s], PSTAGE_BYTES);
+                    if (qd.fmt) {
+                        // the raw B tile first, on its own barrier: the converters are on the critical path
+                        mbar_expect_tx(&rawf_bar[s], PBN * raw_row_bytes(qd.fmt) + raw_scale_bytes(qd.fmt, PBN));
+                        load_raw_b<PBN>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, k, n0, &rawf_bar[s]);
+                        mbar_expect_tx(&full_bar[s], 2 * A_BYTES);
+                    } else {
+                        mbar_expect_tx(&full_bar[s], PSTAGE_BYTES);
+                        tma_load_2d(st + 2 * A_BYTES, &tB_hi, k * BK, n0, &full_bar[s]);
+                        tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, k * BK, n0, &full_bar[s]);
+                    }
                     tma_load_2d(st, &tA_hi, k * BK, m0, &full_bar[s]);
                     tma_load_2d(st + A_BYTES, &tA_lo, k * BK, m0, &full_bar[s]);
-                    tma_load_2d(st + 2 * A_BYTES, &tB_hi, k * BK, n0, &full_bar[s]);
-                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, k * BK, n0, &full_bar[s]);
                 }
             }
             if (*(volatile int *) &abort_sh) {
                 // let the copies already issued land before the CTA exits
                 for (int j = kt - PSTAGES < 0 ? 0 : kt - PSTAGES; j < kt; j++) {
                     mbar_wait(&full_bar[j % PSTAGES], (uint32_t) (j / PSTAGES) & 1u, 5, &g_gemm_error);
+                    if (qd.fmt) mbar_wait(&rawf_bar[j % PSTAGES], (uint32_t) (j / PSTAGES) & 1u, 5, &g_gemm_error);
                 }
             }
         }
@@ -644,7 +864,8 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                 for (int k = kb; k < ke; k++, kt++) {
                     const int s = kt % PSTAGES;
                     const uint32_t ph = (uint32_t) (kt / PSTAGES) & 1u;
-                    if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error)) { abort_sh = 1; break; }
+                    if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error) ||
+                        (qd.fmt && !mbar_wait_spin(&conv_bar[s], ph, 2, &g_gemm_error))) { abort_sh = 1; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t a_hi = smem_u32(smem + (size_t) s * PSTAGE_BYTES);
                     const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES;   // B_lo follows B_hi
@@ -659,6 +880,28 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                 }
                 if (*(volatile int *) &abort_sh) break;
                 mma_commit(&accf_bar[b]);
+            }
+        }
+    } else if (warp >= 2 + PEPI_WARPS) {
+        if (qd.fmt) {
+            // converter warps: the raw B tile of every stage into its split planes, in the producer's order
+            const int ct = (int) threadIdx.x - (2 + PEPI_WARPS) * 32;
+            int kt = 0;
+            for (int u = blockIdx.x; u < total && !*(volatile int *) &abort_sh; u += gridDim.x) {
+                const int kb = (u % splits) * kq, ke = min(num_k, kb + kq);
+                bool good = true;
+                for (int k = kb; k < ke; k++, kt++) {
+                    const int s = kt % PSTAGES;
+                    const uint32_t ph = (uint32_t) (kt / PSTAGES) & 1u;
+                    if (!mbar_wait_spin(&rawf_bar[s], ph, 6, &g_gemm_error) ||
+                        !convert_stage<PBN, 32 * PCONV_WARPS>(smem + (size_t) s * PSTAGE_BYTES + 2 * A_BYTES, qd, ct, lane, &raw_bar[s], ph)) {
+                        good = false;
+                        break;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&conv_bar[s]);
+                }
+                if (!good) { abort_sh = 1; break; }
             }
         }
     } else {
@@ -827,6 +1070,45 @@ bool make_map(CUtensorMap * map, const float * base, int rows, int cols, int ld,
     return r == CUDA_SUCCESS;
 }
 
+// a row-major 2-D map without swizzle over raw block values or scales: `inner` elements per row of
+// `esize` bytes, rows `stride` bytes apart, boxes of box_inner x box_rows
+bool make_raw_map(CUtensorMap * map, const void * base, CUtensorMapDataType dt, int esize, uint64_t inner, uint64_t rows,
+                  uint64_t stride, uint32_t box_inner, uint32_t box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t) inner, (cuuint64_t) rows};
+    const cuuint64_t strides[1] = {(cuuint64_t) stride};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    (void) esize;
+    return g_encode(map, dt, 2, (void *) base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The B operand's two maps for tiles of `bn` rows: its split planes (hi, lo), or a weight's block values
+// and scales (QuantB; qd says which). False with a log line when a map cannot be made.
+bool make_b_maps(const SplitMat & B, int N, int K, int bn, CUtensorMap * t0, CUtensorMap * t1, QDesc * qd) {
+    *qd = QDesc{};
+    if (!B.q.fmt) return make_map(t0, B.hi, N, K, B.ld, bn) && make_map(t1, B.lo, N, K, B.ld, bn);
+    const QuantB & q = B.q;
+    if (K % 32 || (q.orient == 1 && N % 32) || (q.orient == 0 && N % 8) || !q.q || (q.fmt != QF_F16 && !q.d)) {
+        log("jepa: gemm: block-plane operand of N %d K %d (orientation %d) is not in whole blocks\n", N, K, q.orient);
+        return false;
+    }
+    qd->fmt = q.fmt;
+    qd->orient = q.orient;
+    bool ok;
+    if (q.fmt == QF_Q8) ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t) K, (uint64_t) N, (uint64_t) K, 32, (uint32_t) bn);
+    else if (q.fmt == QF_Q4) ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t) K / 2, (uint64_t) N, (uint64_t) K / 2, 16, (uint32_t) bn);
+    else ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t) K, (uint64_t) N, (uint64_t) K * 2, 32, (uint32_t) bn);
+    if (ok && q.fmt != QF_F16) {
+        ok = q.orient == 0 ? make_raw_map(t1, q.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t) N, (uint64_t) K / 32, (uint64_t) N * 2, (uint32_t) bn, 1)
+                           : make_raw_map(t1, q.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t) K, (uint64_t) N / 32, (uint64_t) K * 2, 32, (uint32_t) bn / 32);
+    } else if (ok) {
+        *t1 = *t0;   // f16: no scales (the map is never used)
+    }
+    if (!ok) log("jepa: gemm: cuTensorMapEncodeTiled refused a block-plane operand (N %d K %d, format %d)\n", N, K, q.fmt);
+    return ok;
+}
+
 // rows of the split-K receive buffer: (splits - 1) x ceil(128 / splits), at most 114 (7 splits)
 constexpr int recv_rows() {
     int r = 0;
@@ -897,8 +1179,9 @@ template <int BN, int STAGES, int MODE>
 int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
     if (BN != 64 && splits > 1) { log("jepa: gemm: split-K needs the 64-wide tile\n"); return -1; }
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+    QDesc qd;
     if (!make_map(&ta_hi, A.hi, M, K, A.ld, BM) || !make_map(&ta_lo, A.lo, M, K, A.ld, BM) ||
-        !make_map(&tb_hi, B.hi, N, K, B.ld, BN) || !make_map(&tb_lo, B.lo, N, K, B.ld, BN)) {
+        !make_b_maps(B, N, K, BN, &tb_hi, &tb_lo, &qd)) {
         log("jepa: gemm: cuTensorMapEncodeTiled refused an operand (M %d N %d K %d, ld %d / %d)\n", M, N, K, A.ld, B.ld);
         return -1;
     }
@@ -918,7 +1201,7 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
     attr[1].val.clusterDim.z = (unsigned) splits;
     cfg.attrs = attr;
     cfg.numAttrs = splits > 1 ? 2 : 1;
-    JB_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tf32x3<BN, STAGES, MODE>, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, splits, ep));
+    JB_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tf32x3<BN, STAGES, MODE>, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, splits, qd, ep));
     return 0;
 }
 
@@ -926,8 +1209,9 @@ template <int MODE>
 int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
     if (splits < 1 || splits > GEMM_KSPLIT_MAX) { log("jepa: gemm: %d K parts (at most %d)\n", splits, GEMM_KSPLIT_MAX); return -1; }
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+    QDesc qd;
     if (!make_map(&ta_hi, A.hi, M, K, A.ld, BM) || !make_map(&ta_lo, A.lo, M, K, A.ld, BM) ||
-        !make_map(&tb_hi, B.hi, N, K, B.ld, PBN) || !make_map(&tb_lo, B.lo, N, K, B.ld, PBN)) {
+        !make_b_maps(B, N, K, PBN, &tb_hi, &tb_lo, &qd)) {
         log("jepa: gemm: cuTensorMapEncodeTiled refused an operand (M %d N %d K %d, ld %d / %d)\n", M, N, K, A.ld, B.ld);
         return -1;
     }
@@ -947,7 +1231,7 @@ int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, int sp
     const long units = (long) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN) * splits;
     const unsigned grid = (unsigned) std::max(1L, std::min<long>(units, sms[dev]));
     JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE>, dim3(grid), dim3(PTHREADS), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K,
-                       splits, ep));
+                       splits, qd, ep));
     return 0;
 }
 
@@ -977,6 +1261,8 @@ int p_splits(int N, int K) {
 }
 
 }  // namespace
+
+bool gemm_blocks_pay(int N, int K) { return !(N >= 4096 || (N >= 768 && K >= 768)); }
 
 size_t gemm_fixup_floats(int M, int N, int K) {
     const int s = p_splits(N, K);
@@ -1033,6 +1319,10 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
     if ((A.ld & 3) || (B.ld & 3) || ((uintptr_t) A.hi & 15) || ((uintptr_t) A.lo & 15) || ((uintptr_t) B.hi & 15) ||
         ((uintptr_t) B.lo & 15)) {
         log("jepa: gemm: operands need 16-byte aligned rows (ld %d / %d)\n", A.ld, B.ld);
+        return -1;
+    }
+    if (B.q.fmt && (((uintptr_t) B.q.q & 15) || ((uintptr_t) B.q.d & 15))) {
+        log("jepa: gemm: block planes need 16-byte aligned bases\n");
         return -1;
     }
     GemmEpi e = ep;

@@ -520,7 +520,7 @@ int HPlanner::lin_fwd(const DLin & L, const float * x, int ldx, const float * x_
         ep.out_hi = y_hi; ep.out_lo = y_lo; ep.ld_split = ldy;
         ep.mode = y_hi ? (y ? EPI_F32_SPLIT : EPI_SPLIT) : EPI_F32;
         launches++;
-        return wgemm(w, {x_hi, x_lo, ld}, {L.w_hi, L.w_lo, L.in}, M, L.out, L.in, ep, st);
+        return wgemm(w, {x_hi, x_lo, ld}, L.fwd(), M, L.out, L.in, ep, st);
     }
     linear_simt(x, ldx, L.w, L.b, y, ldy, M, L.out, L.in, st);
     launches++;
@@ -541,7 +541,7 @@ int HPlanner::lin_bwd(const DLin & L, const float * dy, int lddy, const float * 
         GemmEpi ep;
         ep.out0 = dx; ep.ld0 = lddx;
         launches++;
-        return wgemm(w, {dy_hi, dy_lo, ld}, {L.wt_hi, L.wt_lo, L.out}, M, L.in, L.out, ep, st);
+        return wgemm(w, {dy_hi, dy_lo, ld}, L.bwd(), M, L.in, L.out, ep, st);
     }
     linear_simt(dy, lddy, L.wt, nullptr, dx, lddx, M, L.in, L.out, st);
     launches++;
@@ -564,7 +564,7 @@ int HPlanner::step_modulation(Workspace & w, int t0, int nt) {
     ep.out0 = w.mod + mod_row0(w, t0) * ldm; ep.ld0 = ldm;
     launches++;
     const size_t r0 = (size_t) t0 * w.S * P;
-    return wgemm(w, {w.cs_hi + r0, w.cs_lo + r0, P}, {L.adaln.w_hi, L.adaln.w_lo, P}, nt * w.S, ldm, P, ep, w.st);
+    return wgemm(w, {w.cs_hi + r0, w.cs_lo + r0, P}, L.adaln.fwd(), nt * w.S, ldm, P, ep, w.st);
 }
 
 int HPlanner::step_modulation_bwd(Workspace & w, int t0, int nt) {
@@ -574,7 +574,7 @@ int HPlanner::step_modulation_bwd(Workspace & w, int t0, int nt) {
     ep.out0 = w.dcs + (size_t) t0 * w.S * P; ep.ld0 = P;
     launches++;
     const size_t m0 = dmod_row0(w, t0) * ldm;
-    return wgemm(w, {w.dmod_hi + m0, w.dmod_lo + m0, ldm}, {L.adaln.wt_hi, L.adaln.wt_lo, ldm}, nt * w.S, P, ldm, ep, w.st);
+    return wgemm(w, {w.dmod_hi + m0, w.dmod_lo + m0, ldm}, L.adaln.bwd(), nt * w.S, P, ldm, ep, w.st);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -633,17 +633,17 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
             GemmEpi e2;
             e2.mode = EPI_GATED; e2.bias = B.ov.b; e2.out0 = o; e2.ld0 = P; e2.aux = xin; e2.ld_aux = P;
             e2.gate = mod_l + 2 * P; e2.ld_gate = ldm; e2.out1 = xm; e2.ld1 = P;
-            if (wgemm(w, {w.h_hi, w.h_lo, P}, {B.ov.w_hi, B.ov.w_lo, P}, S, P, P, e2, st)) return -1;
+            if (wgemm(w, {w.h_hi, w.h_lo, P}, B.ov.fwd(), S, P, P, e2, st)) return -1;
             block_pre(xm, P, mod_l, ldm, 3 * P, 4 * P, B.ln2_w, B.ln2_b, adaln_eps, ln_eps, w.h_hi, w.h_lo, P,
                       w.stm0 + tl * S, w.stm1 + tl * S, S, P, st);
             GemmEpi e3;
             // (u keeps gelu'(pre-activation) for the backward's EPI_MUL_SPLIT)
             e3.mode = EPI_GELU_D_SPLIT; e3.bias = B.up.b; e3.out0 = u; e3.ld0 = F; e3.out_hi = w.g_hi; e3.out_lo = w.g_lo; e3.ld_split = F;
-            if (wgemm(w, {w.h_hi, w.h_lo, P}, {B.up.w_hi, B.up.w_lo, P}, S, F, P, e3, st)) return -1;
+            if (wgemm(w, {w.h_hi, w.h_lo, P}, B.up.fwd(), S, F, P, e3, st)) return -1;
             GemmEpi e4;
             e4.mode = EPI_GATED; e4.bias = B.down.b; e4.out0 = dn; e4.ld0 = P; e4.aux = xm; e4.ld_aux = P;
             e4.gate = mod_l + 5 * P; e4.ld_gate = ldm; e4.out1 = xout; e4.ld1 = P;
-            if (wgemm(w, {w.g_hi, w.g_lo, F}, {B.down.w_hi, B.down.w_lo, F}, S, P, F, e4, st)) return -1;
+            if (wgemm(w, {w.g_hi, w.g_lo, F}, B.down.fwd(), S, P, F, e4, st)) return -1;
             launches += 5;
         }
         const float * xL = x0 + (size_t) NL * S * P;
@@ -694,7 +694,7 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
                 GemmEpi ep;
                 ep.mode = EPI_GELU_SPLIT; ep.bias = U.enc_fc1.b; ep.out0 = e.u; ep.ld0 = H; ep.out_hi = e.g_hi; ep.out_lo = e.g_lo; ep.ld_split = H;
                 launches++;
-                if (wgemm(w, {e.h_hi, e.h_lo, Din}, {U.enc_fc1.w_hi, U.enc_fc1.w_lo, Din}, n, H, Din, ep, st)) return -1;
+                if (wgemm(w, {e.h_hi, e.h_lo, Din}, U.enc_fc1.fwd(), n, H, Din, ep, st)) return -1;
             } else {
                 layer_norm(e.in, Din, U.enc_in_w, U.enc_in_b, ln_eps, w.tmpR2, Din, nullptr, nullptr, nullptr, n, Din, st);
                 linear_simt(w.tmpR2, Din, U.enc_fc1.w, U.enc_fc1.b, e.u, H, n, H, Din, st);
@@ -812,10 +812,10 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             split_f32(gy, Dout, e.d_hi, e.d_lo, Dout, n, Dout, st);
             GemmEpi ep;
             ep.mode = EPI_DGELU_SPLIT; ep.aux = e.u; ep.ld_aux = H; ep.out_hi = e.g_hi; ep.out_lo = e.g_lo; ep.ld_split = H;
-            if (wgemm(w, {e.d_hi, e.d_lo, Dout}, {U.enc_fc2.wt_hi, U.enc_fc2.wt_lo, Dout}, n, H, Dout, ep, st)) return -1;
+            if (wgemm(w, {e.d_hi, e.d_lo, Dout}, U.enc_fc2.bwd(), n, H, Dout, ep, st)) return -1;
             GemmEpi ep2;
             ep2.out0 = e.gin; ep2.ld0 = Din;
-            if (wgemm(w, {e.g_hi, e.g_lo, H}, {U.enc_fc1.wt_hi, U.enc_fc1.wt_lo, H}, n, Din, H, ep2, st)) return -1;
+            if (wgemm(w, {e.g_hi, e.g_lo, H}, U.enc_fc1.bwd(), n, Din, H, ep2, st)) return -1;
             launches += 3;
         } else {
             if (lin_bwd(U.enc_fc2, gy, Dout, nullptr, nullptr, n, w.tmpR2, H, w)) return -1;
@@ -872,10 +872,10 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             // MLP half
             GemmEpi e1;
             e1.mode = EPI_MUL_SPLIT; e1.aux = w.u + tl * S * F; e1.ld_aux = F; e1.out_hi = w.du_hi; e1.out_lo = w.du_lo; e1.ld_split = F;
-            if (wgemm(w, {w.d_hi, w.d_lo, P}, {B.down.wt_hi, B.down.wt_lo, P}, S, F, P, e1, st)) return -1;
+            if (wgemm(w, {w.d_hi, w.d_lo, P}, B.down.bwd(), S, F, P, e1, st)) return -1;
             GemmEpi e2;
             e2.out0 = w.gh; e2.ld0 = P;
-            if (wgemm(w, {w.du_hi, w.du_lo, F}, {B.up.wt_hi, B.up.wt_lo, F}, S, P, F, e2, st)) return -1;
+            if (wgemm(w, {w.du_hi, w.du_lo, F}, B.up.bwd(), S, P, F, e2, st)) return -1;
             BlockBwdArgs a{};
             a.gh = w.gh; a.ldgh = P; a.gres = w.gx; a.ldres = P; a.x = w.xmid + tl * S * P; a.ldx = P;
             a.st0 = w.stm0 + tl * S; a.st1 = w.stm1 + tl * S; a.ln_w = B.ln2_w; a.ln_b = B.ln2_b;
@@ -888,7 +888,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
             // attention half (one query over one key: the value path, through the composed linear)
             GemmEpi e4;
             e4.out0 = w.gh; e4.ld0 = P;
-            if (wgemm(w, {w.d_hi, w.d_lo, P}, {B.ov.wt_hi, B.ov.wt_lo, P}, S, P, P, e4, st)) return -1;
+            if (wgemm(w, {w.d_hi, w.d_lo, P}, B.ov.bwd(), S, P, P, e4, st)) return -1;
             BlockBwdArgs b{};
             b.gh = w.gh; b.ldgh = P; b.gres = w.gmid; b.ldres = P; b.x = xin; b.ldx = P;
             b.st0 = w.sta0 + tl * S; b.st1 = w.sta1 + tl * S; b.ln_w = B.ln1_w; b.ln_b = B.ln1_b;

@@ -18,8 +18,14 @@ struct DLin {
     int in = 0, out = 0;
     float * w = nullptr, * wt = nullptr;
     float * w_hi = nullptr, * w_lo = nullptr, * wt_hi = nullptr, * wt_lo = nullptr;
+    // the GGUF block planes the GEMM dequantises in its mainloop, per orientation (fmt QF_NONE: the hi / lo
+    // planes above serve that orientation)
+    QuantB fq, tq;
     float * b = nullptr;
     explicit operator bool() const { return in > 0; }
+    // the B operand of y = x W^T (forward) and of dx = dy W (transposed)
+    SplitMat fwd() const { SplitMat m{w_hi, w_lo, in}; m.q = fq; return m; }
+    SplitMat bwd() const { SplitMat m{wt_hi, wt_lo, out}; m.q = tq; return m; }
     bool tc_fwd() const { return in >= 16 && (in % 4) == 0 && out >= 16; }
     bool tc_bwd() const { return out >= 16 && (out % 4) == 0 && in >= 16; }
 };

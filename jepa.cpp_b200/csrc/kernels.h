@@ -46,11 +46,46 @@ struct GemmEpi {
     int * fix_count = nullptr; size_t fix_counters = 0;
 };
 
+// A weight operand B[N][K] kept in its GGUF block values and dequantised inside the GEMM mainloop: the
+// producer's TMA stages a K-step's raw tile (the block values of BN rows x 32 columns and their f16 scales)
+// and converter warps write the split planes the tensor core reads. Values are exactly those of a
+// load-time dequantisation (d * q is exact in float32, and so is its hi / lo split), so a product's bits do
+// not depend on the layout the weight is kept in.
+//   QF_Q8   q: int8 [N][K] (row stride K bytes)
+//   QF_Q4   q: the 4-bit block values [N][K / 2], element 2j in the low nibble of byte j, 2j + 1 in the high
+//   QF_F16  q: f16 bits [N][K]
+// Scales (Q8, Q4: f16 bits): orient 0, one per row and 32-column block, stored [K / 32][N] (the forward
+// operand W[out][in]); orient 1, one per 32-row group and column, stored [N / 32][K] (the transposed
+// operand W^T, whose rows are the blocks' columns). Both orientations of a weight share one scale array.
+enum QFmt : int { QF_NONE = 0, QF_Q8 = 1, QF_Q4 = 2, QF_F16 = 3 };
+struct QuantB {
+    int fmt = QF_NONE;
+    int orient = 0;
+    const void * q = nullptr;
+    const uint16_t * d = nullptr;
+};
+
 struct SplitMat {                    // a split operand: two float32 planes with one leading dimension
     const float * hi = nullptr;
     const float * lo = nullptr;
     int ld = 0;
+    QuantB q;                        // B only: when q.fmt is set, the block planes replace hi / lo
 };
+
+// The block planes of a GGUF weight [rows][ne0] (type 8 = q8_0, 2 = q4_0, 1 = f16) for both GEMM
+// orientations, from its raw rows on the device: q / qt hold the forward ([rows][ne0]) and transposed
+// ([ne0][rows]) values in the format's QuantB layout, d the shared scales [ne0 / 32][rows] (null for f16).
+// Sizes: quant_plane_bytes each for q and qt, quant_scale_count f16 values for d.
+size_t quant_plane_bytes(uint32_t type, int64_t rows, int64_t ne0);
+size_t quant_scale_count(uint32_t type, int64_t rows, int64_t ne0);
+int quant_planes(uint32_t type, const void * raw, int64_t rows, int64_t ne0, void * q, void * qt, uint16_t * d, cudaStream_t st);
+// Whether the GEMM can read W [rows][ne0] of this type in its block planes, forward (N = rows, K = ne0)
+// or transposed (N = ne0, K = rows).
+bool quant_ok(uint32_t type, int64_t rows, int64_t ne0);
+// Whether a product of this (N, K) runs on the 64-wide split-K kernel, where block planes cost little
+// (measured ~8 % per launch at 256 x 384 x 384); the persistent kernel's products (N >= 4096, or N and K
+// >= 768) pay 1.35 - 1.5x for them, their raw tile sharing a full stage's shared memory.
+bool gemm_blocks_pay(int N, int K);
 
 // Returns 0, or -1 after logging (unsupported shape / a CUDA error).
 int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st);

@@ -95,6 +95,106 @@ extern "C" int jepa_b200_gemm_ksplit(const float * A, const float * B, int M, in
     return gemm_host(A, B, M, N, K, C, true, "jepa_b200_gemm_ksplit");
 }
 
+namespace {
+
+// a weight's block planes on the device, from its raw GGUF rows (host)
+struct QuantWeight {
+    DevBuf raw, q, qt, d;
+    bool make(uint32_t type, const void * w_raw, int rows, int ne0, cudaStream_t st) {
+        const size_t rb = jb::row_bytes(type, ne0);
+        const size_t nq = jb::quant_plane_bytes(type, rows, ne0), nd = jb::quant_scale_count(type, rows, ne0);
+        if (!rb || !nq || !raw.alloc(rb * (size_t) rows) || !q.alloc(nq) || !qt.alloc(nq) || !d.alloc(std::max<size_t>(nd, 1) * 2)) return false;
+        if (cudaMemcpyAsync(raw.p, w_raw, rb * (size_t) rows, cudaMemcpyHostToDevice, st) != cudaSuccess) return false;
+        return jb::quant_planes(type, raw.p, rows, ne0, q.p, qt.p, (uint16_t *) d.p, st) == 0;
+    }
+    jb::SplitMat operand(uint32_t type, int transposed) const {
+        jb::SplitMat m;
+        m.q.fmt = type == 8 ? jb::QF_Q8 : type == 2 ? jb::QF_Q4 : jb::QF_F16;
+        m.q.orient = transposed ? 1 : 0;
+        m.q.q = transposed ? qt.p : q.p;
+        m.q.d = type == 1 ? nullptr : (const uint16_t *) d.p;
+        return m;
+    }
+};
+
+}  // namespace
+
+// C = A W^T (transposed = 0: A [M][ne0], C [M][rows]) or C = A W (transposed = 1: A [M][rows], C [M][ne0]),
+// W [rows][ne0] the raw rows of a GGUF weight of `type` (8 q8_0, 2 q4_0, 1 f16), read by the GEMM in its
+// block planes and dequantised in the mainloop. ksplit = 1: the planner's K-split configuration.
+extern "C" int jepa_b200_gemm_quant(uint32_t type, const void * w_raw, int rows, int ne0, int transposed, const float * A, int M,
+                                    float * C, int ksplit) {
+    if (!w_raw || !A || !C || M < 1 || !jb::quant_ok(type, rows, ne0)) {
+        jb::log("jepa: jepa_b200_gemm_quant: need host buffers, M >= 1 and a q8_0 / q4_0 / f16 weight in whole 32 x 32 blocks\n");
+        return -1;
+    }
+    const int N = transposed ? ne0 : rows, K = transposed ? rows : ne0;
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    if (jb::gemm_error_clear(st) != 0) { cudaStreamDestroy(st); return -1; }
+    QuantWeight w;
+    DevBuf ar, ah, al, c, fix, cnt;
+    int rc = -1;
+    jb::GemmEpi ep;
+    if (w.make(type, w_raw, rows, ne0, st) && upload_split(A, (size_t) M * K, ar, ah, al, M, K, st) && c.alloc((size_t) M * N * 4) &&
+        (!ksplit || alloc_fixup(fix, cnt, M, N, K, ep, st))) {
+        ep.out0 = c.f();
+        ep.ld0 = N;
+        rc = jb::gemm_tc({ah.f(), al.f(), K}, w.operand(type, transposed), M, N, K, ep, st);
+        if (rc == 0 && !jb::cuda_ok(cudaMemcpyAsync(C, c.p, (size_t) M * N * 4, cudaMemcpyDeviceToHost, st), "copy C")) rc = -1;
+        if (rc == 0 && !jb::cuda_ok(cudaStreamSynchronize(st), "gemm")) rc = -1;
+        if (rc == 0 && jb::gemm_error_flag(st) != 0) {
+            jb::log("jepa: jepa_b200_gemm_quant: the tensor-core kernel timed out waiting on its pipeline\n");
+            rc = -1;
+        }
+    } else {
+        jb::log("jepa: jepa_b200_gemm_quant: device allocation, upload or block planes failed\n");
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
+// mean device time of `reps` back-to-back launches of the planner's GEMM at (M, N, K) with B a q8_0 / q4_0 /
+// f16 weight in block planes (zero values), forward or transposed
+extern "C" int jepa_b200_gemm_quant_bench(uint32_t type, int M, int N, int K, int transposed, int reps, double * ms) {
+    const int rows = transposed ? K : N, ne0 = transposed ? N : K;
+    if (M < 1 || reps < 1 || !ms || !jb::quant_ok(type, rows, ne0)) return -1;
+    cudaStream_t st;
+    JB_CUDA(cudaStreamCreate(&st));
+    QuantWeight w;
+    DevBuf ah, al, c, fix, cnt;
+    int rc = -1;
+    jb::GemmEpi ep;
+    std::vector<uint8_t> zeros(jb::row_bytes(type, ne0) * (size_t) rows, 0);
+    if (w.make(type, zeros.data(), rows, ne0, st) && ah.alloc((size_t) M * K * 4) && al.alloc((size_t) M * K * 4) &&
+        c.alloc((size_t) M * N * 4) && alloc_fixup(fix, cnt, M, N, K, ep, st)) {
+        cudaMemsetAsync(ah.p, 0, (size_t) M * K * 4, st);
+        cudaMemsetAsync(al.p, 0, (size_t) M * K * 4, st);
+        ep.out0 = c.f();
+        ep.ld0 = N;
+        const jb::SplitMat B = w.operand(type, transposed);
+        rc = jb::gemm_tc({ah.f(), al.f(), K}, B, M, N, K, ep, st);   // warm-up
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaEventRecord(e0, st);
+        for (int i = 0; i < reps && rc == 0; i++) rc = jb::gemm_tc({ah.f(), al.f(), K}, B, M, N, K, ep, st);
+        cudaEventRecord(e1, st);
+        if (rc == 0 && jb::cuda_ok(cudaEventSynchronize(e1), "gemm bench")) {
+            float t = 0;
+            cudaEventElapsedTime(&t, e0, e1);
+            *ms = t / reps;
+        } else {
+            rc = -1;
+        }
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        if (rc == 0 && jb::gemm_error_flag(st) != 0) rc = -1;
+    }
+    cudaStreamDestroy(st);
+    return rc;
+}
+
 extern "C" int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms) {
     if (M < 1 || N < 1 || K < 1 || (K & 3) || reps < 1 || !ms) return -1;
     cudaStream_t st;

@@ -1,6 +1,11 @@
-// Weight upload from a GGUF model to the device: float32 planes, their transposes and the 3xTF32 split
-// planes of the tensor-core products (dequantised on the device, bit-exact with the block formats).
-// Every allocation goes into the owner's list, which frees them.
+// Weight upload from a GGUF model to the device: float32 planes, their transposes and, per orientation of
+// each linear, the operand of its tensor-core products -- the 3xTF32 hi / lo planes (dequantised on the
+// device, bit-exact with the block formats), or the GGUF block planes the GEMM dequantises in its mainloop
+// (q8_0, q4_0, f16; 2.06 B per weight for both orientations of a q8_0 weight, against 16 for the planes).
+// JEPA_B200_WEIGHT_LAYOUT chooses: "planes", "blocks" (every orientation the block planes serve), or "auto"
+// (the default: block planes for the products of the 64-wide split-K kernel, hi / lo planes for the
+// persistent kernel's). Both layouts give the same bits. Every allocation goes into the owner's list, which
+// frees them.
 #pragma once
 
 #include "hplan.h"
@@ -10,10 +15,22 @@
 #include "common.h"
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 #include <vector>
 
 namespace jb {
+
+enum WeightLayout : int { WL_AUTO = 0, WL_PLANES = 1, WL_BLOCKS = 2 };
+inline int weight_layout() {
+    const char * e = std::getenv("JEPA_B200_WEIGHT_LAYOUT");
+    if (!e || !*e || !std::strcmp(e, "auto")) return WL_AUTO;
+    if (!std::strcmp(e, "planes")) return WL_PLANES;
+    if (!std::strcmp(e, "blocks")) return WL_BLOCKS;
+    log("jepa: JEPA_B200_WEIGHT_LAYOUT=%s is not planes, blocks or auto: using auto\n", e);
+    return WL_AUTO;
+}
 
 struct Uploader {
     std::vector<void *> & allocs;   // every allocation, freed by the owner
@@ -21,6 +38,8 @@ struct Uploader {
     cudaStream_t st;
     bool ok = true;
     std::vector<void *> temps;
+    int layout = weight_layout();
+    size_t block_bytes = 0, plane_bytes = 0;   // device bytes of the two operand layouts uploaded
 
     template <class T> T * alloc(size_t n) {
         void * p = nullptr;
@@ -59,16 +78,62 @@ struct Uploader {
         ok = ok && good;
         return good;
     }
+    // the hi / lo planes of the orientations the block planes do not serve (and the f32 transpose, which the
+    // SIMT backward of a small linear reads)
     void finish(DLin & L) {
         if (!ok) return;
-        L.wt = alloc<float>((size_t) L.in * L.out);
-        L.w_hi = alloc<float>((size_t) L.in * L.out); L.w_lo = alloc<float>((size_t) L.in * L.out);
-        L.wt_hi = alloc<float>((size_t) L.in * L.out); L.wt_lo = alloc<float>((size_t) L.in * L.out);
-        if (!ok) return;
-        transpose_f32(L.w, L.wt, L.out, L.in, st);
-        split_f32(L.w, L.in, L.w_hi, L.w_lo, L.in, L.out, L.in, st);
-        split_f32(L.wt, L.out, L.wt_hi, L.wt_lo, L.out, L.in, L.out, st);
+        const size_t n = (size_t) L.in * L.out;
+        if (!L.tq.fmt) {
+            L.wt = alloc<float>(n);
+            L.wt_hi = alloc<float>(n); L.wt_lo = alloc<float>(n);
+            if (!ok) return;
+            transpose_f32(L.w, L.wt, L.out, L.in, st);
+            split_f32(L.wt, L.out, L.wt_hi, L.wt_lo, L.out, L.in, L.out, st);
+            plane_bytes += 8 * n;
+        }
+        if (!L.fq.fmt) {
+            L.w_hi = alloc<float>(n); L.w_lo = alloc<float>(n);
+            if (!ok) return;
+            split_f32(L.w, L.in, L.w_hi, L.w_lo, L.in, L.out, L.in, st);
+            plane_bytes += 8 * n;
+        }
         ok = cuda_ok(cudaStreamSynchronize(st), "weight layout") && ok;
+    }
+    // the block planes of rows [row0, row0 + rows) of t for the orientations chosen (fwd: y = x W^T, N = rows,
+    // K = in; bwd: dx = dy W, N = in, K = rows)
+    void blocks(DLin & L, const gguf_tensor * t, int64_t row0, int64_t rows, bool fwd, bool bwd) {
+        if (!ok || (!fwd && !bwd)) return;
+        const int64_t ne0 = t->ne[0];
+        const size_t rb = row_bytes(t->type, ne0), nq = quant_plane_bytes(t->type, rows, ne0);
+        const size_t nd = quant_scale_count(t->type, rows, ne0);
+        void * raw = nullptr, * spare = nullptr;
+        if (cudaMalloc(&raw, rb * (size_t) rows) != cudaSuccess || cudaMalloc(&spare, nq) != cudaSuccess) {
+            cudaGetLastError();
+            if (raw) cudaFree(raw);
+            ok = false;
+            log("jepa: hjepa planner: out of device memory while uploading the weights\n");
+            return;
+        }
+        void * q = fwd ? alloc<uint8_t>(nq) : spare, * qt = bwd ? alloc<uint8_t>(nq) : spare;
+        uint16_t * d = nd ? alloc<uint16_t>(nd) : nullptr;
+        bool good = ok && cuda_ok(cudaMemcpyAsync(raw, t->data + rb * (size_t) row0, rb * (size_t) rows, cudaMemcpyHostToDevice, st), "upload") &&
+                    quant_planes(t->type, raw, rows, ne0, q, qt, d, st) == 0;
+        good = cuda_ok(cudaStreamSynchronize(st), "block planes") && good;
+        cudaFree(raw);
+        cudaFree(spare);
+        ok = ok && good;
+        if (!ok) return;
+        const int fmt = t->type == 8 ? QF_Q8 : t->type == 2 ? QF_Q4 : QF_F16;
+        if (fwd) L.fq = QuantB{fmt, 0, q, d};
+        if (bwd) L.tq = QuantB{fmt, 1, qt, d};
+        block_bytes += (fwd ? nq : 0) + (bwd ? nq : 0) + 2 * nd;
+    }
+    // which orientations of a [rows][in] weight of this type take block planes
+    void choose(uint32_t type, int64_t rows, int64_t in, bool & fwd, bool & bwd) const {
+        fwd = bwd = false;
+        if (layout == WL_PLANES || !quant_ok(type, rows, in)) return;
+        fwd = layout == WL_BLOCKS || gemm_blocks_pay((int) rows, (int) in);
+        bwd = layout == WL_BLOCKS || gemm_blocks_pay((int) in, (int) rows);
     }
     // out(V(h)) as one linear: W_ov = W_out W_v (a 3xTF32 product on the device), b_ov = W_out b_v + b_out
     DLin compose(const DLin & v, const DLin & out) {
@@ -81,7 +146,18 @@ struct Uploader {
         GemmEpi ep;
         ep.out0 = L.w;
         ep.ld0 = L.in;
-        if (gemm_tc({out.w_hi, out.w_lo, out.in}, {v.wt_hi, v.wt_lo, v.out}, out.out, v.in, v.out, ep, st)) { ok = false; return DLin(); }
+        // A: W_out's hi / lo planes (temporary ones when its forward product reads block planes)
+        const float * a_hi = out.w_hi, * a_lo = out.w_lo;
+        void * tmp = nullptr;
+        if (!a_hi) {
+            if (cudaMalloc(&tmp, (size_t) 8 * out.in * out.out) != cudaSuccess) { cudaGetLastError(); ok = false; return DLin(); }
+            a_hi = (const float *) tmp;
+            a_lo = a_hi + (size_t) out.in * out.out;
+            split_f32(out.w, out.in, (float *) a_hi, (float *) a_lo, out.in, out.out, out.in, st);
+        }
+        const int rc = gemm_tc({a_hi, a_lo, out.in}, v.bwd(), out.out, v.in, v.out, ep, st);
+        if (tmp) { cudaStreamSynchronize(st); cudaFree(tmp); }
+        if (rc) { ok = false; return DLin(); }
         if (v.b || out.b) {
             L.b = alloc<float>((size_t) L.out);
             if (!L.b) return DLin();
@@ -131,6 +207,9 @@ struct Uploader {
         L.w = alloc<float>((size_t) L.in * L.out);
         if (!L.w || !dequant_into(t, row0, rows, L.w)) return DLin();
         if (m.get(name + ".bias")) L.b = vec(name + ".bias", row0, rows);
+        bool bf, bb;
+        choose(t->type, rows, L.in, bf, bb);
+        blocks(L, t, row0, rows, bf, bb);
         finish(L);
         return L;
     }

@@ -1,12 +1,14 @@
 """Kernel microbenchmark: the planners' tcgen05 GEMMs at given shapes, through the C ABI.
 
-    python -m jepa_b200.kbench M N K [reps] [--f16]
+    python -m jepa_b200.kbench M N K [reps] [--f16 | --blocks=q8_0|q4_0|f16 [--transposed]]
     python -m jepa_b200.kbench --attn n_cand n_frames rows heads hd [reps] [impl: 0 auto, 1 mma.sync, 2 tcgen05]
     python -m jepa_b200.kbench --ac samples cem_steps [model.gguf]
     python -m jepa_b200.kbench --hjepa config candidates [steps] [model.gguf]
 
 Prints the mean device time per launch (CUDA events) and the algorithmic TFLOP/s (2 M N K per launch).
-Without --f16 it times the H-JEPA planner's 3xTF32 GEMM, with --f16 the V-JEPA 2-AC predictor's f16 GEMM.
+Without --f16 it times the H-JEPA planner's 3xTF32 GEMM, with --f16 the V-JEPA 2-AC predictor's f16 GEMM;
+--blocks times the 3xTF32 GEMM with its weight operand in GGUF block planes dequantised in the mainloop (forward
+B = W [N][K], or with --transposed the backward operand W^T of a weight [K][N]).
 --attn times the AC predictor's attention (the last frame's rows over all frames' keys).
 --ac runs one V-JEPA 2-AC CEM plan (horizon 2, two observed frames) on a model of the benchmark's size
 (24 x 1024, 16 heads, MLP 4096, 16 x 16 patches of 1408-d latents, q8_0; written to the given path, or a
@@ -32,6 +34,15 @@ def gemm(M: int, N: int, K: int, reps: int = 20, f16: bool = False) -> float:
     fn = L.jepa_b200_gemm_f16_bench if f16 else L.jepa_b200_gemm_bench
     fn.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
     if fn(M, N, K, reps, C.byref(ms)) != 0:
+        raise RuntimeError(jlib.error_text())
+    return ms.value
+
+
+def gemm_blocks(M: int, N: int, K: int, ggml_type: int, transposed: bool, reps: int = 20) -> float:
+    ms = C.c_double()
+    L = jlib.load()
+    L.jepa_b200_gemm_quant_bench.argtypes = [C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
+    if L.jepa_b200_gemm_quant_bench(ggml_type, M, N, K, int(transposed), reps, C.byref(ms)) != 0:
         raise RuntimeError(jlib.error_text())
     return ms.value
 
@@ -137,6 +148,13 @@ if __name__ == "__main__":
     f16 = "--f16" in sys.argv
     M, N, K = (int(x) for x in args[:3])
     reps = int(args[3]) if len(args) > 3 else 20
-    t = gemm(M, N, K, reps, f16)
-    kind = "f16" if f16 else "3xtf32"
+    blk = [x.split("=", 1)[1] for x in sys.argv if x.startswith("--blocks=")]
+    if blk:
+        gt = {"q8_0": 8, "q4_0": 2, "f16": 1}[blk[0]]
+        tr = "--transposed" in sys.argv
+        t = gemm_blocks(M, N, K, gt, tr, reps)
+        kind = f"3xtf32, B in {blk[0]} block planes{' (transposed)' if tr else ''}"
+    else:
+        t = gemm(M, N, K, reps, f16)
+        kind = "f16" if f16 else "3xtf32"
     print(f"gemm[{kind}] M={M} N={N} K={K}: {t * 1e3:.2f} us/launch, {2.0 * M * N * K / (t * 1e-3) / 1e12:.2f} TFLOP/s")
