@@ -370,7 +370,8 @@ def ac_config_dict(spec, world: int) -> dict:
                         f"(16 heads, MLP 4096), q8_0",
             "candidates_total": AC_K,
             "parallelism": f"candidates split over {world} GPU(s) (strong scaling), one NCCL all-gather of energies "
-                           f"per CEM iteration"}
+                           f"per CEM iteration",
+            "l2": "no flush: the working set (keys / values 40 GB, activations 4 GB at one GPU) is far above L2"}
 
 
 def ac_inputs(spec: synth.ACSpec, K: int):
@@ -501,10 +502,9 @@ def run_ac(args, rank, world, local, dist, primary: bool):
         "metric": METRIC, "value": value, "unit": AC_UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f16", "data": "synthetic (seeded random-init q8_0 GGUF, N(0,1) context / goal latents, N(0,1) CEM noise)",
-        "config": dict(ac_config_dict(spec, world),
-                       l2="working set (keys / values 40 GB, activations 4 GB at one GPU) far above L2",
-                       arith="f16 operands, f32 accumulate (tcgen05 kind::f16), f32 residual stream",
-                       gflop_per_candidate_iteration={"algorithmic": round(alg, 1), "executed": round(ex, 1)}),
+        "config": ac_config_dict(spec, world),
+        "arith": "f16 operands, f32 accumulate (tcgen05 kind::f16), f32 residual stream",
+        "gflop_per_candidate_iteration": {"algorithmic": round(alg, 1), "executed": round(ex, 1)},
         "e2e": {"value": e2e, "unit": AC_UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
@@ -597,8 +597,8 @@ def run_hjepa(args, rank, world, local, dist):
             "ms_per_step": dev_ms / K, "higher_is_better": True,
             "scaling": "strong" if strong_scaling(cfg) else "weak", "vs_baseline": None,
             "dtype": "f32", "data": f"synthetic (seeded random-init {spec.ftype} GGUF, N(0,1) latents, U[-1,1] candidates)",
-            "config": dict(hjepa_config_dict(cfg, spec, plans, world),
-                           arith="3xTF32 tensor-core GEMMs (tcgen05 kind::tf32, f32 accuracy), f32 element-wise"),
+            "config": hjepa_config_dict(cfg, spec, plans, world),
+            "arith": "3xTF32 tensor-core GEMMs (tcgen05 kind::tf32, f32 accuracy), f32 element-wise",
             "e2e": {"value": grad_steps / wall, "unit": UNIT, "h2d_bytes_per_step": int(h2d / K),
                     "d2h_bytes_per_step": int(d2h / K)},
             "gpu_launches": int(launches),
