@@ -371,8 +371,9 @@ __device__ __forceinline__ bool convert_rows(uint8_t * bh, int ct, int lane, uin
     return true;
 }
 
-template <int BN, int CT>
+template <int BN, int CT, bool QB>
 __device__ __forceinline__ bool convert_stage(uint8_t * bh, const QDesc & qd, int ct, int lane, uint64_t * raw_bar, uint32_t ph) {
+    if constexpr (!QB) return false;
     switch (qd.fmt * 2 + qd.orient) {
         case QF_Q8 * 2: return convert_rows<BN, CT, QF_Q8, 0>(bh, ct, lane, raw_bar, ph);
         case QF_Q8 * 2 + 1: return convert_rows<BN, CT, QF_Q8, 1>(bh, ct, lane, raw_bar, ph);
@@ -383,9 +384,10 @@ __device__ __forceinline__ bool convert_stage(uint8_t * bh, const QDesc & qd, in
 }
 
 // the TMA copies of one stage's raw B tile (K-step kt of the BN rows from n0) onto `bar`
-template <int BN>
+template <int BN, bool QB>
 __device__ __forceinline__ void load_raw_b(uint8_t * b_lo_area, const CUtensorMap * tq, const CUtensorMap * td, const QDesc & qd,
                                            int kt, int n0, uint64_t * bar) {
+    if constexpr (!QB) return;
     tma_load_2d(b_lo_area, tq, qd.fmt == QF_Q4 ? kt * 16 : kt * 32, n0, bar);
     if (qd.fmt == QF_Q8 || qd.fmt == QF_Q4) {
         uint8_t * ds = b_lo_area + BN * raw_row_bytes(qd.fmt);
@@ -411,7 +413,7 @@ __host__ __device__ constexpr int split_rows(int splits) { return (BM + splits -
 // hides behind it. Cluster barriers: one arrive at the start (the receive
 // barriers are initialised) waited on before the first push, one after the receive completes waited on
 // before exit (no CTA leaves while a push to or from it may be in flight).
-template <int BN, int STAGES, int MODE>
+template <int BN, int STAGES, int MODE, bool QB>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
               const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
@@ -422,6 +424,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     // bytes a stage's copies deliver: A_hi, A_lo, B_hi, B_lo on the stage's full barrier; with a weight in block
     // planes, A alone there and the raw B tile on its own barrier (the converters need B only)
     const uint32_t raw_tx = BN * raw_row_bytes(qd.fmt) + raw_scale_bytes(qd.fmt, BN);
+    // block planes: a template switch, so that the plane-operand kernels carry none of the converters' code
+    // (these kernels are latency-bound, and code between the accumulator and the stores costs fetches)
+    const bool qb = QB && qd.fmt != QF_NONE;
     // two accumulators: hi*hi in columns [0, BN), the small cross terms hi*lo + lo*hi in [BN, 2 BN).
     // The tensor core's float32 accumulation rounds toward zero per instruction; keeping the small terms
     // apart cuts the number of truncations the large partial sum sees by three.
@@ -500,9 +505,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     if (warp == 0 && lane == 0) {
         for (int i = 0; i < pre_stages; i++) {
             uint8_t * st = smem + (size_t) i * STAGE_BYTES;
-            if (qd.fmt) {
+            if (qb) {
                 mbar_expect_tx(&rawf_bar[i], raw_tx);
-                load_raw_b<BN>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, kt0 + i, n0, &rawf_bar[i]);
+                load_raw_b<BN, QB>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, kt0 + i, n0, &rawf_bar[i]);
             } else {
                 mbar_expect_tx(&full_bar[i], STAGE_BYTES);
                 tma_load_2d(st + 2 * A_BYTES, &tB_hi, (kt0 + i) * BK, n0, &full_bar[i]);
@@ -530,7 +535,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
     // wait for it after their loop (their epilogue items' operands are read from there on). No thread lets
     // the next kernel launch before it has waited: that kernel's early reads assume this one's predecessor
     // has finished.
-    const bool conv_early = qd.fmt && warp >= 6 && warp < 6 + CONV_WARPS;
+    const bool conv_early = qb && warp >= 6 && warp < 6 + CONV_WARPS;
     if (!conv_early) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -549,16 +554,16 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 if (i >= pre_stages && *(volatile int *) &abort_sh) break;
                 uint8_t * st = smem + (size_t) s * STAGE_BYTES;
                 if (i >= pre_stages) {
-                    if (qd.fmt) {
+                    if (qb) {
                         mbar_expect_tx(&rawf_bar[s], raw_tx);
-                        load_raw_b<BN>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, kt, n0, &rawf_bar[s]);
+                        load_raw_b<BN, QB>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, kt, n0, &rawf_bar[s]);
                     } else {
                         mbar_expect_tx(&full_bar[s], STAGE_BYTES);
                         tma_load_2d(st + 2 * A_BYTES, &tB_hi, kt * BK, n0, &full_bar[s]);
                         tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, kt * BK, n0, &full_bar[s]);
                     }
                 }
-                if (qd.fmt) mbar_expect_tx(&full_bar[s], 2 * A_BYTES);
+                if (qb) mbar_expect_tx(&full_bar[s], 2 * A_BYTES);
                 tma_load_2d(st, &tA_hi, kt * BK, m0, &full_bar[s]);
                 tma_load_2d(st + A_BYTES, &tA_lo, kt * BK, m0, &full_bar[s]);
                 issued = i + 1;
@@ -567,7 +572,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 // drain: the copies of the last stages it armed must land before the buffers are reused
                 for (int i = issued - STAGES < 0 ? 0 : issued - STAGES; i < issued; i++) {
                     mbar_wait(&full_bar[i % STAGES], (uint32_t) (i / STAGES) & 1u, 5, &g_gemm_error);
-                    if (qd.fmt) mbar_wait(&rawf_bar[i % STAGES], (uint32_t) (i / STAGES) & 1u, 5, &g_gemm_error);
+                    if (qb) mbar_wait(&rawf_bar[i % STAGES], (uint32_t) (i / STAGES) & 1u, 5, &g_gemm_error);
                 }
             }
         }
@@ -579,7 +584,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
                 const int s = i % STAGES;
                 const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
                 if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error) ||
-                    (qd.fmt && !mbar_wait_spin(&conv_bar[s], ph, 2, &g_gemm_error))) { abort_sh = 1; break; }
+                    (qb && !mbar_wait_spin(&conv_bar[s], ph, 2, &g_gemm_error))) { abort_sh = 1; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t a_hi = smem_u32(smem + (size_t) s * STAGE_BYTES);
                 const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES;   // B_lo follows B_hi
@@ -598,14 +603,14 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
         __syncwarp();
         if (splits > 1) cluster_wait();
     } else if (warp >= 6) {
-        if (qd.fmt && warp < 6 + CONV_WARPS) {
+        if (qb && warp < 6 + CONV_WARPS) {
             // converter warps: the raw B tile of every stage into its split planes
             const int ct = (int) threadIdx.x - 6 * 32;
             for (int i = 0; i < nkt; i++) {
                 const int s = i % STAGES;
                 const uint32_t ph = (uint32_t) (i / STAGES) & 1u;
                 if (!mbar_wait_spin(&rawf_bar[s], ph, 6, &g_gemm_error) ||
-                    !convert_stage<BN, 32 * CONV_WARPS>(smem + (size_t) s * STAGE_BYTES + 2 * A_BYTES, qd, ct, lane, &raw_bar[s], ph)) {
+                    !convert_stage<BN, 32 * CONV_WARPS, QB>(smem + (size_t) s * STAGE_BYTES + 2 * A_BYTES, qd, ct, lane, &raw_bar[s], ph)) {
                     abort_sh = 1;
                     break;
                 }
@@ -750,14 +755,15 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
 // 4 KB shared buffer (16-byte chunk c of row r at c ^ (r & 7)) and applies the fused epilogue from there
 // four rows per instruction: coalesced loads and stores. A tile's arithmetic is the split kernel's at
 // one split (the same MMAs in the same order), so a row's bits do not depend on the batch.
-constexpr int PBN = 128, PSTAGES = 3, PEPI_WARPS = 8, PTHREADS = 64 + 32 * PEPI_WARPS + 32 * PCONV_WARPS;
+constexpr int PBN = 128, PSTAGES = 3, PEPI_WARPS = 8, PTHREADS = 64 + 32 * PEPI_WARPS;
+constexpr int PTHREADS_QB = PTHREADS + 32 * PCONV_WARPS;   // with the converter warps
 constexpr int FIX_ROWS = 4;   // K-split fix-up: row groups of partial tiles loaded at once per lane
 constexpr uint32_t PSTAGE_BYTES = 2 * BM * BK * 4 + 2 * PBN * BK * 4;
 constexpr size_t PSMEM_BYTES = (size_t) PSTAGES * PSTAGE_BYTES + (size_t) PEPI_WARPS * 32 * 32 * 4 + 1024;
 static_assert(PSMEM_BYTES + 256 <= 227 * 1024, "persistent tf32x3 GEMM: stages and staging buffers fit");
 
-template <int MODE>
-__global__ void __launch_bounds__(PTHREADS, 1)
+template <int MODE, bool QB>
+__global__ void __launch_bounds__(QB ? PTHREADS_QB : PTHREADS, 1)
 k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
                 const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
                 int M, int N, int K, int splits, const QDesc qd, const __grid_constant__ GemmEpi ep) {
@@ -783,9 +789,11 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_k = (K + BK - 1) / BK;
     const int tiles_n = (N + PBN - 1) / PBN;
-    // work units: unit u is K-part u % splits of output tile u / splits (splits == 1: whole tiles)
+    // work units: unit u is K-part u % splits of output tile u / splits (splits == 1: whole tiles): a tile's parts
+    // run side by side, its A rows and B slice shared in L2
     const int total = ((M + BM - 1) / BM) * tiles_n * splits;
     const int kq = (num_k + splits - 1) / splits;
+    const bool qb = QB && qd.fmt != QF_NONE;   // block planes (a template switch: the plane kernels carry no converter code)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < PSTAGES; s++) {
@@ -830,25 +838,27 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                     if (kt >= PSTAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, 1, &g_gemm_error)) { abort_sh = 1; break; }
                     if (*(volatile int *) &abort_sh) break;
                     uint8_t * st = smem + (size_t) s * PSTAGE_BYTES;
-                    if (qd.fmt) {
+                    if (qb) {
                         // the raw B tile first, on its own barrier: the converters are on the critical path
                         mbar_expect_tx(&rawf_bar[s], PBN * raw_row_bytes(qd.fmt) + raw_scale_bytes(qd.fmt, PBN));
-                        load_raw_b<PBN>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, k, n0, &rawf_bar[s]);
+                        load_raw_b<PBN, QB>(st + 2 * A_BYTES + B_BYTES, &tB_hi, &tB_lo, qd, k, n0, &rawf_bar[s]);
                         mbar_expect_tx(&full_bar[s], 2 * A_BYTES);
+                        tma_load_2d(st, &tA_hi, k * BK, m0, &full_bar[s]);
+                        tma_load_2d(st + A_BYTES, &tA_lo, k * BK, m0, &full_bar[s]);
                     } else {
                         mbar_expect_tx(&full_bar[s], PSTAGE_BYTES);
+                        tma_load_2d(st, &tA_hi, k * BK, m0, &full_bar[s]);
+                        tma_load_2d(st + A_BYTES, &tA_lo, k * BK, m0, &full_bar[s]);
                         tma_load_2d(st + 2 * A_BYTES, &tB_hi, k * BK, n0, &full_bar[s]);
                         tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tB_lo, k * BK, n0, &full_bar[s]);
                     }
-                    tma_load_2d(st, &tA_hi, k * BK, m0, &full_bar[s]);
-                    tma_load_2d(st + A_BYTES, &tA_lo, k * BK, m0, &full_bar[s]);
                 }
             }
             if (*(volatile int *) &abort_sh) {
                 // let the copies already issued land before the CTA exits
                 for (int j = kt - PSTAGES < 0 ? 0 : kt - PSTAGES; j < kt; j++) {
                     mbar_wait(&full_bar[j % PSTAGES], (uint32_t) (j / PSTAGES) & 1u, 5, &g_gemm_error);
-                    if (qd.fmt) mbar_wait(&rawf_bar[j % PSTAGES], (uint32_t) (j / PSTAGES) & 1u, 5, &g_gemm_error);
+                    if (qb) mbar_wait(&rawf_bar[j % PSTAGES], (uint32_t) (j / PSTAGES) & 1u, 5, &g_gemm_error);
                 }
             }
         }
@@ -865,7 +875,7 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                     const int s = kt % PSTAGES;
                     const uint32_t ph = (uint32_t) (kt / PSTAGES) & 1u;
                     if (!mbar_wait(&full_bar[s], ph, 2, &g_gemm_error) ||
-                        (qd.fmt && !mbar_wait_spin(&conv_bar[s], ph, 2, &g_gemm_error))) { abort_sh = 1; break; }
+                        (qb && !mbar_wait_spin(&conv_bar[s], ph, 2, &g_gemm_error))) { abort_sh = 1; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t a_hi = smem_u32(smem + (size_t) s * PSTAGE_BYTES);
                     const uint32_t a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES;   // B_lo follows B_hi
@@ -883,7 +893,7 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
             }
         }
     } else if (warp >= 2 + PEPI_WARPS) {
-        if (qd.fmt) {
+        if (qb) {
             // converter warps: the raw B tile of every stage into its split planes, in the producer's order
             const int ct = (int) threadIdx.x - (2 + PEPI_WARPS) * 32;
             int kt = 0;
@@ -894,7 +904,7 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                     const int s = kt % PSTAGES;
                     const uint32_t ph = (uint32_t) (kt / PSTAGES) & 1u;
                     if (!mbar_wait_spin(&rawf_bar[s], ph, 6, &g_gemm_error) ||
-                        !convert_stage<PBN, 32 * PCONV_WARPS>(smem + (size_t) s * PSTAGE_BYTES + 2 * A_BYTES, qd, ct, lane, &raw_bar[s], ph)) {
+                        !convert_stage<PBN, 32 * PCONV_WARPS, QB>(smem + (size_t) s * PSTAGE_BYTES + 2 * A_BYTES, qd, ct, lane, &raw_bar[s], ph)) {
                         good = false;
                         break;
                     }
@@ -990,12 +1000,12 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                     for (int jj = 0; jj < FIX_ROWS; jj++) {
                         const int idx = (j0 + jj) * 32 + lane, r = idx >> 4, c = idx & 15;
                         const int row = row0 + r, col = half * 64 + 4 * c;
-                        float4 s = v[jj][0];
+                        float4 acc = v[jj][0];
 #pragma unroll
                         for (int p = 1; p < GEMM_KSPLIT_MAX; p++) {
-                            if (p < splits) s = f4_add(s, v[jj][p]);   // parts in order 0, 1, ...
+                            if (p < splits) acc = f4_add(acc, v[jj][p]);   // parts in order 0, 1, ...
                         }
-                        if (row < M) apply_epi4<MODE>(ep, row, n0 + col, N, s);
+                        if (row < M) apply_epi4<MODE>(ep, row, n0 + col, N, acc);
                     }
                 }
                 continue;
@@ -1124,7 +1134,7 @@ constexpr size_t smem_bytes() {
 static_assert(smem_bytes<64, 4>() + 256 <= 227 * 1024, "four 64-wide stages and the receive buffer fit in shared memory");
 
 // the kernel's shared-memory and cluster attributes, once per device
-template <int BN, int STAGES, int MODE>
+template <int BN, int STAGES, int MODE, bool QB>
 bool set_attrs() {
     static std::mutex mu;
     static bool done[64] = {};
@@ -1132,9 +1142,9 @@ bool set_attrs() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
     std::lock_guard<std::mutex> lock(mu);
     if (!done[dev]) {
-        if (cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES, MODE, QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int) smem_bytes<BN, STAGES>()) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES, MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+            cudaFuncSetAttribute(k_gemm_tf32x3<BN, STAGES, MODE, QB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
             return false;
         }
         done[dev] = true;
@@ -1155,7 +1165,7 @@ int resident_clusters(int s) {
         int n = 0;
         if (s == 1) {
             cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        } else if (set_attrs<64, 4, EPI_F32>()) {
+        } else if (set_attrs<64, 4, EPI_F32, false>()) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(1, 1, (unsigned) s);
             cfg.blockDim = dim3(GEMM_THREADS);
@@ -1167,7 +1177,7 @@ int resident_clusters(int s) {
             attr[0].val.clusterDim.z = (unsigned) s;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            if (cudaOccupancyMaxActiveClusters(&n, k_gemm_tf32x3<64, 4, EPI_F32>, &cfg) != cudaSuccess) n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, k_gemm_tf32x3<64, 4, EPI_F32, false>, &cfg) != cudaSuccess) n = 0;
         }
         cudaGetLastError();
         cache[dev][s] = n > 0 ? n : -1;
@@ -1186,7 +1196,11 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
         return -1;
     }
     constexpr size_t smem = smem_bytes<BN, STAGES>();
-    if (!set_attrs<BN, STAGES, MODE>()) { log("jepa: gemm: cudaFuncSetAttribute failed\n"); return -1; }
+    const bool qb = qd.fmt != QF_NONE;
+    if (!(qb ? set_attrs<BN, STAGES, MODE, true>() : set_attrs<BN, STAGES, MODE, false>())) {
+        log("jepa: gemm: cudaFuncSetAttribute failed\n");
+        return -1;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) ((M + BM - 1) / BM), (unsigned) ((N + BN - 1) / BN), (unsigned) splits);
     cfg.blockDim = dim3(GEMM_THREADS);
@@ -1201,7 +1215,8 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
     attr[1].val.clusterDim.z = (unsigned) splits;
     cfg.attrs = attr;
     cfg.numAttrs = splits > 1 ? 2 : 1;
-    JB_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tf32x3<BN, STAGES, MODE>, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, splits, qd, ep));
+    if (qb) JB_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tf32x3<BN, STAGES, MODE, true>, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, splits, qd, ep));
+    else JB_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tf32x3<BN, STAGES, MODE, false>, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, splits, qd, ep));
     return 0;
 }
 
@@ -1223,15 +1238,21 @@ int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, int sp
     {
         std::lock_guard<std::mutex> lock(mu);
         if (!done[dev]) {
-            JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_p<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) PSMEM_BYTES));
+            JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_p<MODE, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) PSMEM_BYTES));
+            JB_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3_p<MODE, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) PSMEM_BYTES));
             JB_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
             done[dev] = true;
         }
     }
     const long units = (long) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN) * splits;
     const unsigned grid = (unsigned) std::max(1L, std::min<long>(units, sms[dev]));
-    JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE>, dim3(grid), dim3(PTHREADS), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo, M, N, K,
-                       splits, qd, ep));
+    if (qd.fmt != QF_NONE) {
+        JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE, true>, dim3(grid), dim3(PTHREADS_QB), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo,
+                           M, N, K, splits, qd, ep));
+    } else {
+        JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE, false>, dim3(grid), dim3(PTHREADS), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo,
+                           M, N, K, splits, qd, ep));
+    }
     return 0;
 }
 

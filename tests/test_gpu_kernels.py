@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 # split-K 64-wide tiles (N or K < 768), and the 128-wide unsplit tiles (N, K >= 768, or N >= 4096) with ragged
 # M and N edges
 @pytest.mark.parametrize("M,N,K", [(2048, 768, 3072), (256, 768, 3072), (1024, 768, 2048), (2048, 768, 8192), (1024, 768, 12000),
-                                   (300, 1000, 9000), (2048, 768, 55296), (130, 900, 8196), (200, 1000, 2052)])
+                                   (300, 1000, 9000), (2048, 768, 55296), (130, 900, 8196), (200, 1000, 2052),
+                                   (300, 800, 20000), (130, 768, 16384)])
 def test_gemm_ksplit_matches_f64_and_the_unsplit_kernel(M, N, K):
     """The planner's configuration of the persistent GEMM: K split in three parts, the partial tiles summed
     in a fixed order by the part that finishes last (ragged M, N and K edges included)."""
