@@ -261,7 +261,7 @@ int jepa_encode(jepa_context * ctx, const jepa_input * in, jepa_output * out) {
         log("jepa: input %dx%d is not a multiple of the patch size %d\n", in->height, in->width, P);
         return -1;
     }
-    if (e.act != "gelu_erf" && e.act != "silu" && e.act != "relu") {
+    if (e.act != "gelu_erf" && e.act != "gelu_tanh" && e.act != "silu" && e.act != "relu") {
         log("jepa: jepa_encode: encoder activation '%s' is not supported by this engine\n", e.act.c_str());
         return -1;
     }
@@ -339,7 +339,7 @@ int jepa_encode(jepa_context * ctx, const jepa_input * in, jepa_output * out) {
         } else {
             e3.out0 = u.f(); e3.ld0 = Fl;
             if (lin_tc(L.up, h_hi.f(), h_lo.f(), D, M, e3, st)) return -1;
-            act_fwd(u.f(), Fl, a.f(), Fl, M, Fl, e.act == "silu" ? 2 : 3, st);
+            act_fwd(u.f(), Fl, a.f(), Fl, M, Fl, e.act == "silu" ? 2 : e.act == "gelu_tanh" ? 4 : 3, st);
             split_f32(a.f(), Fl, g_hi.f(), g_lo.f(), Fl, M, Fl, st);
         }
         GemmEpi e4;

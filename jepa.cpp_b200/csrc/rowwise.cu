@@ -540,14 +540,20 @@ __global__ void k_add_row(const float * __restrict__ x, int ldx, const float * _
     y[(size_t) r * ldy + c] = x[(size_t) r * ldx + c] + row[c];
 }
 
+// activation codes: 1 GELU (erf), 2 SiLU, 3 ReLU, 4 GELU (tanh form: 0.5 v (1 + tanh(sqrt(2 / pi) (v + 0.044715 v^3))))
 __device__ __forceinline__ float act_f(float v, int act) {
     if (act == 2) return v / (1.0f + expf(-v));
     if (act == 3) return v > 0 ? v : 0.0f;
+    if (act == 4) return 0.5f * v * (1.0f + tanhf(0.79788456080286536f * (v + 0.044715f * v * v * v)));
     return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
 }
 __device__ __forceinline__ float act_d(float v, int act) {
     if (act == 2) { const float s = 1.0f / (1.0f + expf(-v)); return s * (1.0f + v * (1.0f - s)); }
     if (act == 3) return v > 0 ? 1.0f : 0.0f;
+    if (act == 4) {
+        const float t = tanhf(0.79788456080286536f * (v + 0.044715f * v * v * v));
+        return 0.5f * (1.0f + t) + 0.5f * v * (1.0f - t * t) * 0.79788456080286536f * (1.0f + 3.0f * 0.044715f * v * v);
+    }
     return 0.5f * (1.0f + erff(v * 0.70710678118654752f)) + v * 0.39894228040143268f * expf(-0.5f * v * v);
 }
 

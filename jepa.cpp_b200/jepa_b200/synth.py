@@ -66,6 +66,7 @@ class HJepaSpec:
     enc_layers: int = 1
     enc_heads: int = 0
     enc_ffn: int = 0
+    enc_act: str = "gelu_erf"      # jepa.enc.act of the encoder stub: gelu_erf | gelu_tanh | silu | relu
     rand_all: bool = False         # every parameter random (forged test models)
     w_std: float = 0.02
     cond_std: float = 0.02         # cond_proj / adaln / act_embed init std
@@ -143,7 +144,7 @@ def write_hjepa(path: str, spec: HJepaSpec, seed: int = 0) -> None:
                  ("patch_size", 14), ("tubelet_size", 1), ("img_size", 224), ("n_frames", 1), ("in_chans", 3)):
         w.add_kv("jepa.enc." + k, v)
     w.add_kv("jepa.enc.ln_eps", 1e-12)
-    w.add_kv("jepa.enc.act", "gelu_erf")
+    w.add_kv("jepa.enc.act", spec.enc_act)
     w.add_kv("jepa.enc.pos_type", "learned")
     w.add_kv("jepa.enc.cls_token", True)
     w.add_kv("jepa.enc.qkv_fused", True)

@@ -34,6 +34,18 @@ def _gelu(x):
     return (0.5 * x * (1.0 + erf(x / math.sqrt(2.0)))).astype(f32)
 
 
+def _act(name):
+    """The encoder MLP's activation by its jepa.enc.act name (scripts/jepa_convert/selftest.py:104-111 `act_fn`;
+    relu as the loader accepts it, src/jepa-gguf.cpp:26-35)."""
+    if name == "gelu_tanh":
+        return lambda x: (0.5 * x * (1 + np.tanh(math.sqrt(2 / math.pi) * (x + 0.044715 * x ** 3)))).astype(f32)
+    if name == "silu":
+        return lambda x: (x / (1.0 + np.exp(-x))).astype(f32)
+    if name == "relu":
+        return lambda x: np.maximum(x, 0).astype(f32)
+    return _gelu
+
+
 def patch_rows(img, P):
     """img [C][H][W] -> [n_patches][C P P]: patches h-major, C, then P x P inside a row (jepa_patchify)."""
     C, H, W = img.shape
@@ -49,6 +61,7 @@ def encode(path: str, images) -> np.ndarray:
     D, P, H = int(g("embed_dim")), int(g("patch_size")), int(g("n_head"))
     eps = float(g("ln_eps", 1e-6))
     n_reg = int(g("n_registers", 0) or 0)
+    act = _act(str(g("act", "gelu_erf")))
     out = []
     for img in np.asarray(images, f32):
         x = patch_rows(img, P) @ T["enc.patch_embed.weight"].T + T["enc.patch_embed.bias"]
@@ -72,7 +85,7 @@ def encode(path: str, images) -> np.ndarray:
                 a = a * T[b + "ls1"]
             x = (x + a).astype(f32)
             h = _ln(x, T[b + "ln2.weight"], T[b + "ln2.bias"], eps)
-            f = _gelu(h @ T[b + "ffn_up.weight"].T + T.get(b + "ffn_up.bias", 0))
+            f = act(h @ T[b + "ffn_up.weight"].T + T.get(b + "ffn_up.bias", 0))
             f = f @ T[b + "ffn_down.weight"].T + T.get(b + "ffn_down.bias", 0)
             if b + "ls2" in T:
                 f = f * T[b + "ls2"]
@@ -138,6 +151,7 @@ def encode_video(path: str, clips) -> np.ndarray:
     g = lambda k, d=None: meta.get("jepa.enc." + k, d)
     D, P, H = int(g("embed_dim")), int(g("patch_size")), int(g("n_head"))
     eps = float(g("ln_eps", 1e-6))
+    act = _act(str(g("act", "gelu_erf")))
     hd = D // H
     out = []
     for clip in np.asarray(clips, f32):
@@ -172,7 +186,7 @@ def encode_video(path: str, clips) -> np.ndarray:
             a = ((p / p.sum(-1, keepdims=True)) @ v).transpose(1, 0, 2).reshape(-1, D).astype(f32)
             x = (x + a @ T_[b + "attn_out.weight"].T + T_.get(b + "attn_out.bias", 0)).astype(f32)
             h = _ln(x, T_[b + "ln2.weight"], T_[b + "ln2.bias"], eps)
-            f = _gelu(h @ T_[b + "ffn_up.weight"].T + T_.get(b + "ffn_up.bias", 0))
+            f = act(h @ T_[b + "ffn_up.weight"].T + T_.get(b + "ffn_up.bias", 0))
             x = (x + f @ T_[b + "ffn_down.weight"].T + T_.get(b + "ffn_down.bias", 0)).astype(f32)
         out.append(_ln(x, T_["enc.norm.weight"], T_["enc.norm.bias"], eps))
     return np.concatenate(out, 0)

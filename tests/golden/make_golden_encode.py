@@ -8,8 +8,9 @@ with the reference checked out at $JEPA_REF):
 
     JEPA_REF=/path/to/jepa.cpp python tests/golden/make_golden_encode.py
 
-Models: 'ea' (f32, 96 wide, 3 heads of 32, 2 blocks) and 'eb' (q8_0 blocks, 128 wide, 2 heads of 64, 1 block);
-both encode 224 x 224 images in 14 x 14 patches (256 patches + CLS). Images are N(0, 1) per pixel (seed).
+Models: 'ea' (f32, 96 wide, 3 heads of 32, 2 blocks), 'eb' (q8_0 blocks, 128 wide, 2 heads of 64, 1 block) and
+'ec' (f16, 64 wide, 2 heads of 32, 1 block, the tanh form of GELU that HF ViT checkpoints use); all encode
+224 x 224 images in 14 x 14 patches (256 patches + CLS). Images are N(0, 1) per pixel (seed).
 """
 from __future__ import annotations
 
@@ -37,7 +38,9 @@ def model_specs():
                          enc_heads=3, enc_ffn=192)
     eb = synth.HJepaSpec(levels=[L], ftype="q8_0", rand_all=True, w_std=0.1, name="golden-eb", enc_dim=128, enc_layers=1,
                          enc_heads=2, enc_ffn=256)
-    return {"ea": (ea, 41, 2), "eb": (eb, 42, 1)}
+    ec = synth.HJepaSpec(levels=[L], ftype="f16", rand_all=True, w_std=0.1, name="golden-ec", enc_dim=64, enc_layers=1,
+                         enc_heads=2, enc_ffn=192, enc_act="gelu_tanh")
+    return {"ea": (ea, 41, 2), "eb": (eb, 42, 1), "ec": (ec, 43, 1)}
 
 
 def build_model(name: str, workdir: str) -> tuple[str, str]:
