@@ -56,7 +56,9 @@ bool EncEngine::build(const jepa_model & m, cudaStream_t st) {
     for (int i = 0; i < e.n_layer && up.ok; i++) {
         const std::string p = "enc.blk." + std::to_string(i) + ".";
         EncLayer L;
-        L.qkv = up.lin_fwd_only(p + "attn_qkv");
+        // the fused q / k / v linear, or the three a file keeps apart stacked into one (src/jepa.cpp:399-412)
+        L.qkv = m.get(p + "attn_qkv.weight") ? up.lin_fwd_only(p + "attn_qkv")
+                                             : up.lin_fwd_only_stacked({p + "attn_q", p + "attn_k", p + "attn_v"});
         L.out = up.lin_fwd_only(p + "attn_out");
         L.up = up.lin_fwd_only(p + "ffn_up");
         L.down = up.lin_fwd_only(p + "ffn_down");
@@ -66,7 +68,7 @@ bool EncEngine::build(const jepa_model & m, cudaStream_t st) {
         L.ls2 = m.get(p + "ls2") ? up.vec(p + "ls2") : ones;
         if (!(L.qkv && L.out && L.up && L.down) || L.qkv.out != 3 * D || L.qkv.in != D || L.out.out != D || L.up.in != D ||
             L.down.out != D || L.down.in != L.up.out) {
-            log("jepa: jepa_encode: block %d is not a fused-qkv pre-norm block of width %d\n", i, D);
+            log("jepa: jepa_encode: block %d is not a pre-norm block of width %d with q, k and v of that width\n", i, D);
             return false;
         }
         layers.push_back(L);

@@ -197,6 +197,43 @@ struct Uploader {
         ok = cuda_ok(cudaStreamSynchronize(st), "weight layout") && ok;
         return L;
     }
+    // several forward-only linears of one input width stacked into one (their rows in order, a bias of zeros
+    // where one has none): the attention's q, k and v when a file keeps them apart
+    DLin lin_fwd_only_stacked(const std::vector<std::string> & names) {
+        DLin L;
+        std::vector<const gguf_tensor *> ts;
+        for (const std::string & n : names) {
+            const gguf_tensor * t = m.get(n + ".weight");
+            if (!t || !ok || (!ts.empty() && t->ne[0] != ts[0]->ne[0])) return L;
+            ts.push_back(t);
+            L.out += (int) t->ne[1];
+        }
+        L.in = (int) ts[0]->ne[0];
+        L.w = alloc<float>((size_t) L.in * L.out);
+        bool any_bias = false;
+        for (const std::string & n : names) any_bias = any_bias || m.get(n + ".bias");
+        if (any_bias) L.b = alloc<float>((size_t) L.out);
+        if (!ok) return DLin();
+        if (L.b) cudaMemsetAsync(L.b, 0, (size_t) L.out * 4, st);
+        int64_t r0 = 0;
+        for (size_t i = 0; i < ts.size(); i++) {
+            if (!dequant_into(ts[i], 0, ts[i]->ne[1], L.w + (size_t) r0 * L.in)) return DLin();
+            if (m.get(names[i] + ".bias")) {
+                float * b = vec(names[i] + ".bias");
+                if (!b || !cuda_ok(cudaMemcpyAsync(L.b + r0, b, (size_t) ts[i]->ne[1] * 4, cudaMemcpyDeviceToDevice, st), "stack")) {
+                    ok = false;
+                    return DLin();
+                }
+            }
+            r0 += ts[i]->ne[1];
+        }
+        L.w_hi = alloc<float>((size_t) L.in * L.out);
+        L.w_lo = alloc<float>((size_t) L.in * L.out);
+        if (!ok) return DLin();
+        split_f32(L.w, L.in, L.w_hi, L.w_lo, L.in, L.out, L.in, st);
+        ok = cuda_ok(cudaStreamSynchronize(st), "weight layout") && ok;
+        return L;
+    }
     DLin lin(const std::string & name, int64_t row0 = 0, int64_t rows = -1) {
         DLin L;
         const gguf_tensor * t = m.get(name + ".weight");

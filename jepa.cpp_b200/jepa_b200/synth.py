@@ -67,6 +67,7 @@ class HJepaSpec:
     enc_heads: int = 0
     enc_ffn: int = 0
     enc_act: str = "gelu_erf"      # jepa.enc.act of the encoder stub: gelu_erf | gelu_tanh | silu | relu
+    enc_qkv_fused: bool = True     # False: the same q / k / v rows written as attn_q, attn_k, attn_v
     rand_all: bool = False         # every parameter random (forged test models)
     w_std: float = 0.02
     cond_std: float = 0.02         # cond_proj / adaln / act_embed init std
@@ -115,6 +116,17 @@ class _Gen:
             b = self.rng.normal(0.0, s, n_out) if self.spec.rand_all else np.zeros(n_out)
             self.tensor(name + ".bias", b.astype(np.float32))
 
+    def lin_split(self, names: list, n_in: int, n_out: int) -> None:
+        """lin() of one [n_out][n_in] linear (the same draws), written as len(names) linears of equal row slices."""
+        s = self.spec.w_std
+        wt = self.rng.normal(0.0, s, (n_out, n_in)).astype(np.float32)
+        b = (self.rng.normal(0.0, s, n_out) if self.spec.rand_all else np.zeros(n_out)).astype(np.float32)
+        k = n_out // len(names)
+        for i, nm in enumerate(names):
+            self.tensor(nm + ".weight", np.ascontiguousarray(wt[i * k:(i + 1) * k]))
+        for i, nm in enumerate(names):
+            self.tensor(nm + ".bias", np.ascontiguousarray(b[i * k:(i + 1) * k]))
+
     def norm(self, name: str, d: int) -> None:
         if self.spec.rand_all:
             self.tensor(name + ".weight", (1.0 + self.rng.normal(0.0, 0.1, d)).astype(np.float32))
@@ -147,7 +159,7 @@ def write_hjepa(path: str, spec: HJepaSpec, seed: int = 0) -> None:
     w.add_kv("jepa.enc.act", spec.enc_act)
     w.add_kv("jepa.enc.pos_type", "learned")
     w.add_kv("jepa.enc.cls_token", True)
-    w.add_kv("jepa.enc.qkv_fused", True)
+    w.add_kv("jepa.enc.qkv_fused", spec.enc_qkv_fused)
     # hierarchy metadata: one array entry per level, level 1 first
     w.add_kv("jepa.hjepa.n_levels", len(L))
     w.add_kv("jepa.hjepa.ln_eps", 1e-5)
@@ -183,7 +195,10 @@ def write_hjepa(path: str, spec: HJepaSpec, seed: int = 0) -> None:
     for i in range(spec.enc_layers):
         p = f"enc.blk.{i}."
         g.norm(p + "ln1", Dv)
-        g.lin(p + "attn_qkv", Dv, 3 * Dv)
+        if spec.enc_qkv_fused:
+            g.lin(p + "attn_qkv", Dv, 3 * Dv)
+        else:
+            g.lin_split([p + "attn_q", p + "attn_k", p + "attn_v"], Dv, 3 * Dv)
         g.lin(p + "attn_out", Dv, Dv)
         g.norm(p + "ln2", Dv)
         g.lin(p + "ffn_up", Dv, ef)

@@ -95,3 +95,35 @@ def test_gpu_encode_refuses_what_does_not_fit(planners):
         P.encode(np.zeros((1, 1, 224, 224), np.float32))
     with pytest.raises(RuntimeError, match="multiple of the patch size"):
         P.encode(np.zeros((1, 3, 225, 224), np.float32))
+
+
+def _split_qkv_model(tmp_path):
+    """Model 'ea' with every block's q / k / v rows written as attn_q, attn_k, attn_v (qkv_fused = false)."""
+    import dataclasses as dc
+    from jepa_b200 import synth
+    spec, seed, _ = MG.model_specs()["ea"]
+    path = str(tmp_path / "ea-split.gguf")
+    synth.write_hjepa(path, dc.replace(spec, enc_qkv_fused=False), seed=seed)
+    return path
+
+
+def test_split_qkv_model_holds_the_fused_rows(models, tmp_path):
+    """The forged split model carries exactly the fused model's q / k / v rows (the generator's draws)."""
+    Tf, _ = EO.load_tensors(models["ea"])
+    Ts, meta = EO.load_tensors(_split_qkv_model(tmp_path))
+    assert meta["jepa.enc.qkv_fused"] is False or meta["jepa.enc.qkv_fused"] == 0
+    for i in range(2):
+        b = f"enc.blk.{i}."
+        for part in ("weight", "bias"):
+            cat = np.concatenate([Ts[b + f"attn_{x}.{part}"] for x in "qkv"], 0)
+            assert np.array_equal(cat, Tf[b + f"attn_qkv.{part}"])
+
+
+@pytest.mark.gpu
+def test_gpu_encode_with_separate_q_k_v(tmp_path):
+    """A file with q, k and v as three linears (src/jepa.cpp:409-412) encodes as its fused twin: the golden 'ea'."""
+    from jepa_b200.hjepa import Planner
+    P = Planner(_split_qkv_model(tmp_path))
+    y = P.encode(MG.images("ea"))
+    P.close()
+    assert rel(y, GOLDEN["ea"]) < 1e-4
