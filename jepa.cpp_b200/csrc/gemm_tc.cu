@@ -1283,8 +1283,6 @@ int p_splits(int N, int K) {
 
 }  // namespace
 
-bool gemm_blocks_pay(int N, int K) { return !(N >= 4096 || (N >= 768 && K >= 768)); }
-
 size_t gemm_fixup_floats(int M, int N, int K) {
     const int s = p_splits(N, K);
     return s > 1 ? (size_t) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN) * s * (BM * PBN) : 0;

@@ -82,10 +82,6 @@ int quant_planes(uint32_t type, const void * raw, int64_t rows, int64_t ne0, voi
 // Whether the GEMM can read W [rows][ne0] of this type in its block planes, forward (N = rows, K = ne0)
 // or transposed (N = ne0, K = rows).
 bool quant_ok(uint32_t type, int64_t rows, int64_t ne0);
-// Whether a product of this (N, K) runs on the 64-wide split-K kernel, where block planes cost little
-// (measured ~8 % per launch at 256 x 384 x 384); the persistent kernel's products (N >= 4096, or N and K
-// >= 768) pay 1.35 - 1.5x for them, their raw tile sharing a full stage's shared memory.
-bool gemm_blocks_pay(int N, int K);
 
 // Returns 0, or -1 after logging (unsupported shape / a CUDA error).
 int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const GemmEpi & ep, cudaStream_t st);

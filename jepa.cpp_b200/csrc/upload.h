@@ -3,9 +3,11 @@
 // device, bit-exact with the block formats), or the GGUF block planes the GEMM dequantises in its mainloop
 // (q8_0, q4_0, f16; 2.06 B per weight for both orientations of a q8_0 weight, against 16 for the planes).
 // JEPA_B200_WEIGHT_LAYOUT chooses: "planes", "blocks" (every orientation the block planes serve), or "auto"
-// (the default: block planes for the products of the 64-wide split-K kernel, hi / lo planes for the
-// persistent kernel's). Both layouts give the same bits. Every allocation goes into the owner's list, which
-// frees them.
+// (the default): hi / lo planes, the faster layout on every product measured (block planes cost 3-10 % of a
+// plan on the 64-wide split-K products and 1.35-1.5x per launch on the persistent kernel's), unless the
+// planes of the model's quantised weights would take more than a quarter of the device's free memory --
+// then block planes everywhere they serve. Both layouts give the same bits. Every allocation goes into the
+// owner's list, which frees them.
 #pragma once
 
 #include "hplan.h"
@@ -32,13 +34,26 @@ inline int weight_layout() {
     return WL_AUTO;
 }
 
+// The layout "auto" resolves to for a model on the current device: planes unless the hi / lo planes and f32
+// copies of its quantised and f16 matrices (24 B per value) would take more than a quarter of the free memory.
+inline int resolve_layout(int layout, const jepa_model & m) {
+    if (layout != WL_AUTO) return layout;
+    size_t values = 0;
+    for (const gguf_tensor & t : m.file->tensors) {
+        if ((t.type == 8 || t.type == 2 || t.type == 1) && t.n_dims == 2) values += (size_t) t.nelements();
+    }
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) { cudaGetLastError(); return WL_PLANES; }
+    return 24 * values > free_b / 4 ? WL_BLOCKS : WL_PLANES;
+}
+
 struct Uploader {
     std::vector<void *> & allocs;   // every allocation, freed by the owner
     const jepa_model & m;
     cudaStream_t st;
     bool ok = true;
     std::vector<void *> temps;
-    int layout = weight_layout();
+    int layout = resolve_layout(weight_layout(), m);
     size_t block_bytes = 0, plane_bytes = 0;   // device bytes of the two operand layouts uploaded
 
     template <class T> T * alloc(size_t n) {
@@ -130,10 +145,7 @@ struct Uploader {
     }
     // which orientations of a [rows][in] weight of this type take block planes
     void choose(uint32_t type, int64_t rows, int64_t in, bool & fwd, bool & bwd) const {
-        fwd = bwd = false;
-        if (layout == WL_PLANES || !quant_ok(type, rows, in)) return;
-        fwd = layout == WL_BLOCKS || gemm_blocks_pay((int) rows, (int) in);
-        bwd = layout == WL_BLOCKS || gemm_blocks_pay((int) in, (int) rows);
+        fwd = bwd = layout == WL_BLOCKS && quant_ok(type, rows, in);
     }
     // out(V(h)) as one linear: W_ov = W_out W_v (a 3xTF32 product on the device), b_ov = W_out b_v + b_out
     DLin compose(const DLin & v, const DLin & out) {

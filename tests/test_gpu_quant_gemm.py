@@ -95,8 +95,8 @@ def test_block_planes_refuse_partial_blocks():
 @pytest.mark.parametrize("ftype", ["q8_0", "q4_0", "f16"])
 @pytest.mark.parametrize("width,ffn,heads", [(384, 1536, 6), (768, 3072, 12)])
 def test_planner_weight_layouts_give_the_same_bits(tmp_path, monkeypatch, ftype, width, ffn, heads):
-    """The planner with its linears in hi / lo planes, in block planes everywhere, and in the default mixed
-    layout (block planes for the 64-wide split-K products) returns identical costs and action gradients."""
+    """The planner with its linears in hi / lo planes, in block planes everywhere, and in the default layout
+    (planes unless they would crowd the device's memory) returns identical costs and action gradients."""
     from jepa_b200 import synth
     from jepa_b200.hjepa import Planner
     spec = synth.HJepaSpec(levels=[synth.Level(width, 2, heads, ffn, 2)], ftype=ftype, name="layouts")
