@@ -1346,13 +1346,18 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
     }
     GemmEpi e = ep;
     e.vec = vec_ok(ep, N) ? 1 : 0;
-    // The tile shape and the K split depend on (N, K) only, never on M: a row's arithmetic (and so its
-    // bits) is then the same whatever batch of rows it is computed in.
+    // The tile shape and the K split depend on (N, K), and for the wide products on one row threshold: a row's
+    // arithmetic (and so its bits) is the same in every batch on the same side of it.
     // Wide outputs (the adaLN modulation of every step at once) and wide products (output and reduction both
     // at least 768: the widest predictors, which plan thousands of candidates, so there are tiles enough to
-    // fill the device) take the persistent kernel's 128 x 128 tiles and no K split: twice the columns per A
-    // tile read, no exchange, and each tile's epilogue overlapping the next tile's products.
-    if (N >= 4096 || (N >= 768 && K >= 768)) {
+    // fill the device) take the persistent kernel's 128 x 128 tiles: twice the columns per A tile read, no
+    // exchange, and each tile's epilogue overlapping the next tile's products. With at most two row tiles
+    // (a 4096-candidate level split over 8 GPUs: two chains of 256 rows) a product narrower than 4096 has
+    // too few such tiles for the device and takes the split-K clusters below instead (measured at 256 rows, us
+    // per launch: N 768 K 768 15.7 -> 7.8, N 3072 K 768 15.7 -> 14.0, N 768 K 3072 23.7 -> 14.1, N 768
+    // K 55,296 317 -> 153; at 384 rows and more the persistent kernel wins or ties).
+    const bool few_rows = M <= 2 * BM && N < 4096;
+    if ((N >= 4096 || (N >= 768 && K >= 768)) && !few_rows) {
         int splits = p_splits(N, K);
         if (splits > 1 && (!ep.fix || !ep.fix_count || ep.fix_floats < gemm_fixup_floats(M, N, K) ||
                            ep.fix_counters < gemm_fixup_counters(M, N, K))) {
