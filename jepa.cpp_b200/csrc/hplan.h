@@ -125,7 +125,8 @@ struct Workspace {
     long long gen = 0;                // creation number (keys the graphs that span several workspaces)
     // step-at-a-time modulation (when every step's [T S][6PL] modulation and its gradient do not fit): the
     // adaLN GEMM runs per step in the forward and again in the backward, dmod is folded into dcs per step.
-    // Bit-identical to the all-steps mode (a GEMM row does not depend on the batch it is in).
+    // Bit-identical to the all-steps mode while the step's rows and all steps' rows take the same GEMM kernel
+    // (always below 768 wide; at 768 and wider, when a step has more than 256 rows), else equal to rounding.
     bool step_mod = false;
     // within step_mod: every step's forward modulation is still kept ([T S][6PL], one copy), so the backward
     // reads it instead of recomputing it; only the gradient is folded per step (dmod holds one step's rows)

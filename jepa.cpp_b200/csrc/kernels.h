@@ -88,7 +88,8 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
 // The persistent kernel splits the K range of narrow, long products (at most 8 column tiles, K >= 2048) in
 // GEMM_KSPLIT parts when the caller passes fix-up scratch: each part's partial tile goes to the scratch and
 // the last part to finish sums the parts in a fixed order and applies the epilogue. The split depends on
-// (N, K) only, so a row's bits still do not depend on the batch. These give the scratch a call needs:
+// (N, K) only. (Which kernel a wide product takes also depends on whether it has at most 256 rows: a row's
+// bits are the same in every batch on one side of that threshold.) These give the scratch a call needs:
 // partial-tile floats and tile counters (0 when the shape is not split).
 constexpr int GEMM_KSPLIT = 3;
 constexpr int GEMM_KSPLIT_MAX = 4;   // the most parts the persistent kernel's fix-up sums
