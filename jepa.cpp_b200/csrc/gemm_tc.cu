@@ -758,6 +758,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__
 constexpr int PBN = 128, PSTAGES = 3, PEPI_WARPS = 8, PTHREADS = 64 + 32 * PEPI_WARPS;
 constexpr int PTHREADS_QB = PTHREADS + 32 * PCONV_WARPS;   // with the converter warps
 constexpr int FIX_ROWS = 4;   // K-split fix-up: row groups of partial tiles loaded at once per lane
+constexpr int PGROUP_M = 16;  // row tiles per group of the m-fastest tile order (2048 rows: 12.6 MB of A planes at K = 768)
 constexpr uint32_t PSTAGE_BYTES = 2 * BM * BK * 4 + 2 * PBN * BK * 4;
 constexpr size_t PSMEM_BYTES = (size_t) PSTAGES * PSTAGE_BYTES + (size_t) PEPI_WARPS * 32 * 32 * 4 + 1024;
 static_assert(PSMEM_BYTES + 256 <= 227 * 1024, "persistent tf32x3 GEMM: stages and staging buffers fit");
@@ -766,7 +767,7 @@ template <int MODE, bool QB>
 __global__ void __launch_bounds__(QB ? PTHREADS_QB : PTHREADS, 1)
 k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
                 const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
-                int M, int N, int K, int splits, const QDesc qd, const __grid_constant__ GemmEpi ep) {
+                int M, int N, int K, int splits, int m_fast, const QDesc qd, const __grid_constant__ GemmEpi ep) {
     constexpr uint32_t A_BYTES = BM * BK * 4;
     constexpr uint32_t B_BYTES = PBN * BK * 4;
     constexpr uint32_t TMEM_COLS = 4 * PBN;   // two accumulator pairs [hi*hi | cross terms], 256 columns each
@@ -788,9 +789,23 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_k = (K + BK - 1) / BK;
-    const int tiles_n = (N + PBN - 1) / PBN;
+    const int tiles_n = (N + PBN - 1) / PBN, tiles_m = (M + BM - 1) / BM;
     // work units: unit u is K-part u % splits of output tile u / splits (splits == 1: whole tiles): a tile's parts
-    // run side by side, its A rows and B slice shared in L2
+    // run side by side, its A rows and B slice shared in L2. Tiles in n-fastest order (the CTAs side by side
+    // share an A row tile) or, for a wide output whose B operand is too large to stay in L2 (m_fast), in
+    // groups of PGROUP_M row tiles walked m-fastest: the CTAs side by side share a B column tile, read from
+    // DRAM once per group rather than once per row tile, and the group's A rows stay in L2
+    auto tile_origin = [&](int t, int & m0, int & n0) {
+        if (m_fast) {
+            const int g = t / (PGROUP_M * tiles_n), r = t - g * PGROUP_M * tiles_n;
+            const int gm = min(PGROUP_M, tiles_m - g * PGROUP_M);
+            m0 = (g * PGROUP_M + r % gm) * BM;
+            n0 = (r / gm) * PBN;
+        } else {
+            m0 = (t / tiles_n) * BM;
+            n0 = (t % tiles_n) * PBN;
+        }
+    };
     const int total = ((M + BM - 1) / BM) * tiles_n * splits;
     const int kq = (num_k + splits - 1) / splits;
     const bool qb = QB && qd.fmt != QF_NONE;   // block planes (a template switch: the plane kernels carry no converter code)
@@ -830,7 +845,8 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
             int kt = 0;
             for (int u = blockIdx.x; u < total && !*(volatile int *) &abort_sh; u += gridDim.x) {
                 const int t = u / splits, part = u % splits;
-                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * PBN;
+                int m0, n0;
+                tile_origin(t, m0, n0);
                 const int kb = part * kq, ke = min(num_k, kb + kq);
                 for (int k = kb; k < ke; k++, kt++) {
                     const int s = kt % PSTAGES;
@@ -934,7 +950,8 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
                 abort_sh = 1;
                 break;
             }
-            const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * PBN;
+            int m0, n0;
+            tile_origin(t, m0, n0);
             const int row0 = m0 + q * 32;
             if (splits > 1) {
                 // this part's partial tile (hi*hi + cross terms) into its scratch slot, row-major
@@ -1220,6 +1237,14 @@ int launch(const SplitMat & A, const SplitMat & B, int M, int N, int K, int spli
     return 0;
 }
 
+// The persistent kernel's tile order: grouped m-fastest for wide outputs (N >= 4096) whose B operand (N x K
+// hi / lo planes) is too large to stay in L2 (above 48 MB: the adaLN modulation's 340 MB at config 5), when there
+// is more than one row tile; n-fastest otherwise. Measured at N 55,296 K 768: 2048 rows 904 -> 616 us, 8192 rows
+// 3577 -> 2475 us; the narrow adaLN backward (N 768) keeps n-fastest (626 against 650 us m-fastest).
+int p_tile_order(int M, int N, int K) {
+    return N >= 4096 && (size_t) N * (size_t) K * 8 > ((size_t) 48 << 20) && (M + BM - 1) / BM > 1 ? 1 : 0;
+}
+
 template <int MODE>
 int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, int splits, const GemmEpi & ep, cudaStream_t st) {
     if (splits < 1 || splits > GEMM_KSPLIT_MAX) { log("jepa: gemm: %d K parts (at most %d)\n", splits, GEMM_KSPLIT_MAX); return -1; }
@@ -1246,12 +1271,13 @@ int launch_p(const SplitMat & A, const SplitMat & B, int M, int N, int K, int sp
     }
     const long units = (long) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN) * splits;
     const unsigned grid = (unsigned) std::max(1L, std::min<long>(units, sms[dev]));
+    const int m_fast = p_tile_order(M, N, K);
     if (qd.fmt != QF_NONE) {
         JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE, true>, dim3(grid), dim3(PTHREADS_QB), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo,
-                           M, N, K, splits, qd, ep));
+                           M, N, K, splits, m_fast, qd, ep));
     } else {
         JB_CUDA(launch_pdl(k_gemm_tf32x3_p<MODE, false>, dim3(grid), dim3(PTHREADS), PSMEM_BYTES, st, ta_hi, ta_lo, tb_hi, tb_lo,
-                           M, N, K, splits, qd, ep));
+                           M, N, K, splits, m_fast, qd, ep));
     }
     return 0;
 }
