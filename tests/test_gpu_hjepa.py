@@ -67,8 +67,8 @@ def test_plan_cost_matches_oracle(tmpdir_mod, ftype, level, goal_level, T, dense
 
 
 def wide(tmp, ftype):
-    """A predictor 768 wide (one block, MLP 768): its per-step products and its adaLN GEMM (6 x 768 outputs)
-    take the 128-wide unsplit tiles, every epilogue mode included."""
+    """A predictor 768 wide (one block, MLP 768): with more than 256 rows its per-step products and its adaLN
+    GEMM (6 x 768 outputs) take the persistent kernel's 128-wide tiles, every epilogue mode included."""
     spec = synth.HJepaSpec(levels=[synth.Level(768, 1, 12, 768, 2)], ftype=ftype, rand_all=True, cond_std=0.3, w_std=0.03)
     path = os.path.join(tmp, f"wide-{ftype}.gguf")
     if not os.path.exists(path):
@@ -84,15 +84,19 @@ def test_wide_predictor_matches_oracle(tmpdir_mod, ftype):
     rng = np.random.default_rng(31)
     s0 = rng.normal(size=768).astype(np.float32)
     goal = rng.normal(size=(1, 768)).astype(np.float32)
-    acts = rng.uniform(-1, 1, (37, 3, 2)).astype(np.float32)
+    # 300 candidates: the persistent kernel's tiles (more than 256 rows), every fused epilogue of the block
+    acts = rng.uniform(-1, 1, (300, 3, 2)).astype(np.float32)
     costs, grad = P.plan_cost(1, s0, goal, acts)
     oc, og, _ = O.batch_cost(m, O.CostSpec(level=1, horizon=3, s0=s0, goal=goal), acts)
     assert rel_err(costs, oc) < REL, rel_err(costs, oc)
     assert rel_err(grad, og) < REL, rel_err(grad, og)
-    # unsplit tiles: a row's bits do not depend on the batch either
-    c_sub, g_sub = P.plan_cost(1, s0, goal, np.ascontiguousarray(acts[5:20]))
-    assert np.array_equal(costs[5:20], c_sub)
-    assert np.array_equal(grad[5:20], g_sub)
+    # a row's bits do not depend on the batch among batches of more than 256 rows either
+    c_sub, g_sub = P.plan_cost(1, s0, goal, np.ascontiguousarray(acts[5:270]))
+    assert np.array_equal(costs[5:270], c_sub)
+    assert np.array_equal(grad[5:270], g_sub)
+    # 256 rows and fewer take the split-K clusters: the same rows agree to rounding
+    c_few, g_few = P.plan_cost(1, s0, goal, np.ascontiguousarray(acts[5:20]))
+    assert rel_err(c_few, costs[5:20]) < REL and rel_err(g_few, grad[5:20]) < REL
 
 
 def test_rows_do_not_depend_on_the_batch(tmpdir_mod):
