@@ -622,7 +622,8 @@ def run_hjepa(args, rank, world, local, dist):
         if world == 1 and not args.no_cpu_baseline:
             try:
                 threads = os.cpu_count() or 1
-                rate, secs, sample = reference_rate(path, spec, plans, S, threads, len(plans), 1)
+                # the reference arm's warm-up count, then one evaluation per level
+                rate, secs, sample = reference_rate(path, spec, plans, S, threads, len(plans), max(1, args.warmup))
                 if rate is not None:
                     res["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": threads, "kind": "reference",
                                            "sample": sample}
