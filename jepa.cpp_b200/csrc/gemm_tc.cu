@@ -216,13 +216,6 @@ __device__ __forceinline__ uint32_t cluster_rank() {
     return r;
 }
 
-__device__ __forceinline__ float4 ld_peer4(uint32_t local_saddr, uint32_t rank) {
-    uint32_t remote;
-    float4 v;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_saddr), "r"(rank));
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(remote) : "memory");
-    return v;
-}
 
 __device__ __forceinline__ uint32_t peer_addr(uint32_t local_saddr, uint32_t rank) {
     uint32_t remote;
@@ -1097,15 +1090,14 @@ bool make_map(CUtensorMap * map, const float * base, int rows, int cols, int ld,
     return r == CUDA_SUCCESS;
 }
 
-// a row-major 2-D map without swizzle over raw block values or scales: `inner` elements per row of
-// `esize` bytes, rows `stride` bytes apart, boxes of box_inner x box_rows
-bool make_raw_map(CUtensorMap * map, const void * base, CUtensorMapDataType dt, int esize, uint64_t inner, uint64_t rows,
+// a row-major 2-D map without swizzle over raw block values or scales: `inner` elements of type dt per row,
+// rows `stride` bytes apart, boxes of box_inner x box_rows
+bool make_raw_map(CUtensorMap * map, const void * base, CUtensorMapDataType dt, uint64_t inner, uint64_t rows,
                   uint64_t stride, uint32_t box_inner, uint32_t box_rows) {
     const cuuint64_t dims[2] = {(cuuint64_t) inner, (cuuint64_t) rows};
     const cuuint64_t strides[1] = {(cuuint64_t) stride};
     const cuuint32_t box[2] = {box_inner, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    (void) esize;
     return g_encode(map, dt, 2, (void *) base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1123,12 +1115,12 @@ bool make_b_maps(const SplitMat & B, int N, int K, int bn, CUtensorMap * t0, CUt
     qd->fmt = q.fmt;
     qd->orient = q.orient;
     bool ok;
-    if (q.fmt == QF_Q8) ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t) K, (uint64_t) N, (uint64_t) K, 32, (uint32_t) bn);
-    else if (q.fmt == QF_Q4) ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t) K / 2, (uint64_t) N, (uint64_t) K / 2, 16, (uint32_t) bn);
-    else ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t) K, (uint64_t) N, (uint64_t) K * 2, 32, (uint32_t) bn);
+    if (q.fmt == QF_Q8) ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t) K, (uint64_t) N, (uint64_t) K, 32, (uint32_t) bn);
+    else if (q.fmt == QF_Q4) ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t) K / 2, (uint64_t) N, (uint64_t) K / 2, 16, (uint32_t) bn);
+    else ok = make_raw_map(t0, q.q, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t) K, (uint64_t) N, (uint64_t) K * 2, 32, (uint32_t) bn);
     if (ok && q.fmt != QF_F16) {
-        ok = q.orient == 0 ? make_raw_map(t1, q.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t) N, (uint64_t) K / 32, (uint64_t) N * 2, (uint32_t) bn, 1)
-                           : make_raw_map(t1, q.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t) K, (uint64_t) N / 32, (uint64_t) K * 2, 32, (uint32_t) bn / 32);
+        ok = q.orient == 0 ? make_raw_map(t1, q.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t) N, (uint64_t) K / 32, (uint64_t) N * 2, (uint32_t) bn, 1)
+                           : make_raw_map(t1, q.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t) K, (uint64_t) N / 32, (uint64_t) K * 2, 32, (uint32_t) bn / 32);
     } else if (ok) {
         *t1 = *t0;   // f16: no scales (the map is never used)
     }

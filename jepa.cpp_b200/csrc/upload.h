@@ -121,8 +121,9 @@ struct Uploader {
         const int64_t ne0 = t->ne[0];
         const size_t rb = row_bytes(t->type, ne0), nq = quant_plane_bytes(t->type, rows, ne0);
         const size_t nd = quant_scale_count(t->type, rows, ne0);
+        // the orientation not kept is written to a temporary (quant_planes fills both)
         void * raw = nullptr, * spare = nullptr;
-        if (cudaMalloc(&raw, rb * (size_t) rows) != cudaSuccess || cudaMalloc(&spare, nq) != cudaSuccess) {
+        if (cudaMalloc(&raw, rb * (size_t) rows) != cudaSuccess || (!(fwd && bwd) && cudaMalloc(&spare, nq) != cudaSuccess)) {
             cudaGetLastError();
             if (raw) cudaFree(raw);
             ok = false;
@@ -135,7 +136,7 @@ struct Uploader {
                     quant_planes(t->type, raw, rows, ne0, q, qt, d, st) == 0;
         good = cuda_ok(cudaStreamSynchronize(st), "block planes") && good;
         cudaFree(raw);
-        cudaFree(spare);
+        if (spare) cudaFree(spare);
         ok = ok && good;
         if (!ok) return;
         const int fmt = t->type == 8 ? QF_Q8 : t->type == 2 ? QF_Q4 : QF_F16;
