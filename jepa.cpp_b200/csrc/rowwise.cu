@@ -257,6 +257,24 @@ __device__ __forceinline__ double row_sum(double v, const RowPos<W> & p) {
     return s;
 }
 
+// two row sums at once (the same sums in the same order as two row_sum calls: the same bits), one exchange
+// through shared memory instead of two
+template <int W>
+__device__ __forceinline__ void row_sum2(double & a, double & b, const RowPos<W> & p) {
+    a = warp_sum(a);
+    b = warp_sum(b);
+    if (W == 1) return;
+    __shared__ double red2[8][W][2];
+    if (p.lane == 0) { red2[p.rr][p.wir][0] = a; red2[p.rr][p.wir][1] = b; }
+    __syncthreads();
+    double sa = red2[p.rr][0][0], sb = red2[p.rr][0][1];
+#pragma unroll
+    for (int w = 1; w < W; w++) { sa += red2[p.rr][w][0]; sb += red2[p.rr][w][1]; }
+    __syncthreads();
+    a = sa;
+    b = sb;
+}
+
 template <int V, int W>
 __device__ __forceinline__ void stats_of(const float (&v)[V], int D, const RowPos<W> & p, float eps, double & mean, float & inv) {
     double s = 0;
@@ -380,8 +398,9 @@ k_layer_norm_bwd_v(const float * __restrict__ gy, int ldgy, const float * __rest
         m1 += gh[k];
         m2 += (double) gh[k] * xh[k];
     }
-    m1 = row_sum<W>(m1, p) / D;
-    m2 = row_sum<W>(m2, p) / D;
+    row_sum2<W>(m1, m2, p);
+    m1 = m1 / D;
+    m2 = m2 / D;
     if (!valid) return;
 #pragma unroll
     for (int k = 0; k < V; k++) {
@@ -441,8 +460,9 @@ __global__ void __launch_bounds__(32 * W * rows_per_block<W>()) k_block_bwd_v(Bl
             n1 += gz[k];
             n2 += (double) gz[k] * z[k];
         }
-        n1 = row_sum<W>(n1, p) / D;
-        n2 = row_sum<W>(n2, p) / D;
+        row_sum2<W>(n1, n2, p);
+        n1 = n1 / D;
+        n2 = n2 / D;
 #pragma unroll
         for (int k = 0; k < V; k++) gz[k] = (float) (((double) gz[k] - n1 - (double) z[k] * n2) * (double) s1.inv);
     }
@@ -461,8 +481,9 @@ __global__ void __launch_bounds__(32 * W * rows_per_block<W>()) k_block_bwd_v(Bl
         m1 += gz[k];
         m2 += (double) gz[k] * xh[k];
     }
-    m1 = row_sum<W>(m1, p) / D;
-    m2 = row_sum<W>(m2, p) / D;
+    row_sum2<W>(m1, m2, p);
+    m1 = m1 / D;
+    m2 = m2 / D;
     if (!valid) return;
 #pragma unroll
     for (int k = 0; k < V; k++) {
