@@ -242,35 +242,36 @@ __device__ __forceinline__ void load_row(const float * __restrict__ p, int D, in
     for (int k = 0; k < V; k++) { const int i = t + 32 * W * k; v[k] = i < D ? p[i] : 0.0f; }
 }
 
-// the sum of a row's per-thread partials (every thread of the block calls it, valid row or not)
+// The sum of a row's per-thread partials (every thread of the block calls it, valid row or not). The W warp
+// partials go through one of two shared slots, which calls alternate: a slot is written again only two
+// reductions later, after the intervening reduction's barrier, which every thread reaches after its reads of
+// this one -- so one barrier per reduction suffices.
 template <int W>
-__device__ __forceinline__ double row_sum(double v, const RowPos<W> & p) {
+__device__ __forceinline__ double row_sum(double v, const RowPos<W> & p, int slot) {
     v = warp_sum(v);
     if (W == 1) return v;
-    __shared__ double red[8][W];
-    if (p.lane == 0) red[p.rr][p.wir] = v;
+    __shared__ double red[2][8][W];
+    if (p.lane == 0) red[slot][p.rr][p.wir] = v;
     __syncthreads();
-    double s = red[p.rr][0];
+    double s = red[slot][p.rr][0];
 #pragma unroll
-    for (int w = 1; w < W; w++) s += red[p.rr][w];
-    __syncthreads();
+    for (int w = 1; w < W; w++) s += red[slot][p.rr][w];
     return s;
 }
 
 // two row sums at once (the same sums in the same order as two row_sum calls: the same bits), one exchange
 // through shared memory instead of two
 template <int W>
-__device__ __forceinline__ void row_sum2(double & a, double & b, const RowPos<W> & p) {
+__device__ __forceinline__ void row_sum2(double & a, double & b, const RowPos<W> & p, int slot) {
     a = warp_sum(a);
     b = warp_sum(b);
     if (W == 1) return;
-    __shared__ double red2[8][W][2];
-    if (p.lane == 0) { red2[p.rr][p.wir][0] = a; red2[p.rr][p.wir][1] = b; }
+    __shared__ double red2[2][8][W][2];
+    if (p.lane == 0) { red2[slot][p.rr][p.wir][0] = a; red2[slot][p.rr][p.wir][1] = b; }
     __syncthreads();
-    double sa = red2[p.rr][0][0], sb = red2[p.rr][0][1];
+    double sa = red2[slot][p.rr][0][0], sb = red2[slot][p.rr][0][1];
 #pragma unroll
-    for (int w = 1; w < W; w++) { sa += red2[p.rr][w][0]; sb += red2[p.rr][w][1]; }
-    __syncthreads();
+    for (int w = 1; w < W; w++) { sa += red2[slot][p.rr][w][0]; sb += red2[slot][p.rr][w][1]; }
     a = sa;
     b = sb;
 }
@@ -280,11 +281,11 @@ __device__ __forceinline__ void stats_of(const float (&v)[V], int D, const RowPo
     double s = 0;
 #pragma unroll
     for (int k = 0; k < V; k++) if (p.t + 32 * W * k < D) s += (double) v[k];
-    mean = row_sum<W>(s, p) / D;
+    mean = row_sum<W>(s, p, 0) / D;
     double q = 0;
 #pragma unroll
     for (int k = 0; k < V; k++) if (p.t + 32 * W * k < D) { const double c = (double) v[k] - mean; q += c * c; }
-    inv = (float) (1.0 / sqrt(row_sum<W>(q, p) / D + (double) eps));
+    inv = (float) (1.0 / sqrt(row_sum<W>(q, p, 1) / D + (double) eps));
 }
 
 template <int W> __host__ __device__ constexpr int rows_per_block() { return W == 1 ? FAST_ROWS : WIDE_ROWS; }
@@ -398,7 +399,7 @@ k_layer_norm_bwd_v(const float * __restrict__ gy, int ldgy, const float * __rest
         m1 += gh[k];
         m2 += (double) gh[k] * xh[k];
     }
-    row_sum2<W>(m1, m2, p);
+    row_sum2<W>(m1, m2, p, 0);
     m1 = m1 / D;
     m2 = m2 / D;
     if (!valid) return;
@@ -460,7 +461,7 @@ __global__ void __launch_bounds__(32 * W * rows_per_block<W>()) k_block_bwd_v(Bl
             n1 += gz[k];
             n2 += (double) gz[k] * z[k];
         }
-        row_sum2<W>(n1, n2, p);
+        row_sum2<W>(n1, n2, p, 0);
         n1 = n1 / D;
         n2 = n2 / D;
 #pragma unroll
@@ -481,7 +482,7 @@ __global__ void __launch_bounds__(32 * W * rows_per_block<W>()) k_block_bwd_v(Bl
         m1 += gz[k];
         m2 += (double) gz[k] * xh[k];
     }
-    row_sum2<W>(m1, m2, p);
+    row_sum2<W>(m1, m2, p, 1);   // (slot 0: the inner LayerNorm's sums)
     m1 = m1 / D;
     m2 = m2 / D;
     if (!valid) return;
