@@ -244,10 +244,9 @@ struct QDesc {
 // converter warps: four in the split-K cluster kernel (its reduction warps are idle in the mainloop), PCONV_WARPS
 // in the persistent kernel (added warps: its register budget caps them)
 constexpr int CONV_WARPS = 4;
-#ifndef JB_PCONV_WARPS
-#define JB_PCONV_WARPS 2
-#endif
-constexpr int PCONV_WARPS = JB_PCONV_WARPS;
+// (two, 384 threads, no spill; four at 448 threads measured 22.8 against 24-25 us per launch at 2048 x 768 x 768
+// but cap the kernel at 128 registers, which spills its epilogue)
+constexpr int PCONV_WARPS = 2;
 
 // raw bytes of one row of a K-step (32 values) and of the K-step's scales, for BN rows
 __host__ __device__ constexpr uint32_t raw_row_bytes(int fmt) { return fmt == QF_Q8 ? 32u : fmt == QF_Q4 ? 16u : fmt == QF_F16 ? 64u : 0u; }
