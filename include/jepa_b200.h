@@ -28,6 +28,14 @@ int jepa_b200_gemm(const float * A, const float * B, int M, int N, int K, float 
 // planner passes that scratch on every such product). Agrees with jepa_b200_gemm to rounding.
 int jepa_b200_gemm_ksplit(const float * A, const float * B, int M, int N, int K, float * C);
 
+// The launch the planner's GEMM makes for a product of shape M x N x K, computed on the host (no device
+// needed): out[0] = 1 for the persistent 128 x 128 kernel, 0 for the 64-wide split-K clusters; out[1] = the
+// persistent kernel's K parts in the planner's configuration (1 = whole tiles; 0 for the clusters, whose split
+// follows the device's cluster occupancy); out[2] = 1 when the persistent kernel walks grouped row tiles
+// rows-fastest. A row's bits depend only on this plan, so rows of batches with the same plan agree bit for bit.
+// Returns 0, or -1 for a null `out` or a non-positive size. No counterpart in the reference.
+int jepa_b200_gemm_plan(int M, int N, int K, int * out);
+
 // The planner-configuration product timed on the device: `reps` launches on device-resident operands,
 // returns the mean milliseconds per launch in *ms (CUDA events around the launches).
 int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms);

@@ -1300,6 +1300,24 @@ int p_splits(int N, int K) {
 
 }  // namespace
 
+// Which kernel a product takes (host arithmetic on the shape alone). Wide outputs (the adaLN modulation of
+// every step at once) and wide products (output and reduction both at least 768: the widest predictors,
+// which plan thousands of candidates, so there are tiles enough to fill the device) take the persistent
+// kernel's 128 x 128 tiles: twice the columns per A tile read, no exchange, and each tile's epilogue
+// overlapping the next tile's products. With at most two row tiles (a 4096-candidate level split over 8
+// GPUs: two chains of 256 rows) a product narrower than 4096 has too few such tiles for the device and takes
+// the split-K clusters instead (measured at 256 rows, us per launch: N 768 K 768 15.7 -> 7.8, N 3072 K 768
+// 15.7 -> 14.0, N 768 K 3072 23.7 -> 14.1, N 768 K 55,296 317 -> 153; at 384 rows and more the persistent
+// kernel wins or ties).
+GemmPlan gemm_plan(int M, int N, int K) {
+    GemmPlan p;
+    const bool few_rows = M <= 2 * BM && N < 4096;
+    p.persistent = (N >= 4096 || (N >= 768 && K >= 768)) && !few_rows;
+    p.k_parts = p.persistent ? p_splits(N, K) : 0;
+    p.m_fast = p.persistent ? p_tile_order(M, N, K) : 0;
+    return p;
+}
+
 size_t gemm_fixup_floats(int M, int N, int K) {
     const int s = p_splits(N, K);
     return s > 1 ? (size_t) ((M + BM - 1) / BM) * ((N + PBN - 1) / PBN) * s * (BM * PBN) : 0;
@@ -1365,17 +1383,9 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
     e.vec = vec_ok(ep, N) ? 1 : 0;
     // The tile shape and the K split depend on (N, K), and for the wide products on one row threshold: a row's
     // arithmetic (and so its bits) is the same in every batch on the same side of it.
-    // Wide outputs (the adaLN modulation of every step at once) and wide products (output and reduction both
-    // at least 768: the widest predictors, which plan thousands of candidates, so there are tiles enough to
-    // fill the device) take the persistent kernel's 128 x 128 tiles: twice the columns per A tile read, no
-    // exchange, and each tile's epilogue overlapping the next tile's products. With at most two row tiles
-    // (a 4096-candidate level split over 8 GPUs: two chains of 256 rows) a product narrower than 4096 has
-    // too few such tiles for the device and takes the split-K clusters below instead (measured at 256 rows, us
-    // per launch: N 768 K 768 15.7 -> 7.8, N 3072 K 768 15.7 -> 14.0, N 768 K 3072 23.7 -> 14.1, N 768
-    // K 55,296 317 -> 153; at 384 rows and more the persistent kernel wins or ties).
-    const bool few_rows = M <= 2 * BM && N < 4096;
-    if ((N >= 4096 || (N >= 768 && K >= 768)) && !few_rows) {
-        int splits = p_splits(N, K);
+    const GemmPlan plan = gemm_plan(M, N, K);
+    if (plan.persistent) {
+        int splits = plan.k_parts;
         if (splits > 1 && (!ep.fix || !ep.fix_count || ep.fix_floats < gemm_fixup_floats(M, N, K) ||
                            ep.fix_counters < gemm_fixup_counters(M, N, K))) {
             splits = 1;   // no scratch from the caller: whole tiles

@@ -93,6 +93,15 @@ int gemm_tc(const SplitMat & A, const SplitMat & B, int M, int N, int K, const G
 // partial-tile floats and tile counters (0 when the shape is not split).
 constexpr int GEMM_KSPLIT = 3;
 constexpr int GEMM_KSPLIT_MAX = 4;   // the most parts the persistent kernel's fix-up sums
+// The launch gemm_tc makes for a shape: the persistent 128 x 128 kernel or the 64-wide split-K clusters
+// (whose split is chosen from the device's cluster occupancy at launch); for the persistent kernel, its K
+// parts when the caller passes fix-up scratch, and its tile order (1 = grouped rows-fastest).
+struct GemmPlan {
+    bool persistent = false;
+    int k_parts = 0;
+    int m_fast = 0;
+};
+GemmPlan gemm_plan(int M, int N, int K);
 size_t gemm_fixup_floats(int M, int N, int K);
 size_t gemm_fixup_counters(int M, int N, int K);
 

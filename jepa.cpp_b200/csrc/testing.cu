@@ -95,6 +95,15 @@ extern "C" int jepa_b200_gemm_ksplit(const float * A, const float * B, int M, in
     return gemm_host(A, B, M, N, K, C, true, "jepa_b200_gemm_ksplit");
 }
 
+extern "C" int jepa_b200_gemm_plan(int M, int N, int K, int * out) {
+    if (!out || M <= 0 || N <= 0 || K <= 0) return -1;
+    const jb::GemmPlan p = jb::gemm_plan(M, N, K);
+    out[0] = p.persistent ? 1 : 0;
+    out[1] = p.k_parts;
+    out[2] = p.m_fast;
+    return 0;
+}
+
 namespace {
 
 // a weight's block planes on the device, from its raw GGUF rows (host)

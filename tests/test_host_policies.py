@@ -6,6 +6,9 @@ exactly. Here the receding-horizon schedule (jepa_hjepa_horizons) is compared, o
 horizons, pre-decay horizons, strides, replanning intervals and budgets, with the reference's
 src/hjepa-plan.cpp built unmodified (oracle/_ref). The host GGUF row decoder (gguf.h dequant_row, which
 the oracle's shim also uses) is pinned bit for bit against gguf-py, an independent implementation.
+The GEMM's dispatch (which kernel, how many K parts, which tile order a shape takes) is host arithmetic
+too; its measured rules, and the row threshold that keeps a row's bits independent of its batch, are pinned
+here.
 """
 import ctypes as C
 import os
@@ -84,3 +87,55 @@ def test_host_dequant_rows_match_gguf_py():
         got = np.zeros_like(x)
         assert L.jepa_b200_host_dequant(code, blob.ctypes.data, x.shape[0], x.shape[1], capi.fptr(got)) == 0
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), qt
+
+
+def _gemm_plan(M, N, K):
+    L = jlib.load()
+    L.jepa_b200_gemm_plan.argtypes = [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)]
+    L.jepa_b200_gemm_plan.restype = C.c_int
+    out = (C.c_int * 3)()
+    rc = L.jepa_b200_gemm_plan(M, N, K, out)
+    return rc, tuple(out)
+
+
+# (M, N, K) -> (persistent, K parts, grouped rows-fastest): the measured dispatch rules of the GEMM
+@pytest.mark.parametrize("M,N,K,want", [
+    (300, 768, 768, (1, 1, 0)),        # config 5's widths: persistent, whole tiles
+    (256, 768, 768, (0, 0, 0)),        # at most two row tiles of a narrow output: split-K clusters
+    (257, 768, 768, (1, 1, 0)),        # one row past the threshold
+    (256, 55296, 768, (1, 1, 1)),      # adaLN modulation: wide output, 340 MB of B planes, two row tiles
+    (128, 55296, 768, (1, 1, 0)),      # one row tile: nothing to group
+    (2048, 4608, 768, (1, 1, 0)),      # one layer's modulation: 28 MB of B planes stays in L2
+    (2048, 768, 55296, (1, 3, 0)),     # adaLN backward: narrow, long: K in three parts
+    (1024, 768, 2048, (1, 3, 0)),      # the shortest split K
+    (1024, 768, 2047, (1, 1, 0)),
+    (1024, 1024, 3072, (1, 3, 0)),     # 8 column tiles
+    (1024, 1025, 3072, (1, 1, 0)),     # 9 column tiles: enough to fill the device unsplit
+    (1024, 3072, 3072, (1, 1, 0)),
+    (1024, 512, 4096, (0, 0, 0)),      # narrow output, below 768
+    (1024, 768, 512, (0, 0, 0)),       # short reduction
+    (1024, 4096, 512, (1, 1, 0)),      # wide output, short reduction
+])
+def test_gemm_plan_rules(M, N, K, want):
+    rc, got = _gemm_plan(M, N, K)
+    assert rc == 0 and got == want, (M, N, K, got)
+
+
+def test_gemm_plan_rejects_bad_shapes():
+    assert _gemm_plan(0, 768, 768)[0] == -1
+    assert _gemm_plan(16, -1, 768)[0] == -1
+
+
+def test_gemm_plan_is_constant_on_each_side_of_the_row_threshold():
+    """A row's arithmetic (kernel, K split) depends on the batch only through M <= 256: every batch on one side
+    of it computes a row the same way, which is what makes a candidate's cost independent of how many other
+    candidates share its batch (the tile order changes no value)."""
+    rng = np.random.default_rng(5)
+    shapes = [(768, 768), (768, 3072), (3072, 768), (768, 55296), (55296, 768), (384, 1536), (1536, 384)]
+    shapes += [(int(rng.integers(1, 9000)), int(rng.integers(1, 9000))) for _ in range(40)]
+    for N, K in shapes:
+        small = {_gemm_plan(M, N, K)[1][:2] for M in (1, 17, 128, 129, 200, 256)}
+        large = {_gemm_plan(M, N, K)[1][:2] for M in (257, 300, 1024, 4096, 65536, 131072)}
+        assert len(small) == 1 and len(large) == 1, (N, K, small, large)
+        if N >= 4096:
+            assert small == large, (N, K)
