@@ -36,6 +36,12 @@ int jepa_b200_gemm_ksplit(const float * A, const float * B, int M, int N, int K,
 // Returns 0, or -1 for a null `out` or a non-positive size. No counterpart in the reference.
 int jepa_b200_gemm_plan(int M, int N, int K, int * out);
 
+// The persistent kernel's output tiles for that shape in the order its CTAs take them, computed on the host by
+// the kernel's own tile-origin function: m0[t], n0[t] = first row and column of tile t. Returns the tile
+// count, 0 when the shape takes the split-K clusters, -1 for null buffers, non-positive sizes or more than
+// `cap` tiles. No counterpart in the reference.
+int jepa_b200_gemm_tile_walk(int M, int N, int K, int * m0, int * n0, int cap);
+
 // The planner-configuration product timed on the device: `reps` launches on device-resident operands,
 // returns the mean milliseconds per launch in *ms (CUDA events around the launches).
 int jepa_b200_gemm_bench(int M, int N, int K, int reps, double * ms);

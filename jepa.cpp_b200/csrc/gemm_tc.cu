@@ -755,6 +755,23 @@ constexpr uint32_t PSTAGE_BYTES = 2 * BM * BK * 4 + 2 * PBN * BK * 4;
 constexpr size_t PSMEM_BYTES = (size_t) PSTAGES * PSTAGE_BYTES + (size_t) PEPI_WARPS * 32 * 32 * 4 + 1024;
 static_assert(PSMEM_BYTES + 256 <= 227 * 1024, "persistent tf32x3 GEMM: stages and staging buffers fit");
 
+// Origin (first row, first column) of output tile t in the persistent kernel's walk: n-fastest (the CTAs side
+// by side share an A row tile) or, for m_fast, groups of PGROUP_M row tiles walked m-fastest, the last group
+// holding the row tiles left over (the CTAs side by side share a B column tile). Host and device share it, so
+// the host can check that a walk visits every output tile once.
+__host__ __device__ inline void p_tile_origin(int t, int tiles_m, int tiles_n, int m_fast, int & m0, int & n0) {
+    if (m_fast) {
+        const int g = t / (PGROUP_M * tiles_n), r = t - g * PGROUP_M * tiles_n;
+        const int left = tiles_m - g * PGROUP_M;
+        const int gm = left < PGROUP_M ? left : PGROUP_M;
+        m0 = (g * PGROUP_M + r % gm) * BM;
+        n0 = (r / gm) * PBN;
+    } else {
+        m0 = (t / tiles_n) * BM;
+        n0 = (t % tiles_n) * PBN;
+    }
+}
+
 template <int MODE, bool QB>
 __global__ void __launch_bounds__(QB ? PTHREADS_QB : PTHREADS, 1)
 k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
@@ -783,21 +800,10 @@ k_gemm_tf32x3_p(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant
     const int num_k = (K + BK - 1) / BK;
     const int tiles_n = (N + PBN - 1) / PBN, tiles_m = (M + BM - 1) / BM;
     // work units: unit u is K-part u % splits of output tile u / splits (splits == 1: whole tiles): a tile's parts
-    // run side by side, its A rows and B slice shared in L2. Tiles in n-fastest order (the CTAs side by side
-    // share an A row tile) or, for a wide output whose B operand is too large to stay in L2 (m_fast), in
-    // groups of PGROUP_M row tiles walked m-fastest: the CTAs side by side share a B column tile, read from
-    // DRAM once per group rather than once per row tile, and the group's A rows stay in L2
-    auto tile_origin = [&](int t, int & m0, int & n0) {
-        if (m_fast) {
-            const int g = t / (PGROUP_M * tiles_n), r = t - g * PGROUP_M * tiles_n;
-            const int gm = min(PGROUP_M, tiles_m - g * PGROUP_M);
-            m0 = (g * PGROUP_M + r % gm) * BM;
-            n0 = (r / gm) * PBN;
-        } else {
-            m0 = (t / tiles_n) * BM;
-            n0 = (t % tiles_n) * PBN;
-        }
-    };
+    // run side by side, its A rows and B slice shared in L2. Tiles in n-fastest order, or, for a wide output
+    // whose B operand is too large to stay in L2 (m_fast), in groups of row tiles walked m-fastest: a B column
+    // tile is read from DRAM once per group rather than once per row tile, and the group's A rows stay in L2
+    auto tile_origin = [&](int t, int & m0, int & n0) { p_tile_origin(t, tiles_m, tiles_n, m_fast, m0, n0); };
     const int total = ((M + BM - 1) / BM) * tiles_n * splits;
     const int kq = (num_k + splits - 1) / splits;
     const bool qb = QB && qd.fmt != QF_NONE;   // block planes (a template switch: the plane kernels carry no converter code)
@@ -1316,6 +1322,16 @@ GemmPlan gemm_plan(int M, int N, int K) {
     p.k_parts = p.persistent ? p_splits(N, K) : 0;
     p.m_fast = p.persistent ? p_tile_order(M, N, K) : 0;
     return p;
+}
+
+int gemm_tile_walk(int M, int N, int K, int * m0, int * n0, int cap) {
+    const GemmPlan p = gemm_plan(M, N, K);
+    if (!p.persistent) return 0;
+    const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + PBN - 1) / PBN;
+    const long total = (long) tiles_m * tiles_n;
+    if (total > cap) return -1;
+    for (int t = 0; t < (int) total; t++) p_tile_origin(t, tiles_m, tiles_n, p.m_fast, m0[t], n0[t]);
+    return (int) total;
 }
 
 size_t gemm_fixup_floats(int M, int N, int K) {

@@ -102,6 +102,10 @@ struct GemmPlan {
     int m_fast = 0;
 };
 GemmPlan gemm_plan(int M, int N, int K);
+// The persistent kernel's output tiles in walk order (the kernel's own origin function, run on the host):
+// writes each tile's first row and column, returns the tile count, 0 when the shape takes the split-K
+// clusters, -1 when more than `cap` tiles.
+int gemm_tile_walk(int M, int N, int K, int * m0, int * n0, int cap);
 size_t gemm_fixup_floats(int M, int N, int K);
 size_t gemm_fixup_counters(int M, int N, int K);
 

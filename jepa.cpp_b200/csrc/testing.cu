@@ -104,6 +104,11 @@ extern "C" int jepa_b200_gemm_plan(int M, int N, int K, int * out) {
     return 0;
 }
 
+extern "C" int jepa_b200_gemm_tile_walk(int M, int N, int K, int * m0, int * n0, int cap) {
+    if (!m0 || !n0 || cap < 0 || M <= 0 || N <= 0 || K <= 0) return -1;
+    return jb::gemm_tile_walk(M, N, K, m0, n0, cap);
+}
+
 namespace {
 
 // a weight's block planes on the device, from its raw GGUF rows (host)

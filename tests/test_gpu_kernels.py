@@ -55,6 +55,29 @@ def test_gemm_3xtf32_matches_f64(M, N, K):
     assert err < 1e-5 * max(1.0, K / 1536), err
 
 
+def test_gemm_grouped_tile_order_matches_f64_and_changes_no_value():
+    """A wide output whose B planes do not fit in L2 (N 8192, K 1536: 100 MB) walks groups of 16 row tiles
+    rows-fastest; at 2100 rows the last group holds one ragged row tile. Every tile is computed (f64 check),
+    and a row's bits are those of a 1024-row batch of the same rows (walked in another order)."""
+    L = jlib.load()
+    L.jepa_b200_gemm_plan.argtypes = [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)]
+    M, N, K = 2100, 8192, 1536
+    for m in (M, 1024):
+        plan = (C.c_int * 3)()
+        assert L.jepa_b200_gemm_plan(m, N, K, plan) == 0 and tuple(plan) == (1, 1, 1)
+    rng = np.random.default_rng(77)
+    A = rng.normal(size=(M, K)).astype(np.float32)
+    B = rng.normal(size=(N, K)).astype(np.float32)
+    Cm = np.zeros((M, N), np.float32)
+    assert L.jepa_b200_gemm(capi.fptr(A), capi.fptr(B), M, N, K, capi.fptr(Cm)) == 0, jlib.error_text()
+    ref = A.astype(np.float64) @ B.astype(np.float64).T
+    assert np.abs(Cm - ref).max() / np.abs(ref).max() < 1e-5
+    A2 = np.ascontiguousarray(A[1000:2024])
+    C2 = np.zeros((1024, N), np.float32)
+    assert L.jepa_b200_gemm(capi.fptr(A2), capi.fptr(B), 1024, N, K, capi.fptr(C2)) == 0, jlib.error_text()
+    assert np.array_equal(C2.view(np.uint32), Cm[1000:2024].view(np.uint32))
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (16, 1024, 1408), (300, 192, 96), (1, 8, 8), (1000, 3072, 1024),
                                    (517, 1024, 4096), (2064, 1408, 1024), (40000, 512, 256)])
 def test_gemm_f16_matches_f64_of_f16_operands(M, N, K):

@@ -139,3 +139,45 @@ def test_gemm_plan_is_constant_on_each_side_of_the_row_threshold():
         assert len(small) == 1 and len(large) == 1, (N, K, small, large)
         if N >= 4096:
             assert small == large, (N, K)
+
+
+def _tile_walk(M, N, K):
+    L = jlib.load()
+    L.jepa_b200_gemm_tile_walk.argtypes = [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int]
+    L.jepa_b200_gemm_tile_walk.restype = C.c_int
+    cap = ((M + 127) // 128) * ((N + 127) // 128)
+    m0, n0 = (C.c_int * max(cap, 1))(), (C.c_int * max(cap, 1))()
+    n = L.jepa_b200_gemm_tile_walk(M, N, K, m0, n0, cap)
+    return n, np.array(m0[:max(n, 0)]), np.array(n0[:max(n, 0)])
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (300, 768, 768), (2048, 3072, 768), (2048, 768, 55296),                 # n-fastest
+    (256, 55296, 768), (2048, 55296, 768), (2100, 55296, 768),              # grouped: one group, whole, ragged
+    (5000, 55296, 768), (131072, 55296, 768), (16 * 128 + 1, 8192, 8192),   # many groups, a one-tile last group
+])
+def test_gemm_tile_walk_visits_every_tile_once(M, N, K):
+    """The persistent kernel's tile walk (its own origin function, run on the host) is a permutation of the
+    output tiles: every tile is computed, none twice, whatever the group raggedness. In the grouped order the
+    tiles that run side by side share a B column tile."""
+    n, m0, n0 = _tile_walk(M, N, K)
+    tm, tn = (M + 127) // 128, (N + 127) // 128
+    assert n == tm * tn
+    assert np.all(m0 % 128 == 0) and np.all(n0 % 128 == 0) and m0.max() < M and n0.max() < N
+    keys = (m0 // 128) * tn + n0 // 128
+    assert np.array_equal(np.sort(keys), np.arange(n))
+    _, plan = _gemm_plan(M, N, K)
+    if plan[2]:
+        # within a group, consecutive tiles step down the rows of one column tile
+        g = min(16, tm)
+        assert np.all(n0[:g] == 0) and np.array_equal(m0[:g], np.arange(g) * 128)
+    else:
+        assert np.array_equal(keys, np.arange(n))
+
+
+def test_gemm_tile_walk_refusals():
+    n, _, _ = _tile_walk(256, 768, 768)          # split-K clusters: no persistent walk
+    assert n == 0
+    L = jlib.load()
+    m0, n0 = (C.c_int * 4)(), (C.c_int * 4)()
+    assert L.jepa_b200_gemm_tile_walk(1024, 1024, 1024, m0, n0, 4) == -1   # 64 tiles, room for 4
