@@ -583,7 +583,7 @@ int HPlanner::step_modulation_bwd(Workspace & w, int t0, int nt) {
 int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
     cudaStream_t st = w.st;
     const DLevel & L = levels[(size_t) w.level - 1];
-    const int S = w.S, T = w.T, D = L.D, P = L.P, F = L.F, I = L.I, NL = L.L, A = L.A;
+    const int S = w.S, T = w.T, D = L.D, P = L.P, F = L.F, NL = L.L, A = L.A;
     const int R = S * T, ldm = 6 * P * NL;
     // ---- conditioning path over every step at once
     const float * cur = w.a_all;
@@ -675,7 +675,6 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
     if (want_grad) { fill_f32(w.gstate, 0.0f, (size_t) (T + 1) * S * D, st); launches++; }
     int n_list = T;   // scored candidates: list positions 1..n_list
     const float * base = w.states + (size_t) S * D;   // position 1
-    float * gbase = w.gstate + (size_t) S * D;
     int Dl = D;
     for (size_t k = 0; k < w.enc.size(); k++) {
         EncStage & e = w.enc[k];
@@ -711,13 +710,11 @@ int HPlanner::forward(Workspace & w, const CostSpec & cs, bool want_grad) {
         }
         if (want_grad) { fill_f32(e.gout, 0.0f, (size_t) n * Dout, st); launches++; }
         base = e.out;
-        gbase = e.gout;
         n_list = e.n;
         Dl = Dout;
     }
     const int W = std::min(std::max(1, cs.cost_last_n), n_list);
     // pointer tables were written when the workspace's graph was planned (solve / plan_cost)
-    (void) gbase;
     cost_l2(w.pred_ptrs, w.goals, w.weights, w.gpred_ptrs, W, S, Dl, Dl, w.cost, want_grad, st);
     launches++;
     // the action cost comes after the state cost, as the reference adds them (hjepa-plan.cpp:769-791)
@@ -782,7 +779,7 @@ int HPlanner::backward(Workspace & w, const CostSpec & cs) {
     (void) cs;
     cudaStream_t st = w.st;
     const DLevel & L = levels[(size_t) w.level - 1];
-    const int S = w.S, T = w.T, D = L.D, P = L.P, F = L.F, I = L.I, NL = L.L, A = L.A;
+    const int S = w.S, T = w.T, D = L.D, P = L.P, F = L.F, NL = L.L, A = L.A;
     const int R = S * T, ldm = 6 * P * NL;
     // ---- the action cost's encoder, into the gradient of the pooled action embeddings
     if (w.pool.Wa > 0 && pool_backward(w)) return -1;
